@@ -1,0 +1,380 @@
+#!/usr/bin/env python
+"""bench.py -- MoE-layer decode tokens/s and Q4_K expert GEMV HBM GB/s.
+
+Workload (one "step" = one decode token through one MoE layer):
+  Mixtral-8x7B-shaped MoE FFN layer: hidden 4096, 8 experts, top-2 softmax
+  routing renormalised, SwiGLU experts 4096->14336->4096 stored Q4_K
+  (793 MB of expert weights per layer), fp32 router 4096x8.  Input tokens are
+  N(0,1), RMSNorm'd by the layer ingress; the layer adds the residual
+  (DistributedPipelineCoordinator.ExecuteStep semantics).  Weights are the
+  documented seeded synthetic generator (no checkpoints exist offline).
+
+  ours       : the sm_100a kernels (router -> fused gate/up+SwiGLU GEMV ->
+               down GEMV + weighted combine), replayed as one CUDA graph per
+               step; 16 input tokens rotate so consecutive steps route to
+               different experts; the 793 MB expert working set is > L2.
+  reference  : the CPU port of the reference's CPU path (CpuWarmExpertPoolWorker
+               shape: per expert gate/up/down mat-vec + SwiGLU, k-ordered
+               combine) with all host threads.  The reference itself is C#
+               (.NET) with its mat-vec in an un-vendored package and cannot run.
+
+Multi-GPU (torchrun): each rank runs its own decode stream on its own GPU
+(weak scaling, replicas of the layer, no data-path collective yet).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+WORKLOAD = dict(name="mixtral8x7b_moe_layer_decode", D=4096, F=14336, E=8, k=2, T=1, seed=20241201,
+                flags=3)  # GLC_FWD_RMSNORM | GLC_FWD_RESIDUAL
+N_TOKENS = 16
+METRIC = "MoE-layer decode tokens/s & Q4_K expert GEMV HBM GB/s vs 8 TB/s, 1/2/4/8 GPU"
+UNIT = "tokens/s"
+REF_BUDGET_S = 120.0
+
+
+def q4k_row_bytes(k):
+    return (k // 256) * 144
+
+
+def algorithmic_bytes(w):
+    """Bytes a step must move: k experts' Q4_K weights + router + activations."""
+    D, F, E, k, T = w["D"], w["F"], w["E"], w["k"], w["T"]
+    gateup = T * k * 2 * F * q4k_row_bytes(D) + T * D * 4 + T * k * F * 4
+    down = T * k * D * q4k_row_bytes(F) + T * k * F * 4 + 2 * T * D * 4
+    router = D * E * 4 + 2 * T * D * 4
+    return {"gateup": gateup, "down": down, "router": router, "step": gateup + down + router}
+
+
+def peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profile_traffic(kernel_tag):
+    """dram bytes per launch from the committed ncu summary (profiles/), or None."""
+    path = os.path.join(REPO, "profiles", f"{kernel_tag}.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":")[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.samples = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.samples.append(parts)
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        return self.summary()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for s in self.samples:
+            for n, v in zip(names, s[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(self.samples)}
+
+
+def make_tokens(w, n):
+    rng = np.random.default_rng(w["seed"])
+    return rng.standard_normal((n, w["T"], w["D"])).astype(np.float32)
+
+
+# --------------------------------------------------------------------- CPU legs
+def cpu_layer(w):
+    from oracle import oracle as o
+    D, F, E = w["D"], w["F"], w["E"]
+    L = {}
+    for m, key, rows, K in ((0, "gate", F, D), (1, "up", F, D), (2, "down", D, F)):
+        L[key] = np.concatenate([o.synth_q4k(w["seed"], o.expert_tag(e, m), rows, K) for e in range(E)])
+    L["router"] = o.fill_normal(w["seed"], 2, 0.02, D * E)
+    return o, L
+
+
+def cpu_run(o, L, w, tokens, budget_s, nthreads, min_tokens=2):
+    """Time the CPU port token by token until budget_s is spent; returns tokens/s."""
+    D = w["D"]
+    out = np.empty(D, np.float32)
+    done, t0 = 0, time.perf_counter()
+    while True:
+        x = tokens[done % len(tokens)][0]
+        o.lib().oc_cpu_moe_token_fast(L["gate"], L["up"], L["down"], L["router"], D, w["F"], w["E"],
+                                      w["k"], 1, w["flags"], x, out, nthreads)
+        done += 1
+        el = time.perf_counter() - t0
+        if (el >= budget_s and done >= min_tokens) or done >= 100000:
+            return done / el, done, el
+
+
+def run_reference(args, w):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    nthreads = os.cpu_count() or 1
+    o, L = cpu_layer(w)
+    tokens = make_tokens(w, N_TOKENS)
+    out = np.empty(w["D"], np.float32)
+
+    def one(i):
+        o.lib().oc_cpu_moe_token_fast(L["gate"], L["up"], L["down"], L["router"], w["D"], w["F"],
+                                      w["E"], w["k"], 1, w["flags"], tokens[i % N_TOKENS][0], out,
+                                      nthreads)
+
+    for i in range(min(args.warmup, 3)):
+        one(i)
+    # A step is one decode token through the layer, as in the GPU arm; the
+    # run stops after REF_BUDGET_S so that any --steps finishes in minutes.
+    done, t0 = 0, time.perf_counter()
+    while done < args.steps and time.perf_counter() - t0 < REF_BUDGET_S:
+        one(done)
+        done += 1
+    total_s = time.perf_counter() - t0
+    value = done / total_s
+    sample = (f"{done} of {args.steps} requested decode steps (time cap {REF_BUDGET_S:.0f} s), "
+              f"same layer and inputs as the GPU arm")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": done, "steps_requested": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 / value,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q4k-f32",
+        "data": "synthetic (seeded generator; no checkpoint offline)",
+        "config": {"workload": w["name"], "hidden": w["D"], "ffn": w["F"], "experts": w["E"],
+                   "top_k": w["k"], "tokens_per_step": w["T"], "weights": "Q4_K"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": nthreads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "CPU port of the reference CPU path (CpuWarmExpertPoolWorker + k-ordered combine); "
+                "the reference C#/.NET build and its Glacier.Inference package are not runnable here",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------------- GPU leg
+def run_ours(args, w):
+    import torch
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    from glacier.inference import distributed_b200 as glc
+
+    D, T = w["D"], w["T"]
+    worker = glc.GpuExpertStageWorker(D, w["F"], w["E"], w["k"], renormalize=True, device=local,
+                                      max_tokens=T)
+    worker.synth_layer(0, w["seed"])
+    stream = torch.cuda.Stream()
+    s = stream.cuda_stream
+    tokens = torch.from_numpy(make_tokens(w, N_TOKENS)).cuda()
+    x_in = torch.empty(T, D, device="cuda")
+    out = torch.empty(T, D, device="cuda")
+    x_in.copy_(tokens[0])
+    torch.cuda.synchronize()
+    worker.graph_build(0, x_in.data_ptr(), T, w["flags"], out.data_ptr())
+
+    def step(i):
+        x_in.copy_(tokens[i % N_TOKENS], non_blocking=True)
+        worker.graph_launch(s)
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i)
+    torch.cuda.synchronize()
+    worker.poll_error()
+
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    ms_total = ev0.elapsed_time(ev1)
+    clocks = sampler.stop() if sampler else None
+    worker.poll_error()
+    t = torch.tensor([ms_total], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_total = float(t.item())
+    value = world * args.steps * T / (ms_total / 1000.0)
+
+    # Per-kernel device times (CUDA events on the launching stream, same step).
+    worker.set_profiling(True)
+    kt = []
+    nprof = min(max(args.steps, 20), 400)
+    with torch.cuda.stream(stream):
+        for i in range(nprof):
+            x_in.copy_(tokens[i % N_TOKENS], non_blocking=True)
+            worker.forward_dev(0, x_in.data_ptr(), T, w["flags"], out.data_ptr(), stream=s)
+            kt.append(worker.kernel_times_ms())
+    worker.set_profiling(False)
+    kt = np.array(kt)  # [n, 3]: router, gate/up, down
+    med = np.median(kt, axis=0)
+    avg = kt.mean(axis=0)
+    ab = algorithmic_bytes(w)
+    peak, peak_kind = peaks()
+    gu_gbs = ab["gateup"] / (avg[1] * 1e-3) / 1e9
+    dn_gbs = ab["down"] / (avg[2] * 1e-3) / 1e9
+    layer_gbs = ab["step"] / (ms_total / args.steps * 1e-3) / 1e9
+
+    # End to end through the public host API: pinned host input -> H2D ->
+    # layer -> D2H output + expert ids/weights, every step.
+    e2e_steps = min(args.steps, 2000)
+    hx = torch.from_numpy(make_tokens(w, N_TOKENS)).pin_memory().numpy()
+    hout = torch.empty(T, D, pin_memory=True).numpy()
+    hids = torch.empty(T, w["k"], dtype=torch.int32, pin_memory=True).numpy()
+    hw = torch.empty(T, w["k"], pin_memory=True).numpy()
+    import ctypes as C
+    L = glc.lib()
+    for i in range(min(args.warmup, 20)):
+        glc._lib.check(L.glc_moe_forward(worker._handle(), 0, hx[i % N_TOKENS].ctypes.data, T,
+                                         w["flags"], hout.ctypes.data, hids.ctypes.data, hw.ctypes.data))
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        glc._lib.check(L.glc_moe_forward(worker._handle(), 0, hx[i % N_TOKENS].ctypes.data, T,
+                                         w["flags"], hout.ctypes.data, hids.ctypes.data, hw.ctypes.data))
+    e2e_s = time.perf_counter() - t0
+    te = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = world * e2e_steps * T / float(te.item())
+    del C
+
+    cpu_baseline = None
+    if rank == 0 and world == 1 and not args.skip_cpu_baseline:
+        o, Lc = cpu_layer(w)
+        nthreads = os.cpu_count() or 1
+        r, n, el = cpu_run(o, Lc, w, make_tokens(w, N_TOKENS), args.cpu_seconds, nthreads)
+        cpu_baseline = {"value": r, "unit": UNIT, "cores": nthreads, "kind": "port",
+                        "sample": f"{n} decode tokens in {el:.1f} s through the CPU port of the "
+                                  f"reference CPU path, same layer and inputs"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_total / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "q4k-int16dp-f32",
+            "data": "synthetic (seeded generator; no checkpoint offline)",
+            "config": {"workload": w["name"], "hidden": D, "ffn": w["F"], "experts": w["E"],
+                       "top_k": w["k"], "tokens_per_step_per_gpu": T, "weights": "Q4_K",
+                       "parallelism": f"replica x{world}" if world > 1 else "single",
+                       "l2": "inputs larger than L2: 793 MB expert working set, 16 rotating tokens",
+                       "submission": "one CUDA graph per step (router, gate/up+SwiGLU, down+combine)"},
+            "roofline": {"bound": "hbm", "kernel": "q4k_gemv gate/up+SwiGLU",
+                         "achieved": gu_gbs, "peak": peak, "unit": "GB/s", "frac": gu_gbs / peak,
+                         "peak_kind": peak_kind,
+                         "algorithmic_bytes_per_launch": ab["gateup"],
+                         "avg_launch_ms": float(avg[1]),
+                         "traffic": profile_traffic("q4k_gemv_gateup_mixtral_decode")},
+            "kernels": {"router_ms": float(avg[0]), "gateup_ms": float(avg[1]), "down_ms": float(avg[2]),
+                        "gateup_ms_median": float(med[1]), "down_ms_median": float(med[2]),
+                        "down_gbs": dn_gbs, "down_frac": dn_gbs / peak,
+                        "layer_gbs": layer_gbs, "layer_frac": layer_gbs / peak,
+                        "algorithmic_bytes_per_step": ab["step"]},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": T * D * 4,
+                    "d2h_bytes_per_step": T * D * 4 + T * w["k"] * 8, "steps": e2e_steps,
+                    "api": "glc_moe_forward (host buffers, synchronous)"},
+            "gpu_launches": 3 * args.steps,
+            "clocks": clocks,
+        }
+        if cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline
+        print(json.dumps(line), flush=True)
+    worker.dispose()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=200)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--skip-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    w = dict(WORKLOAD)
+    if args.impl == "reference":
+        return run_reference(args, w)
+    return run_ours(args, w)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,7 @@
+"""B200 (sm_100a) backend for the quantized MoE feed-forward hot path of
+Glacier.Inference.Distributed: Q4_K expert GEMV / grouped GEMM, router,
+dispatch, SwiGLU, weighted combine and the INT8 stage-boundary wire codec,
+behind the C ABI in include/glacier_b200.h."""
+from ._lib import GlcError, LIB_PATH, lib  # noqa: F401
+from .api import (FusedActivationHeader, GpuExpertStageWorker, QuantizationKernels,  # noqa: F401
+                  WirePrecisionMode, device_count, gemv_q4k_dev, q4k_row_bytes, router_topk_dev)

@@ -1,0 +1,256 @@
+"""Host-side mirror of the reference's operator API for the MoE FFN hot path.
+
+Names follow the reference so that callers (and tests) read like the
+reference's own code:
+
+* ``GpuExpertStageWorker.process_activation``  -> IInferenceStageWorker.ProcessActivation
+  (IInferenceStageWorker.cs:43; CpuWarmExpertPoolWorker.cs:203-278)
+* ``GpuExpertStageWorker.process_routed_topk`` -> GpuFirstExpertStageWorker.ProcessRoutedTopK
+  (GpuFirstExpertStageWorker.cs:416-583)
+* ``GpuExpertStageWorker.forward``             -> router + DistributedPipelineCoordinator.ExecuteStep
+  (DistributedPipelineCoordinator.cs:72-137) for T tokens
+* ``QuantizationKernels``                       -> Protocol/QuantizationKernels.cs:57-163
+* ``FusedActivationHeader``                     -> Protocol/FusedActivationHeader.cs:41-218
+
+Every call goes through the C ABI of libglacier_b200.so; nothing here computes.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _lib
+from ._lib import GlcError, check, lib
+
+WirePrecisionMode = type("WirePrecisionMode", (), {
+    "FP32": 0, "FP16": 1, "INT8_Symmetric": 2, "FP8_E4M3": 3})
+
+
+def _ptr(a: np.ndarray | None):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+def q4k_row_bytes(k: int) -> int:
+    return int(lib().glc_q4k_row_bytes(int(k)))
+
+
+def device_count() -> int:
+    n = C.c_int32(0)
+    st = lib().glc_device_count(C.byref(n))
+    return int(n.value) if st == 0 else 0
+
+
+class GpuExpertStageWorker:
+    """One MoE layer family resident in HBM on one device (GGUF Q4_K experts)."""
+
+    def __init__(self, hidden_dim: int, expert_ffn_dim: int, num_experts: int, top_k: int, *,
+                 shared_ffn_dim: int = 0, renormalize: bool = True, device: int = 0,
+                 num_layers: int = 1, max_tokens: int = 1, expert_begin: int = 0,
+                 expert_count: int = 0):
+        self.desc = _lib.MoeDesc(hidden_dim, expert_ffn_dim, num_experts, top_k, shared_ffn_dim,
+                                 int(renormalize), _lib.GLC_GGUF_Q4_K, device, num_layers,
+                                 max_tokens, expert_begin, expert_count)
+        h = C.c_void_p()
+        check(lib().glc_moe_create(C.byref(self.desc), C.byref(h)))
+        self._h = h
+        self.hidden_dim, self.expert_ffn_dim = hidden_dim, expert_ffn_dim
+        self.num_experts, self.top_k = num_experts, top_k
+        self.max_tokens = max_tokens
+
+    # -- lifecycle --------------------------------------------------------
+    def dispose(self) -> None:
+        if self._h:
+            check(lib().glc_moe_destroy(self._h))
+            self._h = None
+
+    close = dispose
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.dispose()
+
+    def _handle(self):
+        if not self._h:
+            raise GlcError(-5, "handle was disposed")
+        return self._h
+
+    # -- weights ----------------------------------------------------------
+    def load_layer(self, layer: int, gate_exps: np.ndarray, up_exps: np.ndarray,
+                   down_exps: np.ndarray, router: np.ndarray | None = None,
+                   shared_gate=None, shared_up=None, shared_down=None, shared_gate_vec=None):
+        keep = [np.ascontiguousarray(a) if a is not None else None for a in
+                (gate_exps, up_exps, down_exps, router, shared_gate, shared_up, shared_down,
+                 shared_gate_vec)]
+        w = _lib.LayerWeights(*[_ptr(a) for a in keep])
+        check(lib().glc_moe_load_layer(self._handle(), layer, C.byref(w)))
+
+    def synth_layer(self, layer: int, seed: int) -> None:
+        check(lib().glc_moe_synth_layer(self._handle(), layer, C.c_uint64(seed)))
+
+    def layer_device_ptrs(self, layer: int = 0):
+        g, u, d, r = C.c_void_p(), C.c_void_p(), C.c_void_p(), C.c_void_p()
+        check(lib().glc_moe_layer_device_ptrs(self._handle(), layer, C.byref(g), C.byref(u),
+                                              C.byref(d), C.byref(r)))
+        return g.value, u.value, d.value, r.value
+
+    # -- telemetry --------------------------------------------------------
+    def set_profiling(self, enable: bool) -> None:
+        check(lib().glc_moe_set_profiling(self._handle(), int(enable)))
+
+    def kernel_times_ms(self) -> list[float]:
+        buf = (C.c_float * 16)()
+        n = C.c_int32(0)
+        check(lib().glc_moe_kernel_times(self._handle(), buf, 16, C.byref(n)))
+        return [float(buf[i]) for i in range(min(n.value, 16))]
+
+    def poll_error(self) -> None:
+        check(lib().glc_moe_poll_error(self._handle()))
+
+    # -- operator API -----------------------------------------------------
+    def process_activation(self, layer: int, expert_id: int, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32)
+        if x.size < self.hidden_dim:
+            raise GlcError(-1, f"Input activation size ({x.nbytes} bytes) is smaller than required "
+                               f"hidden dimension ({4 * self.hidden_dim} bytes for D={self.hidden_dim}).")
+        y = np.empty(self.hidden_dim, np.float32)
+        check(lib().glc_expert_forward(self._handle(), layer, expert_id, _ptr(x), _ptr(y)))
+        return y
+
+    def process_routed_topk(self, layer: int, x: np.ndarray, ids, weights) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32)
+        ids = np.ascontiguousarray(ids, np.int32)
+        weights = np.ascontiguousarray(weights, np.float32)
+        k = min(ids.size, weights.size)
+        out = np.empty(self.hidden_dim, np.float32)
+        check(lib().glc_routed_topk(self._handle(), layer, _ptr(x), _ptr(ids), _ptr(weights), k,
+                                    _ptr(out)))
+        return out
+
+    def forward(self, layer: int, x: np.ndarray, flags: int = 0):
+        x = np.ascontiguousarray(x, np.float32)
+        if x.ndim == 1:
+            x = x[None, :]
+        T = x.shape[0]
+        out = np.empty_like(x)
+        ids = np.empty((T, self.top_k), np.int32)
+        w = np.empty((T, self.top_k), np.float32)
+        check(lib().glc_moe_forward(self._handle(), layer, _ptr(x), T, flags, _ptr(out), _ptr(ids),
+                                    _ptr(w)))
+        return out, ids, w
+
+    def forward_dev(self, layer: int, x_ptr: int, T: int, flags: int, out_ptr: int,
+                    ids_ptr: int | None = None, w_ptr: int | None = None, stream: int | None = None):
+        check(lib().glc_moe_forward_dev(self._handle(), layer, x_ptr, T, flags, out_ptr, ids_ptr,
+                                        w_ptr, stream))
+
+    def graph_build(self, layer: int, x_ptr: int, T: int, flags: int, out_ptr: int) -> None:
+        check(lib().glc_moe_graph_build(self._handle(), layer, x_ptr, T, flags, out_ptr))
+
+    def graph_launch(self, stream: int | None = None) -> None:
+        check(lib().glc_moe_graph_launch(self._handle(), stream))
+
+    def process_activation_dev(self, layer: int, expert_id: int, x_ptr: int, y_ptr: int,
+                               stream: int | None = None):
+        check(lib().glc_expert_forward_dev(self._handle(), layer, expert_id, x_ptr, y_ptr, stream))
+
+
+def gemv_q4k_dev(W_ptr: int, x_ptr: int, y_ptr: int, K: int, N: int, stream: int | None = None):
+    """QuantKernels.MatVecMul(Q4_K, W, x, y, nCols=K, nRows=N) on device pointers."""
+    check(lib().glc_gemv_q4k_dev(W_ptr, x_ptr, y_ptr, K, N, stream))
+
+
+def router_topk_dev(x_ptr, router_ptr, T, D, E, k, renormalize, rmsnorm, xin_ptr, logits_ptr,
+                    ids_ptr, w_ptr, stream=None):
+    check(lib().glc_router_topk_dev(x_ptr, router_ptr, T, D, E, k, int(renormalize), int(rmsnorm),
+                                    xin_ptr, logits_ptr, ids_ptr, w_ptr, stream))
+
+
+class QuantizationKernels:
+    """GPU implementation of the wire codec, same names and byte layout as the reference."""
+
+    @staticmethod
+    def GetPackedTokenBytes(mode: int, dim: int) -> int:
+        return int(lib().glc_wire_token_bytes(mode, dim))
+
+    @staticmethod
+    def GetPackedBatchBytes(mode: int, dim: int, token_count: int) -> int:
+        return QuantizationKernels.GetPackedTokenBytes(mode, dim) * token_count
+
+    @staticmethod
+    def QuantizeBatch(x: np.ndarray, destination: np.ndarray, dim: int, token_count: int,
+                      mode: int) -> None:
+        x = np.ascontiguousarray(x, np.float32)
+        if x.size < dim * token_count:
+            raise GlcError(-1, "Input float span smaller than dim * tokenCount")
+        check(lib().glc_wire_quantize(mode, _ptr(x), token_count, dim, _ptr(destination),
+                                      destination.nbytes))
+
+    @staticmethod
+    def DequantizeBatch(source: np.ndarray, destination: np.ndarray, dim: int, token_count: int,
+                        mode: int) -> None:
+        if destination.size < dim * token_count:
+            raise GlcError(-1, "Destination float span smaller than dim * tokenCount")
+        src = np.ascontiguousarray(source, np.uint8)
+        check(lib().glc_wire_dequantize(mode, _ptr(src), src.nbytes, token_count, dim,
+                                        _ptr(destination)))
+
+    @staticmethod
+    def QuantizeToken(x: np.ndarray, destination: np.ndarray, mode: int) -> float:
+        x = np.ascontiguousarray(x, np.float32).reshape(-1)
+        QuantizationKernels.QuantizeBatch(x, destination, x.size, 1, mode)
+        if mode in (2, 3):
+            return float(np.frombuffer(destination[:4].tobytes(), "<f4")[0])
+        return 1.0
+
+    @staticmethod
+    def DequantizeToken(source: np.ndarray, destination: np.ndarray, mode: int) -> None:
+        QuantizationKernels.DequantizeBatch(source, destination, destination.size, 1, mode)
+
+    @staticmethod
+    def quantize_dev(mode: int, x_ptr: int, T: int, D: int, out_ptr: int, stream=None) -> None:
+        check(lib().glc_wire_quantize_dev(mode, x_ptr, T, D, out_ptr, stream))
+
+    @staticmethod
+    def dequantize_dev(mode: int, in_ptr: int, T: int, D: int, out_ptr: int, stream=None) -> None:
+        check(lib().glc_wire_dequantize_dev(mode, in_ptr, T, D, out_ptr, stream))
+
+
+@dataclass
+class FusedActivationHeader:
+    sequence_id: int
+    token_index: int
+    layer_index: int
+    hidden_dim: int
+    precision_mode: int
+    flags: int = 0
+    scale: float = 1.0
+    batch_tokens: int = 0
+    HeaderSize = 32
+    FusedMagic = 0x47414354
+
+    def _c(self) -> _lib.FusedHeader:
+        return _lib.FusedHeader(self.sequence_id, self.token_index, self.layer_index,
+                                self.hidden_dim, self.precision_mode, self.flags,
+                                self.batch_tokens, self.scale)
+
+    def write_to(self) -> bytes:
+        buf = (C.c_uint8 * 32)()
+        check(lib().glc_fused_header_write(C.byref(self._c()), buf))
+        return bytes(buf)
+
+    @staticmethod
+    def read_from(data: bytes) -> "FusedActivationHeader":
+        if len(data) < 32:
+            raise GlcError(-1, "Source too small for FusedActivationHeader")
+        buf = (C.c_uint8 * 32).from_buffer_copy(bytes(data[:32]))
+        h = _lib.FusedHeader()
+        check(lib().glc_fused_header_read(buf, C.byref(h)))
+        return FusedActivationHeader(h.sequence_id, h.token_index, h.layer_index, h.hidden_dim,
+                                     h.precision_mode, h.flags, h.scale, h.batch_tokens)
+
+    def get_payload_byte_count(self) -> int:
+        return int(lib().glc_fused_header_payload_bytes(C.byref(self._c())))

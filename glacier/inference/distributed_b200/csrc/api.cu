@@ -1,0 +1,787 @@
+// api.cu -- the C ABI of libglacier_b200.so (include/glacier_b200.h).
+//
+// Host orchestration of the sm_100a kernels behind the reference's operator
+// API: IInferenceStageWorker.ProcessActivation (IInferenceStageWorker.cs:43),
+// GpuFirstExpertStageWorker.ProcessRoutedTopK (GpuFirstExpertStageWorker.cs:416),
+// the MoE layer step (DistributedPipelineCoordinator.ExecuteStep, :72) and the
+// QuantizationKernels wire codec (Protocol/QuantizationKernels.cs:86-163).
+// There is no CPU fallback: every compute entry point runs on the GPU or
+// returns an error.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../../../include/glacier_b200.h"
+#include "kernels.h"
+#include "synth.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+#define CUDA_TRY(expr)                                                                        \
+    do {                                                                                      \
+        cudaError_t e_ = (expr);                                                              \
+        if (e_ != cudaSuccess)                                                                \
+            return fail(e_ == cudaErrorMemoryAllocation ? GLC_ERR_OOM : GLC_ERR_CUDA,         \
+                        "%s failed: %s (%s:%d)", #expr, cudaGetErrorString(e_), __FILE__,     \
+                        __LINE__);                                                            \
+    } while (0)
+
+int64_t rowbytes(int k) { return (int64_t)(k / 256) * 144; }
+
+int host_threads() {
+    unsigned n = std::thread::hardware_concurrency();
+    return n == 0 ? 1 : (int)std::min(n, 32u);
+}
+
+struct LayerDev {
+    uint8_t* gate = nullptr;
+    uint8_t* up = nullptr;
+    uint8_t* down = nullptr;
+    float* router = nullptr;
+    uint8_t* sh_gate = nullptr;
+    uint8_t* sh_up = nullptr;
+    uint8_t* sh_down = nullptr;
+    float* sh_gate_vec = nullptr;
+    bool loaded = false;
+};
+
+}  // namespace
+
+struct glc_moe {
+    glc_moe_desc d{};
+    int num_sms = 0;
+    int disposed = 0;
+    cudaStream_t stream = nullptr;
+    std::vector<LayerDev> layers;
+    // device workspace sized for max_tokens
+    float* x = nullptr;        // [T][D]
+    float* xin = nullptr;      // [T][D]
+    float* out = nullptr;      // [T][D]
+    float* act = nullptr;      // [T*k][F]
+    float* act_sh = nullptr;   // [T][Fs]
+    float* wts = nullptr;      // [T*k]
+    float* gate_out = nullptr; // [T]
+    int* ids = nullptr;        // [T*k]
+    int* zeros_i = nullptr;    // [T] expert id 0 for the shared expert
+    int* err = nullptr;        // device error word
+    // pinned host staging
+    float* h_x = nullptr;
+    float* h_out = nullptr;
+    int* h_ids = nullptr;
+    float* h_w = nullptr;
+    // optional per-kernel CUDA-event timing of the last forward (launch order)
+    int profiling = 0;
+    int n_marks = 0;
+    cudaEvent_t marks[16] = {};
+    // captured decode step
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t graph_exec = nullptr;
+};
+
+namespace {
+
+int check_handle(glc_moe* h) {
+    if (!h) return fail(GLC_ERR_INVALID_ARG, "null handle");
+    if (h->disposed) return fail(GLC_ERR_DISPOSED, "handle was destroyed");
+    cudaError_t e = cudaSetDevice(h->d.device);
+    if (e != cudaSuccess) return fail(GLC_ERR_CUDA, "cudaSetDevice(%d): %s", h->d.device, cudaGetErrorString(e));
+    return GLC_OK;
+}
+
+int local_experts(const glc_moe* h) { return h->d.expert_count > 0 ? h->d.expert_count : h->d.num_experts; }
+
+LayerDev* layer_of(glc_moe* h, int layer) {
+    // LayerIndex is clamped like CpuWarmExpertPoolWorker.cs:243.
+    int n = (int)h->layers.size();
+    int l = layer < 0 ? 0 : (layer >= n ? n - 1 : layer);
+    return &h->layers[l];
+}
+
+// Records a timing mark on `st` when profiling is enabled (marks[i+1]-marks[i]
+// is the device time of the i-th kernel of the last forward).
+void mark(glc_moe* h, cudaStream_t st) {
+    if (!h->profiling || h->n_marks >= 16) return;
+    cudaEventRecord(h->marks[h->n_marks++], st);
+}
+
+int check_device_error(glc_moe* h) {
+    int code = 0;
+    CUDA_TRY(cudaMemcpy(&code, h->err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (code != 0) {
+        cudaMemset(h->err, 0, sizeof(int));
+        return fail(GLC_ERR_TIMEOUT, "device-side wait gave up (code %d)", code);
+    }
+    return GLC_OK;
+}
+
+// Decode-path expert launches: gate/up + SwiGLU over `npairs` (token, slot)
+// pairs, then the down projection with the weighted combine per token.
+int run_experts(glc_moe* h, LayerDev* L, const float* xin, int T, int k, const int* ids,
+                const float* wts, const float* resid, float* out, cudaStream_t st) {
+    const int D = h->d.hidden_dim, F = h->d.expert_ffn_dim, E = local_experts(h);
+    glc::GemvParams g{};
+    g.mode = glc::kGemvGateUp;
+    g.K = D;
+    g.rows = F;
+    g.nseg = T * k;
+    g.kslots = k;
+    g.num_experts = E;
+    g.A = L->gate;
+    g.B = L->up;
+    g.expert_bytes = (long long)F * rowbytes(D);
+    g.ids = ids;
+    g.x = xin;
+    g.y = h->act;
+    g.err = h->err;
+    CUDA_TRY(glc::gemv_launch(g, h->num_sms, st));
+    mark(h, st);
+    glc::GemvParams dn{};
+    dn.mode = glc::kGemvDownCombine;
+    dn.K = F;
+    dn.rows = D;
+    dn.nseg = T;
+    dn.kslots = k;
+    dn.num_experts = E;
+    dn.A = L->down;
+    dn.expert_bytes = (long long)D * rowbytes(F);
+    dn.ids = ids;
+    dn.cw = wts;
+    dn.x = h->act;
+    dn.resid = resid;
+    dn.y = out;
+    dn.err = h->err;
+    CUDA_TRY(glc::gemv_launch(dn, h->num_sms, st));
+    mark(h, st);
+    return GLC_OK;
+}
+
+int run_shared_expert(glc_moe* h, LayerDev* L, const float* xin, int T, float* out, cudaStream_t st) {
+    const int D = h->d.hidden_dim, Fs = h->d.shared_ffn_dim;
+    glc::GemvParams g{};
+    g.mode = glc::kGemvGateUp;
+    g.K = D;
+    g.rows = Fs;
+    g.nseg = T;
+    g.kslots = 1;
+    g.num_experts = 1;
+    g.A = L->sh_gate;
+    g.B = L->sh_up;
+    g.expert_bytes = 0;
+    g.ids = h->zeros_i;
+    g.x = xin;
+    g.y = h->act_sh;
+    g.err = h->err;
+    CUDA_TRY(glc::gemv_launch(g, h->num_sms, st));
+    mark(h, st);
+    glc::GemvParams dn{};
+    dn.mode = glc::kGemvDownCombine;
+    dn.K = Fs;
+    dn.rows = D;
+    dn.nseg = T;
+    dn.kslots = 1;
+    dn.num_experts = 1;
+    dn.A = L->sh_down;
+    dn.expert_bytes = 0;
+    dn.ids = h->zeros_i;
+    dn.cw = h->gate_out;
+    dn.x = h->act_sh;
+    dn.y = out;
+    dn.accumulate = 1;
+    dn.err = h->err;
+    CUDA_TRY(glc::gemv_launch(dn, h->num_sms, st));
+    mark(h, st);
+    return GLC_OK;
+}
+
+void free_layer(LayerDev& L) {
+    cudaFree(L.gate); cudaFree(L.up); cudaFree(L.down); cudaFree(L.router);
+    cudaFree(L.sh_gate); cudaFree(L.sh_up); cudaFree(L.sh_down); cudaFree(L.sh_gate_vec);
+    L = LayerDev{};
+}
+
+int alloc_layer(glc_moe* h, LayerDev& L) {
+    if (L.gate) return GLC_OK;
+    const int D = h->d.hidden_dim, F = h->d.expert_ffn_dim, E = h->d.num_experts, El = local_experts(h);
+    const size_t gsz = (size_t)El * F * rowbytes(D), dsz = (size_t)El * D * rowbytes(F);
+    CUDA_TRY(cudaMalloc(&L.gate, gsz));
+    CUDA_TRY(cudaMalloc(&L.up, gsz));
+    CUDA_TRY(cudaMalloc(&L.down, dsz));
+    CUDA_TRY(cudaMalloc(&L.router, sizeof(float) * (size_t)D * E));
+    if (h->d.shared_ffn_dim > 0) {
+        const int Fs = h->d.shared_ffn_dim;
+        CUDA_TRY(cudaMalloc(&L.sh_gate, (size_t)Fs * rowbytes(D)));
+        CUDA_TRY(cudaMalloc(&L.sh_up, (size_t)Fs * rowbytes(D)));
+        CUDA_TRY(cudaMalloc(&L.sh_down, (size_t)D * rowbytes(Fs)));
+        CUDA_TRY(cudaMalloc(&L.sh_gate_vec, sizeof(float) * D));
+    }
+    return GLC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int glc_abi_version(void) { return GLC_ABI_VERSION; }
+
+const char* glc_last_error(void) { return g_last_error.c_str(); }
+
+int glc_device_count(int32_t* count) {
+    if (!count) return fail(GLC_ERR_INVALID_ARG, "null count");
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) {
+        *count = 0;
+        return fail(GLC_ERR_CUDA, "cudaGetDeviceCount: %s", cudaGetErrorString(e));
+    }
+    *count = n;
+    return GLC_OK;
+}
+
+int64_t glc_q4k_row_bytes(int32_t k) {
+    if (k <= 0 || (k % 256) != 0) return -1;
+    return rowbytes(k);
+}
+
+int glc_moe_create(const glc_moe_desc* desc, glc_moe** out) {
+    if (!desc || !out) return fail(GLC_ERR_INVALID_ARG, "null argument");
+    *out = nullptr;
+    const glc_moe_desc& d = *desc;
+    if (d.hidden_dim <= 0 || d.expert_ffn_dim <= 0 || d.num_experts <= 0)
+        return fail(GLC_ERR_INVALID_ARG, "dimensions must be positive (D=%d F=%d E=%d)", d.hidden_dim,
+                    d.expert_ffn_dim, d.num_experts);
+    if (d.weight_type != GLC_GGUF_Q4_K)
+        return fail(GLC_ERR_UNSUPPORTED, "weight type %d not supported (Q4_K = 12)", d.weight_type);
+    if (d.hidden_dim % 256 || d.expert_ffn_dim % 256 || (d.shared_ffn_dim > 0 && d.shared_ffn_dim % 256))
+        return fail(GLC_ERR_UNSUPPORTED, "Q4_K needs dimensions that are multiples of 256");
+    if (d.top_k <= 0 || d.top_k > d.num_experts || d.top_k > 16 || d.num_experts > 64)
+        return fail(GLC_ERR_INVALID_ARG, "top_k %d / num_experts %d out of range", d.top_k, d.num_experts);
+    if (d.num_layers <= 0 || d.max_tokens <= 0) return fail(GLC_ERR_INVALID_ARG, "num_layers and max_tokens must be positive");
+    if (d.expert_begin < 0 || d.expert_count < 0 || d.expert_begin + (d.expert_count ? d.expert_count : d.num_experts) > d.num_experts)
+        return fail(GLC_ERR_INVALID_ARG, "expert shard out of range");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return fail(GLC_ERR_CUDA, "no CUDA device");
+    if (d.device < 0 || d.device >= ndev) return fail(GLC_ERR_INVALID_ARG, "device %d out of range", d.device);
+    CUDA_TRY(cudaSetDevice(d.device));
+    cudaDeviceProp prop;
+    CUDA_TRY(cudaGetDeviceProperties(&prop, d.device));
+    if (prop.major < 10) return fail(GLC_ERR_UNSUPPORTED, "device %d is sm_%d%d; sm_100a required", d.device, prop.major, prop.minor);
+
+    glc_moe* h = new glc_moe();
+    h->d = d;
+    h->num_sms = prop.multiProcessorCount;
+    h->layers.resize(d.num_layers);
+    const size_t T = d.max_tokens, D = d.hidden_dim, F = d.expert_ffn_dim, k = d.top_k;
+    const size_t Fs = d.shared_ffn_dim > 0 ? d.shared_ffn_dim : 0;
+    auto cleanup = [&](int rc) { glc_moe_destroy(h); return rc; };
+#define ALLOC(ptr, bytes)                                                                     \
+    do {                                                                                      \
+        cudaError_t e_ = cudaMalloc(&(ptr), (bytes));                                         \
+        if (e_ != cudaSuccess) return cleanup(fail(GLC_ERR_OOM, "cudaMalloc %zu: %s", (size_t)(bytes), cudaGetErrorString(e_))); \
+    } while (0)
+    if (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess)
+        return cleanup(fail(GLC_ERR_CUDA, "cudaStreamCreate failed"));
+    ALLOC(h->x, sizeof(float) * T * D);
+    ALLOC(h->xin, sizeof(float) * T * D);
+    ALLOC(h->out, sizeof(float) * T * D);
+    ALLOC(h->act, sizeof(float) * T * k * F);
+    if (Fs) ALLOC(h->act_sh, sizeof(float) * T * Fs);
+    ALLOC(h->wts, sizeof(float) * T * k);
+    ALLOC(h->gate_out, sizeof(float) * T);
+    ALLOC(h->ids, sizeof(int) * T * k);
+    ALLOC(h->zeros_i, sizeof(int) * T);
+    ALLOC(h->err, sizeof(int));
+#undef ALLOC
+    cudaMemset(h->zeros_i, 0, sizeof(int) * T);
+    cudaMemset(h->err, 0, sizeof(int));
+    if (cudaMallocHost(&h->h_x, sizeof(float) * T * D) != cudaSuccess ||
+        cudaMallocHost(&h->h_out, sizeof(float) * T * D) != cudaSuccess ||
+        cudaMallocHost(&h->h_ids, sizeof(int) * T * k) != cudaSuccess ||
+        cudaMallocHost(&h->h_w, sizeof(float) * T * k) != cudaSuccess)
+        return cleanup(fail(GLC_ERR_OOM, "cudaMallocHost failed"));
+    if (cudaDeviceSynchronize() != cudaSuccess) return cleanup(fail(GLC_ERR_CUDA, "device sync failed"));
+    *out = h;
+    return GLC_OK;
+}
+
+int glc_moe_destroy(glc_moe* h) {
+    if (!h) return GLC_OK;
+    cudaSetDevice(h->d.device);
+    if (h->stream) cudaStreamSynchronize(h->stream);
+    for (auto& L : h->layers) free_layer(L);
+    for (auto& e : h->marks)
+        if (e) cudaEventDestroy(e);
+    if (h->graph_exec) cudaGraphExecDestroy(h->graph_exec);
+    if (h->graph) cudaGraphDestroy(h->graph);
+    cudaFree(h->x); cudaFree(h->xin); cudaFree(h->out); cudaFree(h->act); cudaFree(h->act_sh);
+    cudaFree(h->wts); cudaFree(h->gate_out); cudaFree(h->ids); cudaFree(h->zeros_i); cudaFree(h->err);
+    cudaFreeHost(h->h_x); cudaFreeHost(h->h_out); cudaFreeHost(h->h_ids); cudaFreeHost(h->h_w);
+    if (h->stream) cudaStreamDestroy(h->stream);
+    h->disposed = 1;
+    delete h;
+    return GLC_OK;
+}
+
+int glc_moe_load_layer(glc_moe* h, int32_t layer, const glc_layer_weights* w) {
+    int rc = check_handle(h);
+    if (rc) return rc;
+    if (!w || !w->gate_exps || !w->up_exps || !w->down_exps) return fail(GLC_ERR_INVALID_ARG, "null weight pointer");
+    if (layer < 0 || layer >= h->d.num_layers) return fail(GLC_ERR_INVALID_ARG, "layer %d out of range", layer);
+    LayerDev& L = h->layers[layer];
+    rc = alloc_layer(h, L);
+    if (rc) return rc;
+    const int D = h->d.hidden_dim, F = h->d.expert_ffn_dim, E = h->d.num_experts, El = local_experts(h);
+    const size_t gsz = (size_t)El * F * rowbytes(D), dsz = (size_t)El * D * rowbytes(F);
+    CUDA_TRY(cudaMemcpy(L.gate, w->gate_exps, gsz, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(L.up, w->up_exps, gsz, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(L.down, w->down_exps, dsz, cudaMemcpyHostToDevice));
+    if (w->router) CUDA_TRY(cudaMemcpy(L.router, w->router, sizeof(float) * (size_t)D * E, cudaMemcpyHostToDevice));
+    else CUDA_TRY(cudaMemset(L.router, 0, sizeof(float) * (size_t)D * E));
+    if (h->d.shared_ffn_dim > 0) {
+        const int Fs = h->d.shared_ffn_dim;
+        if (!w->shared_gate || !w->shared_up || !w->shared_down || !w->shared_gate_vec)
+            return fail(GLC_ERR_INVALID_ARG, "shared expert weights missing");
+        CUDA_TRY(cudaMemcpy(L.sh_gate, w->shared_gate, (size_t)Fs * rowbytes(D), cudaMemcpyHostToDevice));
+        CUDA_TRY(cudaMemcpy(L.sh_up, w->shared_up, (size_t)Fs * rowbytes(D), cudaMemcpyHostToDevice));
+        CUDA_TRY(cudaMemcpy(L.sh_down, w->shared_down, (size_t)D * rowbytes(Fs), cudaMemcpyHostToDevice));
+        CUDA_TRY(cudaMemcpy(L.sh_gate_vec, w->shared_gate_vec, sizeof(float) * D, cudaMemcpyHostToDevice));
+    }
+    L.loaded = true;
+    return GLC_OK;
+}
+
+int glc_moe_synth_layer(glc_moe* h, int32_t layer, uint64_t seed) {
+    int rc = check_handle(h);
+    if (rc) return rc;
+    if (layer < 0 || layer >= h->d.num_layers) return fail(GLC_ERR_INVALID_ARG, "layer %d out of range", layer);
+    LayerDev& L = h->layers[layer];
+    rc = alloc_layer(h, L);
+    if (rc) return rc;
+    const int D = h->d.hidden_dim, F = h->d.expert_ffn_dim, E = h->d.num_experts, El = local_experts(h);
+    const int nt = host_threads();
+    // Stage one matrix at a time through a host buffer.
+    const size_t gsl = (size_t)F * rowbytes(D), dsl = (size_t)D * rowbytes(F);
+    std::vector<uint8_t> buf(std::max(gsl, dsl));
+    for (int el = 0; el < El; ++el) {
+        const int e = h->d.expert_begin + el;
+        glc::synth_q4k(seed, glc::expert_tag(e, 0), 0.01f, buf.data(), gsl / 144, nt);
+        CUDA_TRY(cudaMemcpy(L.gate + el * gsl, buf.data(), gsl, cudaMemcpyHostToDevice));
+        glc::synth_q4k(seed, glc::expert_tag(e, 1), 0.01f, buf.data(), gsl / 144, nt);
+        CUDA_TRY(cudaMemcpy(L.up + el * gsl, buf.data(), gsl, cudaMemcpyHostToDevice));
+        glc::synth_q4k(seed, glc::expert_tag(e, 2), 0.01f, buf.data(), dsl / 144, nt);
+        CUDA_TRY(cudaMemcpy(L.down + el * dsl, buf.data(), dsl, cudaMemcpyHostToDevice));
+    }
+    std::vector<float> r((size_t)D * E);
+    glc::synth_normal(seed, glc::kTagRouter, 0.02f, r.data(), r.size(), nt);
+    CUDA_TRY(cudaMemcpy(L.router, r.data(), sizeof(float) * r.size(), cudaMemcpyHostToDevice));
+    if (h->d.shared_ffn_dim > 0) {
+        const int Fs = h->d.shared_ffn_dim;
+        const int se = glc::kSharedExpertIndex;
+        const size_t sg = (size_t)Fs * rowbytes(D), sd = (size_t)D * rowbytes(Fs);
+        std::vector<uint8_t> sb(std::max(sg, sd));
+        glc::synth_q4k(seed, glc::expert_tag(se, 0), 0.01f, sb.data(), sg / 144, nt);
+        CUDA_TRY(cudaMemcpy(L.sh_gate, sb.data(), sg, cudaMemcpyHostToDevice));
+        glc::synth_q4k(seed, glc::expert_tag(se, 1), 0.01f, sb.data(), sg / 144, nt);
+        CUDA_TRY(cudaMemcpy(L.sh_up, sb.data(), sg, cudaMemcpyHostToDevice));
+        glc::synth_q4k(seed, glc::expert_tag(se, 2), 0.01f, sb.data(), sd / 144, nt);
+        CUDA_TRY(cudaMemcpy(L.sh_down, sb.data(), sd, cudaMemcpyHostToDevice));
+        std::vector<float> gv(D);
+        glc::synth_normal(seed, glc::kTagSharedGate, 0.02f, gv.data(), D, 1);
+        CUDA_TRY(cudaMemcpy(L.sh_gate_vec, gv.data(), sizeof(float) * D, cudaMemcpyHostToDevice));
+    }
+    L.loaded = true;
+    return GLC_OK;
+}
+
+int glc_moe_set_profiling(glc_moe* h, int32_t enable) {
+    int rc = check_handle(h);
+    if (rc) return rc;
+    if (enable && !h->marks[0])
+        for (auto& e : h->marks) CUDA_TRY(cudaEventCreate(&e));
+    h->profiling = enable ? 1 : 0;
+    h->n_marks = 0;
+    return GLC_OK;
+}
+
+int glc_moe_kernel_times(glc_moe* h, float* ms, int32_t max_kernels, int32_t* n_kernels) {
+    int rc = check_handle(h);
+    if (rc) return rc;
+    if (!ms || !n_kernels) return fail(GLC_ERR_INVALID_ARG, "null pointer");
+    const int n = h->n_marks > 1 ? h->n_marks - 1 : 0;
+    *n_kernels = n;
+    for (int i = 0; i < n && i < max_kernels; ++i) {
+        CUDA_TRY(cudaEventSynchronize(h->marks[i + 1]));
+        CUDA_TRY(cudaEventElapsedTime(&ms[i], h->marks[i], h->marks[i + 1]));
+    }
+    return GLC_OK;
+}
+
+int glc_moe_poll_error(glc_moe* h) {
+    int rc = check_handle(h);
+    if (rc) return rc;
+    CUDA_TRY(cudaStreamSynchronize(h->stream));
+    return check_device_error(h);
+}
+
+int glc_moe_layer_device_ptrs(glc_moe* h, int32_t layer, const void** gate, const void** up,
+                              const void** down, const float** router) {
+    int rc = check_handle(h);
+    if (rc) return rc;
+    LayerDev* L = layer_of(h, layer);
+    if (!L->loaded) return fail(GLC_ERR_STATE, "layer %d has no weights", layer);
+    if (gate) *gate = L->gate;
+    if (up) *up = L->up;
+    if (down) *down = L->down;
+    if (router) *router = L->router;
+    return GLC_OK;
+}
+
+int glc_expert_forward_dev(glc_moe* h, int32_t layer, int32_t expert, const float* x, float* y, void* stream) {
+    int rc = check_handle(h);
+    if (rc) return rc;
+    if (!x || !y) return fail(GLC_ERR_INVALID_ARG, "null activation pointer");
+    LayerDev* L = layer_of(h, layer);
+    if (!L->loaded) return fail(GLC_ERR_STATE, "layer %d has no weights", layer);
+    cudaStream_t st = stream ? (cudaStream_t)stream : h->stream;
+    // ExpertId is clamped to [0, E) (CpuWarmExpertPoolWorker.cs:263).
+    const int El = local_experts(h);
+    int e = expert - h->d.expert_begin;
+    e = e < 0 ? 0 : (e >= El ? El - 1 : e);
+    h->h_ids[0] = e;
+    h->h_w[0] = 1.0f;
+    CUDA_TRY(cudaMemcpyAsync(h->ids, h->h_ids, sizeof(int), cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(h->wts, h->h_w, sizeof(float), cudaMemcpyHostToDevice, st));
+    return run_experts(h, L, x, 1, 1, h->ids, h->wts, nullptr, y, st);
+}
+
+int glc_expert_forward(glc_moe* h, int32_t layer, int32_t expert, const float* x, float* y) {
+    int rc = check_handle(h);
+    if (rc) return rc;
+    if (!x || !y) return fail(GLC_ERR_INVALID_ARG, "null activation pointer");
+    const int D = h->d.hidden_dim;
+    CUDA_TRY(cudaMemcpyAsync(h->x, x, sizeof(float) * D, cudaMemcpyHostToDevice, h->stream));
+    rc = glc_expert_forward_dev(h, layer, expert, h->x, h->out, h->stream);
+    if (rc) return rc;
+    CUDA_TRY(cudaMemcpyAsync(y, h->out, sizeof(float) * D, cudaMemcpyDeviceToHost, h->stream));
+    CUDA_TRY(cudaStreamSynchronize(h->stream));
+    return check_device_error(h);
+}
+
+int glc_routed_topk(glc_moe* h, int32_t layer, const float* x, const int32_t* ids, const float* w,
+                    int32_t k, float* out) {
+    int rc = check_handle(h);
+    if (rc) return rc;
+    if (!x || !out) return fail(GLC_ERR_INVALID_ARG, "null activation pointer");
+    const int D = h->d.hidden_dim;
+    if (k <= 0 || !ids || !w) {  // empty selection -> zeros (GpuFirstExpertStageWorker.cs:431-437)
+        std::memset(out, 0, sizeof(float) * D);
+        return GLC_OK;
+    }
+    if (k > h->d.top_k * h->d.max_tokens) return fail(GLC_ERR_INVALID_ARG, "k=%d exceeds workspace", k);
+    LayerDev* L = layer_of(h, layer);
+    if (!L->loaded) return fail(GLC_ERR_STATE, "layer %d has no weights", layer);
+    const int El = local_experts(h);
+    for (int j = 0; j < k; ++j) {
+        int e = ids[j] - h->d.expert_begin;
+        h->h_ids[j] = e < 0 ? 0 : (e >= El ? El - 1 : e);
+        h->h_w[j] = w[j];
+    }
+    cudaStream_t st = h->stream;
+    CUDA_TRY(cudaMemcpyAsync(h->x, x, sizeof(float) * D, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(h->ids, h->h_ids, sizeof(int) * k, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(h->wts, h->h_w, sizeof(float) * k, cudaMemcpyHostToDevice, st));
+    if (k > h->d.top_k * h->d.max_tokens) return fail(GLC_ERR_INVALID_ARG, "k too large");
+    rc = run_experts(h, L, h->x, 1, k, h->ids, h->wts, nullptr, h->out, st);
+    if (rc) return rc;
+    CUDA_TRY(cudaMemcpyAsync(out, h->out, sizeof(float) * D, cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaStreamSynchronize(st));
+    return check_device_error(h);
+}
+
+int glc_moe_forward_dev(glc_moe* h, int32_t layer, const float* x, int32_t T, uint32_t flags, float* out,
+                        int32_t* ids_out, float* w_out, void* stream) {
+    int rc = check_handle(h);
+    if (rc) return rc;
+    if (T <= 0) return GLC_OK;
+    if (!x || !out) return fail(GLC_ERR_INVALID_ARG, "null activation pointer");
+    if (T > h->d.max_tokens) return fail(GLC_ERR_INVALID_ARG, "T=%d exceeds max_tokens=%d", T, h->d.max_tokens);
+    if (local_experts(h) != h->d.num_experts)
+        return fail(GLC_ERR_STATE, "full-layer forward on an expert shard needs the expert-parallel path");
+    LayerDev* L = layer_of(h, layer);
+    if (!L->loaded) return fail(GLC_ERR_STATE, "layer %d has no weights", layer);
+    cudaStream_t st = stream ? (cudaStream_t)stream : h->stream;
+    const int D = h->d.hidden_dim, E = h->d.num_experts, k = h->d.top_k;
+    glc::RouterParams rp{};
+    rp.x = x;
+    rp.Wr = L->router;
+    rp.T = T;
+    rp.D = D;
+    rp.E = E;
+    rp.k = k;
+    rp.renorm = h->d.renormalize;
+    rp.rmsnorm = (flags & GLC_FWD_RMSNORM) ? 1 : 0;
+    rp.xin = h->xin;
+    rp.ids = h->ids;
+    rp.w = h->wts;
+    rp.gate_vec = h->d.shared_ffn_dim > 0 ? L->sh_gate_vec : nullptr;
+    rp.gate_out = h->gate_out;
+    h->n_marks = 0;
+    mark(h, st);
+    CUDA_TRY(glc::router_launch(rp, st));
+    mark(h, st);
+    rc = run_experts(h, L, h->xin, T, k, h->ids, h->wts, (flags & GLC_FWD_RESIDUAL) ? x : nullptr, out, st);
+    if (rc) return rc;
+    if (h->d.shared_ffn_dim > 0) {
+        rc = run_shared_expert(h, L, h->xin, T, out, st);
+        if (rc) return rc;
+    }
+    if (ids_out) CUDA_TRY(cudaMemcpyAsync(ids_out, h->ids, sizeof(int) * T * k, cudaMemcpyDeviceToDevice, st));
+    if (w_out) CUDA_TRY(cudaMemcpyAsync(w_out, h->wts, sizeof(float) * T * k, cudaMemcpyDeviceToDevice, st));
+    return GLC_OK;
+}
+
+int glc_moe_forward(glc_moe* h, int32_t layer, const float* x, int32_t T, uint32_t flags, float* out,
+                    int32_t* ids_out, float* w_out) {
+    int rc = check_handle(h);
+    if (rc) return rc;
+    if (T <= 0) return GLC_OK;
+    if (!x || !out) return fail(GLC_ERR_INVALID_ARG, "null activation pointer");
+    if (T > h->d.max_tokens) return fail(GLC_ERR_INVALID_ARG, "T=%d exceeds max_tokens=%d", T, h->d.max_tokens);
+    const int D = h->d.hidden_dim, k = h->d.top_k;
+    cudaStream_t st = h->stream;
+    CUDA_TRY(cudaMemcpyAsync(h->x, x, sizeof(float) * (size_t)T * D, cudaMemcpyHostToDevice, st));
+    rc = glc_moe_forward_dev(h, layer, h->x, T, flags, h->out, nullptr, nullptr, st);
+    if (rc) return rc;
+    CUDA_TRY(cudaMemcpyAsync(out, h->out, sizeof(float) * (size_t)T * D, cudaMemcpyDeviceToHost, st));
+    if (ids_out) CUDA_TRY(cudaMemcpyAsync(ids_out, h->ids, sizeof(int) * (size_t)T * k, cudaMemcpyDeviceToHost, st));
+    if (w_out) CUDA_TRY(cudaMemcpyAsync(w_out, h->wts, sizeof(float) * (size_t)T * k, cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaStreamSynchronize(st));
+    return check_device_error(h);
+}
+
+int glc_moe_graph_build(glc_moe* h, int32_t layer, const float* x, int32_t T, uint32_t flags, float* out) {
+    int rc = check_handle(h);
+    if (rc) return rc;
+    if (!x || !out || T <= 0) return fail(GLC_ERR_INVALID_ARG, "bad graph arguments");
+    // One eager run first: first-use set-up (shared-memory opt-in) is not capturable.
+    rc = glc_moe_forward_dev(h, layer, x, T, flags, out, nullptr, nullptr, h->stream);
+    if (rc) return rc;
+    CUDA_TRY(cudaStreamSynchronize(h->stream));
+    if (h->graph_exec) { cudaGraphExecDestroy(h->graph_exec); h->graph_exec = nullptr; }
+    if (h->graph) { cudaGraphDestroy(h->graph); h->graph = nullptr; }
+    const int prof = h->profiling;
+    h->profiling = 0;
+    CUDA_TRY(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
+    rc = glc_moe_forward_dev(h, layer, x, T, flags, out, nullptr, nullptr, h->stream);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(h->stream, &g);
+    h->profiling = prof;
+    if (rc) { if (g) cudaGraphDestroy(g); return rc; }
+    if (e != cudaSuccess) return fail(GLC_ERR_CUDA, "stream capture: %s", cudaGetErrorString(e));
+    h->graph = g;
+    CUDA_TRY(cudaGraphInstantiate(&h->graph_exec, g, 0));
+    return GLC_OK;
+}
+
+int glc_moe_graph_launch(glc_moe* h, void* stream) {
+    int rc = check_handle(h);
+    if (rc) return rc;
+    if (!h->graph_exec) return fail(GLC_ERR_STATE, "no graph built");
+    CUDA_TRY(cudaGraphLaunch(h->graph_exec, stream ? (cudaStream_t)stream : h->stream));
+    return GLC_OK;
+}
+
+int glc_gemv_q4k_dev(const void* W, const float* x, float* y, int32_t K, int32_t N, void* stream) {
+    if (!W || !x || !y) return fail(GLC_ERR_INVALID_ARG, "null pointer");
+    if (N <= 0 || K <= 0) return fail(GLC_ERR_INVALID_ARG, "K and N must be positive");
+    if (K % 256) return fail(GLC_ERR_UNSUPPORTED, "Dimension %d is not a multiple of 256 for quantization Q4_K.", K);
+    static int* err_words[glc::kMaxDevices] = {nullptr};
+    static std::mutex mu;
+    int dev = 0;
+    CUDA_TRY(cudaGetDevice(&dev));
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!err_words[dev]) {
+            CUDA_TRY(cudaMalloc(&err_words[dev], sizeof(int)));
+            CUDA_TRY(cudaMemset(err_words[dev], 0, sizeof(int)));
+        }
+    }
+    int nsm = 0;
+    CUDA_TRY(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+    glc::GemvParams p{};
+    p.mode = glc::kGemvPlain;
+    p.K = K;
+    p.rows = N;
+    p.nseg = 1;
+    p.kslots = 1;
+    p.num_experts = 1;
+    p.A = (const uint8_t*)W;
+    p.x = x;
+    p.y = y;
+    p.err = err_words[dev];
+    CUDA_TRY(glc::gemv_launch(p, nsm, (cudaStream_t)stream));
+    return GLC_OK;
+}
+
+int glc_router_topk_dev(const float* x, const float* router_w, int32_t T, int32_t D, int32_t E, int32_t k,
+                        int32_t renormalize, int32_t rmsnorm, float* xin_out, float* logits_out,
+                        int32_t* ids_out, float* w_out, void* stream) {
+    if (!x || !router_w || !ids_out || !w_out) return fail(GLC_ERR_INVALID_ARG, "null pointer");
+    if (T < 0 || D <= 0 || E <= 0 || E > 64 || k <= 0 || k > E || k > 16)
+        return fail(GLC_ERR_INVALID_ARG, "router shape out of range (T=%d D=%d E=%d k=%d)", T, D, E, k);
+    glc::RouterParams rp{};
+    rp.x = x;
+    rp.Wr = router_w;
+    rp.T = T;
+    rp.D = D;
+    rp.E = E;
+    rp.k = k;
+    rp.renorm = renormalize;
+    rp.rmsnorm = rmsnorm;
+    rp.xin = xin_out;
+    rp.logits = logits_out;
+    rp.ids = ids_out;
+    rp.w = w_out;
+    CUDA_TRY(glc::router_launch(rp, (cudaStream_t)stream));
+    return GLC_OK;
+}
+
+int32_t glc_wire_token_bytes(int32_t mode, int32_t dim) {
+    switch (mode) {
+        case GLC_WIRE_FP32: return dim * 4;
+        case GLC_WIRE_FP16: return dim * 2;
+        case GLC_WIRE_INT8: return dim + 4;
+        case GLC_WIRE_FP8_E4M3: return dim + 4;
+        default: return dim * 2;
+    }
+}
+
+int glc_wire_quantize_dev(int32_t mode, const float* x, int32_t T, int32_t D, uint8_t* out, void* stream) {
+    if (T < 0 || D < 0) return fail(GLC_ERR_INVALID_ARG, "negative shape");
+    if (T == 0 || D == 0) return GLC_OK;
+    if (!x || !out) return fail(GLC_ERR_INVALID_ARG, "null pointer");
+    CUDA_TRY(glc::wire_quantize_launch(mode, x, T, D, out, (cudaStream_t)stream));
+    return GLC_OK;
+}
+
+int glc_wire_dequantize_dev(int32_t mode, const uint8_t* in, int32_t T, int32_t D, float* out, void* stream) {
+    if (T < 0 || D < 0) return fail(GLC_ERR_INVALID_ARG, "negative shape");
+    if (T == 0 || D == 0) return GLC_OK;
+    if (!in || !out) return fail(GLC_ERR_INVALID_ARG, "null pointer");
+    CUDA_TRY(glc::wire_dequantize_launch(mode, in, T, D, out, (cudaStream_t)stream));
+    return GLC_OK;
+}
+
+int glc_wire_quantize(int32_t mode, const float* x, int32_t T, int32_t D, uint8_t* out, size_t out_bytes) {
+    if (T < 0 || D < 0) return fail(GLC_ERR_INVALID_ARG, "negative shape");
+    const size_t need = (size_t)glc_wire_token_bytes(mode, D) * (size_t)T;
+    if (out_bytes < need)  // QuantizeBatch: destination too small (QuantizationKernels.cs:89-90)
+        return fail(GLC_ERR_INVALID_ARG, "Destination buffer too small (%zu < %zu)", out_bytes, need);
+    if (need == 0) return GLC_OK;
+    if (!x || !out) return fail(GLC_ERR_INVALID_ARG, "null pointer");
+    float* dx = nullptr;
+    uint8_t* dq = nullptr;
+    CUDA_TRY(cudaMalloc(&dx, sizeof(float) * (size_t)T * D));
+    cudaError_t e = cudaMalloc(&dq, need);
+    if (e != cudaSuccess) { cudaFree(dx); return fail(GLC_ERR_OOM, "cudaMalloc failed"); }
+    e = cudaMemcpy(dx, x, sizeof(float) * (size_t)T * D, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = glc::wire_quantize_launch(mode, dx, T, D, dq, nullptr);
+    if (e == cudaSuccess) e = cudaMemcpy(out, dq, need, cudaMemcpyDeviceToHost);
+    cudaFree(dx);
+    cudaFree(dq);
+    if (e != cudaSuccess) return fail(GLC_ERR_CUDA, "wire quantize: %s", cudaGetErrorString(e));
+    return GLC_OK;
+}
+
+int glc_wire_dequantize(int32_t mode, const uint8_t* in, size_t in_bytes, int32_t T, int32_t D, float* out) {
+    if (T < 0 || D < 0) return fail(GLC_ERR_INVALID_ARG, "negative shape");
+    const size_t need = (size_t)glc_wire_token_bytes(mode, D) * (size_t)T;
+    if (in_bytes < need) return fail(GLC_ERR_INVALID_ARG, "Source buffer too small (%zu < %zu)", in_bytes, need);
+    if (need == 0) return GLC_OK;
+    if (!in || !out) return fail(GLC_ERR_INVALID_ARG, "null pointer");
+    float* dx = nullptr;
+    uint8_t* dq = nullptr;
+    CUDA_TRY(cudaMalloc(&dq, need));
+    cudaError_t e = cudaMalloc(&dx, sizeof(float) * (size_t)T * D);
+    if (e != cudaSuccess) { cudaFree(dq); return fail(GLC_ERR_OOM, "cudaMalloc failed"); }
+    e = cudaMemcpy(dq, in, need, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = glc::wire_dequantize_launch(mode, dq, T, D, dx, nullptr);
+    if (e == cudaSuccess) e = cudaMemcpy(out, dx, sizeof(float) * (size_t)T * D, cudaMemcpyDeviceToHost);
+    cudaFree(dx);
+    cudaFree(dq);
+    if (e != cudaSuccess) return fail(GLC_ERR_CUDA, "wire dequantize: %s", cudaGetErrorString(e));
+    return GLC_OK;
+}
+
+static void put_u32(uint8_t* p, uint32_t v) { for (int i = 0; i < 4; ++i) p[i] = (uint8_t)(v >> (8 * i)); }
+static uint32_t get_u32(const uint8_t* p) {
+    return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+
+int glc_fused_header_write(const glc_fused_header* h, uint8_t* o) {
+    if (!h || !o) return fail(GLC_ERR_INVALID_ARG, "null pointer");
+    put_u32(o, 0x47414354u);  // "GACT"
+    put_u32(o + 4, (uint32_t)h->sequence_id);
+    put_u32(o + 8, (uint32_t)(h->sequence_id >> 32));
+    put_u32(o + 12, (uint32_t)h->token_index);
+    put_u32(o + 16, (uint32_t)h->layer_index);
+    put_u32(o + 20, (uint32_t)h->hidden_dim);
+    o[24] = h->precision_mode;
+    o[25] = h->flags;
+    o[26] = (uint8_t)h->batch_tokens;
+    o[27] = (uint8_t)(h->batch_tokens >> 8);
+    uint32_t s;
+    std::memcpy(&s, &h->scale, 4);
+    put_u32(o + 28, s);
+    return GLC_OK;
+}
+
+int glc_fused_header_read(const uint8_t* in, glc_fused_header* h) {
+    if (!in || !h) return fail(GLC_ERR_INVALID_ARG, "null pointer");
+    const uint32_t magic = get_u32(in);
+    if (magic != 0x47414354u)  // ReadFrom throws InvalidOperationException (FusedActivationHeader.cs:158-159)
+        return fail(GLC_ERR_INVALID_ARG, "Invalid FusedActivationHeader magic: 0x%08X, expected 0x47414354", magic);
+    h->sequence_id = (uint64_t)get_u32(in + 4) | ((uint64_t)get_u32(in + 8) << 32);
+    h->token_index = (int32_t)get_u32(in + 12);
+    h->layer_index = (int32_t)get_u32(in + 16);
+    h->hidden_dim = (int32_t)get_u32(in + 20);
+    h->precision_mode = in[24];
+    h->flags = in[25];
+    h->batch_tokens = (uint16_t)(in[26] | (in[27] << 8));
+    const uint32_t s = get_u32(in + 28);
+    std::memcpy(&h->scale, &s, 4);
+    return GLC_OK;
+}
+
+int32_t glc_fused_header_payload_bytes(const glc_fused_header* h) {
+    if (!h) return fail(GLC_ERR_INVALID_ARG, "null pointer");
+    const int tokens = h->batch_tokens > 0 ? h->batch_tokens : 1;
+    if (h->flags & 0x10) return tokens * 4;  // Stage0TokenInput: token ids
+    switch (h->precision_mode) {
+        case GLC_WIRE_FP32: return h->hidden_dim * tokens * 4;
+        case GLC_WIRE_FP16: return h->hidden_dim * tokens * 2;
+        case GLC_WIRE_INT8: return (h->hidden_dim + 4) * tokens;
+        case GLC_WIRE_FP8_E4M3: return (h->hidden_dim + 4) * tokens;
+        default: return h->hidden_dim * tokens * 2;
+    }
+}
+
+}  // extern "C"

@@ -1,0 +1,192 @@
+/*
+ * glacier_b200.h -- C ABI of libglacier_b200.so, the B200 (sm_100a) backend for
+ * the quantized Mixture-of-Experts feed-forward hot path of
+ * Glacier.Inference.Distributed.
+ *
+ * Conventions
+ *   - Every function returns an int status: GLC_OK (0) or a negative GLC_ERR_*.
+ *     glc_last_error() returns a thread-local message for the last failure.
+ *   - Pointers are HOST memory unless the function name ends in _dev; _dev
+ *     functions take DEVICE pointers and a cudaStream_t passed as void*, and
+ *     return without synchronising the stream.
+ *   - The library never frees caller memory, never calls exit() and never traps.
+ *   - A glc_moe handle owns one device and one stream. Calls on one handle must
+ *     be serialised by the caller (the reference serialises GPU work with
+ *     lock(_gpuLock), GpuFirstExpertStageWorker.cs:447). Handles on different
+ *     devices are independent.
+ *   - Weight blobs use the GGUF layout the reference uses:
+ *     [expert][rows][rowBytes] (CpuWarmExpertPoolWorker.cs:247-253), Q4_K rows
+ *     of K/256 super-blocks of 144 bytes.
+ */
+#ifndef GLACIER_B200_H
+#define GLACIER_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GLC_ABI_VERSION 1
+
+/* status codes */
+#define GLC_OK 0
+#define GLC_ERR_INVALID_ARG -1   /* ArgumentException / ArgumentOutOfRangeException */
+#define GLC_ERR_CUDA -2
+#define GLC_ERR_OOM -3
+#define GLC_ERR_UNSUPPORTED -4   /* NotSupportedException (e.g. K % 256 != 0 for Q4_K) */
+#define GLC_ERR_DISPOSED -5      /* ObjectDisposedException */
+#define GLC_ERR_NCCL -6
+#define GLC_ERR_TIMEOUT -7       /* a bounded device-side wait gave up */
+#define GLC_ERR_STATE -8
+
+/* GGUF tensor types accepted for expert weights (GGUF type ids). */
+#define GLC_GGUF_Q4_K 12
+
+/* wire precision modes (WirePrecisionMode, Protocol/FusedActivationHeader.cs:12-18) */
+#define GLC_WIRE_FP32 0
+#define GLC_WIRE_FP16 1
+#define GLC_WIRE_INT8 2
+#define GLC_WIRE_FP8_E4M3 3
+
+/* layer-forward flags */
+#define GLC_FWD_RMSNORM 1u   /* xin = RMSNorm(x), no weight, eps 1e-5 (StageWorkers.cs:89-91) */
+#define GLC_FWD_RESIDUAL 2u  /* out = x + sum_k w_k y_k (DistributedPipelineCoordinator.cs:104-134) */
+
+typedef struct glc_moe glc_moe;
+
+/* Shapes of one MoE layer family.  Replaces the constructor arguments of
+ * GpuFirstExpertStageWorker (GpuFirstExpertStageWorker.cs:109-124) and
+ * CpuWarmExpertPoolWorker (CpuWarmExpertPoolWorker.cs:89-100). */
+typedef struct glc_moe_desc {
+    int32_t hidden_dim;      /* D (multiple of 256) */
+    int32_t expert_ffn_dim;  /* F (multiple of 256) */
+    int32_t num_experts;     /* E, total routed experts of the layer */
+    int32_t top_k;           /* k */
+    int32_t shared_ffn_dim;  /* Fs of the sigmoid-gated shared expert, 0 = none */
+    int32_t renormalize;     /* 1: softmax -> top-k -> renormalise; 0: plain softmax weights */
+    int32_t weight_type;     /* GLC_GGUF_Q4_K */
+    int32_t device;          /* CUDA ordinal */
+    int32_t num_layers;      /* layers held by the handle (header.LayerIndex is clamped) */
+    int32_t max_tokens;      /* largest T passed to glc_moe_forward* */
+    int32_t expert_begin;    /* first expert held on this device (expert parallelism) */
+    int32_t expert_count;    /* experts held on this device (0 = all E) */
+} glc_moe_desc;
+
+/* Host-side weights of one layer (copied to HBM by glc_moe_load_layer).
+ * gate/up: [expert_count][F][rowBytes(D)]; down: [expert_count][D][rowBytes(F)];
+ * router: fp32 [D][E]; shared_*: one expert of width Fs; shared_gate: fp32 [D]. */
+typedef struct glc_layer_weights {
+    const void* gate_exps;
+    const void* up_exps;
+    const void* down_exps;
+    const float* router;
+    const void* shared_gate;
+    const void* shared_up;
+    const void* shared_down;
+    const float* shared_gate_vec;
+} glc_layer_weights;
+
+/* ---- library ---- */
+int glc_abi_version(void);
+const char* glc_last_error(void);
+int glc_device_count(int32_t* count);
+/* GetRowBytes for Q4_K (the external GgufTypes.GetRowBytes, CpuWarmExpertPoolWorker.cs:133). */
+int64_t glc_q4k_row_bytes(int32_t k);
+
+/* ---- MoE handle lifecycle (GpuFirstExpertStageWorker ctor / Dispose, :109-167, :785-834) ---- */
+int glc_moe_create(const glc_moe_desc* desc, glc_moe** out);
+int glc_moe_destroy(glc_moe* h);
+int glc_moe_load_layer(glc_moe* h, int32_t layer, const glc_layer_weights* w);
+/* Fill a layer with the documented seeded synthetic weights (SplitMix64 streams,
+ * Q4_K d/dmin = fp16(|N(0,sigma_d)|), uniform 6-bit scales/mins and 4-bit quants,
+ * router N(0, 0.02), shared gate N(0, 0.02)).  Only this device's experts are made. */
+int glc_moe_synth_layer(glc_moe* h, int32_t layer, uint64_t seed);
+/* Device pointers of a resident layer (for the _dev raw primitives). */
+int glc_moe_layer_device_ptrs(glc_moe* h, int32_t layer, const void** gate, const void** up,
+                              const void** down, const float** router);
+
+/* Telemetry (the CUDA-event counterpart of StageTelemetry / GpuFirstWorkerTelemetry,
+ * Program.cs:28, GpuFirstExpertStageWorker.cs:21-31): when enabled, every
+ * forward records an event after each kernel; glc_moe_kernel_times returns the
+ * device milliseconds of each kernel of the last forward, in launch order
+ * (router, gate/up, down[, shared gate/up, shared down]). */
+int glc_moe_set_profiling(glc_moe* h, int32_t enable);
+int glc_moe_kernel_times(glc_moe* h, float* ms, int32_t max_kernels, int32_t* n_kernels);
+/* Reads and clears the device error word of the handle (GLC_ERR_TIMEOUT when a
+ * bounded device-side wait gave up during an asynchronous _dev call). */
+int glc_moe_poll_error(glc_moe* h);
+
+/* ---- per-expert stage worker: IInferenceStageWorker.ProcessActivation
+ *      (IInferenceStageWorker.cs:43; zero-alloc overload CpuWarmExpertPoolWorker.cs:232).
+ *      y = W2 * SwiGLU(W1 x, W3 x) for expert `expert` (clamped to [0,E)) of
+ *      layer `layer` (clamped). x, y: host fp32 [D]. ---- */
+int glc_expert_forward(glc_moe* h, int32_t layer, int32_t expert, const float* x, float* y);
+int glc_expert_forward_dev(glc_moe* h, int32_t layer, int32_t expert, const float* x, float* y,
+                           void* stream);
+
+/* ---- routed top-k: GpuFirstExpertStageWorker.ProcessRoutedTopK (:416-423).
+ *      out = sum_j w[j] * Expert_{ids[j]}(x), accumulated in j order; out cleared
+ *      first; k == 0 gives zeros; ids clamped to [0,E). Host fp32 [D]. ---- */
+int glc_routed_topk(glc_moe* h, int32_t layer, const float* x, const int32_t* ids,
+                    const float* w, int32_t k, float* out);
+
+/* ---- full MoE layer for T tokens: router (gate GEMV + softmax + top-k +
+ *      renormalise), dispatch, experts, combine. x, out: fp32 [T][D]; ids_out
+ *      int32 [T][k], w_out fp32 [T][k] (either may be NULL).  T == 1 runs the
+ *      decode path (dequant-fused GEMV kernels); T > 1 the batched path. ---- */
+int glc_moe_forward(glc_moe* h, int32_t layer, const float* x, int32_t T, uint32_t flags,
+                    float* out, int32_t* ids_out, float* w_out);
+int glc_moe_forward_dev(glc_moe* h, int32_t layer, const float* x, int32_t T, uint32_t flags,
+                        float* out, int32_t* ids_out, float* w_out, void* stream);
+
+/* ---- one-submission decode step: the CUDA-graph counterpart of the single
+ *      D3D12 command list GpuFirstExpertStageWorker records per call
+ *      (GpuFirstExpertStageWorker.cs:463-534).  build captures
+ *      glc_moe_forward_dev(layer, x, T, flags, out) into a graph held by the
+ *      handle (pointers are baked in; refill x between launches); launch
+ *      replays it on `stream`.  A second build replaces the first. ---- */
+int glc_moe_graph_build(glc_moe* h, int32_t layer, const float* x, int32_t T, uint32_t flags,
+                        float* out);
+int glc_moe_graph_launch(glc_moe* h, void* stream);
+
+/* ---- raw primitive: QuantKernels.MatVecMul(Q4_K, W, x, y, nCols=K, nRows=N)
+ *      (call shape CpuWarmExpertPoolWorker.cs:379). K % 256 != 0 -> GLC_ERR_UNSUPPORTED. ---- */
+int glc_gemv_q4k_dev(const void* W, const float* x, float* y, int32_t K, int32_t N, void* stream);
+
+/* ---- router alone (for tests and for callers that route elsewhere) ---- */
+int glc_router_topk_dev(const float* x, const float* router_w, int32_t T, int32_t D, int32_t E,
+                        int32_t k, int32_t renormalize, int32_t rmsnorm, float* xin_out,
+                        float* logits_out, int32_t* ids_out, float* w_out, void* stream);
+
+/* ---- wire codec: QuantizationKernels (Protocol/QuantizationKernels.cs:57-163) ---- */
+int32_t glc_wire_token_bytes(int32_t mode, int32_t dim);
+int glc_wire_quantize(int32_t mode, const float* x, int32_t T, int32_t D, uint8_t* out,
+                      size_t out_bytes);
+int glc_wire_dequantize(int32_t mode, const uint8_t* in, size_t in_bytes, int32_t T, int32_t D,
+                        float* out);
+int glc_wire_quantize_dev(int32_t mode, const float* x, int32_t T, int32_t D, uint8_t* out,
+                          void* stream);
+int glc_wire_dequantize_dev(int32_t mode, const uint8_t* in, int32_t T, int32_t D, float* out,
+                            void* stream);
+
+/* ---- FusedActivationHeader (Protocol/FusedActivationHeader.cs:41-218) ---- */
+typedef struct glc_fused_header {
+    uint64_t sequence_id;
+    int32_t token_index;
+    int32_t layer_index;
+    int32_t hidden_dim;
+    uint8_t precision_mode;
+    uint8_t flags;
+    uint16_t batch_tokens;
+    float scale;
+} glc_fused_header;
+int glc_fused_header_write(const glc_fused_header* h, uint8_t* out32);
+int glc_fused_header_read(const uint8_t* in32, glc_fused_header* h);
+int32_t glc_fused_header_payload_bytes(const glc_fused_header* h);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,285 @@
+"""GPU parity against the CPU oracle, through the C ABI.
+
+Tolerances: expert ids and wire bytes bit-exact; fp32 layer outputs rel-L2
+<= 1e-3 (the bound of the task), GEMV outputs rel-L2 <= 1e-4 (the int16
+activation quantisation of the decode kernel contributes ~1e-5).
+"""
+import json
+import os
+import struct
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF = json.load(open(os.path.join(REPO, "tests", "golden", "reference_vectors.json")))
+Q4K = json.load(open(os.path.join(REPO, "tests", "golden", "q4k_known_answers.json")))
+LAYER_TOL = 1e-3
+GEMV_TOL = 1e-4
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def dev(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def stream(torch):
+    return torch.cuda.current_stream().cuda_stream
+
+
+def make_layer(oracle, seed, D, F, E, k, renorm=True, Fs=0):
+    L = {"D": D, "F": F, "E": E, "k": k, "renorm": renorm, "Fs": Fs}
+    L["gate"] = np.concatenate([oracle.synth_q4k(seed, oracle.expert_tag(e, 0), F, D) for e in range(E)])
+    L["up"] = np.concatenate([oracle.synth_q4k(seed, oracle.expert_tag(e, 1), F, D) for e in range(E)])
+    L["down"] = np.concatenate([oracle.synth_q4k(seed, oracle.expert_tag(e, 2), D, F) for e in range(E)])
+    L["router"] = oracle.fill_normal(seed, 2, 0.02, D * E)
+    if Fs:
+        L["sh_gate"] = oracle.synth_q4k(seed, oracle.expert_tag(65535, 0), Fs, D)
+        L["sh_up"] = oracle.synth_q4k(seed, oracle.expert_tag(65535, 1), Fs, D)
+        L["sh_down"] = oracle.synth_q4k(seed, oracle.expert_tag(65535, 2), D, Fs)
+        L["sh_gate_vec"] = oracle.fill_normal(seed, 3, 0.02, D)
+    return L
+
+
+def worker_for(glc, L, max_tokens=4, synth_seed=None):
+    w = glc.GpuExpertStageWorker(L["D"], L["F"], L["E"], L["k"], shared_ffn_dim=L["Fs"],
+                                 renormalize=L["renorm"], max_tokens=max_tokens)
+    if synth_seed is None:
+        w.load_layer(0, L["gate"], L["up"], L["down"], L["router"], L.get("sh_gate"),
+                     L.get("sh_up"), L.get("sh_down"), L.get("sh_gate_vec"))
+    else:
+        w.synth_layer(0, synth_seed)
+    return w
+
+
+@pytest.mark.parametrize("K,N", [(256, 64), (1024, 300), (4096, 1000), (14336, 517), (2560, 129),
+                                 (3584, 700), (20480, 64)])
+def test_gemv_q4k_matches_oracle(cuda, glc, oracle, K, N):
+    torch = cuda
+    W = oracle.synth_q4k(11 + K, 5, N, K)
+    x = oracle.fill_normal(11 + N, 1, 1.0, K)
+    Wd, xd = dev(torch, W), dev(torch, x)
+    yd = torch.empty(N, dtype=torch.float32, device="cuda")
+    glc.gemv_q4k_dev(Wd.data_ptr(), xd.data_ptr(), yd.data_ptr(), K, N, stream(torch))
+    torch.cuda.synchronize()
+    assert rel_l2(yd.cpu().numpy(), oracle.gemv(W, x, K, N)) <= GEMV_TOL
+
+
+def test_gemv_known_answer_blocks(cuda, glc, oracle):
+    torch = cuda
+    W = np.concatenate([np.array(c["block"], np.uint8) for c in Q4K["cases"]])
+    N = len(Q4K["cases"])
+    x = np.linspace(-1.0, 1.0, 256, dtype=np.float32)
+    want = np.array([np.dot(np.array(c["dequant"], np.float64), x.astype(np.float64))
+                     for c in Q4K["cases"]])
+    yd = torch.empty(N, dtype=torch.float32, device="cuda")
+    glc.gemv_q4k_dev(dev(torch, W).data_ptr(), dev(torch, x).data_ptr(), yd.data_ptr(), 256, N,
+                     stream(torch))
+    torch.cuda.synchronize()
+    y = yd.cpu().numpy().astype(np.float64)
+    scale = np.array([np.abs(np.array(c["dequant"])).sum() for c in Q4K["cases"]])
+    assert np.all(np.abs(y - want) <= 1e-4 * scale)
+
+
+def test_gemv_rejects_bad_k(cuda, glc):
+    with pytest.raises(glc.GlcError, match="multiple of 256"):
+        glc.gemv_q4k_dev(1, 1, 1, 300, 4, None)
+
+
+def test_synth_layer_matches_oracle_bytes(cuda, glc, oracle):
+    from cuda.bindings import runtime as rt
+    D, F, E, k = 512, 768, 4, 2
+    L = make_layer(oracle, 21, D, F, E, k)
+    w = worker_for(glc, L, synth_seed=21)
+    g, u, d, r = w.layer_device_ptrs(0)
+    for ptr, ref in ((g, L["gate"]), (u, L["up"]), (d, L["down"]), (r, L["router"].view(np.uint8))):
+        host = np.empty(ref.nbytes, np.uint8)
+        err, = rt.cudaMemcpy(host.ctypes.data, ptr, ref.nbytes, rt.cudaMemcpyKind.cudaMemcpyDeviceToHost)
+        assert int(err) == 0
+        assert np.array_equal(host, ref.view(np.uint8))
+    w.dispose()
+
+
+@pytest.mark.parametrize("E,k,renorm", [(8, 2, True), (64, 8, False), (16, 4, True)])
+def test_router_bit_exact(cuda, glc, oracle, E, k, renorm):
+    torch = cuda
+    D, T = 4096 if E == 8 else 3584, 33
+    x = oracle.fill_normal(5 + E, 1, 1.0, T * D).reshape(T, D)
+    Wr = oracle.fill_normal(5 + E, 2, 0.02, D * E)
+    xd = dev(torch, x)
+    xin = torch.empty(T, D, device="cuda")
+    logits = torch.empty(T, E, device="cuda")
+    ids = torch.empty(T, k, dtype=torch.int32, device="cuda")
+    w = torch.empty(T, k, device="cuda")
+    for rms in (0, 1):
+        glc.router_topk_dev(xd.data_ptr(), dev(torch, Wr).data_ptr(), T, D, E, k, renorm, rms,
+                            xin.data_ptr(), logits.data_ptr(), ids.data_ptr(), w.data_ptr(),
+                            stream(torch))
+        torch.cuda.synchronize()
+        for t in range(T):
+            xt = oracle.rmsnorm(x[t]) if rms else x[t]
+            assert np.array_equal(xin[t].cpu().numpy().view(np.uint32), xt.view(np.uint32))
+            lg, oid, ow = oracle.router(xt, Wr, E, k, renorm)
+            assert np.array_equal(logits[t].cpu().numpy().view(np.uint32), lg.view(np.uint32))
+            assert np.array_equal(ids[t].cpu().numpy(), oid)
+            np.testing.assert_allclose(w[t].cpu().numpy(), ow, rtol=2e-6, atol=1e-7)
+
+
+def test_router_tie_break_lower_index(cuda, glc):
+    torch = cuda
+    D, E, k = 256, 8, 3
+    x = torch.zeros(1, D, device="cuda")
+    x[0, 0] = 1.0
+    Wr = torch.zeros(D, E, device="cuda")
+    Wr[0] = torch.tensor([1.0, 3.0, 3.0, 2.0, 0.0, 3.0, -1.0, 3.0])
+    ids = torch.empty(1, k, dtype=torch.int32, device="cuda")
+    w = torch.empty(1, k, device="cuda")
+    glc.router_topk_dev(x.data_ptr(), Wr.data_ptr(), 1, D, E, k, 1, 0, None, None, ids.data_ptr(),
+                        w.data_ptr(), stream(torch))
+    torch.cuda.synchronize()
+    assert ids.cpu().numpy().tolist() == [[1, 2, 5]]
+
+
+def test_process_activation_matches_oracle(cuda, glc, oracle):
+    D, F, E, k = 1024, 2048, 4, 2
+    L = make_layer(oracle, 31, D, F, E, k)
+    w = worker_for(glc, L)
+    x = oracle.fill_normal(31, 1, 1.0, D)
+    gsl, dsl = F * (D // 256) * 144, D * (F // 256) * 144
+    for e in (0, 3, 7, -2):  # out-of-range ids are clamped like CpuWarmExpertPoolWorker.cs:263
+        ec = min(max(e, 0), E - 1)
+        y = w.process_activation(0, e, x)
+        ref = oracle.expert_forward(L["gate"][ec * gsl:(ec + 1) * gsl], L["up"][ec * gsl:(ec + 1) * gsl],
+                                    L["down"][ec * dsl:(ec + 1) * dsl], D, F, x)
+        assert rel_l2(y, ref) <= LAYER_TOL
+    with pytest.raises(glc.GlcError, match="smaller than required"):
+        w.process_activation(0, 0, x[:10])
+    w.dispose()
+    with pytest.raises(glc.GlcError):
+        w.process_activation(0, 0, x)
+
+
+def test_process_routed_topk_matches_oracle(cuda, glc, oracle):
+    D, F, E, k = 512, 1024, 8, 2
+    L = make_layer(oracle, 41, D, F, E, k)
+    w = worker_for(glc, L)
+    x = oracle.fill_normal(41, 1, 1.0, D)
+    ids = np.array([5, 1, 9], np.int32)
+    wt = np.array([0.5, 0.3, 0.2], np.float32)
+    y = w.process_routed_topk(0, x, ids, wt)
+    ref = oracle.routed_topk(L["gate"], L["up"], L["down"], D, F, E, x, ids, wt)
+    assert rel_l2(y, ref) <= LAYER_TOL
+    assert not w.process_routed_topk(0, x, np.array([], np.int32), np.array([], np.float32)).any()
+    w.dispose()
+
+
+@pytest.mark.parametrize("T,flags", [(1, 0), (1, 3), (4, 1), (3, 2)])
+def test_moe_forward_small_matches_oracle(cuda, glc, oracle, T, flags):
+    D, F, E, k = 512, 1024, 8, 2
+    L = make_layer(oracle, 51 + T, D, F, E, k)
+    w = worker_for(glc, L, max_tokens=8)
+    x = oracle.fill_normal(51, 1, 1.0, T * D).reshape(T, D)
+    out, ids, wt = w.forward(0, x, flags)
+    ro, rids, rw = oracle.moe_forward(L, x, flags)
+    assert np.array_equal(ids, rids)
+    np.testing.assert_allclose(wt, rw, rtol=2e-6, atol=1e-7)
+    assert rel_l2(out, ro) <= LAYER_TOL
+    w.dispose()
+
+
+def test_moe_forward_qwen_shared_expert(cuda, glc, oracle):
+    D, F, E, k, Fs = 512, 512, 16, 4, 1024
+    L = make_layer(oracle, 61, D, F, E, k, renorm=False, Fs=Fs)
+    w = worker_for(glc, L, max_tokens=4)
+    x = oracle.fill_normal(61, 1, 1.0, 2 * D).reshape(2, D)
+    out, ids, wt = w.forward(0, x, 0)
+    ro, rids, rw = oracle.moe_forward(L, x, 0)
+    assert np.array_equal(ids, rids)
+    assert rel_l2(out, ro) <= LAYER_TOL
+    w.dispose()
+
+
+def test_moe_forward_mixtral_decode_full_size(cuda, glc, oracle):
+    """Mixtral-8x7B layer, decode of one RMSNorm'd token (D=4096, F=14336, E=8, k=2)."""
+    D, F, E, k = 4096, 14336, 8, 2
+    L = make_layer(oracle, 1234, D, F, E, k)
+    w = worker_for(glc, L, max_tokens=1, synth_seed=1234)
+    x = oracle.rmsnorm(oracle.fill_normal(1234, 1, 1.0, D))[None, :]
+    out, ids, wt = w.forward(0, x, 0)
+    ro, rids, rw = oracle.moe_forward(L, x, 0)
+    assert np.array_equal(ids, rids)
+    assert rel_l2(out, ro) <= LAYER_TOL
+    w.dispose()
+
+
+# ------------------------------------------------------------------ wire codec
+def _gpu_quant(torch, glc, mode, x):
+    T, D = x.shape
+    tb = glc.QuantizationKernels.GetPackedTokenBytes(mode, D)
+    out = torch.zeros(T * tb, dtype=torch.uint8, device="cuda")
+    glc.QuantizationKernels.quantize_dev(mode, dev(torch, x).data_ptr(), T, D, out.data_ptr(), stream(torch))
+    back = torch.empty(T, D, device="cuda")
+    glc.QuantizationKernels.dequantize_dev(mode, out.data_ptr(), T, D, back.data_ptr(), stream(torch))
+    torch.cuda.synchronize()
+    return out.cpu().numpy(), back.cpu().numpy()
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2, 3])
+@pytest.mark.parametrize("T,D", [(1, 5120), (17, 4096), (3, 67), (256, 3584), (2, 1)])
+def test_wire_codec_bit_exact(cuda, glc, oracle, mode, T, D):
+    torch = cuda
+    rng = np.random.default_rng(T * 1000 + D + mode)
+    x = (rng.standard_normal((T, D)) * rng.choice([1e-3, 1.0, 50.0], size=(T, 1))).astype(np.float32)
+    if T >= 3:
+        x[1] = 0.0
+        x[2, 0] = np.inf if D > 1 else 0.0
+    if T >= 17:
+        x[5, 3] = np.nan
+        x[6] *= 1e-12
+        x[7, :8] = [0.5, 1.5, 2.5, -0.5, -1.5, 127.0, -127.0, 1e-40]
+    q, back = _gpu_quant(torch, glc, mode, x)
+    want = oracle.wire_quantize(mode, x)
+    assert np.array_equal(q, want)
+    ref_back = oracle.wire_dequantize(mode, want, T, D)
+    assert np.array_equal(back.view(np.uint32), ref_back.view(np.uint32)) or (
+        np.array_equal(np.isnan(back), np.isnan(ref_back)) and np.array_equal(
+            np.nan_to_num(back), np.nan_to_num(ref_back)))
+
+
+def test_wire_golden_round_half_even(cuda, glc):
+    torch = cuda
+    c = REF["int8_round_half_even"]
+    x = np.array(c["input"], np.float32)[None, :]
+    q, back = _gpu_quant(torch, glc, 2, x)
+    codes = q[4:].view(np.int8)
+    for i, v in c["expect_codes"].items():
+        assert codes[int(i)] == v
+    for i, v in c["expect_dequant"].items():
+        assert round(float(back[0, int(i)]) - v, 4) == 0
+    c = REF["int8_scale_first4"]
+    x = np.zeros((1, c["dim"]), np.float32)
+    for i, v in c["nonzero"].items():
+        x[0, int(i)] = v
+    q, _ = _gpu_quant(torch, glc, 2, x)
+    assert round(struct.unpack("<f", bytes(q[:4]))[0] - c["expect_scale"], 5) == 0
+    assert q[4].view(np.int8) == 127 and q[104].view(np.int8) == -127
+
+
+def test_wire_host_api_roundtrip(cuda, glc, oracle):
+    x = oracle.fill_normal(3, 1, 2.0, 32 * 5120).reshape(32, 5120)
+    QK = glc.QuantizationKernels
+    buf = np.zeros(QK.GetPackedBatchBytes(2, 5120, 32), np.uint8)
+    QK.QuantizeBatch(x, buf, 5120, 32, 2)
+    assert np.array_equal(buf, oracle.wire_quantize(2, x))
+    out = np.zeros((32, 5120), np.float32)
+    QK.DequantizeBatch(buf, out, 5120, 32, 2)
+    for t in range(32):
+        a, b = x[t].astype(np.float64), out[t].astype(np.float64)
+        assert a @ b / (np.linalg.norm(a) * np.linalg.norm(b)) > 0.9995
