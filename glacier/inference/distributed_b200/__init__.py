@@ -4,4 +4,5 @@ dispatch, SwiGLU, weighted combine and the INT8 stage-boundary wire codec,
 behind the C ABI in include/glacier_b200.h."""
 from ._lib import GlcError, LIB_PATH, lib  # noqa: F401
 from .api import (FusedActivationHeader, GpuExpertStageWorker, QuantizationKernels,  # noqa: F401
-                  WirePrecisionMode, device_count, gemv_q4k_dev, q4k_row_bytes, router_topk_dev)
+                  WirePrecisionMode, device_count, dispatch_plan_dev, gemv_q4k_dev,
+                  q4k_row_bytes, router_topk_dev)

@@ -163,6 +163,10 @@ def gemv_q4k_dev(W_ptr: int, x_ptr: int, y_ptr: int, K: int, N: int, stream: int
     check(lib().glc_gemv_q4k_dev(W_ptr, x_ptr, y_ptr, K, N, stream))
 
 
+def dispatch_plan_dev(ids_ptr, P, E, counts_ptr, offsets_ptr, perm_ptr, inv_ptr, stream=None):
+    check(lib().glc_dispatch_plan_dev(ids_ptr, P, E, counts_ptr, offsets_ptr, perm_ptr, inv_ptr, stream))
+
+
 def router_topk_dev(x_ptr, router_ptr, T, D, E, k, renormalize, rmsnorm, xin_ptr, logits_ptr,
                     ids_ptr, w_ptr, stream=None):
     check(lib().glc_router_topk_dev(x_ptr, router_ptr, T, D, E, k, int(renormalize), int(rmsnorm),

@@ -20,7 +20,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-ffp-contract=off",
           "-I", CSRC, "-I", INCLUDE, "--expt-relaxed-constexpr"]
-SOURCES = ["api.cu", "gemv_q4k.cu", "router.cu", "wire.cu", "synth.cpp"]
+SOURCES = ["api.cu", "gemv_q4k.cu", "router.cu", "wire.cu", "prefill.cu", "grouped_mma.cu", "synth.cpp"]
 HEADERS = ["common.cuh", "kernels.h", "synth.h"]
 
 
@@ -43,7 +43,7 @@ def build(force: bool = False) -> str:
         objs = list(ex.map(lambda s: _compile(s, force), SOURCES))
     if force or not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs):
         tmp = LIB + ".tmp"
-        subprocess.check_call([NVCC, *ARCH, "-shared", "-o", tmp, *objs, "-lcuda"])
+        subprocess.check_call([NVCC, *ARCH, "-shared", "-o", tmp, *objs])
         os.replace(tmp, LIB)
     return LIB
 

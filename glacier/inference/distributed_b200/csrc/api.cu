@@ -62,6 +62,11 @@ struct LayerDev {
     uint8_t* sh_down = nullptr;
     float* sh_gate_vec = nullptr;
     bool loaded = false;
+    // 2-D TMA descriptors of the expert tensors ([E*rows][rowBytes], box 144 x 128)
+    alignas(64) uint8_t tmap_gate[128];
+    alignas(64) uint8_t tmap_up[128];
+    alignas(64) uint8_t tmap_down[128];
+    bool tmaps = false;
 };
 
 }  // namespace
@@ -83,6 +88,13 @@ struct glc_moe {
     int* ids = nullptr;        // [T*k]
     int* zeros_i = nullptr;    // [T] expert id 0 for the shared expert
     int* err = nullptr;        // device error word
+    // batched (T > 1) path
+    glc::DispatchPlan plan{};
+    int plan_gmax = 0;
+    uint8_t* btiles = nullptr;  // swizzled fp16 hi/lo B tiles
+    size_t btiles_bytes = 0;
+    float* rscale = nullptr;    // [T*k]
+    float* ysort = nullptr;     // [T*k][D]
     // pinned host staging
     float* h_x = nullptr;
     float* h_out = nullptr;
@@ -212,6 +224,54 @@ int run_shared_expert(glc_moe* h, LayerDev* L, const float* xin, int T, float* o
     return GLC_OK;
 }
 
+int make_layer_tmaps(glc_moe* h, LayerDev& L) {
+    const int D = h->d.hidden_dim, F = h->d.expert_ffn_dim, El = local_experts(h);
+    if (glc::make_q4k_tensor_map(L.tmap_gate, L.gate, (long long)El * F, (int)rowbytes(D)) ||
+        glc::make_q4k_tensor_map(L.tmap_up, L.up, (long long)El * F, (int)rowbytes(D)) ||
+        glc::make_q4k_tensor_map(L.tmap_down, L.down, (long long)El * D, (int)rowbytes(F)))
+        return fail(GLC_ERR_CUDA, "cuTensorMapEncodeTiled failed for the expert tensors");
+    L.tmaps = true;
+    return GLC_OK;
+}
+
+// Batched path (T > 1): dispatch plan, fp16 hi/lo operand tiles, grouped
+// tcgen05 GEMMs (gate/up + SwiGLU, then down), k-ordered weighted combine.
+int run_experts_grouped(glc_moe* h, LayerDev* L, const float* xin, int T, int k, const int* ids,
+                        const float* wts, const float* resid, float* out, cudaStream_t st) {
+    const int D = h->d.hidden_dim, F = h->d.expert_ffn_dim, E = local_experts(h);
+    const int P = T * k;
+    if (!L->tmaps) return fail(GLC_ERR_STATE, "layer has no tensor maps");
+    CUDA_TRY(glc::dispatch_plan_launch(ids, P, E, h->plan, st));
+    mark(h, st);
+    CUDA_TRY(glc::split_rows_launch(xin, P, D, k, 1, h->plan, h->btiles, h->rscale, st));
+    mark(h, st);
+    const int gmax = glc::plan_max_groups(P, E);
+    glc::GroupedParams g{};
+    g.K = D;
+    g.rows_per_e = F;
+    g.nm = 2;
+    g.num_experts = E;
+    g.plan = h->plan;
+    g.btiles = h->btiles;
+    g.rscale = h->rscale;
+    g.out = h->act;
+    g.err = h->err;
+    CUDA_TRY(glc::grouped_launch(L->tmap_gate, L->tmap_up, g, gmax * (F / 128), h->num_sms, st));
+    mark(h, st);
+    CUDA_TRY(glc::split_rows_launch(h->act, P, F, k, 0, h->plan, h->btiles, h->rscale, st));
+    mark(h, st);
+    glc::GroupedParams dn = g;
+    dn.K = F;
+    dn.rows_per_e = D;
+    dn.nm = 1;
+    dn.out = h->ysort;
+    CUDA_TRY(glc::grouped_launch(L->tmap_down, nullptr, dn, gmax * (D / 128), h->num_sms, st));
+    mark(h, st);
+    CUDA_TRY(glc::combine_launch(h->ysort, T, D, k, h->plan.inv, wts, resid, out, st));
+    mark(h, st);
+    return GLC_OK;
+}
+
 void free_layer(LayerDev& L) {
     cudaFree(L.gate); cudaFree(L.up); cudaFree(L.down); cudaFree(L.router);
     cudaFree(L.sh_gate); cudaFree(L.sh_up); cudaFree(L.sh_down); cudaFree(L.sh_gate_vec);
@@ -309,6 +369,29 @@ int glc_moe_create(const glc_moe_desc* desc, glc_moe** out) {
     ALLOC(h->ids, sizeof(int) * T * k);
     ALLOC(h->zeros_i, sizeof(int) * T);
     ALLOC(h->err, sizeof(int));
+    {
+        const size_t P = T * k;
+        const int E = d.num_experts;
+        const int gmax = glc::plan_max_groups((int)P, E);
+        h->plan_gmax = gmax;
+        ALLOC(h->plan.counts, sizeof(int) * E);
+        ALLOC(h->plan.offsets, sizeof(int) * (E + 1));
+        ALLOC(h->plan.perm, sizeof(int) * P);
+        ALLOC(h->plan.inv, sizeof(int) * P);
+        ALLOC(h->plan.grp_first, sizeof(int) * E);
+        ALLOC(h->plan.grp_e, sizeof(int) * gmax);
+        ALLOC(h->plan.grp_ntok, sizeof(int) * gmax);
+        ALLOC(h->plan.grp_N, sizeof(int) * gmax);
+        ALLOC(h->plan.grp_pos0, sizeof(int) * gmax);
+        ALLOC(h->plan.grp_units, sizeof(int) * gmax);
+        ALLOC(h->plan.meta, sizeof(int) * 2);
+        // B tiles: sum_g N_g <= 2 * (P + 7 * groups) rows, 512 B per row per 256 of K
+        const size_t units = 2 * (P + 7 * (size_t)gmax);
+        h->btiles_bytes = units * 512 * (size_t)(std::max(D, F) / 256);
+        ALLOC(h->btiles, h->btiles_bytes);
+        ALLOC(h->rscale, sizeof(float) * P);
+        ALLOC(h->ysort, sizeof(float) * P * D);
+    }
 #undef ALLOC
     cudaMemset(h->zeros_i, 0, sizeof(int) * T);
     cudaMemset(h->err, 0, sizeof(int));
@@ -333,6 +416,10 @@ int glc_moe_destroy(glc_moe* h) {
     if (h->graph) cudaGraphDestroy(h->graph);
     cudaFree(h->x); cudaFree(h->xin); cudaFree(h->out); cudaFree(h->act); cudaFree(h->act_sh);
     cudaFree(h->wts); cudaFree(h->gate_out); cudaFree(h->ids); cudaFree(h->zeros_i); cudaFree(h->err);
+    cudaFree(h->plan.counts); cudaFree(h->plan.offsets); cudaFree(h->plan.perm); cudaFree(h->plan.inv);
+    cudaFree(h->plan.grp_first); cudaFree(h->plan.grp_e); cudaFree(h->plan.grp_ntok); cudaFree(h->plan.grp_N);
+    cudaFree(h->plan.grp_pos0); cudaFree(h->plan.grp_units); cudaFree(h->plan.meta);
+    cudaFree(h->btiles); cudaFree(h->rscale); cudaFree(h->ysort);
     cudaFreeHost(h->h_x); cudaFreeHost(h->h_out); cudaFreeHost(h->h_ids); cudaFreeHost(h->h_w);
     if (h->stream) cudaStreamDestroy(h->stream);
     h->disposed = 1;
@@ -365,7 +452,7 @@ int glc_moe_load_layer(glc_moe* h, int32_t layer, const glc_layer_weights* w) {
         CUDA_TRY(cudaMemcpy(L.sh_gate_vec, w->shared_gate_vec, sizeof(float) * D, cudaMemcpyHostToDevice));
     }
     L.loaded = true;
-    return GLC_OK;
+    return make_layer_tmaps(h, L);
 }
 
 int glc_moe_synth_layer(glc_moe* h, int32_t layer, uint64_t seed) {
@@ -408,7 +495,7 @@ int glc_moe_synth_layer(glc_moe* h, int32_t layer, uint64_t seed) {
         CUDA_TRY(cudaMemcpy(L.sh_gate_vec, gv.data(), sizeof(float) * D, cudaMemcpyHostToDevice));
     }
     L.loaded = true;
-    return GLC_OK;
+    return make_layer_tmaps(h, L);
 }
 
 int glc_moe_set_profiling(glc_moe* h, int32_t enable) {
@@ -547,7 +634,11 @@ int glc_moe_forward_dev(glc_moe* h, int32_t layer, const float* x, int32_t T, ui
     mark(h, st);
     CUDA_TRY(glc::router_launch(rp, st));
     mark(h, st);
-    rc = run_experts(h, L, h->xin, T, k, h->ids, h->wts, (flags & GLC_FWD_RESIDUAL) ? x : nullptr, out, st);
+    // T == 1 (decode): dequant-fused GEMVs; T > 1: grouped tensor-core GEMMs.
+    const bool grouped = (flags & GLC_FWD_BATCHED) ? true : (flags & GLC_FWD_DECODE) ? false : (T > 1);
+    const float* resid = (flags & GLC_FWD_RESIDUAL) ? x : nullptr;
+    rc = grouped ? run_experts_grouped(h, L, h->xin, T, k, h->ids, h->wts, resid, out, st)
+                 : run_experts(h, L, h->xin, T, k, h->ids, h->wts, resid, out, st);
     if (rc) return rc;
     if (h->d.shared_ffn_dim > 0) {
         rc = run_shared_expert(h, L, h->xin, T, out, st);
@@ -661,6 +752,32 @@ int glc_router_topk_dev(const float* x, const float* router_w, int32_t T, int32_
     rp.ids = ids_out;
     rp.w = w_out;
     CUDA_TRY(glc::router_launch(rp, (cudaStream_t)stream));
+    return GLC_OK;
+}
+
+int glc_dispatch_plan_dev(const int32_t* ids, int32_t P, int32_t E, int32_t* counts, int32_t* offsets,
+                          int32_t* perm, int32_t* inv, void* stream) {
+    if (!ids || !counts || !offsets || !perm || !inv) return fail(GLC_ERR_INVALID_ARG, "null pointer");
+    if (P < 0 || E <= 0 || E > 64) return fail(GLC_ERR_INVALID_ARG, "P=%d E=%d out of range", P, E);
+    const int gmax = glc::plan_max_groups(P, E);
+    int* scratch = nullptr;  // group table, not returned
+    CUDA_TRY(cudaMalloc(&scratch, sizeof(int) * (size_t)(6 * gmax + E + 2)));
+    glc::DispatchPlan plan{};
+    plan.counts = counts;
+    plan.offsets = offsets;
+    plan.perm = perm;
+    plan.inv = inv;
+    plan.grp_e = scratch;
+    plan.grp_ntok = scratch + gmax;
+    plan.grp_N = scratch + 2 * gmax;
+    plan.grp_pos0 = scratch + 3 * gmax;
+    plan.grp_units = scratch + 4 * gmax;
+    plan.grp_first = scratch + 5 * gmax;
+    plan.meta = scratch + 5 * gmax + E;
+    cudaError_t e = glc::dispatch_plan_launch(ids, P, E, plan, (cudaStream_t)stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
+    cudaFree(scratch);
+    if (e != cudaSuccess) return fail(GLC_ERR_CUDA, "dispatch plan: %s", cudaGetErrorString(e));
     return GLC_OK;
 }
 

@@ -14,12 +14,14 @@
 //     with an L2 evict-first policy (weights are read once).
 //   * Consumer warps never touch global weights.  Lane u of a row owns one
 //     32-byte quant chunk c of super-block sb (64 weights, two 32-weight
-//     sub-blocks).  The lane's 64 activations are quantised once per input
-//     vector to int16 with one fp32 scale per 32-block (error <= 2^-16 of the
-//     block max), kept in registers, and every 8 weights cost 2 LOPs + 4 dp2a
-//     (int16 x uint8 -> int32): no per-weight float conversion.
-//     y_row = sum_sb d*(sc_a*s_a*Ia + sc_b*s_b*Ib/16) - dmin*(m_a*Sa + m_b*Sb)
-//     where Ia/Ib are the integer dot products and Sa/Sb the fp32 sums of the
+//     sub-blocks).  The lane's 64 activations are pre-scaled once per input
+//     vector and kept in registers; every 8 weights cost 1 SHF + 8 LOP (mask a
+//     nibble into the low bits of an fp32, exactly q * 2^(sh-149)) + 4 packed
+//     fp32 FMAs (fma.rn.f32x2): no conversion instruction and no integer
+//     dot-product unit (the transcendental/conversion pipe is what limited an
+//     int16 x uint8 dp2a formulation on sm_100).
+//     y_row = sum_sb d*(sc_a*A + sc_b*B) - dmin*(m_a*Sa + m_b*Sb), where A/B
+//     are the sub-block dot products sum q*x and Sa/Sb the fp32 sums of the
 //     32 activations of each sub-block (the Q4_K min term).
 //   * Lane partials are reduced by warp shuffles, the per-segment sums are
 //     kept in shared memory and summed in fixed order at the end (deterministic).
@@ -45,15 +47,24 @@ __device__ __forceinline__ void for_each_stage(const GemvParams& p, int r0, int 
     }
 }
 
+// Nibble -> float without a conversion instruction: any bit pattern b < 2^24
+// read as an fp32 is exactly b * 2^-149 (the subnormal binade and the first
+// normal binade share the ulp 2^-149).  So (word & (0xF << sh)) is the float
+// q * 2^(sh-149) after a single AND, and the activation it multiplies is
+// pre-scaled by 2^(125-sh-E) (E: exponent bound of its 32-block), giving
+// q * x * 2^(-24-E) per fused multiply-add, exact up to the fp32 rounding of the
+// accumulation.  Quant positions inside a 32-bit word of qs (byte i holds
+// sub-block A weight 4m+i in its low nibble, sub-block B weight 4m+i in its
+// high nibble): A shifts {0, 8, 16, 8(after >>16)}, B shifts {4, 12, 20, 12}.
 struct XRegs {
-    int xa[16];
-    int xb[16];
-    float sA, sB16, sumA, sumB;
+    float2 xa[16];  // sub-block A pairs (4m,4m+1), (4m+2,4m+3), pre-scaled
+    float2 xb[16];  // sub-block B pairs
+    float fA, fB;   // 2^(24+E) per sub-block
+    float sumA, sumB;
 };
 
-// Quantise one 32-block of activations to 16 int16 pairs; returns the block
-// scale (max|x| / 32767) and the fp32 block sum.
-__device__ __forceinline__ void quant_block32(const float4* xp, int (&dst)[16], float& scale, float& sum) {
+__device__ __forceinline__ void prep_block32(const float4* xp, float2 (&dst)[16], const int (&sh)[4], float& f,
+                                             float& sum) {
     float v[32];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -63,30 +74,37 @@ __device__ __forceinline__ void quant_block32(const float4* xp, int (&dst)[16], 
     float mx = 0.f, s = 0.f;
 #pragma unroll
     for (int i = 0; i < 32; ++i) { mx = fmaxf(mx, fabsf(v[i])); s += v[i]; }
-    const float inv = mx > 0.f ? 32767.0f / mx : 0.f;
+    // E: smallest power of two strictly above max|x| (0 for an all-zero block)
+    const int E = mx > 0.f ? ((int)((__float_as_uint(mx) >> 23) & 0xFFu) - 126) : 0;
+    float scl[4];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        const int q0 = __float2int_rn(v[2 * i] * inv);
-        const int q1 = __float2int_rn(v[2 * i + 1] * inv);
-        dst[i] = (q0 & 0xFFFF) | (q1 << 16);
+    for (int i = 0; i < 4; ++i) scl[i] = ldexpf(1.0f, 125 - sh[i] - E);
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+        dst[2 * m] = make_float2(v[4 * m] * scl[0], v[4 * m + 1] * scl[1]);
+        dst[2 * m + 1] = make_float2(v[4 * m + 2] * scl[2], v[4 * m + 3] * scl[3]);
     }
-    scale = mx * (1.0f / 32767.0f);
+    f = ldexpf(1.0f, 24 + E);
     sum = s;
 }
 
-// Quantise the lane's 64 activations (two 32-blocks) to int16 pairs.
+// Prepare the lane's 64 activations (two 32-blocks).
 __device__ __forceinline__ void load_x(XRegs& r, const float* xrow, int sb, int c, bool active) {
     if (!active) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) r.xa[i] = r.xb[i] = 0;
-        r.sA = r.sB16 = r.sumA = r.sumB = 0.f;
+        for (int i = 0; i < 16; ++i) r.xa[i] = r.xb[i] = make_float2(0.f, 0.f);
+        r.fA = r.fB = r.sumA = r.sumB = 0.f;
         return;
     }
     const float4* xp = reinterpret_cast<const float4*>(xrow + sb * 256 + 64 * c);
-    float sB;
-    quant_block32(xp, r.xa, r.sA, r.sumA);
-    quant_block32(xp + 8, r.xb, sB, r.sumB);
-    r.sB16 = sB * 0.0625f;
+    const int shA[4] = {0, 8, 16, 8};
+    const int shB[4] = {4, 12, 20, 12};
+    prep_block32(xp, r.xa, shA, r.fA, r.sumA);
+    prep_block32(xp + 8, r.xb, shB, r.fB, r.sumB);
+}
+
+__device__ __forceinline__ float2 f2(uint32_t a, uint32_t b) {
+    return make_float2(__uint_as_float(a), __uint_as_float(b));
 }
 
 // One lane's contribution to one row: chunk c of super-block sb.
@@ -96,16 +114,17 @@ __device__ __forceinline__ float row_unit(const uint8_t* row, int sb, int c, con
     const uint4 q0 = lds128(blk + 16 + 32 * c);
     const uint4 q1 = lds128(blk + 32 + 32 * c);
     const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-    int ia = 0, ib = 0;
+    float2 a0 = make_float2(0.f, 0.f), a1 = a0, b0 = a0, b1 = a0;
 #pragma unroll
     for (int m = 0; m < 8; ++m) {
-        const uint32_t lo = w[m] & 0x0F0F0F0Fu;
-        const uint32_t hi = w[m] & 0xF0F0F0F0u;
-        ia = dp2a_lo(r.xa[2 * m], lo, ia);
-        ia = dp2a_hi(r.xa[2 * m + 1], lo, ia);
-        ib = dp2a_lo(r.xb[2 * m], hi, ib);
-        ib = dp2a_hi(r.xb[2 * m + 1], hi, ib);
+        const uint32_t x = w[m], x2 = w[m] >> 16;
+        a0 = __ffma2_rn(f2(x & 0xFu, x & 0xF00u), r.xa[2 * m], a0);
+        a1 = __ffma2_rn(f2(x & 0xF0000u, x2 & 0xF00u), r.xa[2 * m + 1], a1);
+        b0 = __ffma2_rn(f2(x & 0xF0u, x & 0xF000u), r.xb[2 * m], b0);
+        b1 = __ffma2_rn(f2(x & 0xF00000u, x2 & 0xF000u), r.xb[2 * m + 1], b1);
     }
+    const float accA = (a0.x + a0.y) + (a1.x + a1.y);
+    const float accB = (b0.x + b0.y) + (b1.x + b1.y);
     const float d = __half2float(__ushort_as_half((unsigned short)(h.x & 0xFFFFu)));
     const float dmin = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
     const int sh = (c & 1) * 16;
@@ -120,9 +139,7 @@ __device__ __forceinline__ float row_unit(const uint8_t* row, int sb, int c, con
     }
     const float sc0 = (float)(scp & 0xFFu), sc1 = (float)((scp >> 8) & 0xFFu);
     const float m0 = (float)(mp & 0xFFu), m1 = (float)((mp >> 8) & 0xFFu);
-    const float fa = (float)ia * r.sA;
-    const float fb = (float)ib * r.sB16;
-    return d * (fa * sc0 + fb * sc1) - dmin * (m0 * r.sumA + m1 * r.sumB);
+    return d * ((accA * r.fA) * sc0 + (accB * r.fB) * sc1) - dmin * (m0 * r.sumA + m1 * r.sumB);
 }
 
 __device__ __forceinline__ int clamp_expert(int e, int E) { return e < 0 ? 0 : (e >= E ? E - 1 : e); }
@@ -259,8 +276,8 @@ int gemv_configure(GemvParams& p, int num_sms, size_t smem_limit, size_t* smem_b
     if (p.K <= 0 || (p.K & 255) || p.rows <= 0 || p.nseg <= 0) return -1;
     const int U = (p.K >> 8) * 4;
     const int nsegw = (U + 31) / 32;
-    if (nsegw > 16) return -1;  // K > 32768 not supported by the register layout
-    const int G = (16 / nsegw) > 0 ? 16 / nsegw : 1;
+    if (nsegw > kGemvMaxConsumerWarps) return -1;  // K > 24576 not supported by the warp layout
+    const int G = kGemvMaxConsumerWarps / nsegw;
     p.nsegw = nsegw;
     p.nw = nsegw * G;
     const int NM = (p.mode == kGemvGateUp) ? 2 : 1;

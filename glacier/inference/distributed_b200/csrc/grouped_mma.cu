@@ -1,0 +1,431 @@
+// grouped_mma.cu -- grouped expert GEMM for the batched (prefill) MoE path on
+// sm_100a tensor cores (tcgen05 + TMEM), with Q4_K weights dequantised on the
+// fly.  Replaces the per-token expert loop behind IClusterStageModel.ForwardBatchStage
+// (IClusterStageModel.cs:24) for MoE layers.
+//
+// One work item = (group g of <= 32 tokens routed to expert e, 128 output rows).
+//   D[128 x N] = A[128 x K] * B[N x K]^T,  A = expert weight rows (fp16 values
+//   d*sc*q - dmin*m, one rounding), B = the group's activations as fp16 hi/lo
+//   halves (N = 2 * roundup8(ntok)); the epilogue adds the hi and lo columns and
+//   applies the row's power-of-two scale, so activations keep ~22 bits.
+//
+// Warp roles (448 threads, one CTA per SM, persistent over work items):
+//   w0      TMA: raw Q4_K tiles (2-D tensor map, box 144 B x 128 rows, one
+//           super-block) + the B tile of the super-block (1-D bulk copy),
+//           completing on raw_full[stage]; no multicast.
+//   w1..w8  dequantise: warp group h (w1-4 / w5-8) turns half h of the
+//           super-block (K = 128h..128h+127) of its 32 rows into fp16 pairs
+//           (PRMT + LOP3 nibble -> 1024+q half trick, two HFMA2s, exact q*sc)
+//           and stores them to TMEM with tcgen05.st: A never touches shared
+//           memory, which keeps shared-memory traffic at ~2x the HBM bytes.
+//   w9      allocates TMEM and issues tcgen05.mma (A from TMEM, B from a
+//           SWIZZLE_128B shared-memory descriptor), commits to mbarriers.
+//   w10..13 epilogue: tcgen05.ld of the accumulators, SwiGLU (gate/up) or the
+//           plain projection (down), coalesced fp32 stores per token.
+// TMEM columns: A half-stage h, matrix m at [128h + 64m, +64); accumulator of
+// matrix m at [256 + 64m, +N).
+#include <cuda.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace glc {
+
+constexpr int kTcThreads = 14 * 32;
+constexpr int kRawTile = 128 * 144;          // one super-block x 128 rows
+constexpr int kBStageBytes = 64 * 512;       // N_max rows x 256 K x fp16
+constexpr uint32_t kTmemCols = 512;
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+        "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void bulk_g2s_plain(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16 (fp16 x fp16 -> fp32).
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+#define TC_ST32(taddr, r)                                                                                  \
+    asm volatile(                                                                                          \
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16," \
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),                  \
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),  \
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),       \
+        "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),      \
+        "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])                   \
+        : "memory")
+
+#define TC_LD32(taddr, r)                                                                                  \
+    asm volatile(                                                                                          \
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16," \
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"                             \
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),   \
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),         \
+          "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),       \
+          "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),       \
+          "=r"(r[29]), "=r"(r[30]), "=r"(r[31])                                                           \
+        : "r"(taddr)                                                                                      \
+        : "memory")
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+__device__ __forceinline__ uint32_t hfma2_u(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ uint32_t h2_bits(float v) {
+    const __half h = __float2half_rn(v);
+    const uint32_t u = __half_as_ushort(h);
+    return u | (u << 16);
+}
+
+// SWIZZLE_128B K-major shared-memory matrix descriptor (sm_100 format):
+// start>>4 [0,14), LBO>>4 [16,30) (unused for swizzled K-major, 1), SBO>>4
+// [32,46) = 1024 B between 8-row groups, version 1 at [46,48), layout 2 at [61,64).
+__device__ __forceinline__ uint64_t sw128_desc(const void* p) {
+    const uint64_t a = smem_u32(p);
+    return ((a >> 4) & 0x3FFFull) | (1ull << 16) | ((1024ull >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// kind::f16 instruction descriptor: D f32, A/B f16, both K-major, M = 128.
+__device__ __forceinline__ uint32_t idesc_f16(int N) {
+    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+
+// Dequantise one 64-weight chunk (qs bytes [32c, 32c+32) of a super-block row)
+// into 32 packed fp16 pairs: words 0..15 = sub-block 2c (K 0..31 of the chunk),
+// words 16..31 = sub-block 2c+1 (K 32..63).
+__device__ __forceinline__ void dequant_chunk(const uint8_t* blk, int c, uint32_t (&r)[32]) {
+    const uint4 h = lds128(blk);
+    const uint4 q0 = lds128(blk + 16 + 32 * c);
+    const uint4 q1 = lds128(blk + 32 + 32 * c);
+    const int sh = (c & 1) * 16;
+    const uint32_t Y = h.y >> sh, Z = h.z >> sh, W = h.w >> sh;
+    uint32_t scp, mp;
+    if (c < 2) {
+        scp = Y & 0x3F3Fu;
+        mp = Z & 0x3F3Fu;
+    } else {
+        scp = (W & 0x0F0Fu) | ((Y >> 2) & 0x3030u);
+        mp = ((W >> 4) & 0x0F0Fu) | ((Z >> 2) & 0x3030u);
+    }
+    const float d = __half2float(__ushort_as_half((unsigned short)(h.x & 0xFFFFu)));
+    const float dmin = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
+    const float sc0 = (float)(scp & 0xFFu), sc1 = (float)((scp >> 8) & 0xFFu);
+    const float m0 = (float)(mp & 0xFFu), m1 = (float)((mp >> 8) & 0xFFu);
+    const uint32_t dd = (h.x & 0xFFFFu) | (h.x << 16);
+    const uint32_t a_lo = h2_bits(sc0), b_lo = h2_bits(-1024.0f * sc0);
+    const uint32_t a_hi = h2_bits(sc1 * 0.0625f), b_hi = h2_bits(-64.0f * sc1);
+    const uint32_t n_lo = h2_bits(-(dmin * m0)), n_hi = h2_bits(-(dmin * m1));
+    (void)d;
+    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const uint32_t t0 = prmt(w[i], 0u, 0x4140u);  // bytes 0,1 -> halves
+        const uint32_t t1 = prmt(w[i], 0u, 0x4342u);  // bytes 2,3 -> halves
+        const uint32_t l0 = (t0 & 0x000F000Fu) | 0x64006400u;
+        const uint32_t l1 = (t1 & 0x000F000Fu) | 0x64006400u;
+        const uint32_t g0 = (t0 & 0x00F000F0u) | 0x64006400u;
+        const uint32_t g1 = (t1 & 0x00F000F0u) | 0x64006400u;
+        r[2 * i] = hfma2_u(hfma2_u(l0, a_lo, b_lo), dd, n_lo);
+        r[2 * i + 1] = hfma2_u(hfma2_u(l1, a_lo, b_lo), dd, n_lo);
+        r[16 + 2 * i] = hfma2_u(hfma2_u(g0, a_hi, b_hi), dd, n_hi);
+        r[16 + 2 * i + 1] = hfma2_u(hfma2_u(g1, a_hi, b_hi), dd, n_hi);
+    }
+}
+
+template <int HALF>
+__device__ __forceinline__ float acc_col(const uint32_t (&a0)[32], const uint32_t (&a1)[32], int c) {
+    return __uint_as_float(c < 32 ? a0[c & 31] : a1[c & 31]);
+}
+
+// Epilogue of one row for the group's tokens: column n (hi) + column HALF + n
+// (lo), times the token's power-of-two scale; SwiGLU when both matrices ran.
+template <int HALF>
+__device__ __forceinline__ void epilogue_store(const uint32_t (&a0)[32], const uint32_t (&a1)[32],
+                                               const uint32_t (&b0)[32], const uint32_t (&b1)[32], int nm,
+                                               int ntok, const float* rs, float* o, int stride) {
+#pragma unroll
+    for (int n = 0; n < HALF; ++n) {
+        if (n < ntok) {
+            const float sc = __ldg(rs + n);
+            float v = (acc_col<HALF>(a0, a1, n) + acc_col<HALF>(a0, a1, HALF + n)) * sc;
+            if (nm == 2) {
+                const float u = (acc_col<HALF>(b0, b1, n) + acc_col<HALF>(b0, b1, HALF + n)) * sc;
+                v = (v / (1.0f + expf(-v))) * u;
+            }
+            o[(size_t)n * stride] = v;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    grouped_q4k_mma_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                           const __grid_constant__ GroupedParams p, int stages) {
+    extern __shared__ uint8_t smem_raw[];
+    // 1024-byte aligned base for the SWIZZLE_128B B tiles.
+    uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    const int S = stages;
+    uint8_t* bst = smem;                                  // [S][kBStageBytes]
+    uint8_t* raw = bst + (size_t)S * kBStageBytes;        // [S][nm][kRawTile]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(raw + (size_t)S * p.nm * kRawTile);
+    uint64_t* raw_full = bars;
+    uint64_t* raw_empty = bars + S;
+    uint64_t* a_full = bars + 2 * S;
+    uint64_t* a_empty = a_full + 2;
+    uint64_t* acc_full = a_empty + 2;
+    uint64_t* acc_empty = acc_full + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nm = p.nm;
+    const int nsb = p.K >> 8;
+    const int mtiles = p.rows_per_e >> 7;
+    const int ngroups = p.plan.meta[0];
+    const int nitems = ngroups * mtiles;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&raw_full[s], 1);
+            mbar_init(&raw_empty[s], 8 + 1);
+        }
+        for (int h = 0; h < 2; ++h) {
+            mbar_init(&a_full[h], 4);
+            mbar_init(&a_empty[h], 1);
+        }
+        mbar_init(acc_full, 1);
+        mbar_init(acc_empty, 4);
+        fence_mbar_init();
+    }
+    if (warp == 9) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // --------------------------------------------------------------- TMA
+        if (lane == 0) {
+            bool ok = true;
+            int it = 0;
+            for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
+                const int g = item / mtiles, mt = item - g * mtiles;
+                const int e = p.plan.grp_e[g];
+                const int N = p.plan.grp_N[g];
+                const uint8_t* bsrc = p.btiles + (size_t)p.plan.grp_units[g] * 512u * nsb;
+                const int row0 = e * p.rows_per_e + mt * 128;
+                for (int s = 0; s < nsb; ++s, ++it) {
+                    const int stg = it % S;
+                    const uint32_t ph = (uint32_t)(it / S) & 1u;
+                    if (!mbar_wait(&raw_empty[stg], ph ^ 1u, p.err, kDevTimeoutEmpty)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&raw_full[stg], (uint32_t)(nm * kRawTile + N * 512));
+                    uint8_t* rdst = raw + (size_t)stg * nm * kRawTile;
+                    tma_load_2d(rdst, &tmA, s * 144, row0, &raw_full[stg]);
+                    if (nm == 2) tma_load_2d(rdst + kRawTile, &tmB, s * 144, row0, &raw_full[stg]);
+                    bulk_g2s_plain(bst + (size_t)stg * kBStageBytes, bsrc + (size_t)s * N * 512, (uint32_t)(N * 512),
+                                   &raw_full[stg]);
+                }
+            }
+        }
+    } else if (warp >= 1 && warp <= 8) {
+        // ------------------------------------------------------- dequantise
+        const int h = (warp - 1) >> 2;         // half of the super-block
+        const int q = warp & 3;                // TMEM lane quarter of this warp
+        const int row = 32 * q + lane;
+        const uint32_t trow = tmem + ((uint32_t)(32 * q) << 16);
+        bool ok = true;
+        int it = 0;
+        for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
+            for (int s = 0; s < nsb; ++s, ++it) {
+                const int stg = it % S;
+                const uint32_t ph = (uint32_t)(it / S) & 1u;
+                if (!mbar_wait(&raw_full[stg], ph, p.err, kDevTimeoutFull)) { ok = false; break; }
+                if (!mbar_wait(&a_empty[h], ((uint32_t)it & 1u) ^ 1u, p.err, kDevTimeoutEmpty)) { ok = false; break; }
+                tc_fence_after();
+                const uint8_t* rsrc = raw + (size_t)stg * nm * kRawTile + (size_t)row * 144;
+                for (int m = 0; m < nm; ++m) {
+#pragma unroll
+                    for (int cc = 0; cc < 2; ++cc) {
+                        uint32_t r[32];
+                        dequant_chunk(rsrc + (size_t)m * kRawTile, 2 * h + cc, r);
+                        TC_ST32(trow + (uint32_t)(128 * h + 64 * m + 32 * cc), r);
+                    }
+                }
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&a_full[h]);
+                    mbar_arrive(&raw_empty[stg]);
+                }
+            }
+        }
+    } else if (warp == 9) {
+        // ---------------------------------------------------------------- MMA
+        if (lane == 0) {
+            bool ok = true;
+            int it = 0, icount = 0;
+            for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x, ++icount) {
+                const int g = item / mtiles;
+                const int N = p.plan.grp_N[g];
+                const uint32_t idesc = idesc_f16(N);
+                if (!mbar_wait(acc_empty, ((uint32_t)icount & 1u) ^ 1u, p.err, kDevTimeoutEmpty)) { ok = false; break; }
+                tc_fence_after();
+                for (int s = 0; s < nsb; ++s, ++it) {
+                    const int stg = it % S;
+                    const uint32_t ph = (uint32_t)(it / S) & 1u;
+                    if (!mbar_wait(&raw_full[stg], ph, p.err, kDevTimeoutFull)) { ok = false; break; }
+                    const uint8_t* bs = bst + (size_t)stg * kBStageBytes;
+                    for (int h = 0; h < 2; ++h) {
+                        if (!mbar_wait(&a_full[h], (uint32_t)it & 1u, p.err, kDevTimeoutFull)) { ok = false; break; }
+                        tc_fence_after();
+#pragma unroll
+                        for (int kk = 0; kk < 8; ++kk) {
+                            const int c = 2 * h + (kk >> 2), kq = kk & 3;
+                            const uint64_t bd = sw128_desc(bs + (size_t)c * N * 128 + kq * 32);
+                            for (int m = 0; m < nm; ++m) {
+                                tc_mma_ts(tmem + 256u + 64u * m, tmem + (uint32_t)(128 * h + 64 * m + 8 * kk), bd,
+                                          idesc, (s | h | kk) != 0);
+                            }
+                        }
+                        tc_commit(&a_empty[h]);
+                    }
+                    if (!ok) break;
+                    tc_commit(&raw_empty[stg]);
+                }
+                if (ok) tc_commit(acc_full);
+            }
+        }
+    } else {
+        // ----------------------------------------------------------- epilogue
+        const int q = warp & 3;
+        const int row = 32 * q + lane;
+        const uint32_t trow = tmem + ((uint32_t)(32 * q) << 16);
+        bool ok = true;
+        int icount = 0;
+        for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x, ++icount) {
+            const int g = item / mtiles, mt = item - g * mtiles;
+            const int N = p.plan.grp_N[g];
+            const int ntok = p.plan.grp_ntok[g];
+            const int pos0 = p.plan.grp_pos0[g];
+            if (!mbar_wait(acc_full, (uint32_t)icount & 1u, p.err, kDevTimeoutFull)) { ok = false; break; }
+            tc_fence_after();
+            uint32_t a0[32], a1[32], b0[32], b1[32];
+            TC_LD32(trow + 256u, a0);
+            TC_LD32(trow + 256u + 32u, a1);
+            if (nm == 2) {
+                TC_LD32(trow + 320u, b0);
+                TC_LD32(trow + 320u + 32u, b1);
+            }
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty);
+            float* o = p.out + (size_t)pos0 * p.rows_per_e + (size_t)mt * 128 + row;
+            const float* rs = p.rscale + pos0;
+            switch (N) {  // hi columns [0, N/2), lo columns [N/2, N)
+                case 16: epilogue_store<8>(a0, a1, b0, b1, nm, ntok, rs, o, p.rows_per_e); break;
+                case 32: epilogue_store<16>(a0, a1, b0, b1, nm, ntok, rs, o, p.rows_per_e); break;
+                case 48: epilogue_store<24>(a0, a1, b0, b1, nm, ntok, rs, o, p.rows_per_e); break;
+                default: epilogue_store<32>(a0, a1, b0, b1, nm, ntok, rs, o, p.rows_per_e); break;
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 9) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    }
+}
+
+// ---------------------------------------------------------------- host side
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int make_q4k_tensor_map(void* tmap64, const void* base, long long rows, int row_bytes) {
+    static PFN_encodeTiled fn = nullptr;
+    if (!fn) {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult qr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &qr) != cudaSuccess ||
+            qr != cudaDriverEntryPointSuccess || !ptr)
+            return -1;
+        fn = (PFN_encodeTiled)ptr;
+    }
+    const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+    const cuuint32_t box[2] = {144, 128};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(reinterpret_cast<CUtensorMap*>(tmap64), CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base),
+                    dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : -2;
+}
+
+cudaError_t grouped_launch(const void* tmapA, const void* tmapB, const GroupedParams& p, int max_items, int num_sms,
+                           cudaStream_t st) {
+    if ((p.K & 255) || (p.rows_per_e & 127) || (p.nm != 1 && p.nm != 2)) return cudaErrorInvalidValue;
+    static int optin[kMaxDevices] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    if (!optin[dev]) {
+        int v = 0;
+        cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        cudaError_t e = cudaFuncSetAttribute(grouped_q4k_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, v);
+        if (e != cudaSuccess) return e;
+        optin[dev] = v;
+    }
+    const size_t per_stage = (size_t)kBStageBytes + (size_t)p.nm * kRawTile;
+    const size_t fixed = 1024 + 256;
+    int S = (int)(((size_t)optin[dev] - fixed) / per_stage);
+    if (S > 4) S = 4;
+    if (S < 2) return cudaErrorInvalidValue;
+    const size_t smem = fixed + (size_t)S * per_stage;
+    int grid = num_sms;
+    if (max_items < grid) grid = max_items > 0 ? max_items : 1;
+    const CUtensorMap* a = reinterpret_cast<const CUtensorMap*>(tmapA);
+    const CUtensorMap* b = reinterpret_cast<const CUtensorMap*>(tmapB ? tmapB : tmapA);
+    grouped_q4k_mma_kernel<<<grid, kTcThreads, smem, st>>>(*a, *b, p, S);
+    return cudaGetLastError();
+}
+
+}  // namespace glc

@@ -8,7 +8,8 @@
 namespace glc {
 
 constexpr int kMaxDevices = 64;
-constexpr int kGemvMaxThreads = 17 * 32;  // 16 consumer warps + 1 producer warp
+constexpr int kGemvMaxConsumerWarps = 12;
+constexpr int kGemvMaxThreads = (kGemvMaxConsumerWarps + 1) * 32;  // + 1 producer warp
 
 enum GemvMode : int {
     kGemvPlain = 0,        // y[N] = W x
@@ -56,6 +57,49 @@ struct RouterParams {
     float* gate_out;        // [T] sigmoid(xin . gate_vec)
 };
 cudaError_t router_launch(const RouterParams& p, cudaStream_t stream);
+
+// ---------------------------------------------------------------- batched path
+constexpr int kGroupTokens = 32;  // tokens per MMA group (N = 2*roundup8(ntok) <= 64)
+
+// Device-resident dispatch plan (all arrays device memory).
+struct DispatchPlan {
+    int* counts;      // [E]
+    int* offsets;     // [E+1]
+    int* perm;        // [P] position -> pair
+    int* inv;         // [P] pair -> position
+    int* grp_first;   // [E] first group of expert e
+    int* grp_e;       // [Gmax]
+    int* grp_ntok;    // [Gmax]
+    int* grp_N;       // [Gmax] MMA N (hi + lo rows, multiple of 16)
+    int* grp_pos0;    // [Gmax] first position of the group
+    int* grp_units;   // [Gmax] prefix sum of N over earlier groups (B-tile rows)
+    int* meta;        // [2] = {groups, total units}
+};
+inline int plan_max_groups(int P, int E) { return E + P / kGroupTokens + 1; }
+
+cudaError_t dispatch_plan_launch(const int* ids, int P, int E, const DispatchPlan& plan, cudaStream_t st);
+// B tiles: per group, per super-block s of K: [4 chunks][N rows][128 B] SWIZZLE_128B.
+cudaError_t split_rows_launch(const float* src, int P, int K, int kslots, int src_is_token,
+                              const DispatchPlan& plan, uint8_t* btiles, float* rscale, cudaStream_t st);
+cudaError_t combine_launch(const float* y, int T, int D, int k, const int* inv, const float* w,
+                           const float* resid, float* out, cudaStream_t st);
+
+// Grouped expert GEMM on tcgen05 tensor cores (weights dequantised into TMEM).
+struct GroupedParams {
+    int K;             // reduction length (D for gate/up, F for down)
+    int rows_per_e;    // output rows per expert (F for gate/up, D for down)
+    int nm;            // 2: gate+up with SwiGLU epilogue; 1: down projection
+    int num_experts;   // experts held in the weight tensors (row bound)
+    DispatchPlan plan;
+    const uint8_t* btiles;
+    const float* rscale;  // [P] power-of-two row scales of the B operand
+    float* out;           // nm=2: act [P][F]; nm=1: y [P][D]
+    int* err;
+};
+// Tensor maps are built once per weight tensor (2-D [rows][rowBytes] uint8, box 144 x 128).
+int make_q4k_tensor_map(void* tmap64, const void* base, long long rows, int row_bytes);
+cudaError_t grouped_launch(const void* tmapA, const void* tmapB, const GroupedParams& p, int max_items,
+                           int num_sms, cudaStream_t st);
 
 // Wire codec (QuantizationKernels), one CTA per token.
 cudaError_t wire_quantize_launch(int mode, const float* x, int T, int D, uint8_t* out,

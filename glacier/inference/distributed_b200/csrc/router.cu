@@ -7,117 +7,153 @@
 // GpuFirstExpertStageWorker.ProcessRoutedTopK, GpuFirstExpertStageWorker.cs:416-423);
 // the router itself lives in the un-vendored model code.  Expert ids must be
 // bit-exact against the CPU oracle, so every fp32 sum here uses one canonical
-// order that the oracle replays: 256 strided fused partials, a xor butterfly
-// inside each warp, and a fixed pairwise tree over the 8 warp sums.  Top-k is
-// taken on the logits, so exp() differences cannot change the selection.
+// order that the oracle replays: 256 strided fused partials (d = t, t+256, ...
+// in increasing d), a xor butterfly inside each warp, and a fixed pairwise tree
+// over the 8 warp sums.  Top-k is taken on the logits, so exp() differences
+// cannot change the selection.  Loads are batched UNROLL deep per thread so a
+// single CTA keeps enough requests in flight for the latency-bound T=1 case.
 #include "common.cuh"
 #include "kernels.h"
 
 namespace glc {
 
 constexpr int kRouterThreads = 256;
-constexpr int kRouterMaxAcc = 64;  // tokens-per-CTA x experts held in registers
 
 __device__ __forceinline__ float tree8(const float* s) {
     return ((s[0] + s[1]) + (s[2] + s[3])) + ((s[4] + s[5]) + (s[6] + s[7]));
 }
 
-template <int TBE>
-__global__ void __launch_bounds__(kRouterThreads) router_kernel(const __grid_constant__ RouterParams p,
-                                                                int tb_per_cta) {
-    __shared__ float red[8][kRouterMaxAcc];
-    __shared__ float logits[kRouterMaxAcc];
-    __shared__ float rms_s[kRouterMaxAcc];
-    __shared__ float gate_s[kRouterMaxAcc];
+__device__ __forceinline__ float warp_tree(float v) {
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    return v;
+}
+
+// EP: compile-time expert capacity (runtime E <= EP), TB: tokens per CTA.
+template <int EP, int TB, int UNROLL>
+__global__ void __launch_bounds__(kRouterThreads) router_kernel(const __grid_constant__ RouterParams p) {
+    __shared__ float red[8][TB * EP];
+    __shared__ float logits[TB * EP];
+    __shared__ float rms_s[TB];
+    __shared__ float gate_s[TB];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int E = p.E, D = p.D;
-    const int t0 = blockIdx.x * tb_per_cta;
-    const int ntb = min(tb_per_cta, p.T - t0);
+    const int t0 = blockIdx.x * TB;
+    const int ntb = min(TB, p.T - t0);
+    const float* __restrict__ X = p.x + (size_t)t0 * D;
 
-    // RMSNorm scale per token (canonical sum of squares).
-    for (int tb = 0; tb < ntb; ++tb) {
-        const float* x = p.x + (size_t)(t0 + tb) * D;
-        float rms = 1.0f;
-        if (p.rmsnorm) {
-            float a = 0.f;
-            for (int d = tid; d < D; d += kRouterThreads) a = fmaf(x[d], x[d], a);
+    // ---- RMSNorm scale per token: canonical sum of squares
+    if (p.rmsnorm) {
+        float a[TB];
 #pragma unroll
-            for (int off = 16; off >= 1; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
-            if (lane == 0) red[warp][0] = a;
-            __syncthreads();
-            if (tid == 0) {
-                float s[8];
-                for (int w = 0; w < 8; ++w) s[w] = red[w][0];
-                const float ss = tree8(s);
-                rms_s[tb] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), 1e-5f)));
-            }
-            __syncthreads();
-            rms = rms_s[tb];
+        for (int tb = 0; tb < TB; ++tb) a[tb] = 0.f;
+        for (int d0 = tid; d0 < D; d0 += UNROLL * kRouterThreads) {
+            float v[UNROLL][TB];
+#pragma unroll
+            for (int u = 0; u < UNROLL; ++u)
+#pragma unroll
+                for (int tb = 0; tb < TB; ++tb) {
+                    const int d = d0 + u * kRouterThreads;
+                    v[u][tb] = (d < D && tb < ntb) ? __ldg(X + (size_t)tb * D + d) : 0.f;
+                }
+#pragma unroll
+            for (int u = 0; u < UNROLL; ++u)
+#pragma unroll
+                for (int tb = 0; tb < TB; ++tb)
+                    if (d0 + u * kRouterThreads < D) a[tb] = fmaf(v[u][tb], v[u][tb], a[tb]);
         }
-        if (p.xin) {
-            float* xo = p.xin + (size_t)(t0 + tb) * D;
-            for (int d = tid; d < D; d += kRouterThreads) xo[d] = p.rmsnorm ? __fmul_rn(x[d], rms) : x[d];
-        }
-        if (tid == 0) rms_s[tb] = rms;
-    }
-    __syncthreads();
-
-    // Gate GEMV partials.
-    float acc[TBE];
 #pragma unroll
-    for (int i = 0; i < TBE; ++i) acc[i] = 0.f;
-    float gacc[TBE];
-#pragma unroll
-    for (int i = 0; i < TBE; ++i) gacc[i] = 0.f;
-    for (int d = tid; d < D; d += kRouterThreads) {
-        const float* wr = p.Wr + (size_t)d * E;
-#pragma unroll
-        for (int i = 0; i < TBE; ++i) {
-            const int tb = i / E, e = i - tb * E;
-            if (tb < ntb) {
-                const float xv = p.rmsnorm ? __fmul_rn(p.x[(size_t)(t0 + tb) * D + d], rms_s[tb])
-                                           : p.x[(size_t)(t0 + tb) * D + d];
-                acc[i] = fmaf(xv, __ldg(wr + e), acc[i]);
-                if (p.gate_vec && e == 0) gacc[i] = fmaf(xv, __ldg(p.gate_vec + d), gacc[i]);
-            }
-        }
-    }
-#pragma unroll
-    for (int i = 0; i < TBE; ++i) {
-        float v = acc[i];
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-        if (lane == 0) red[warp][i] = v;
-    }
-    __syncthreads();
-    if (tid < TBE && tid < ntb * E) {
-        float s[8];
-        for (int w = 0; w < 8; ++w) s[w] = red[w][tid];
-        logits[tid] = tree8(s);
-    }
-    __syncthreads();
-    if (p.gate_vec) {
-#pragma unroll
-        for (int i = 0; i < TBE; ++i) {
-            float v = gacc[i];
-#pragma unroll
-            for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-            if (lane == 0) red[warp][i] = v;
+        for (int tb = 0; tb < TB; ++tb) {
+            const float s = warp_tree(a[tb]);
+            if (lane == 0) red[warp][tb] = s;
         }
         __syncthreads();
         if (tid < ntb) {
             float s[8];
-            for (int w = 0; w < 8; ++w) s[w] = red[w][tid * E];
+            for (int w = 0; w < 8; ++w) s[w] = red[w][tid];
+            const float ss = tree8(s);
+            rms_s[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), 1e-5f)));
+        }
+        __syncthreads();
+    }
+
+    // ---- gate GEMV partials (+ shared-expert gate), xin written on the way
+    float acc[TB][EP];
+    float gacc[TB];
+#pragma unroll
+    for (int tb = 0; tb < TB; ++tb) {
+        gacc[tb] = 0.f;
+#pragma unroll
+        for (int e = 0; e < EP; ++e) acc[tb][e] = 0.f;
+    }
+    float rms[TB];
+#pragma unroll
+    for (int tb = 0; tb < TB; ++tb) rms[tb] = p.rmsnorm ? rms_s[tb < ntb ? tb : 0] : 1.0f;
+    for (int d0 = tid; d0 < D; d0 += UNROLL * kRouterThreads) {
+        float xv[UNROLL][TB];
+        float wv[UNROLL][EP];
+        float gv[UNROLL];
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u) {
+            const int d = d0 + u * kRouterThreads;
+            const bool in = d < D;
+#pragma unroll
+            for (int tb = 0; tb < TB; ++tb) {
+                const float raw = (in && tb < ntb) ? __ldg(X + (size_t)tb * D + d) : 0.f;
+                xv[u][tb] = p.rmsnorm ? __fmul_rn(raw, rms[tb]) : raw;
+            }
+#pragma unroll
+            for (int e = 0; e < EP; ++e) wv[u][e] = (in && e < E) ? __ldg(p.Wr + (size_t)d * E + e) : 0.f;
+            gv[u] = (in && p.gate_vec) ? __ldg(p.gate_vec + d) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u) {
+            const int d = d0 + u * kRouterThreads;
+            if (d < D) {
+#pragma unroll
+                for (int tb = 0; tb < TB; ++tb) {
+#pragma unroll
+                    for (int e = 0; e < EP; ++e) acc[tb][e] = fmaf(xv[u][tb], wv[u][e], acc[tb][e]);
+                    gacc[tb] = fmaf(xv[u][tb], gv[u], gacc[tb]);
+                    if (p.xin && tb < ntb) p.xin[(size_t)(t0 + tb) * D + d] = xv[u][tb];
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int tb = 0; tb < TB; ++tb)
+#pragma unroll
+        for (int e = 0; e < EP; ++e) {
+            const float v = warp_tree(acc[tb][e]);
+            if (lane == 0) red[warp][tb * EP + e] = v;
+        }
+    __syncthreads();
+    for (int i = tid; i < ntb * EP; i += kRouterThreads) {
+        float s[8];
+        for (int w = 0; w < 8; ++w) s[w] = red[w][i];
+        logits[i] = tree8(s);
+    }
+    __syncthreads();
+    if (p.gate_vec) {
+#pragma unroll
+        for (int tb = 0; tb < TB; ++tb) {
+            const float v = warp_tree(gacc[tb]);
+            if (lane == 0) red[warp][tb] = v;
+        }
+        __syncthreads();
+        if (tid < ntb) {
+            float s[8];
+            for (int w = 0; w < 8; ++w) s[w] = red[w][tid];
             const float g = tree8(s);
             gate_s[tid] = 1.0f / (1.0f + expf(-g));
         }
         __syncthreads();
     }
 
-    // Softmax / top-k, one thread per token.
+    // ---- softmax / top-k, one thread per token
     if (tid < ntb) {
         const int t = t0 + tid;
-        const float* l = logits + tid * E;
+        const float* l = logits + tid * EP;
         if (p.logits)
             for (int e = 0; e < E; ++e) p.logits[(size_t)t * E + e] = l[e];
         uint64_t taken = 0;
@@ -148,21 +184,23 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(const __grid_con
     }
 }
 
+template <int EP, int TB, int UNROLL>
+static cudaError_t launch_router(const RouterParams& p, cudaStream_t stream) {
+    const int grid = (p.T + TB - 1) / TB;
+    router_kernel<EP, TB, UNROLL><<<grid, kRouterThreads, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
 cudaError_t router_launch(const RouterParams& p, cudaStream_t stream) {
     if (p.T <= 0) return cudaSuccess;
     if (p.E <= 0 || p.E > 64 || p.k <= 0 || p.k > 16 || p.k > p.E || p.D <= 0)
         return cudaErrorInvalidValue;
-    int tb = kRouterMaxAcc / p.E;
-    if (tb < 1) tb = 1;
-    if (tb > p.T) tb = p.T;
-    const int grid = (p.T + tb - 1) / tb;
-    // TBE template: smallest of {8, 16, 32, 64} covering tb * E.
-    const int need = tb * p.E;
-    if (need <= 8) router_kernel<8><<<grid, kRouterThreads, 0, stream>>>(p, tb);
-    else if (need <= 16) router_kernel<16><<<grid, kRouterThreads, 0, stream>>>(p, tb);
-    else if (need <= 32) router_kernel<32><<<grid, kRouterThreads, 0, stream>>>(p, tb);
-    else router_kernel<64><<<grid, kRouterThreads, 0, stream>>>(p, tb);
-    return cudaGetLastError();
+    // Few tokens: one token per CTA for parallelism; many: amortise Wr loads.
+    const bool many = p.T > 64;
+    if (p.E <= 8) return many ? launch_router<8, 4, 4>(p, stream) : launch_router<8, 1, 4>(p, stream);
+    if (p.E <= 16) return many ? launch_router<16, 2, 4>(p, stream) : launch_router<16, 1, 4>(p, stream);
+    if (p.E <= 32) return launch_router<32, 1, 2>(p, stream);
+    return launch_router<64, 1, 2>(p, stream);
 }
 
 }  // namespace glc

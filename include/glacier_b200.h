@@ -53,6 +53,8 @@ extern "C" {
 /* layer-forward flags */
 #define GLC_FWD_RMSNORM 1u   /* xin = RMSNorm(x), no weight, eps 1e-5 (StageWorkers.cs:89-91) */
 #define GLC_FWD_RESIDUAL 2u  /* out = x + sum_k w_k y_k (DistributedPipelineCoordinator.cs:104-134) */
+#define GLC_FWD_DECODE 4u    /* force the per-pair GEMV path (default for T == 1) */
+#define GLC_FWD_BATCHED 8u   /* force the grouped tensor-core path (default for T > 1) */
 
 typedef struct glc_moe glc_moe;
 
@@ -159,6 +161,15 @@ int glc_gemv_q4k_dev(const void* W, const float* x, float* y, int32_t K, int32_t
 int glc_router_topk_dev(const float* x, const float* router_w, int32_t T, int32_t D, int32_t E,
                         int32_t k, int32_t renormalize, int32_t rmsnorm, float* xin_out,
                         float* logits_out, int32_t* ids_out, float* w_out, void* stream);
+
+/* ---- token -> expert dispatch plan (the batched path's histogram / scan /
+ *      stable permutation).  ids: [P] expert per (token, slot) pair; outputs
+ *      counts [E], exclusive offsets [E+1], perm [P] (position -> pair, pairs
+ *      grouped by expert in ascending pair order) and inv [P] (pair -> position).
+ *      The reference has no batching: it runs experts one token at a time
+ *      (DistributedPipelineCoordinator.cs:181-206). ---- */
+int glc_dispatch_plan_dev(const int32_t* ids, int32_t P, int32_t E, int32_t* counts,
+                          int32_t* offsets, int32_t* perm, int32_t* inv, void* stream);
 
 /* ---- wire codec: QuantizationKernels (Protocol/QuantizationKernels.cs:57-163) ---- */
 int32_t glc_wire_token_bytes(int32_t mode, int32_t dim);

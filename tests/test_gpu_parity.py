@@ -80,8 +80,8 @@ def test_gemv_known_answer_blocks(cuda, glc, oracle):
     want = np.array([np.dot(np.array(c["dequant"], np.float64), x.astype(np.float64))
                      for c in Q4K["cases"]])
     yd = torch.empty(N, dtype=torch.float32, device="cuda")
-    glc.gemv_q4k_dev(dev(torch, W).data_ptr(), dev(torch, x).data_ptr(), yd.data_ptr(), 256, N,
-                     stream(torch))
+    Wd, xd = dev(torch, W), dev(torch, x)  # keep the device buffers alive until the sync
+    glc.gemv_q4k_dev(Wd.data_ptr(), xd.data_ptr(), yd.data_ptr(), 256, N, stream(torch))
     torch.cuda.synchronize()
     y = yd.cpu().numpy().astype(np.float64)
     scale = np.array([np.abs(np.array(c["dequant"])).sum() for c in Q4K["cases"]])
@@ -118,8 +118,9 @@ def test_router_bit_exact(cuda, glc, oracle, E, k, renorm):
     logits = torch.empty(T, E, device="cuda")
     ids = torch.empty(T, k, dtype=torch.int32, device="cuda")
     w = torch.empty(T, k, device="cuda")
+    Wrd = dev(torch, Wr)
     for rms in (0, 1):
-        glc.router_topk_dev(xd.data_ptr(), dev(torch, Wr).data_ptr(), T, D, E, k, renorm, rms,
+        glc.router_topk_dev(xd.data_ptr(), Wrd.data_ptr(), T, D, E, k, renorm, rms,
                             xin.data_ptr(), logits.data_ptr(), ids.data_ptr(), w.data_ptr(),
                             stream(torch))
         torch.cuda.synchronize()
@@ -186,7 +187,7 @@ def test_moe_forward_small_matches_oracle(cuda, glc, oracle, T, flags):
     L = make_layer(oracle, 51 + T, D, F, E, k)
     w = worker_for(glc, L, max_tokens=8)
     x = oracle.fill_normal(51, 1, 1.0, T * D).reshape(T, D)
-    out, ids, wt = w.forward(0, x, flags)
+    out, ids, wt = w.forward(0, x, flags | 4)  # GLC_FWD_DECODE: the per-pair GEMV path
     ro, rids, rw = oracle.moe_forward(L, x, flags)
     assert np.array_equal(ids, rids)
     np.testing.assert_allclose(wt, rw, rtol=2e-6, atol=1e-7)
@@ -199,7 +200,7 @@ def test_moe_forward_qwen_shared_expert(cuda, glc, oracle):
     L = make_layer(oracle, 61, D, F, E, k, renorm=False, Fs=Fs)
     w = worker_for(glc, L, max_tokens=4)
     x = oracle.fill_normal(61, 1, 1.0, 2 * D).reshape(2, D)
-    out, ids, wt = w.forward(0, x, 0)
+    out, ids, wt = w.forward(0, x, 4)  # GLC_FWD_DECODE
     ro, rids, rw = oracle.moe_forward(L, x, 0)
     assert np.array_equal(ids, rids)
     assert rel_l2(out, ro) <= LAYER_TOL
@@ -224,7 +225,8 @@ def _gpu_quant(torch, glc, mode, x):
     T, D = x.shape
     tb = glc.QuantizationKernels.GetPackedTokenBytes(mode, D)
     out = torch.zeros(T * tb, dtype=torch.uint8, device="cuda")
-    glc.QuantizationKernels.quantize_dev(mode, dev(torch, x).data_ptr(), T, D, out.data_ptr(), stream(torch))
+    xd = dev(torch, x)
+    glc.QuantizationKernels.quantize_dev(mode, xd.data_ptr(), T, D, out.data_ptr(), stream(torch))
     back = torch.empty(T, D, device="cuda")
     glc.QuantizationKernels.dequantize_dev(mode, out.data_ptr(), T, D, back.data_ptr(), stream(torch))
     torch.cuda.synchronize()
