@@ -40,6 +40,7 @@ sys.path.insert(0, REPO)
 WORKLOAD = dict(name="mixtral8x7b_moe_layer_decode", D=4096, F=14336, E=8, k=2, T=1, seed=20241201,
                 flags=3)  # GLC_FWD_RMSNORM | GLC_FWD_RESIDUAL
 N_TOKENS = 16
+BATCH_TOKENS = 64  # the 64-token batch of the same layer (grouped tensor-core path)
 METRIC = "MoE-layer decode tokens/s & Q4_K expert GEMV HBM GB/s vs 8 TB/s, 1/2/4/8 GPU"
 UNIT = "tokens/s"
 REF_BUDGET_S = 120.0
@@ -222,7 +223,7 @@ def run_ours(args, w):
 
     D, T = w["D"], w["T"]
     worker = glc.GpuExpertStageWorker(D, w["F"], w["E"], w["k"], renormalize=True, device=local,
-                                      max_tokens=T)
+                                      max_tokens=max(T, BATCH_TOKENS))
     worker.synth_layer(0, w["seed"])
     stream = torch.cuda.Stream()
     s = stream.cuda_stream
@@ -312,6 +313,8 @@ def run_ours(args, w):
     e2e_value = world * e2e_steps * T / float(te.item())
     del C
 
+    batched = measure_batched(torch, worker, w, stream, args) if not args.skip_batched else None
+
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.skip_cpu_baseline:
         o, Lc = cpu_layer(w)
@@ -351,12 +354,58 @@ def run_ours(args, w):
         }
         if cpu_baseline:
             line["cpu_baseline"] = cpu_baseline
+        if batched:
+            line["batched_64"] = batched
         print(json.dumps(line), flush=True)
     worker.dispose()
     if dist:
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def measure_batched(torch, worker, w, stream, args):
+    """The same layer on a 64-token batch (router, dispatch plan, operand split,
+    grouped tcgen05 gate/up+SwiGLU, split, grouped down, combine): device time
+    per batch and per kernel, CUDA events on the launching stream."""
+    D, T = w["D"], BATCH_TOKENS
+    rng = np.random.default_rng(w["seed"] + 1)
+    xs = [torch.from_numpy(rng.standard_normal((T, D)).astype(np.float32)).cuda() for _ in range(4)]
+    out = torch.empty(T, D, device="cuda")
+    s = stream.cuda_stream
+    reps = max(10, min(200, args.steps // 100))
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            worker.forward_dev(0, xs[i % 4].data_ptr(), T, w["flags"], out.data_ptr(), stream=s)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(reps):
+            worker.forward_dev(0, xs[i % 4].data_ptr(), T, w["flags"], out.data_ptr(), stream=s)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        worker.set_profiling(True)
+        kt = []
+        for i in range(reps):
+            worker.forward_dev(0, xs[i % 4].data_ptr(), T, w["flags"], out.data_ptr(), stream=s)
+            kt.append(worker.kernel_times_ms())
+        worker.set_profiling(False)
+    worker.poll_error()
+    kt = np.array(kt).mean(axis=0)
+    names = ["router", "dispatch_plan", "split_x", "grouped_gateup", "split_act", "grouped_down", "combine"]
+    expert_bytes = 3 * w["F"] * q4k_row_bytes(w["D"])  # gate + up + down of one expert
+    weight_bytes = w["E"] * expert_bytes  # a 64-token batch touches all 8 experts
+    peak, _ = peaks()
+    gu = kt[3] if len(kt) > 3 else float("nan")
+    dn = kt[5] if len(kt) > 5 else float("nan")
+    return {"workload": "mixtral8x7b_moe_layer_prefill_64", "tokens": T, "ms_per_batch": ms,
+            "tokens_per_s": T / (ms * 1e-3), "weight_bytes": weight_bytes,
+            "layer_gbs": weight_bytes / (ms * 1e-3) / 1e9,
+            "grouped_gateup_gbs": (2 * w["E"] * w["F"] * q4k_row_bytes(D)) / (gu * 1e-3) / 1e9,
+            "grouped_down_gbs": (w["E"] * D * q4k_row_bytes(w["F"])) / (dn * 1e-3) / 1e9,
+            "peak_gbs": peak,
+            "kernel_ms": {n: float(v) for n, v in zip(names, kt)}}
 
 
 def main():
@@ -367,6 +416,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--skip-cpu-baseline", action="store_true")
+    ap.add_argument("--skip-batched", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -8,7 +8,10 @@
 namespace glc {
 
 constexpr int kMaxDevices = 64;
-constexpr int kGemvMaxConsumerWarps = 12;
+#ifndef GLC_GEMV_WARPS
+#define GLC_GEMV_WARPS 15
+#endif
+constexpr int kGemvMaxConsumerWarps = GLC_GEMV_WARPS;
 constexpr int kGemvMaxThreads = (kGemvMaxConsumerWarps + 1) * 32;  // + 1 producer warp
 
 enum GemvMode : int {
