@@ -78,6 +78,7 @@ _SIGNATURES = {
     "glc_gemv_q4k_dev": (C.c_int, [vp, vp, vp, i32, i32, vp]),
     "glc_router_topk_dev": (C.c_int, [vp, vp, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp]),
     "glc_dispatch_plan_dev": (C.c_int, [vp, i32, i32, vp, vp, vp, vp, vp]),
+    "glc_dispatch_plan_noalloc_dev": (C.c_int, [vp, i32, i32, vp, vp, vp, vp, vp]),
     "glc_wire_token_bytes": (i32, [i32, i32]),
     "glc_wire_quantize": (C.c_int, [i32, vp, i32, i32, vp, C.c_size_t]),
     "glc_wire_dequantize": (C.c_int, [i32, vp, C.c_size_t, i32, i32, vp]),

@@ -71,6 +71,15 @@ struct LayerDev {
 
 }  // namespace
 
+namespace glc {
+// Records the thread-local message returned by glc_last_error() for entry
+// points defined in other translation units.
+int set_last_error(int code, const char* msg) {
+    g_last_error = msg;
+    return code;
+}
+}  // namespace glc
+
 struct glc_moe {
     glc_moe_desc d{};
     int num_sms = 0;

@@ -110,4 +110,6 @@ cudaError_t wire_quantize_launch(int mode, const float* x, int T, int D, uint8_t
 cudaError_t wire_dequantize_launch(int mode, const uint8_t* in, int T, int D, float* out,
                                    cudaStream_t stream);
 
+int set_last_error(int code, const char* msg);
+
 }  // namespace glc

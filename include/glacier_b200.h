@@ -171,6 +171,20 @@ int glc_router_topk_dev(const float* x, const float* router_w, int32_t T, int32_
 int glc_dispatch_plan_dev(const int32_t* ids, int32_t P, int32_t E, int32_t* counts,
                           int32_t* offsets, int32_t* perm, int32_t* inv, void* stream);
 
+/* ---- allocation-free dispatch plan.  No counterpart in the reference (its
+ *      hosts never batch tokens per expert).  Same inputs, outputs and results
+ *      as glc_dispatch_plan_dev, for callers that cannot allocate device memory
+ *      on the hot path (cudaMalloc/cudaFree may synchronise the whole device,
+ *      or the host budgets device memory itself): the scratch group table lives
+ *      in a fixed 51 KB device array owned by the library, so the call
+ *      allocates and frees nothing and does not synchronise `stream`.
+ *      Limits: P <= 65536 pairs, E <= 64 experts (larger -> GLC_ERR_INVALID_ARG).
+ *      The first call on a device looks up the array's address (make it before
+ *      any stream capture).  Calls share the array: calls that overlap on the
+ *      GPU race and must be serialised by the caller. ---- */
+int glc_dispatch_plan_noalloc_dev(const int32_t* ids, int32_t P, int32_t E, int32_t* counts,
+                                  int32_t* offsets, int32_t* perm, int32_t* inv, void* stream);
+
 /* ---- wire codec: QuantizationKernels (Protocol/QuantizationKernels.cs:57-163) ---- */
 int32_t glc_wire_token_bytes(int32_t mode, int32_t dim);
 int glc_wire_quantize(int32_t mode, const float* x, int32_t T, int32_t D, uint8_t* out,
