@@ -96,7 +96,7 @@ struct glc_moe {
     float* gate_out = nullptr; // [T]
     int* ids = nullptr;        // [T*k]
     int* zeros_i = nullptr;    // [T] expert id 0 for the shared expert
-    int* err = nullptr;        // device error word
+    int* err = nullptr;        // [0] device error word; [2..3] grid-barrier counter (u64) of the fused decode kernel
     // batched (T > 1) path
     glc::DispatchPlan plan{};
     int plan_gmax = 0;
@@ -148,7 +148,8 @@ int check_device_error(glc_moe* h) {
     int code = 0;
     CUDA_TRY(cudaMemcpy(&code, h->err, sizeof(int), cudaMemcpyDeviceToHost));
     if (code != 0) {
-        cudaMemset(h->err, 0, sizeof(int));
+        // also clears the grid-barrier counter, which a launch that gave up may leave mid-count
+        cudaMemset(h->err, 0, 4 * sizeof(int));
         return fail(GLC_ERR_TIMEOUT, "device-side wait gave up (code %d)", code);
     }
     return GLC_OK;
@@ -377,7 +378,7 @@ int glc_moe_create(const glc_moe_desc* desc, glc_moe** out) {
     ALLOC(h->gate_out, sizeof(float) * T);
     ALLOC(h->ids, sizeof(int) * T * k);
     ALLOC(h->zeros_i, sizeof(int) * T);
-    ALLOC(h->err, sizeof(int));
+    ALLOC(h->err, 4 * sizeof(int));
     {
         const size_t P = T * k;
         const int E = d.num_experts;
@@ -403,7 +404,7 @@ int glc_moe_create(const glc_moe_desc* desc, glc_moe** out) {
     }
 #undef ALLOC
     cudaMemset(h->zeros_i, 0, sizeof(int) * T);
-    cudaMemset(h->err, 0, sizeof(int));
+    cudaMemset(h->err, 0, 4 * sizeof(int));
     if (cudaMallocHost(&h->h_x, sizeof(float) * T * D) != cudaSuccess ||
         cudaMallocHost(&h->h_out, sizeof(float) * T * D) != cudaSuccess ||
         cudaMallocHost(&h->h_ids, sizeof(int) * T * k) != cudaSuccess ||
@@ -625,6 +626,47 @@ int glc_moe_forward_dev(glc_moe* h, int32_t layer, const float* x, int32_t T, ui
     if (!L->loaded) return fail(GLC_ERR_STATE, "layer %d has no weights", layer);
     cudaStream_t st = stream ? (cudaStream_t)stream : h->stream;
     const int D = h->d.hidden_dim, E = h->d.num_experts, k = h->d.top_k;
+    // T == 1 (decode): dequant-fused GEMVs; T > 1: grouped tensor-core GEMMs.
+    const bool grouped = (flags & GLC_FWD_BATCHED) ? true : (flags & GLC_FWD_DECODE) ? false : (T > 1);
+    const float* resid = (flags & GLC_FWD_RESIDUAL) ? x : nullptr;
+    if (!grouped && !(flags & GLC_FWD_UNFUSED) && h->d.shared_ffn_dim == 0) {
+        // Whole layer in one persistent launch when it fits (few tokens, router
+        // and input small enough to stage in shared memory).
+        const int F = h->d.expert_ffn_dim;
+        glc::FusedDecodeParams fp{};
+        fp.x = x;
+        fp.Wr = L->router;
+        fp.resid = resid;
+        fp.gate = L->gate;
+        fp.up = L->up;
+        fp.down = L->down;
+        fp.gu_expert_bytes = (long long)F * rowbytes(D);
+        fp.dn_expert_bytes = (long long)D * rowbytes(F);
+        fp.act = h->act;
+        fp.out = out;
+        fp.xin = nullptr;
+        fp.ids = h->ids;
+        fp.w = h->wts;
+        fp.bar = reinterpret_cast<unsigned long long*>(h->err + 2);
+        fp.err = h->err;
+        fp.T = T;
+        fp.D = D;
+        fp.F = F;
+        fp.E = E;
+        fp.k = k;
+        fp.renorm = h->d.renormalize;
+        fp.rmsnorm = (flags & GLC_FWD_RMSNORM) ? 1 : 0;
+        h->n_marks = 0;
+        mark(h, st);
+        const cudaError_t e = glc::fused_decode_launch(fp, h->num_sms, st);
+        if (e == cudaSuccess) {
+            mark(h, st);
+            if (ids_out) CUDA_TRY(cudaMemcpyAsync(ids_out, h->ids, sizeof(int) * T * k, cudaMemcpyDeviceToDevice, st));
+            if (w_out) CUDA_TRY(cudaMemcpyAsync(w_out, h->wts, sizeof(float) * T * k, cudaMemcpyDeviceToDevice, st));
+            return GLC_OK;
+        }
+        if (e != cudaErrorNotSupported) return fail(GLC_ERR_CUDA, "fused decode launch: %s", cudaGetErrorString(e));
+    }
     glc::RouterParams rp{};
     rp.x = x;
     rp.Wr = L->router;
@@ -643,9 +685,6 @@ int glc_moe_forward_dev(glc_moe* h, int32_t layer, const float* x, int32_t T, ui
     mark(h, st);
     CUDA_TRY(glc::router_launch(rp, st));
     mark(h, st);
-    // T == 1 (decode): dequant-fused GEMVs; T > 1: grouped tensor-core GEMMs.
-    const bool grouped = (flags & GLC_FWD_BATCHED) ? true : (flags & GLC_FWD_DECODE) ? false : (T > 1);
-    const float* resid = (flags & GLC_FWD_RESIDUAL) ? x : nullptr;
     rc = grouped ? run_experts_grouped(h, L, h->xin, T, k, h->ids, h->wts, resid, out, st)
                  : run_experts(h, L, h->xin, T, k, h->ids, h->wts, resid, out, st);
     if (rc) return rc;

@@ -15,6 +15,7 @@ enum : int {
     kDevTimeoutFull = 1,   // consumer gave up waiting for a stage to land
     kDevTimeoutEmpty = 2,  // producer gave up waiting for a stage to be released
     kDevBadArg = 3,
+    kDevTimeoutGrid = 4,   // a CTA gave up waiting at a grid-wide barrier
 };
 
 // Upper bound on any device-side wait, in nanoseconds of %globaltimer.
@@ -125,6 +126,62 @@ __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
     return v;
+}
+
+// Orders this thread's earlier generic-proxy accesses of shared memory before
+// its later async-proxy (bulk copy) writes to the same memory.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ unsigned long long atom_add_acq_rel_gpu_u64(unsigned long long* p, unsigned long long v) {
+    unsigned long long old;
+    asm volatile("atom.add.acq_rel.gpu.global.u64 %0, [%1], %2;" : "=l"(old) : "l"(p), "l"(v) : "memory");
+    return old;
+}
+
+// Grid-wide barrier for a launch whose CTAs are all resident (one per SM),
+// on a 64-bit arrival counter that only ever grows: every launch adds exactly
+// nblocks arrivals, so arrival number `prev` belongs to barrier instance
+// prev / nblocks, which completes when the counter reaches the next multiple
+// of nblocks.  One atomic round trip to arrive, polling to leave, no reset.
+// Called by ONE thread per CTA after the CTA's participating threads have
+// synchronised; the caller synchronises them again afterwards.  Waits at most
+// kWaitLimitNs, then records kDevTimeoutGrid and returns false (the host must
+// then clear the counter before the next launch).
+__device__ __forceinline__ bool grid_barrier(unsigned long long* ctr, unsigned nblocks, int* err) {
+    __threadfence();
+    const unsigned long long prev = atom_add_acq_rel_gpu_u64(ctr, 1ull);
+    const unsigned long long target = (prev / nblocks + 1) * nblocks;
+    if (prev + 1 == target) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (ld_acquire_gpu_u64(ctr) < target) {
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+            if (err) atomicExch(err, kDevTimeoutGrid);
+            return false;
+        }
+        __nanosleep(32);  // keeps the pollers from crowding out the last arrivals at the counter's L2 slice
+    }
+    __threadfence();
+    return true;
+}
+
+// Canonical router reduction steps (the CPU oracle replays the same order):
+// a xor butterfly inside a warp and a fixed pairwise tree over 8 warp sums.
+__device__ __forceinline__ float warp_tree(float v) {
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    return v;
+}
+
+__device__ __forceinline__ float tree8(const float* s) {
+    return ((s[0] + s[1]) + (s[2] + s[3])) + ((s[4] + s[5]) + (s[6] + s[7]));
 }
 
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {

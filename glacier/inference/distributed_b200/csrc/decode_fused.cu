@@ -1,0 +1,479 @@
+// decode_fused.cu -- one persistent launch for the whole MoE feed-forward layer
+// of a few decode tokens on sm_100a.
+//
+// Replaces, for the decode step, the chain the reference runs per token:
+// router (external model code) -> GpuFirstExpertStageWorker.ProcessRoutedTopK
+// (GpuFirstExpertStageWorker.cs:416-583: per selected expert GemvQ4K gate/up,
+// SwiGLU, GemvQ4K down, VecAddWeighted) -> residual add
+// (DistributedPipelineCoordinator.cs:104-134).
+//
+// Why one launch: the layer is HBM-bound (Mixtral-8x7B shape, top-2: 199 MB
+// of Q4_K weights per token) and three launches leave the weight stream idle
+// at every boundary (launch ramp, x staging behind the bulk-copy flood, epilogue
+// tail).  Here every CTA (one per SM, all resident) does:
+//   1. stages the router [D][E] and x [T][D] in shared memory with two bulk
+//      copies, and computes RMSNorm + router logits + top-k itself, in the
+//      canonical reduction order of router.cu (8 warps, 256 strided fused
+//      partials, xor butterfly, pairwise tree) -- so no barrier is needed and
+//      every CTA holds the same bit-exact expert ids;
+//   2. gate/up GEMV + SwiGLU over its balanced share of the (pair, F) rows,
+//      weights streamed by a producer warp through a ring of shared-memory
+//      stages (cp.async.bulk + mbarriers, L2 evict-first);
+//   3. meanwhile the producer runs straight on into this CTA's down-projection
+//      rows, so the ring is full of down weights when the consumers reach the
+//      grid barrier that publishes the activations;
+//   4. down GEMV over its share of the (token, D) rows, all k slots, then the
+//      weighted combine in k order (+ residual).
+// The lane math and the per-row reduction order are those of gemv_q4k.cu, so
+// the results are bit-identical to the three-launch path.
+#include <algorithm>
+
+#include "common.cuh"
+#include "gemv_lane.cuh"
+#include "kernels.h"
+
+#ifndef GLC_FUSED_MAX_STAGES
+#define GLC_FUSED_MAX_STAGES 8
+#endif
+
+namespace glc {
+
+namespace {
+
+constexpr int kRouterWidth = 256;  // threads of the canonical router reduction (8 warps)
+
+// Index, in floats, of element d of a token's normalised input in the padded
+// chunk-major layout the gate/up lanes read: chunk i = (d % 64) / 4 of unit
+// u = d / 64 is float4 number i * (U + 1) + u (U = D / 64 units; the one-unit
+// pad per chunk row keeps both the router's writes and the lanes' 16-byte
+// reads free of shared-memory bank conflicts).  A token takes D + 64 floats.
+__device__ __forceinline__ int xs_index(int d, int U) {
+    return (((d & 63) >> 2) * (U + 1) + (d >> 6)) * 4 + (d & 3);
+}
+
+// RMSNorm (optional) + router logits of every token, threads 0..255, from the
+// raw input xr [T][D]; the normalised input goes to xs (xs_index layout).
+__device__ void router_logits(const FusedDecodeParams& p, const float* Wr, const float* xr, float* xs,
+                              float* red, float* logit, float* rms_s, int tid) {
+    const int warp = tid >> 5, lane = tid & 31;
+    const int D = p.D, E = p.E, U = D >> 6;
+    for (int t = 0; t < p.T; ++t) {
+        const float* xt = xr + (size_t)t * D;
+        float rms = 1.0f;
+        if (p.rmsnorm) {
+            float a = 0.f;
+#pragma unroll 4
+            for (int d = tid; d < D; d += kRouterWidth) a = fmaf(xt[d], xt[d], a);
+            a = warp_tree(a);
+            if (lane == 0) red[warp] = a;
+            named_bar_sync(2, kRouterWidth);
+            if (tid == 0) {
+                const float ss = tree8(red);
+                rms_s[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), 1e-5f)));
+            }
+            named_bar_sync(2, kRouterWidth);
+            rms = rms_s[t];
+        }
+        for (int e0 = 0; e0 < E; e0 += 8) {
+            float acc[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+            if ((E & 3) == 0 && e0 + 8 <= E) {
+                // Two 16-byte reads of the 32 bytes e0..e0+7 of the router row.
+                // At E = 8 rows are 32 B apart across lanes; lanes 4..7 of each
+                // 8 read their second half first so one read covers all banks.
+                const int h = (E == 8) ? ((lane >> 2) & 1) : 0;
+#pragma unroll 4
+                for (int d = tid; d < D; d += kRouterWidth) {
+                    const float raw = xt[d];
+                    const float xv = p.rmsnorm ? __fmul_rn(raw, rms) : raw;
+                    const float4* wr = reinterpret_cast<const float4*>(Wr + (size_t)d * E + e0);
+                    const float4 f = wr[h], g = wr[h ^ 1];
+                    const float4 a = h ? g : f, b = h ? f : g;
+                    acc[0] = fmaf(xv, a.x, acc[0]); acc[1] = fmaf(xv, a.y, acc[1]);
+                    acc[2] = fmaf(xv, a.z, acc[2]); acc[3] = fmaf(xv, a.w, acc[3]);
+                    acc[4] = fmaf(xv, b.x, acc[4]); acc[5] = fmaf(xv, b.y, acc[5]);
+                    acc[6] = fmaf(xv, b.z, acc[6]); acc[7] = fmaf(xv, b.w, acc[7]);
+                }
+            } else {
+                for (int d = tid; d < D; d += kRouterWidth) {
+                    const float raw = xt[d];
+                    const float xv = p.rmsnorm ? __fmul_rn(raw, rms) : raw;
+                    const float* wr = Wr + (size_t)d * E + e0;
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        if (e0 + e < E) acc[e] = fmaf(xv, wr[e], acc[e]);
+                }
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float v = warp_tree(acc[e]);
+                if (lane == 0) red[warp * 8 + e] = v;
+            }
+            named_bar_sync(2, kRouterWidth);
+            if (tid < 8 && e0 + tid < E) {
+                float s[8];
+#pragma unroll
+                for (int w = 0; w < 8; ++w) s[w] = red[w * 8 + tid];
+                logit[t * E + e0 + tid] = tree8(s);
+            }
+            named_bar_sync(2, kRouterWidth);
+        }
+        float* xo = xs + (size_t)t * (D + 64);
+        for (int d = tid; d < D; d += kRouterWidth) xo[xs_index(d, U)] = p.rmsnorm ? __fmul_rn(xt[d], rms) : xt[d];
+    }
+}
+
+// Top-k of one token by one warp (E <= 64: lane l holds experts l and l+32),
+// then softmax weights: the selection order, tie rule (lower index wins; NaN
+// logits count as -inf) and the sequential fp32 sums are those of the router
+// kernel in router.cu, so ids and weights are bit-identical to it.
+__device__ void topk_token_warp(const FusedDecodeParams& p, const float* l, int t, int* s_ids, float* s_w,
+                                int lane) {
+    const int E = p.E, k = p.k;
+    const int e0 = lane, e1 = lane + 32;
+    float v0 = -INFINITY, v1 = -INFINITY;
+    bool a0 = e0 < E, a1 = e1 < E;  // still selectable
+    if (a0) v0 = isnan(l[e0]) ? -INFINITY : l[e0];
+    if (a1) v1 = isnan(l[e1]) ? -INFINITY : l[e1];
+    int first = -1;
+    for (int j = 0; j < k; ++j) {
+        // lane candidate: its better selectable entry (lower index on ties)
+        int bi = a0 ? e0 : (a1 ? e1 : 1 << 30);
+        float bv = a0 ? v0 : (a1 ? v1 : -INFINITY);
+        if (a0 && a1 && v1 > v0) { bi = e1; bv = v1; }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+            // an index of 1<<30 marks "nothing selectable"; it never beats a real entry
+            const bool take = (oi < (1 << 30)) && (bi == (1 << 30) || ov > bv || (ov == bv && oi < bi));
+            if (take) { bv = ov; bi = oi; }
+        }
+        if (bi == e0) a0 = false;
+        if (bi == e1) a1 = false;
+        if (lane == 0) s_ids[t * k + j] = bi;
+        if (j == 0) first = bi;
+    }
+    __syncwarp();
+    if (lane == 0) {
+        const float mx = isnan(l[first]) ? -INFINITY : l[first];
+        float den = 0.f;
+        if (p.renorm) {
+            for (int j = 0; j < k; ++j) den += expf(l[s_ids[t * k + j]] - mx);
+        } else {
+            for (int e = 0; e < E; ++e) den += expf(l[e] - mx);
+        }
+        for (int j = 0; j < k; ++j) s_w[t * k + j] = expf(l[s_ids[t * k + j]] - mx) / den;
+    }
+}
+
+__global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(const __grid_constant__ FusedDecodeParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int s_ok;
+    float* xs = reinterpret_cast<float*>(smem + p.off_xs);
+    float* pgu = reinterpret_cast<float*>(smem + p.off_pgu);
+    float* pdn = reinterpret_cast<float*>(smem + p.off_pdn);
+    float* red = reinterpret_cast<float*>(smem + p.off_red);
+    float* logit = reinterpret_cast<float*>(smem + p.off_logit);
+    float* rms_s = reinterpret_cast<float*>(smem + p.off_rms);
+    int* s_ids = reinterpret_cast<int*>(smem + p.off_ids);
+    float* s_w = reinterpret_cast<float*>(smem + p.off_w);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bars);
+    const int S = p.stages;
+    uint64_t* empty = full + S;
+    uint64_t* xbar = empty + S;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int T = p.T, D = p.D, F = p.F, k = p.k, P = T * k;
+    const int slot = p.slot_bytes;
+
+    if (tid == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kFusedConsumerWarps);
+        }
+        mbar_init(xbar, 1);
+        fence_mbar_init();
+        s_ok = 1;
+    }
+    __syncthreads();
+
+    // ---- 1. stage the router and x in the (still idle) stage ring; RMSNorm,
+    // logits, top-k (every CTA)
+    const uint32_t wb = (uint32_t)D * p.E * 4u;  // a multiple of 1024
+    const float* xraw = reinterpret_cast<const float*>(smem + wb);
+    if (tid == 0) {
+        const uint32_t xb = (uint32_t)T * D * 4u;
+        mbar_arrive_expect_tx(xbar, xb + wb);
+        bulk_g2s_nohint(smem, p.Wr, wb, xbar);
+        bulk_g2s_nohint(smem + wb, p.x, xb, xbar);
+    }
+    if (!mbar_wait(xbar, 0, p.err, kDevTimeoutFull)) s_ok = 0;
+    __syncthreads();
+    const bool staged = s_ok != 0;
+    if (staged && tid < kRouterWidth)
+        router_logits(p, reinterpret_cast<const float*>(smem), xraw, xs, red, logit, rms_s, tid);
+    __syncthreads();
+    if (staged && warp < T) topk_token_warp(p, logit + warp * p.E, warp, s_ids, s_w, lane);
+    __syncthreads();
+    if (!staged) return;  // uniform: every thread read the same s_ok
+    if (blockIdx.x == 0) {
+        if (tid < P) {
+            p.ids[tid] = s_ids[tid];
+            p.w[tid] = s_w[tid];
+        }
+        if (p.xin)
+            for (int i = tid; i < T * D; i += kFusedThreads) {
+                const int t = i / D, d = i - t * D;
+                p.xin[i] = xs[(size_t)t * (D + 64) + xs_index(d, D >> 6)];
+            }
+    }
+
+    const long long gu_total = (long long)P * F, dn_total = (long long)T * D;
+    const int g0 = (int)(gu_total * blockIdx.x / gridDim.x);
+    const int g1 = (int)(gu_total * (blockIdx.x + 1) / gridDim.x);
+    const int q0 = (int)(dn_total * blockIdx.x / gridDim.x);
+    const int q1 = (int)(dn_total * (blockIdx.x + 1) / gridDim.x);
+    const int rbG = (D >> 8) * 144, rbD = (F >> 8) * 144;
+
+    if (warp == kFusedConsumerWarps) {
+        // ------------------------------------------------------ producer warp
+        if (lane == 0) {
+            fence_proxy_async_smem();  // router reads of the ring before bulk writes into it
+            const uint64_t pol = l2_evict_first_policy();
+            bool ok = true;
+            const int nxt = for_each_stage_rows(F, 1, p.gu_R, g0, g1, 0, [&](int sidx, int seg, int, int rin, int nr, int) {
+                if (!ok) return;
+                const int buf = sidx % S;
+                const uint32_t ph = (uint32_t)(sidx / S) & 1u;
+                if (!mbar_wait(&empty[buf], ph ^ 1u, p.err, kDevTimeoutEmpty)) { ok = false; return; }
+                const int e = clamp_expert(s_ids[seg], p.E);
+                const size_t off = (size_t)e * p.gu_expert_bytes + (size_t)rin * rbG;
+                const uint32_t bytes = (uint32_t)(nr * rbG);
+                uint8_t* dst = smem + (size_t)buf * slot;
+                mbar_arrive_expect_tx(&full[buf], 2u * bytes);
+                bulk_g2s(dst, p.gate + off, bytes, &full[buf], pol);
+                bulk_g2s(dst + (size_t)p.gu_R * rbG, p.up + off, bytes, &full[buf], pol);
+            });
+            // Down-projection stages: with the slot-split layout a stage holds the
+            // same dn_R rows of all k selected experts (one copy each), else dn_R
+            // rows of one expert.
+            const int nsl = p.dn_split ? 1 : k, ncp = p.dn_split ? k : 1;
+            for_each_stage_rows(D, nsl, p.dn_R, q0, q1, nxt, [&](int sidx, int seg, int j, int rin, int nr, int) {
+                if (!ok) return;
+                const int buf = sidx % S;
+                const uint32_t ph = (uint32_t)(sidx / S) & 1u;
+                if (!mbar_wait(&empty[buf], ph ^ 1u, p.err, kDevTimeoutEmpty)) { ok = false; return; }
+                const uint32_t bytes = (uint32_t)(nr * rbD);
+                mbar_arrive_expect_tx(&full[buf], bytes * ncp);
+                for (int c = 0; c < ncp; ++c) {
+                    const int e = clamp_expert(s_ids[seg * k + j + c], p.E);
+                    bulk_g2s(smem + (size_t)buf * slot + (size_t)c * p.dn_R * rbD,
+                             p.down + (size_t)e * p.dn_expert_bytes + (size_t)rin * rbD, bytes, &full[buf], pol);
+                }
+            });
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------- consumer warps
+    constexpr int NT = kFusedConsumerWarps * 32;
+    bool ok = true;
+    int nxt;
+    {  // ---- 2. gate/up + SwiGLU
+        const int nsegw = p.gu_nsegw, G = p.gu_G;
+        const bool wact = warp < nsegw * G;  // warps outside the layout only pace the ring
+        const int segw = warp % nsegw, grp = warp / nsegw;
+        const int u = segw * 32 + lane;
+        const bool active = wact && u < (D >> 8) * 4;
+        const int sb = active ? (u >> 2) : 0, c = u & 3;
+        XRegs xr;
+        int cur = -1;
+        nxt = for_each_stage_rows(F, 1, p.gu_R, g0, g1, 0, [&](int sidx, int seg, int, int, int nr, int lr0) {
+            if (!ok) return;
+            const int t = seg / k;
+            if (t != cur) {
+                load_x<kXShared>(xr, reinterpret_cast<const float4*>(xs + (size_t)t * (D + 64)) + u, (D >> 6) + 1, active);
+                cur = t;
+            }
+            const int buf = sidx % S;
+            const uint32_t ph = (uint32_t)(sidx / S) & 1u;
+            if (!mbar_wait(&full[buf], ph, p.err, kDevTimeoutFull)) { ok = false; return; }
+            if (wact)
+                consume_stage(smem + (size_t)buf * slot, nr, p.gu_R, 2, G, grp, rbG, sb, c, active, xr, lane,
+                              [&](int i, int m, float v) { pgu[((size_t)(lr0 + i) * 2 + m) * nsegw + segw] = v; });
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[buf]);
+        });
+    }
+    if (!ok) s_ok = 0;
+    named_bar_sync(1, NT);
+    {
+        const int nsegw = p.gu_nsegw;
+        for (int lr = tid; lr < g1 - g0; lr += NT) {
+            const int g = g0 + lr, seg = g / F, rin = g - seg * F;
+            const float* pp = pgu + (size_t)lr * 2 * nsegw;
+            float gs = 0.f, us = 0.f;
+            for (int q = 0; q < nsegw; ++q) { gs += pp[q]; us += pp[nsegw + q]; }
+            // chunk-major, so that the down-projection lanes load it coalesced
+            p.act[(size_t)seg * F + chunk_major_index(rin >> 6, rin & 63, F >> 6)] = (gs / (1.0f + expf(-gs))) * us;
+        }
+    }
+    named_bar_sync(1, NT);
+    // ---- 3. publish the activations grid-wide (every CTA arrives, even after
+    // a local timeout, so the others are not held for the full wait limit)
+    if (tid == 0) {
+        const bool gok = grid_barrier(p.bar, gridDim.x, p.err);
+        if (!gok) s_ok = 0;
+    }
+    named_bar_sync(1, NT);
+    if (!s_ok) return;
+
+    {  // ---- 4. down projection, all k slots of each row, then the combine
+        const int nsegw = p.dn_nsegw, G = p.dn_G;
+        const bool wact = warp < nsegw * G;
+        const int segw = warp % nsegw, grp = warp / nsegw;
+        // slot-split layout: group grp works on slot grp % k of every stage
+        // (its activations loaded once per token), as group grp / k of G / k
+        const int js = p.dn_split ? grp % k : 0;
+        const int Gs = p.dn_split ? G / k : G, gs = p.dn_split ? grp / k : grp;
+        const int u = segw * 32 + lane;
+        const bool active = wact && u < (F >> 8) * 4;
+        const int sb = active ? (u >> 2) : 0, c = u & 3;
+        XRegs xr;
+        int cur = -1;
+        for_each_stage_rows(D, p.dn_split ? 1 : k, p.dn_R, q0, q1, nxt, [&](int sidx, int seg, int j0, int, int nr, int lr0) {
+            if (!ok) return;
+            const int j = p.dn_split ? js : j0;
+            const int pair = seg * k + j;
+            if (pair != cur) {
+                load_x<kXGlobalCG>(xr, reinterpret_cast<const float4*>(p.act + (size_t)pair * F) + u, F >> 6, active);
+                cur = pair;
+            }
+            const int buf = sidx % S;
+            const uint32_t ph = (uint32_t)(sidx / S) & 1u;
+            if (!mbar_wait(&full[buf], ph, p.err, kDevTimeoutFull)) { ok = false; return; }
+            const uint8_t* st = smem + (size_t)buf * slot + (p.dn_split ? (size_t)j * p.dn_R * rbD : 0);
+            if (wact)
+                consume_stage(st, nr, p.dn_R, 1, Gs, gs, rbD, sb, c, active, xr, lane,
+                              [&](int i, int, float v) { pdn[((size_t)(lr0 + i) * k + j) * nsegw + segw] = v; });
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[buf]);
+        });
+    }
+    if (!ok) s_ok = 0;
+    named_bar_sync(1, NT);
+    if (!s_ok) return;
+    {
+        const int nsegw = p.dn_nsegw;
+        for (int lr = tid; lr < q1 - q0; lr += NT) {
+            const int g = q0 + lr, t = g / D, rin = g - t * D;
+            const size_t o = (size_t)t * D + rin;
+            float acc = p.resid ? p.resid[o] : 0.f;
+            const float* pp = pdn + (size_t)lr * k * nsegw;
+            for (int jj = 0; jj < k; ++jj) {
+                float s = 0.f;
+                for (int q = 0; q < nsegw; ++q) s += pp[jj * nsegw + q];
+                acc = __fadd_rn(__fmul_rn(s, s_w[t * k + jj]), acc);
+            }
+            p.out[o] = acc;
+        }
+    }
+}
+
+size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
+
+}  // namespace
+
+int fused_decode_configure(FusedDecodeParams& p, int num_sms, size_t smem_limit, size_t* smem_bytes, int* grid) {
+    const int T = p.T, D = p.D, F = p.F, E = p.E, k = p.k;
+    if (T < 1 || T > kFusedMaxTokens || E < 1 || E > 64 || k < 1 || k > 16 || k > E) return -1;
+    if (D <= 0 || F <= 0 || (D & 255) || (F & 255) || num_sms < 1) return -1;
+    if (((uintptr_t)p.x | (uintptr_t)p.Wr) & 15u) return -1;
+    if (!p.gate || !p.up || !p.down || !p.act || !p.out || !p.ids || !p.w || !p.bar) return -1;
+    const int gu_nsegw = ((D >> 8) * 4 + 31) / 32, dn_nsegw = ((F >> 8) * 4 + 31) / 32;
+    if (gu_nsegw > kFusedConsumerWarps || dn_nsegw > kFusedConsumerWarps) return -1;
+    const int gu_G = kFusedConsumerWarps / gu_nsegw, dn_G = kFusedConsumerWarps / dn_nsegw;
+    const int rbG = (D >> 8) * 144, rbD = (F >> 8) * 144;
+    // One pass of four row-units per warp per stage.  Down projection: when
+    // top-k divides the group count, every stage holds the same rows of all k
+    // selected experts and each group keeps one slot (slot-split layout).
+    const int dn_split = (dn_G % k == 0) ? 1 : 0;
+    const int gu_R = stage_rows_for(2, gu_G);
+    const int dn_R = dn_split ? stage_rows_for(1, dn_G / k) : stage_rows_for(1, dn_G);
+    const size_t slot = std::max((size_t)2 * gu_R * rbG, (size_t)(dn_split ? k : 1) * dn_R * rbD);
+    const int g = num_sms;
+    const long long P = (long long)T * k;
+    const long long gu_rows = (P * F + g - 1) / g, dn_rows = ((long long)T * D + g - 1) / g;
+    // everything but the ring, in order after it
+    size_t o = 0;
+    const size_t o_xs = o;    o = align16(o + (size_t)T * (D + 64) * 4);
+    const size_t o_pgu = o;   o = align16(o + (size_t)gu_rows * 2 * gu_nsegw * 4);
+    const size_t o_pdn = o;   o = align16(o + (size_t)dn_rows * k * dn_nsegw * 4);
+    const size_t o_red = o;   o = align16(o + 64 * 4);
+    const size_t o_logit = o; o = align16(o + (size_t)T * E * 4);
+    const size_t o_rms = o;   o = align16(o + (size_t)T * 4);
+    const size_t o_ids = o;   o = align16(o + (size_t)P * 4);
+    const size_t o_w = o;     o = align16(o + (size_t)P * 4);
+    const size_t o_bars = o;
+    const size_t fixed = o + (2 * GLC_FUSED_MAX_STAGES + 1) * 8;
+    if (fixed >= smem_limit) return -1;
+    int S = (int)((smem_limit - fixed) / slot);
+    if (S > GLC_FUSED_MAX_STAGES) S = GLC_FUSED_MAX_STAGES;
+    if (S < 2) return -1;
+    const size_t ring = (size_t)S * slot;
+    if ((size_t)D * E * 4 + (size_t)T * D * 4 > ring) return -1;  // router and raw input are staged in the ring
+    if ((size_t)T * D * 4 + (size_t)D * E * 4 >= (1u << 20)) return -1;  // one mbarrier transaction
+    p.gu_nsegw = gu_nsegw; p.gu_G = gu_G; p.gu_R = gu_R;
+    p.dn_nsegw = dn_nsegw; p.dn_G = dn_G; p.dn_R = dn_R; p.dn_split = dn_split;
+    p.stages = S;
+    p.slot_bytes = (int)slot;
+    p.off_xs = (int)(ring + o_xs);
+    p.off_pgu = (int)(ring + o_pgu);
+    p.off_pdn = (int)(ring + o_pdn);
+    p.off_red = (int)(ring + o_red);
+    p.off_logit = (int)(ring + o_logit);
+    p.off_rms = (int)(ring + o_rms);
+    p.off_ids = (int)(ring + o_ids);
+    p.off_w = (int)(ring + o_w);
+    p.off_bars = (int)(ring + o_bars);
+    *smem_bytes = ring + o_bars + (2 * (size_t)S + 1) * 8;
+    *grid = g;
+    return 0;
+}
+
+cudaError_t fused_decode_launch(const FusedDecodeParams& p0, int num_sms, cudaStream_t stream) {
+    FusedDecodeParams p = p0;
+    static int smem_optin[kMaxDevices] = {0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    if (smem_optin[dev] == 0) {
+        int v = 0;
+        e = cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        if (e != cudaSuccess) return e;
+        // static __shared__ of the kernel (s_ok) comes out of the same budget
+        v -= 1024;
+        e = cudaFuncSetAttribute(moe_decode_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, v);
+        if (e != cudaSuccess) return e;
+        smem_optin[dev] = v;
+    }
+    size_t smem = 0;
+    int grid = 0;
+    if (fused_decode_configure(p, num_sms, (size_t)smem_optin[dev], &smem, &grid) != 0) return cudaErrorNotSupported;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kFusedThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;  // all CTAs co-resident: the grid barrier needs it
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, moe_decode_fused_kernel, p);
+}
+
+}  // namespace glc

@@ -61,6 +61,41 @@ struct RouterParams {
 };
 cudaError_t router_launch(const RouterParams& p, cudaStream_t stream);
 
+// Whole MoE layer for a few decode tokens in ONE persistent launch (one CTA
+// per SM, all resident): router (every CTA, canonical order), gate/up GEMV +
+// SwiGLU, grid barrier, down GEMV + k-ordered combine (+ residual).  Results
+// are bit-identical to router_launch + gemv_launch(gate/up) + gemv_launch(down).
+constexpr int kFusedConsumerWarps = 14;
+constexpr int kFusedThreads = (kFusedConsumerWarps + 1) * 32;  // + 1 producer warp
+constexpr int kFusedMaxTokens = 4;
+
+struct FusedDecodeParams {
+    const float* x;       // [T][D] layer input (16-byte aligned)
+    const float* Wr;      // [D][E] router (16-byte aligned)
+    const float* resid;   // [T][D] or nullptr
+    const uint8_t* gate;  // [E][F][D/256*144]
+    const uint8_t* up;
+    const uint8_t* down;  // [E][D][F/256*144]
+    long long gu_expert_bytes, dn_expert_bytes;
+    float* act;           // [T*k][F] SwiGLU activations (scratch)
+    float* out;           // [T][D]
+    float* xin;           // [T][D] normalised input, or nullptr
+    int* ids;             // [T][k] expert ids
+    float* w;             // [T][k] combine weights
+    unsigned long long* bar;  // grid-barrier arrival counter (8-byte aligned), zero at first use
+    int* err;
+    int T, D, F, E, k, renorm, rmsnorm;
+    // filled by fused_decode_configure
+    int gu_nsegw, gu_G, gu_R, dn_nsegw, dn_G, dn_R, dn_split, stages, slot_bytes;
+    int off_xs, off_pgu, off_pdn, off_red, off_logit, off_rms, off_ids, off_w, off_bars;
+};
+// Returns 0 and fills the launch shape when the layer fits the fused kernel
+// (T <= kFusedMaxTokens, E <= 64, router and input staged in shared memory),
+// -1 otherwise (callers then use the separate launches).
+int fused_decode_configure(FusedDecodeParams& p, int num_sms, size_t smem_limit, size_t* smem_bytes, int* grid);
+// Returns cudaErrorNotSupported when the layer does not fit (see above).
+cudaError_t fused_decode_launch(const FusedDecodeParams& p, int num_sms, cudaStream_t stream);
+
 // ---------------------------------------------------------------- batched path
 constexpr int kGroupTokens = 32;  // tokens per MMA group (N = 2*roundup8(ntok) <= 64)
 

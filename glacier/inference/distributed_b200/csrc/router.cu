@@ -19,16 +19,6 @@ namespace glc {
 
 constexpr int kRouterThreads = 256;
 
-__device__ __forceinline__ float tree8(const float* s) {
-    return ((s[0] + s[1]) + (s[2] + s[3])) + ((s[4] + s[5]) + (s[6] + s[7]));
-}
-
-__device__ __forceinline__ float warp_tree(float v) {
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-    return v;
-}
-
 // EP: compile-time expert capacity (runtime E <= EP), TB: tokens per CTA.
 template <int EP, int TB, int UNROLL>
 __global__ void __launch_bounds__(kRouterThreads) router_kernel(const __grid_constant__ RouterParams p) {

@@ -55,6 +55,8 @@ extern "C" {
 #define GLC_FWD_RESIDUAL 2u  /* out = x + sum_k w_k y_k (DistributedPipelineCoordinator.cs:104-134) */
 #define GLC_FWD_DECODE 4u    /* force the per-pair GEMV path (default for T == 1) */
 #define GLC_FWD_BATCHED 8u   /* force the grouped tensor-core path (default for T > 1) */
+#define GLC_FWD_UNFUSED 16u  /* decode path: router, gate/up and down as three launches instead of
+                                the single fused layer launch (same results, bit for bit) */
 
 typedef struct glc_moe glc_moe;
 
