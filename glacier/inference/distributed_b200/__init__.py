@@ -6,3 +6,6 @@ from ._lib import GlcError, LIB_PATH, lib  # noqa: F401
 from .api import (FusedActivationHeader, GpuExpertStageWorker, QuantizationKernels,  # noqa: F401
                   WirePrecisionMode, device_count, dispatch_plan_dev, gemv_q4k_dev,
                   q4k_row_bytes, router_topk_dev)
+# ep / pp import torch.distributed; they are imported on use:
+#   from glacier.inference.distributed_b200.ep import ExpertParallelStageWorker, CudaExpertShard
+#   from glacier.inference.distributed_b200.pp import StageBoundaryLink, CudaWireCodec

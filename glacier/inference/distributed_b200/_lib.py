@@ -18,7 +18,7 @@ STATUS_NAMES = {
 }
 GLC_GGUF_Q4_K = 12
 GLC_WIRE_FP32, GLC_WIRE_FP16, GLC_WIRE_INT8, GLC_WIRE_FP8_E4M3 = 0, 1, 2, 3
-GLC_FWD_RMSNORM, GLC_FWD_RESIDUAL, GLC_FWD_DECODE, GLC_FWD_BATCHED = 1, 2, 4, 8
+GLC_FWD_RMSNORM, GLC_FWD_RESIDUAL, GLC_FWD_DECODE, GLC_FWD_BATCHED, GLC_FWD_UNFUSED = 1, 2, 4, 8, 16
 
 
 class GlcError(RuntimeError):
@@ -79,6 +79,10 @@ _SIGNATURES = {
     "glc_router_topk_dev": (C.c_int, [vp, vp, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp]),
     "glc_dispatch_plan_dev": (C.c_int, [vp, i32, i32, vp, vp, vp, vp, vp]),
     "glc_dispatch_plan_noalloc_dev": (C.c_int, [vp, i32, i32, vp, vp, vp, vp, vp]),
+    "glc_moe_route_dev": (C.c_int, [vp, i32, vp, i32, C.c_uint32, vp, vp, vp, vp]),
+    "glc_moe_ep_dispatch_dev": (C.c_int, [vp, vp, vp, i32, i32, vp, vp, vp, vp, vp, vp, vp]),
+    "glc_moe_experts_dev": (C.c_int, [vp, i32, vp, vp, i32, C.c_uint32, vp, vp]),
+    "glc_moe_combine_dev": (C.c_int, [vp, i32, vp, vp, vp, i32, vp, vp, vp, vp]),
     "glc_wire_token_bytes": (i32, [i32, i32]),
     "glc_wire_quantize": (C.c_int, [i32, vp, i32, i32, vp, C.c_size_t]),
     "glc_wire_dequantize": (C.c_int, [i32, vp, C.c_size_t, i32, i32, vp]),

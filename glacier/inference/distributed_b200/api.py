@@ -157,6 +157,30 @@ class GpuExpertStageWorker:
                                stream: int | None = None):
         check(lib().glc_expert_forward_dev(self._handle(), layer, expert_id, x_ptr, y_ptr, stream))
 
+    # -- expert-parallel steps (device pointers, asynchronous on `stream`) --
+    def route_dev(self, layer: int, x_ptr: int, T: int, flags: int, xin_ptr: int, ids_ptr: int,
+                  w_ptr: int, stream: int | None = None) -> None:
+        check(lib().glc_moe_route_dev(self._handle(), layer, x_ptr, T, flags, xin_ptr, ids_ptr,
+                                      w_ptr, stream))
+
+    def ep_dispatch_dev(self, xin_ptr: int, ids_ptr: int, T: int, world: int, counts_ptr: int,
+                        offsets_ptr: int, perm_ptr: int, inv_ptr: int, rows_ptr: int,
+                        row_ids_ptr: int, stream: int | None = None) -> None:
+        check(lib().glc_moe_ep_dispatch_dev(self._handle(), xin_ptr, ids_ptr, T, world, counts_ptr,
+                                            offsets_ptr, perm_ptr, inv_ptr, rows_ptr, row_ids_ptr,
+                                            stream))
+
+    def experts_dev(self, layer: int, rows_ptr: int, ids_ptr: int, R: int, flags: int, y_ptr: int,
+                    stream: int | None = None) -> None:
+        check(lib().glc_moe_experts_dev(self._handle(), layer, rows_ptr, ids_ptr, R, flags, y_ptr,
+                                        stream))
+
+    def combine_dev(self, layer: int, y_ptr: int, inv_ptr: int, w_ptr: int, T: int,
+                    resid_ptr: int | None, xin_ptr: int | None, out_ptr: int,
+                    stream: int | None = None) -> None:
+        check(lib().glc_moe_combine_dev(self._handle(), layer, y_ptr, inv_ptr, w_ptr, T, resid_ptr,
+                                        xin_ptr, out_ptr, stream))
+
 
 def gemv_q4k_dev(W_ptr: int, x_ptr: int, y_ptr: int, K: int, N: int, stream: int | None = None):
     """QuantKernels.MatVecMul(Q4_K, W, x, y, nCols=K, nRows=N) on device pointers."""

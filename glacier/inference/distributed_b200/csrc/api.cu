@@ -96,6 +96,8 @@ struct glc_moe {
     float* gate_out = nullptr; // [T]
     int* ids = nullptr;        // [T*k]
     int* zeros_i = nullptr;    // [T] expert id 0 for the shared expert
+    float* ones = nullptr;     // [T*k] unit combine weights (per-row expert outputs)
+    int* ep_keys = nullptr;    // [T*k] destination-rank keys of the expert-parallel dispatch
     int* err = nullptr;        // [0] device error word; [2..3] grid-barrier counter (u64) of the fused decode kernel
     // batched (T > 1) path
     glc::DispatchPlan plan{};
@@ -378,6 +380,8 @@ int glc_moe_create(const glc_moe_desc* desc, glc_moe** out) {
     ALLOC(h->gate_out, sizeof(float) * T);
     ALLOC(h->ids, sizeof(int) * T * k);
     ALLOC(h->zeros_i, sizeof(int) * T);
+    ALLOC(h->ones, sizeof(float) * T * k);
+    ALLOC(h->ep_keys, sizeof(int) * T * k);
     ALLOC(h->err, 4 * sizeof(int));
     {
         const size_t P = T * k;
@@ -404,6 +408,8 @@ int glc_moe_create(const glc_moe_desc* desc, glc_moe** out) {
     }
 #undef ALLOC
     cudaMemset(h->zeros_i, 0, sizeof(int) * T);
+    if (glc::fill_launch(h->ones, T * k, 1.0f, h->stream) != cudaSuccess)
+        return cleanup(fail(GLC_ERR_CUDA, "initialising the unit weights failed"));
     cudaMemset(h->err, 0, 4 * sizeof(int));
     if (cudaMallocHost(&h->h_x, sizeof(float) * T * D) != cudaSuccess ||
         cudaMallocHost(&h->h_out, sizeof(float) * T * D) != cudaSuccess ||
@@ -426,6 +432,7 @@ int glc_moe_destroy(glc_moe* h) {
     if (h->graph) cudaGraphDestroy(h->graph);
     cudaFree(h->x); cudaFree(h->xin); cudaFree(h->out); cudaFree(h->act); cudaFree(h->act_sh);
     cudaFree(h->wts); cudaFree(h->gate_out); cudaFree(h->ids); cudaFree(h->zeros_i); cudaFree(h->err);
+    cudaFree(h->ones); cudaFree(h->ep_keys);
     cudaFree(h->plan.counts); cudaFree(h->plan.offsets); cudaFree(h->plan.perm); cudaFree(h->plan.inv);
     cudaFree(h->plan.grp_first); cudaFree(h->plan.grp_e); cudaFree(h->plan.grp_ntok); cudaFree(h->plan.grp_N);
     cudaFree(h->plan.grp_pos0); cudaFree(h->plan.grp_units); cudaFree(h->plan.meta);
@@ -694,6 +701,93 @@ int glc_moe_forward_dev(glc_moe* h, int32_t layer, const float* x, int32_t T, ui
     }
     if (ids_out) CUDA_TRY(cudaMemcpyAsync(ids_out, h->ids, sizeof(int) * T * k, cudaMemcpyDeviceToDevice, st));
     if (w_out) CUDA_TRY(cudaMemcpyAsync(w_out, h->wts, sizeof(float) * T * k, cudaMemcpyDeviceToDevice, st));
+    return GLC_OK;
+}
+
+int glc_moe_route_dev(glc_moe* h, int32_t layer, const float* x, int32_t T, uint32_t flags, float* xin_out,
+                      int32_t* ids_out, float* w_out, void* stream) {
+    int rc = check_handle(h);
+    if (rc) return rc;
+    if (T <= 0) return GLC_OK;
+    if (!x || !xin_out || !ids_out || !w_out) return fail(GLC_ERR_INVALID_ARG, "null pointer");
+    if (T > h->d.max_tokens) return fail(GLC_ERR_INVALID_ARG, "T=%d exceeds max_tokens=%d", T, h->d.max_tokens);
+    LayerDev* L = layer_of(h, layer);
+    if (!L->loaded) return fail(GLC_ERR_STATE, "layer %d has no weights", layer);
+    glc::RouterParams rp{};
+    rp.x = x;
+    rp.Wr = L->router;
+    rp.T = T;
+    rp.D = h->d.hidden_dim;
+    rp.E = h->d.num_experts;
+    rp.k = h->d.top_k;
+    rp.renorm = h->d.renormalize;
+    rp.rmsnorm = (flags & GLC_FWD_RMSNORM) ? 1 : 0;
+    rp.xin = xin_out;
+    rp.ids = ids_out;
+    rp.w = w_out;
+    rp.gate_vec = h->d.shared_ffn_dim > 0 ? L->sh_gate_vec : nullptr;
+    rp.gate_out = h->gate_out;
+    CUDA_TRY(glc::router_launch(rp, stream ? (cudaStream_t)stream : h->stream));
+    return GLC_OK;
+}
+
+int glc_moe_ep_dispatch_dev(glc_moe* h, const float* xin, const int32_t* ids, int32_t T, int32_t world,
+                            int32_t* rank_counts, int32_t* rank_offsets, int32_t* perm, int32_t* inv,
+                            float* send_rows, int32_t* send_ids, void* stream) {
+    int rc = check_handle(h);
+    if (rc) return rc;
+    if (T <= 0) return GLC_OK;
+    if (!xin || !ids || !rank_counts || !rank_offsets || !perm || !inv || !send_rows || !send_ids)
+        return fail(GLC_ERR_INVALID_ARG, "null pointer");
+    if (T > h->d.max_tokens) return fail(GLC_ERR_INVALID_ARG, "T=%d exceeds max_tokens=%d", T, h->d.max_tokens);
+    if (world < 1 || world > 64 || h->d.num_experts % world)
+        return fail(GLC_ERR_INVALID_ARG, "world=%d must divide the %d experts (and be <= 64)", world, h->d.num_experts);
+    glc::DispatchPlan pl = h->plan;  // group-table scratch of the handle, outputs in the caller's buffers
+    pl.counts = rank_counts;
+    pl.offsets = rank_offsets;
+    pl.perm = perm;
+    pl.inv = inv;
+    CUDA_TRY(glc::ep_dispatch_launch(xin, ids, T, h->d.hidden_dim, h->d.top_k, h->d.num_experts, world, h->ep_keys,
+                                     pl, send_rows, send_ids, stream ? (cudaStream_t)stream : h->stream));
+    return GLC_OK;
+}
+
+int glc_moe_experts_dev(glc_moe* h, int32_t layer, const float* rows, const int32_t* expert_ids, int32_t R,
+                        uint32_t flags, float* y_out, void* stream) {
+    int rc = check_handle(h);
+    if (rc) return rc;
+    if (R <= 0) return GLC_OK;
+    if (!rows || !expert_ids || !y_out) return fail(GLC_ERR_INVALID_ARG, "null pointer");
+    const int cap = h->d.max_tokens * h->d.top_k;
+    if (R > cap) return fail(GLC_ERR_INVALID_ARG, "R=%d rows exceed the handle's %d pair slots", R, cap);
+    LayerDev* L = layer_of(h, layer);
+    if (!L->loaded) return fail(GLC_ERR_STATE, "layer %d has no weights", layer);
+    cudaStream_t st = stream ? (cudaStream_t)stream : h->stream;
+    CUDA_TRY(glc::localize_ids_launch(expert_ids, R, h->d.expert_begin, local_experts(h), h->ids, st));
+    // each row is its own "token" with one slot and unit weight: y = expert(row) exactly
+    const bool grouped = (flags & GLC_FWD_BATCHED) ? true : (flags & GLC_FWD_DECODE) ? false : (R > 1);
+    h->n_marks = 0;
+    mark(h, st);
+    return grouped ? run_experts_grouped(h, L, rows, R, 1, h->ids, h->ones, nullptr, y_out, st)
+                   : run_experts(h, L, rows, R, 1, h->ids, h->ones, nullptr, y_out, st);
+}
+
+int glc_moe_combine_dev(glc_moe* h, int32_t layer, const float* y_back, const int32_t* inv, const float* w,
+                        int32_t T, const float* resid, const float* xin, float* out, void* stream) {
+    int rc = check_handle(h);
+    if (rc) return rc;
+    if (T <= 0) return GLC_OK;
+    if (!y_back || !inv || !w || !out) return fail(GLC_ERR_INVALID_ARG, "null pointer");
+    if (T > h->d.max_tokens) return fail(GLC_ERR_INVALID_ARG, "T=%d exceeds max_tokens=%d", T, h->d.max_tokens);
+    LayerDev* L = layer_of(h, layer);
+    cudaStream_t st = stream ? (cudaStream_t)stream : h->stream;
+    CUDA_TRY(glc::combine_launch(y_back, T, h->d.hidden_dim, h->d.top_k, inv, w, resid, out, st));
+    if (h->d.shared_ffn_dim > 0) {
+        if (!L->loaded) return fail(GLC_ERR_STATE, "layer %d has no weights", layer);
+        if (!xin) return fail(GLC_ERR_INVALID_ARG, "the shared expert needs xin");
+        rc = run_shared_expert(h, L, xin, T, out, st);
+        if (rc) return rc;
+    }
     return GLC_OK;
 }
 

@@ -139,6 +139,15 @@ int make_q4k_tensor_map(void* tmap64, const void* base, long long rows, int row_
 cudaError_t grouped_launch(const void* tmapA, const void* tmapB, const GroupedParams& p, int max_items,
                            int num_sms, cudaStream_t st);
 
+// Expert parallelism: pairs grouped by destination rank (rank = expert / (E/world)),
+// stable, with the activation row and global expert id of each pair gathered in
+// that order.  plan.counts/offsets/perm/inv receive the per-rank histogram,
+// offsets and permutation; keys is scratch [T*k].
+cudaError_t ep_dispatch_launch(const float* xin, const int* ids, int T, int D, int k, int num_experts, int world,
+                               int* keys, const DispatchPlan& plan, float* rows, int* row_ids, cudaStream_t st);
+cudaError_t localize_ids_launch(const int* ids, int n, int begin, int count, int* out, cudaStream_t st);
+cudaError_t fill_launch(float* p, int n, float v, cudaStream_t st);
+
 // Wire codec (QuantizationKernels), one CTA per token.
 cudaError_t wire_quantize_launch(int mode, const float* x, int T, int D, uint8_t* out,
                                  cudaStream_t stream);

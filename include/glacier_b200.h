@@ -187,6 +187,46 @@ int glc_dispatch_plan_dev(const int32_t* ids, int32_t P, int32_t E, int32_t* cou
 int glc_dispatch_plan_noalloc_dev(const int32_t* ids, int32_t P, int32_t E, int32_t* counts,
                                   int32_t* offsets, int32_t* perm, int32_t* inv, void* stream);
 
+/* ---- expert parallelism.  No counterpart in the reference: it runs a token's
+ *      experts one after another on one worker (DistributedPipelineCoordinator.cs:
+ *      181-206) and moves activations between LAN nodes.  Here a layer's experts are
+ *      split into contiguous shards, one per rank (glc_moe_desc.expert_begin /
+ *      expert_count; expert e lives on rank e / (E / world)), and a step is
+ *        route -> dispatch plan + gather -> all-to-all (caller, e.g. NCCL) ->
+ *        experts -> reverse all-to-all -> combine.
+ *      All pointers are device memory; every call is asynchronous on `stream`. ---- */
+
+/* RMSNorm (GLC_FWD_RMSNORM) + router + top-k on the handle's layer router (all E
+ * experts, replicated on every rank): xin_out [T][D] normalised input, ids_out
+ * [T][k] global expert ids, w_out [T][k] combine weights.  Also records the
+ * shared-expert gate for a later glc_moe_combine_dev on the same handle. */
+int glc_moe_route_dev(glc_moe* h, int32_t layer, const float* x, int32_t T, uint32_t flags,
+                      float* xin_out, int32_t* ids_out, float* w_out, void* stream);
+
+/* Pairs (t, j) grouped by destination rank, stable: rank_counts [world],
+ * rank_offsets [world+1], perm [T*k] (send position -> pair), inv [T*k]
+ * (pair -> send position); send_rows [T*k][D] = xin row of each pair in send
+ * order, send_ids [T*k] its global expert id.  num_experts % world == 0,
+ * world <= 64. */
+int glc_moe_ep_dispatch_dev(glc_moe* h, const float* xin, const int32_t* ids, int32_t T, int32_t world,
+                            int32_t* rank_counts, int32_t* rank_offsets, int32_t* perm, int32_t* inv,
+                            float* send_rows, int32_t* send_ids, void* stream);
+
+/* y_out[r] = expert_{expert_ids[r]}(rows[r]) (gate, up, SwiGLU, down; no combine)
+ * for R rows whose global ids lie in this handle's shard (ids outside are
+ * clamped into it).  R <= max_tokens * top_k.  flags: GLC_FWD_DECODE forces the
+ * per-row GEMVs, GLC_FWD_BATCHED the grouped tensor-core GEMMs; default GEMV
+ * for R == 1, grouped otherwise. */
+int glc_moe_experts_dev(glc_moe* h, int32_t layer, const float* rows, const int32_t* expert_ids,
+                        int32_t R, uint32_t flags, float* y_out, void* stream);
+
+/* out[t] = (resid[t] | 0) + sum_j w[t][j] * y_back[inv[t*k+j]], in j order
+ * (AccumulatorStageWorker.AccumulateWeightedExpert, StageWorkers.cs:152-160),
+ * then + sigmoid-gated shared expert of xin when the layer has one. */
+int glc_moe_combine_dev(glc_moe* h, int32_t layer, const float* y_back, const int32_t* inv,
+                        const float* w, int32_t T, const float* resid, const float* xin, float* out,
+                        void* stream);
+
 /* ---- wire codec: QuantizationKernels (Protocol/QuantizationKernels.cs:57-163) ---- */
 int32_t glc_wire_token_bytes(int32_t mode, int32_t dim);
 int glc_wire_quantize(int32_t mode, const float* x, int32_t T, int32_t D, uint8_t* out,
