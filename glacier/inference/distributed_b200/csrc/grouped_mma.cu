@@ -9,21 +9,38 @@
 //   halves (N = 2 * roundup8(ntok)); the epilogue adds the hi and lo columns and
 //   applies the row's power-of-two scale, so activations keep ~22 bits.
 //
-// Warp roles (448 threads, one CTA per SM, persistent over work items):
+// Warp roles (512 threads, one CTA per SM, persistent over work items):
 //   w0      TMA: raw Q4_K tiles (2-D tensor map, box 144 B x 128 rows, one
-//           super-block) + the B tile of the super-block (1-D bulk copy),
-//           completing on raw_full[stage]; no multicast.
-//   w1..w8  dequantise: warp group h (w1-4 / w5-8) turns half h of the
-//           super-block (K = 128h..128h+127) of its 32 rows into fp16 pairs
-//           (PRMT + LOP3 nibble -> 1024+q half trick, two HFMA2s, exact q*sc)
-//           and stores them to TMEM with tcgen05.st: A never touches shared
-//           memory, which keeps shared-memory traffic at ~2x the HBM bytes.
-//   w9      allocates TMEM and issues tcgen05.mma (A from TMEM, B from a
-//           SWIZZLE_128B shared-memory descriptor), commits to mbarriers.
+//           super-block) into the raw ring, completing on raw_full[stage]; a
+//           raw stage is refilled as soon as the dequantisers have read it.
+//   w15     loads the B tile of each super-block (1-D bulk copy) into a
+//           separate 2-stage ring that the MMA issuers release; keeping B out
+//           of the raw ring lets the weight prefetch run up to 4 (gate/up) or
+//           8 (down) super-blocks ahead of the dequantisers.  No multicast.
+//   w1..w8  dequantise, two groups of four warps (one TMEM lane quarter each).
+//           Work comes in A units of 128 TMEM columns = 16 MMAs of K 16: half a
+//           super-block of both matrices (gate/up), or a whole super-block of
+//           the one matrix (down); the groups take alternate units.  A warp
+//           turns its 32 rows of the unit into fp16 pairs (PRMT + LOP3 nibble ->
+//           1024+q half trick, two HFMA2s, exact q*sc) and stores them to TMEM
+//           with tcgen05.st: A never touches shared memory, which keeps
+//           shared-memory traffic at ~2x the HBM bytes.
+//   w9, w14 the two MMA issuers (w9 also allocates TMEM).  Issuer i owns
+//           accumulator i and issues the MMAs of sub-unit i of every A unit
+//           (gate/up: matrix i; down: K half i of each super-block), A from
+//           TMEM, B from a SWIZZLE_128B shared-memory descriptor, committing
+//           the unit's slot back to the dequantisers when its MMAs complete.
+//           An issuing thread's own shared-memory accesses (mbarrier waits)
+//           wait behind its queued MMAs (~260 cycles each, measured); with two
+//           issuers one waits while the other's MMAs run, which holds the
+//           tensor core near its ~44-cycle floor per M=128 MMA.
 //   w10..13 epilogue: tcgen05.ld of the accumulators, SwiGLU (gate/up) or the
-//           plain projection (down), coalesced fp32 stores per token.
-// TMEM columns: A half-stage h, matrix m at [128h + 64m, +64); accumulator of
-// matrix m at [256 + 64m, +N).
+//           sum of the two K halves (down), coalesced fp32 stores per token.
+// TMEM columns: accumulator i at [64i, +64); a ring of kAUnits A units at
+// [128 + 128u, +128).  The unit size is set by the tensor core: an M=128
+// kind::f16 MMA costs ~44 cycles for any N <= 64 (measured), and a wait +
+// fence + commit between every 8 MMAs nearly doubled that, so each hand-off
+// covers 16 MMAs; the ring lets dequantisation run up to two units ahead.
 #include <cuda.h>
 
 #include "common.cuh"
@@ -31,7 +48,10 @@
 
 namespace glc {
 
-constexpr int kTcThreads = 14 * 32;
+constexpr int kTcThreads = 16 * 32;
+constexpr int kBStages = 2;          // B-tile ring, separate from the raw-weight ring
+constexpr int kAUnits = 3;           // TMEM A ring: 3 x 128 columns after the 128 accumulator columns
+constexpr uint32_t kAccCols = 128;
 constexpr int kRawTile = 128 * 144;          // one super-block x 128 rows
 constexpr int kBStageBytes = 64 * 512;       // N_max rows x 256 K x fp16
 constexpr uint32_t kTmemCols = 512;
@@ -164,27 +184,51 @@ __device__ __forceinline__ void dequant_chunk(const uint8_t* blk, int c, uint32_
     }
 }
 
-template <int HALF>
-__device__ __forceinline__ float acc_col(const uint32_t (&a0)[32], const uint32_t (&a1)[32], int c) {
-    return __uint_as_float(c < 32 ? a0[c & 31] : a1[c & 31]);
-}
+#define TC_LD8(taddr, r)                                                                                  \
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"                 \
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),      \
+                   "=r"(r[7])                                                                              \
+                 : "r"(taddr)                                                                              \
+                 : "memory")
 
-// Epilogue of one row for the group's tokens: column n (hi) + column HALF + n
-// (lo), times the token's power-of-two scale; SwiGLU when both matrices ran.
+// Epilogue of one row for the group's tokens, in passes of 8 tokens.
+// Accumulator i (TMEM columns [64i, +64)) holds hi columns [0, HALF) and lo
+// columns [HALF, 2 HALF).  Gate/up (nm = 2): accumulator 0 = gate, 1 = up,
+// SwiGLU.  Down (nm = 1): the two accumulators are the two K halves of every
+// super-block, added in fixed order.  The accumulators are released
+// (acc_empty) once the last pass has them in registers.
 template <int HALF>
-__device__ __forceinline__ void epilogue_store(const uint32_t (&a0)[32], const uint32_t (&a1)[32],
-                                               const uint32_t (&b0)[32], const uint32_t (&b1)[32], int nm,
-                                               int ntok, const float* rs, float* o, int stride) {
+__device__ __forceinline__ void epilogue_item(uint32_t trow, int nm, int ntok, const float* rs, float* o, int stride,
+                                              uint64_t* acc_empty, int lane) {
 #pragma unroll
-    for (int n = 0; n < HALF; ++n) {
-        if (n < ntok) {
-            const float sc = __ldg(rs + n);
-            float v = (acc_col<HALF>(a0, a1, n) + acc_col<HALF>(a0, a1, HALF + n)) * sc;
-            if (nm == 2) {
-                const float u = (acc_col<HALF>(b0, b1, n) + acc_col<HALF>(b0, b1, HALF + n)) * sc;
-                v = (v / (1.0f + expf(-v))) * u;
+    for (int p0 = 0; p0 < HALF; p0 += 8) {
+        uint32_t ah[8], al[8], bh[8], bl[8];
+        TC_LD8(trow + (uint32_t)p0, ah);
+        TC_LD8(trow + (uint32_t)(HALF + p0), al);
+        TC_LD8(trow + 64u + (uint32_t)p0, bh);
+        TC_LD8(trow + 64u + (uint32_t)(HALF + p0), bl);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (p0 + 8 >= HALF) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int n = p0 + i;
+            if (n < ntok) {
+                const float sc = __ldg(rs + n);
+                const float gh = __uint_as_float(ah[i]), gl = __uint_as_float(al[i]);
+                const float uh = __uint_as_float(bh[i]), ul = __uint_as_float(bl[i]);
+                float v;
+                if (nm == 2) {
+                    const float g = (gh + gl) * sc, u = (uh + ul) * sc;
+                    v = (g / (1.0f + expf(-g))) * u;
+                } else {
+                    v = ((gh + uh) + (gl + ul)) * sc;
+                }
+                o[(size_t)n * stride] = v;
             }
-            o[(size_t)n * stride] = v;
         }
     }
 }
@@ -192,18 +236,20 @@ __device__ __forceinline__ void epilogue_store(const uint32_t (&a0)[32], const u
 __global__ void __launch_bounds__(kTcThreads, 1)
     grouped_q4k_mma_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                            const __grid_constant__ GroupedParams p, int stages) {
+    // shared memory: [kBStages][kBStageBytes] B ring (1024-aligned) | [S][nm][kRawTile] raw ring | mbarriers
     extern __shared__ uint8_t smem_raw[];
-    // 1024-byte aligned base for the SWIZZLE_128B B tiles.
     uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     const int S = stages;
-    uint8_t* bst = smem;                                  // [S][kBStageBytes]
-    uint8_t* raw = bst + (size_t)S * kBStageBytes;        // [S][nm][kRawTile]
+    uint8_t* bst = smem;
+    uint8_t* raw = bst + (size_t)kBStages * kBStageBytes;
     uint64_t* bars = reinterpret_cast<uint64_t*>(raw + (size_t)S * p.nm * kRawTile);
     uint64_t* raw_full = bars;
     uint64_t* raw_empty = bars + S;
-    uint64_t* a_full = bars + 2 * S;
-    uint64_t* a_empty = a_full + 2;
-    uint64_t* acc_full = a_empty + 2;
+    uint64_t* b_full = bars + 2 * S;
+    uint64_t* b_empty = b_full + kBStages;
+    uint64_t* a_full = b_empty + kBStages;
+    uint64_t* a_empty = a_full + kAUnits;
+    uint64_t* acc_full = a_empty + kAUnits;
     uint64_t* acc_empty = acc_full + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
 
@@ -217,13 +263,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&raw_full[s], 1);
-            mbar_init(&raw_empty[s], 8 + 1);
+            mbar_init(&raw_empty[s], 8);
         }
-        for (int h = 0; h < 2; ++h) {
-            mbar_init(&a_full[h], 4);
-            mbar_init(&a_empty[h], 1);
+        for (int s = 0; s < kBStages; ++s) {
+            mbar_init(&b_full[s], 1);
+            mbar_init(&b_empty[s], 2);
         }
-        mbar_init(acc_full, 1);
+        for (int u = 0; u < kAUnits; ++u) {
+            mbar_init(&a_full[u], 4);
+            mbar_init(&a_empty[u], 2);
+        }
+        mbar_init(acc_full, 2);
         mbar_init(acc_empty, 4);
         fence_mbar_init();
     }
@@ -239,94 +289,127 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
-        // --------------------------------------------------------------- TMA
+        // ---------------------------------------------------------- raw TMA
         if (lane == 0) {
             bool ok = true;
             int it = 0;
             for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
                 const int g = item / mtiles, mt = item - g * mtiles;
                 const int e = p.plan.grp_e[g];
-                const int N = p.plan.grp_N[g];
-                const uint8_t* bsrc = p.btiles + (size_t)p.plan.grp_units[g] * 512u * nsb;
                 const int row0 = e * p.rows_per_e + mt * 128;
                 for (int s = 0; s < nsb; ++s, ++it) {
                     const int stg = it % S;
                     const uint32_t ph = (uint32_t)(it / S) & 1u;
                     if (!mbar_wait(&raw_empty[stg], ph ^ 1u, p.err, kDevTimeoutEmpty)) { ok = false; break; }
-                    mbar_arrive_expect_tx(&raw_full[stg], (uint32_t)(nm * kRawTile + N * 512));
+                    mbar_arrive_expect_tx(&raw_full[stg], (uint32_t)(nm * kRawTile));
                     uint8_t* rdst = raw + (size_t)stg * nm * kRawTile;
                     tma_load_2d(rdst, &tmA, s * 144, row0, &raw_full[stg]);
                     if (nm == 2) tma_load_2d(rdst + kRawTile, &tmB, s * 144, row0, &raw_full[stg]);
+                }
+            }
+        }
+    } else if (warp == 15) {
+        // ------------------------------------------------------------ B tiles
+        if (lane == 0) {
+            bool ok = true;
+            int it = 0;
+            for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
+                const int g = item / mtiles;
+                const int N = p.plan.grp_N[g];
+                const uint8_t* bsrc = p.btiles + (size_t)p.plan.grp_units[g] * 512u * nsb;
+                for (int s = 0; s < nsb; ++s, ++it) {
+                    const int stg = it % kBStages;
+                    const uint32_t ph = (uint32_t)(it / kBStages) & 1u;
+                    if (!mbar_wait(&b_empty[stg], ph ^ 1u, p.err, kDevTimeoutEmpty)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&b_full[stg], (uint32_t)(N * 512));
                     bulk_g2s_plain(bst + (size_t)stg * kBStageBytes, bsrc + (size_t)s * N * 512, (uint32_t)(N * 512),
-                                   &raw_full[stg]);
+                                   &b_full[stg]);
                 }
             }
         }
     } else if (warp >= 1 && warp <= 8) {
         // ------------------------------------------------------- dequantise
-        const int h = (warp - 1) >> 2;         // half of the super-block
+        const int grp = (warp - 1) >> 2;       // takes units u with u % 2 == grp
         const int q = warp & 3;                // TMEM lane quarter of this warp
         const int row = 32 * q + lane;
         const uint32_t trow = tmem + ((uint32_t)(32 * q) << 16);
+        const int upsb = (nm == 2) ? 2 : 1;    // units per super-block
         bool ok = true;
-        int it = 0;
+        int it = 0, u = 0;                     // super-block and unit counters over all items
         for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
-            for (int s = 0; s < nsb; ++s, ++it) {
+            for (int s = 0; s < nsb && ok; ++s, ++it) {
                 const int stg = it % S;
                 const uint32_t ph = (uint32_t)(it / S) & 1u;
                 if (!mbar_wait(&raw_full[stg], ph, p.err, kDevTimeoutFull)) { ok = false; break; }
-                if (!mbar_wait(&a_empty[h], ((uint32_t)it & 1u) ^ 1u, p.err, kDevTimeoutEmpty)) { ok = false; break; }
-                tc_fence_after();
                 const uint8_t* rsrc = raw + (size_t)stg * nm * kRawTile + (size_t)row * 144;
-                for (int m = 0; m < nm; ++m) {
+                for (int j = 0; j < upsb; ++j, ++u) {
+                    if ((u & 1) != grp) continue;
+                    const int slot = u % kAUnits;
+                    const uint32_t uph = ((uint32_t)(u / kAUnits) & 1u) ^ 1u;
+                    if (!mbar_wait(&a_empty[slot], uph, p.err, kDevTimeoutEmpty)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t tcol = kAccCols + 128u * (uint32_t)slot;
+                    // sub-unit v (64 columns): matrix v of half j (gate/up), or half v of matrix 0 (down)
 #pragma unroll
-                    for (int cc = 0; cc < 2; ++cc) {
-                        uint32_t r[32];
-                        dequant_chunk(rsrc + (size_t)m * kRawTile, 2 * h + cc, r);
-                        TC_ST32(trow + (uint32_t)(128 * h + 64 * m + 32 * cc), r);
+                    for (int v = 0; v < 2; ++v) {
+                        const int m = (nm == 2) ? v : 0, hh = (nm == 2) ? j : v;
+#pragma unroll
+                        for (int cc = 0; cc < 2; ++cc) {
+                            uint32_t r[32];
+                            dequant_chunk(rsrc + (size_t)m * kRawTile, 2 * hh + cc, r);
+                            TC_ST32(trow + tcol + 64u * v + 32u * cc, r);
+                        }
                     }
+                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&a_full[slot]);
                 }
-                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-                tc_fence_before();
                 __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&a_full[h]);
-                    mbar_arrive(&raw_empty[stg]);
-                }
+                if (ok && lane == 0) mbar_arrive(&raw_empty[stg]);
             }
         }
-    } else if (warp == 9) {
+    } else if (warp == 9 || warp == 14) {
         // ---------------------------------------------------------------- MMA
+        const int v = (warp == 9) ? 0 : 1;     // this issuer's accumulator / sub-unit
         if (lane == 0) {
             bool ok = true;
-            int it = 0, icount = 0;
+            int it = 0, u = 0, icount = 0;
+            const int upsb = (nm == 2) ? 2 : 1;
+            const uint32_t dcol = tmem + 64u * (uint32_t)v;
             for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x, ++icount) {
                 const int g = item / mtiles;
                 const int N = p.plan.grp_N[g];
                 const uint32_t idesc = idesc_f16(N);
+                const uint32_t cstride = (uint32_t)N * 128u;  // bytes between the 4 K chunks of the B tile
                 if (!mbar_wait(acc_empty, ((uint32_t)icount & 1u) ^ 1u, p.err, kDevTimeoutEmpty)) { ok = false; break; }
                 tc_fence_after();
-                for (int s = 0; s < nsb; ++s, ++it) {
-                    const int stg = it % S;
-                    const uint32_t ph = (uint32_t)(it / S) & 1u;
-                    if (!mbar_wait(&raw_full[stg], ph, p.err, kDevTimeoutFull)) { ok = false; break; }
-                    const uint8_t* bs = bst + (size_t)stg * kBStageBytes;
-                    for (int h = 0; h < 2; ++h) {
-                        if (!mbar_wait(&a_full[h], (uint32_t)it & 1u, p.err, kDevTimeoutFull)) { ok = false; break; }
+                for (int s = 0; s < nsb && ok; ++s, ++it) {
+                    const int stg = it % kBStages;
+                    const uint32_t ph = (uint32_t)(it / kBStages) & 1u;
+                    if (!mbar_wait(&b_full[stg], ph, p.err, kDevTimeoutFull)) { ok = false; break; }
+                    // descriptor of the stage's B tile; K steps add their byte offset >> 4
+                    // to the start-address field (addresses stay below 2^18)
+                    const uint64_t bbase = sw128_desc(bst + (size_t)stg * kBStageBytes);
+                    for (int j = 0; j < upsb; ++j, ++u) {
+                        const int slot = u % kAUnits;
+                        if (!mbar_wait(&a_full[slot], (uint32_t)(u / kAUnits) & 1u, p.err, kDevTimeoutFull)) {
+                            ok = false;
+                            break;
+                        }
                         tc_fence_after();
+                        const int hh = (nm == 2) ? j : v;  // K half of the super-block
+                        const bool first = (s == 0) && (nm == 1 || j == 0);
+                        const uint32_t acol = tmem + kAccCols + 128u * (uint32_t)slot + 64u * (uint32_t)v;
 #pragma unroll
                         for (int kk = 0; kk < 8; ++kk) {
-                            const int c = 2 * h + (kk >> 2), kq = kk & 3;
-                            const uint64_t bd = sw128_desc(bs + (size_t)c * N * 128 + kq * 32);
-                            for (int m = 0; m < nm; ++m) {
-                                tc_mma_ts(tmem + 256u + 64u * m, tmem + (uint32_t)(128 * h + 64 * m + 8 * kk), bd,
-                                          idesc, (s | h | kk) != 0);
-                            }
+                            const uint32_t off = (uint32_t)(2 * hh + (kk >> 2)) * cstride + (uint32_t)(kk & 3) * 32u;
+                            tc_mma_ts(dcol, acol + 8u * kk, bbase + (off >> 4), idesc, (first && kk == 0) ? 0u : 1u);
                         }
-                        tc_commit(&a_empty[h]);
+                        tc_commit(&a_empty[slot]);
                     }
                     if (!ok) break;
-                    tc_commit(&raw_empty[stg]);
+                    tc_commit(&b_empty[stg]);
                 }
                 if (ok) tc_commit(acc_full);
             }
@@ -345,24 +428,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const int pos0 = p.plan.grp_pos0[g];
             if (!mbar_wait(acc_full, (uint32_t)icount & 1u, p.err, kDevTimeoutFull)) { ok = false; break; }
             tc_fence_after();
-            uint32_t a0[32], a1[32], b0[32], b1[32];
-            TC_LD32(trow + 256u, a0);
-            TC_LD32(trow + 256u + 32u, a1);
-            if (nm == 2) {
-                TC_LD32(trow + 320u, b0);
-                TC_LD32(trow + 320u + 32u, b1);
-            }
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(acc_empty);
             float* o = p.out + (size_t)pos0 * p.rows_per_e + (size_t)mt * 128 + row;
             const float* rs = p.rscale + pos0;
-            switch (N) {  // hi columns [0, N/2), lo columns [N/2, N)
-                case 16: epilogue_store<8>(a0, a1, b0, b1, nm, ntok, rs, o, p.rows_per_e); break;
-                case 32: epilogue_store<16>(a0, a1, b0, b1, nm, ntok, rs, o, p.rows_per_e); break;
-                case 48: epilogue_store<24>(a0, a1, b0, b1, nm, ntok, rs, o, p.rows_per_e); break;
-                default: epilogue_store<32>(a0, a1, b0, b1, nm, ntok, rs, o, p.rows_per_e); break;
+            switch (N) {  // hi columns [0, N/2), lo columns [N/2, N) of each accumulator
+                case 16: epilogue_item<8>(trow, nm, ntok, rs, o, p.rows_per_e, acc_empty, lane); break;
+                case 32: epilogue_item<16>(trow, nm, ntok, rs, o, p.rows_per_e, acc_empty, lane); break;
+                case 48: epilogue_item<24>(trow, nm, ntok, rs, o, p.rows_per_e, acc_empty, lane); break;
+                default: epilogue_item<32>(trow, nm, ntok, rs, o, p.rows_per_e, acc_empty, lane); break;
             }
         }
     }
@@ -414,12 +486,12 @@ cudaError_t grouped_launch(const void* tmapA, const void* tmapB, const GroupedPa
         if (e != cudaSuccess) return e;
         optin[dev] = v;
     }
-    const size_t per_stage = (size_t)kBStageBytes + (size_t)p.nm * kRawTile;
-    const size_t fixed = 1024 + 256;
-    int S = (int)(((size_t)optin[dev] - fixed) / per_stage);
-    if (S > 4) S = 4;
+    const size_t per_stage = (size_t)p.nm * kRawTile;
+    const size_t fixed = 1024 + 512;  // alignment slack + mbarriers + TMEM address slot
+    int S = (int)(((size_t)optin[dev] - fixed - (size_t)kBStages * kBStageBytes) / per_stage);
+    if (S > 8) S = 8;
     if (S < 2) return cudaErrorInvalidValue;
-    const size_t smem = fixed + (size_t)S * per_stage;
+    const size_t smem = fixed + (size_t)kBStages * kBStageBytes + (size_t)S * per_stage;
     int grid = num_sms;
     if (max_items < grid) grid = max_items > 0 ? max_items : 1;
     const CUtensorMap* a = reinterpret_cast<const CUtensorMap*>(tmapA);
