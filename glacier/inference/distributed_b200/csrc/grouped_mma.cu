@@ -123,11 +123,6 @@ __device__ __forceinline__ uint32_t hfma2_u(uint32_t a, uint32_t b, uint32_t c) 
     asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
     return d;
 }
-__device__ __forceinline__ uint32_t h2_bits(float v) {
-    const __half h = __float2half_rn(v);
-    const uint32_t u = __half_as_ushort(h);
-    return u | (u << 16);
-}
 
 // SWIZZLE_128B K-major shared-memory matrix descriptor (sm_100 format):
 // start>>4 [0,14), LBO>>4 [16,30) (unused for swizzled K-major, 1), SBO>>4
@@ -142,15 +137,52 @@ __device__ __forceinline__ uint32_t idesc_f16(int N) {
     return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
 
+__device__ __forceinline__ uint32_t hsub2_u(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t hmul2_u(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+// fp16x2 bit patterns of constants
+constexpr uint32_t kH2_1024 = 0x64006400u, kH2_m1024 = 0xE400E400u, kH2_1_16 = 0x2C002C00u, kH2_m64 = 0xD400D400u;
+
+// One super-block row's header: d and -dmin as fp16x2, and the 12 bytes of
+// packed 6-bit scales / mins (GGUF Q4_K).
+struct Q4kRowHdr {
+    uint32_t dd, ndm, y, z, w;
+};
+
+__device__ __forceinline__ Q4kRowHdr load_hdr(const uint8_t* blk) {
+    const uint4 h = lds128(blk);
+    Q4kRowHdr r;
+    r.dd = (h.x & 0xFFFFu) | (h.x << 16);
+    const uint32_t nm = (h.x >> 16) ^ 0x8000u;
+    r.ndm = nm | (nm << 16);
+    r.y = h.y;
+    r.z = h.z;
+    r.w = h.w;
+    return r;
+}
+
 // Dequantise one 64-weight chunk (qs bytes [32c, 32c+32) of a super-block row)
 // into 32 packed fp16 pairs: words 0..15 = sub-block 2c (K 0..31 of the chunk),
-// words 16..31 = sub-block 2c+1 (K 32..63).
-__device__ __forceinline__ void dequant_chunk(const uint8_t* blk, int c, uint32_t (&r)[32]) {
-    const uint4 h = lds128(blk);
+// words 16..31 = sub-block 2c+1 (K 32..63).  weight = d*(sc*q) - dmin*m with
+// sc*q exact (the 1024+q half trick and two HFMA2s) and -dmin*m one rounding.
+// The per-sub-block factors are built without conversion instructions: PRMT
+// puts a 6-bit scale or min x into the mantissa of 1024 + x and one fp16
+// subtraction leaves x exactly; every later product is exact except dmin*m,
+// rounded once like a float -> half conversion of the exact product.
+__device__ __forceinline__ void dequant_chunk(const Q4kRowHdr& hd, const uint8_t* blk, int c, uint32_t (&r)[32]) {
     const uint4 q0 = lds128(blk + 16 + 32 * c);
     const uint4 q1 = lds128(blk + 32 + 32 * c);
+    // 6-bit scale / min of sub-blocks 2c and 2c+1 (get_scale_min_k4): bytes 0 and 1
     const int sh = (c & 1) * 16;
-    const uint32_t Y = h.y >> sh, Z = h.z >> sh, W = h.w >> sh;
+    const uint32_t Y = hd.y >> sh, Z = hd.z >> sh, W = hd.w >> sh;
     uint32_t scp, mp;
     if (c < 2) {
         scp = Y & 0x3F3Fu;
@@ -159,15 +191,13 @@ __device__ __forceinline__ void dequant_chunk(const uint8_t* blk, int c, uint32_
         scp = (W & 0x0F0Fu) | ((Y >> 2) & 0x3030u);
         mp = ((W >> 4) & 0x0F0Fu) | ((Z >> 2) & 0x3030u);
     }
-    const float d = __half2float(__ushort_as_half((unsigned short)(h.x & 0xFFFFu)));
-    const float dmin = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
-    const float sc0 = (float)(scp & 0xFFu), sc1 = (float)((scp >> 8) & 0xFFu);
-    const float m0 = (float)(mp & 0xFFu), m1 = (float)((mp >> 8) & 0xFFu);
-    const uint32_t dd = (h.x & 0xFFFFu) | (h.x << 16);
-    const uint32_t a_lo = h2_bits(sc0), b_lo = h2_bits(-1024.0f * sc0);
-    const uint32_t a_hi = h2_bits(sc1 * 0.0625f), b_hi = h2_bits(-64.0f * sc1);
-    const uint32_t n_lo = h2_bits(-(dmin * m0)), n_hi = h2_bits(-(dmin * m1));
-    (void)d;
+    const uint32_t a_lo = hsub2_u(prmt(scp, 0x64u, 0x4040u), kH2_1024);           // sc0
+    const uint32_t a_hi = hfma2_u(prmt(scp, 0x64u, 0x4141u), kH2_1_16, kH2_m64);  // sc1 / 16
+    const uint32_t b_lo = hmul2_u(a_lo, kH2_m1024);                                // -1024 sc0
+    const uint32_t b_hi = hmul2_u(a_hi, kH2_m1024);                                // -64 sc1
+    const uint32_t n_lo = hmul2_u(hsub2_u(prmt(mp, 0x64u, 0x4040u), kH2_1024), hd.ndm);  // -dmin m0
+    const uint32_t n_hi = hmul2_u(hsub2_u(prmt(mp, 0x64u, 0x4141u), kH2_1024), hd.ndm);  // -dmin m1
+    const uint32_t dd = hd.dd;
     const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -353,10 +383,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
                     for (int v = 0; v < 2; ++v) {
                         const int m = (nm == 2) ? v : 0, hh = (nm == 2) ? j : v;
+                        const uint8_t* blk = rsrc + (size_t)m * kRawTile;
+                        const Q4kRowHdr hd = load_hdr(blk);  // once per row, matrix and unit
 #pragma unroll
                         for (int cc = 0; cc < 2; ++cc) {
                             uint32_t r[32];
-                            dequant_chunk(rsrc + (size_t)m * kRawTile, 2 * hh + cc, r);
+                            dequant_chunk(hd, blk, 2 * hh + cc, r);
                             TC_ST32(trow + tcol + 64u * v + 32u * cc, r);
                         }
                     }
