@@ -221,30 +221,36 @@ __device__ __forceinline__ void dequant_chunk(const Q4kRowHdr& hd, const uint8_t
                  : "r"(taddr)                                                                              \
                  : "memory")
 
-// Epilogue of one row for the group's tokens, in passes of 8 tokens.
-// Accumulator i (TMEM columns [64i, +64)) holds hi columns [0, HALF) and lo
-// columns [HALF, 2 HALF).  Gate/up (nm = 2): accumulator 0 = gate, 1 = up,
-// SwiGLU.  Down (nm = 1): the two accumulators are the two K halves of every
-// super-block, added in fixed order.  The accumulators are released
-// (acc_empty) once the last pass has them in registers.
+// Epilogue of one row for the group's tokens.  Accumulator i (TMEM columns
+// [64i, +64)) holds hi columns [0, HALF) and lo columns [HALF, 2 HALF).
+// Gate/up (nm = 2): accumulator 0 = gate, 1 = up, SwiGLU.  Down (nm = 1): the
+// two accumulators are the two K halves of every super-block, added in fixed
+// order.  The tensor core waits for the accumulators to be released
+// (acc_empty) before the next work item, so up to 16 tokens (64 registers)
+// are loaded in one go and released before any arithmetic; wider groups go
+// in passes of 8 tokens (released after the last pass's loads).
 template <int HALF>
 __device__ __forceinline__ void epilogue_item(uint32_t trow, int nm, int ntok, const float* rs, float* o, int stride,
                                               uint64_t* acc_empty, int lane) {
+    constexpr int PASS = (HALF <= 16) ? HALF : 8;
 #pragma unroll
-    for (int p0 = 0; p0 < HALF; p0 += 8) {
-        uint32_t ah[8], al[8], bh[8], bl[8];
-        TC_LD8(trow + (uint32_t)p0, ah);
-        TC_LD8(trow + (uint32_t)(HALF + p0), al);
-        TC_LD8(trow + 64u + (uint32_t)p0, bh);
-        TC_LD8(trow + 64u + (uint32_t)(HALF + p0), bl);
+    for (int p0 = 0; p0 < HALF; p0 += PASS) {
+        uint32_t ah[PASS], al[PASS], bh[PASS], bl[PASS];
+#pragma unroll
+        for (int c = 0; c < PASS; c += 8) {
+            TC_LD8(trow + (uint32_t)(p0 + c), (&ah[c]));
+            TC_LD8(trow + (uint32_t)(HALF + p0 + c), (&al[c]));
+            TC_LD8(trow + 64u + (uint32_t)(p0 + c), (&bh[c]));
+            TC_LD8(trow + 64u + (uint32_t)(HALF + p0 + c), (&bl[c]));
+        }
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if (p0 + 8 >= HALF) {
+        if (p0 + PASS >= HALF) {
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(acc_empty);
         }
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < PASS; ++i) {
             const int n = p0 + i;
             if (n < ntok) {
                 const float sc = __ldg(rs + n);
