@@ -75,6 +75,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     return false;
 }
 
+// Bounded wait for threads that share their SM sub-partition with warps doing
+// the real work: between polls the thread sleeps `ns` nanoseconds instead of
+// spinning, so it does not take issue slots from them.  Same bound and error
+// reporting as mbar_wait.
+__device__ __forceinline__ bool mbar_wait_backoff(uint64_t* bar, uint32_t parity, int* err, int code, unsigned ns) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (true) {
+        __nanosleep(ns);
+        if (mbar_try_wait(bar, parity)) return true;
+        if (global_timer_ns() - t0 > kWaitLimitNs) break;
+    }
+    if (err) atomicExch(err, code);
+    return false;
+}
+
 // 1-D bulk copy global -> shared, completion counted on `bar` in bytes.
 // dst, src 16-byte aligned; bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,

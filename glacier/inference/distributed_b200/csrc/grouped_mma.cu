@@ -50,6 +50,7 @@ namespace glc {
 
 constexpr int kTcThreads = 16 * 32;
 constexpr int kBStages = 2;          // B-tile ring, separate from the raw-weight ring
+constexpr unsigned kPollNs = 64;     // sleep between polls of the roles that wait most (see mbar_wait_backoff)
 constexpr int kAUnits = 3;           // TMEM A ring: 3 x 128 columns after the 128 accumulator columns
 constexpr uint32_t kAccCols = 128;
 constexpr int kRawTile = 128 * 144;          // one super-block x 128 rows
@@ -157,8 +158,11 @@ struct Q4kRowHdr {
     uint32_t dd, ndm, y, z, w;
 };
 
-__device__ __forceinline__ Q4kRowHdr load_hdr(const uint8_t* blk) {
-    const uint4 h = lds128(blk);
+// Plain (schedulable) 16-byte shared-memory load: the compiler may issue a
+// unit's loads back to back, so one queueing delay behind MMAs covers all of them.
+__device__ __forceinline__ uint4 ld_sh128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+
+__device__ __forceinline__ Q4kRowHdr make_hdr(const uint4 h) {
     Q4kRowHdr r;
     r.dd = (h.x & 0xFFFFu) | (h.x << 16);
     const uint32_t nm = (h.x >> 16) ^ 0x8000u;
@@ -177,9 +181,9 @@ __device__ __forceinline__ Q4kRowHdr load_hdr(const uint8_t* blk) {
 // puts a 6-bit scale or min x into the mantissa of 1024 + x and one fp16
 // subtraction leaves x exactly; every later product is exact except dmin*m,
 // rounded once like a float -> half conversion of the exact product.
-__device__ __forceinline__ void dequant_chunk(const Q4kRowHdr& hd, const uint8_t* blk, int c, uint32_t (&r)[32]) {
-    const uint4 q0 = lds128(blk + 16 + 32 * c);
-    const uint4 q1 = lds128(blk + 32 + 32 * c);
+// q0, q1: qs bytes [32c, 32c+16) and [32c+16, 32c+32) of the row.
+__device__ __forceinline__ void dequant_chunk(const Q4kRowHdr& hd, const uint4 q0, const uint4 q1, int c,
+                                              uint32_t (&r)[32]) {
     // 6-bit scale / min of sub-blocks 2c and 2c+1 (get_scale_min_k4): bytes 0 and 1
     const int sh = (c & 1) * 16;
     const uint32_t Y = hd.y >> sh, Z = hd.z >> sh, W = hd.w >> sh;
@@ -336,7 +340,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 for (int s = 0; s < nsb; ++s, ++it) {
                     const int stg = it % S;
                     const uint32_t ph = (uint32_t)(it / S) & 1u;
-                    if (!mbar_wait(&raw_empty[stg], ph ^ 1u, p.err, kDevTimeoutEmpty)) { ok = false; break; }
+                    if (!mbar_wait_backoff(&raw_empty[stg], ph ^ 1u, p.err, kDevTimeoutEmpty, kPollNs)) { ok = false; break; }
                     mbar_arrive_expect_tx(&raw_full[stg], (uint32_t)(nm * kRawTile));
                     uint8_t* rdst = raw + (size_t)stg * nm * kRawTile;
                     tma_load_2d(rdst, &tmA, s * 144, row0, &raw_full[stg]);
@@ -356,7 +360,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 for (int s = 0; s < nsb; ++s, ++it) {
                     const int stg = it % kBStages;
                     const uint32_t ph = (uint32_t)(it / kBStages) & 1u;
-                    if (!mbar_wait(&b_empty[stg], ph ^ 1u, p.err, kDevTimeoutEmpty)) { ok = false; break; }
+                    if (!mbar_wait_backoff(&b_empty[stg], ph ^ 1u, p.err, kDevTimeoutEmpty, kPollNs)) { ok = false; break; }
                     mbar_arrive_expect_tx(&b_full[stg], (uint32_t)(N * 512));
                     bulk_g2s_plain(bst + (size_t)stg * kBStageBytes, bsrc + (size_t)s * N * 512, (uint32_t)(N * 512),
                                    &b_full[stg]);
@@ -386,15 +390,28 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     tc_fence_after();
                     const uint32_t tcol = kAccCols + 128u * (uint32_t)slot;
                     // sub-unit v (64 columns): matrix v of half j (gate/up), or half v of matrix 0 (down)
+                    // all of the unit's shared-memory reads first: 2 row headers + 8 quant words
+                    uint4 hw[2], qw[2][2][2];
 #pragma unroll
                     for (int v = 0; v < 2; ++v) {
                         const int m = (nm == 2) ? v : 0, hh = (nm == 2) ? j : v;
                         const uint8_t* blk = rsrc + (size_t)m * kRawTile;
-                        const Q4kRowHdr hd = load_hdr(blk);  // once per row, matrix and unit
+                        hw[v] = ld_sh128(blk);
+#pragma unroll
+                        for (int cc = 0; cc < 2; ++cc) {
+                            const int c = 2 * hh + cc;
+                            qw[v][cc][0] = ld_sh128(blk + 16 + 32 * c);
+                            qw[v][cc][1] = ld_sh128(blk + 32 + 32 * c);
+                        }
+                    }
+#pragma unroll
+                    for (int v = 0; v < 2; ++v) {
+                        const int hh = (nm == 2) ? j : v;
+                        const Q4kRowHdr hd = make_hdr(hw[v]);
 #pragma unroll
                         for (int cc = 0; cc < 2; ++cc) {
                             uint32_t r[32];
-                            dequant_chunk(hd, blk, 2 * hh + cc, r);
+                            dequant_chunk(hd, qw[v][cc][0], qw[v][cc][1], 2 * hh + cc, r);
                             TC_ST32(trow + tcol + 64u * v + 32u * cc, r);
                         }
                     }
@@ -420,18 +437,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const int N = p.plan.grp_N[g];
                 const uint32_t idesc = idesc_f16(N);
                 const uint32_t cstride = (uint32_t)N * 128u;  // bytes between the 4 K chunks of the B tile
-                if (!mbar_wait(acc_empty, ((uint32_t)icount & 1u) ^ 1u, p.err, kDevTimeoutEmpty)) { ok = false; break; }
+                if (!mbar_wait_backoff(acc_empty, ((uint32_t)icount & 1u) ^ 1u, p.err, kDevTimeoutEmpty, kPollNs)) { ok = false; break; }
                 tc_fence_after();
                 for (int s = 0; s < nsb && ok; ++s, ++it) {
                     const int stg = it % kBStages;
                     const uint32_t ph = (uint32_t)(it / kBStages) & 1u;
-                    if (!mbar_wait(&b_full[stg], ph, p.err, kDevTimeoutFull)) { ok = false; break; }
+                    if (!mbar_wait_backoff(&b_full[stg], ph, p.err, kDevTimeoutFull, kPollNs)) { ok = false; break; }
                     // descriptor of the stage's B tile; K steps add their byte offset >> 4
                     // to the start-address field (addresses stay below 2^18)
                     const uint64_t bbase = sw128_desc(bst + (size_t)stg * kBStageBytes);
                     for (int j = 0; j < upsb; ++j, ++u) {
                         const int slot = u % kAUnits;
-                        if (!mbar_wait(&a_full[slot], (uint32_t)(u / kAUnits) & 1u, p.err, kDevTimeoutFull)) {
+                        if (!mbar_wait_backoff(&a_full[slot], (uint32_t)(u / kAUnits) & 1u, p.err, kDevTimeoutFull, kPollNs)) {
                             ok = false;
                             break;
                         }
@@ -464,7 +481,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const int N = p.plan.grp_N[g];
             const int ntok = p.plan.grp_ntok[g];
             const int pos0 = p.plan.grp_pos0[g];
-            if (!mbar_wait(acc_full, (uint32_t)icount & 1u, p.err, kDevTimeoutFull)) { ok = false; break; }
+            if (!mbar_wait_backoff(acc_full, (uint32_t)icount & 1u, p.err, kDevTimeoutFull, kPollNs)) { ok = false; break; }
             tc_fence_after();
             float* o = p.out + (size_t)pos0 * p.rows_per_e + (size_t)mt * 128 + row;
             const float* rs = p.rscale + pos0;
