@@ -196,6 +196,32 @@ __device__ __forceinline__ float warp_tree(float v) {
     return v;
 }
 
+// Eight per-lane values reduced across the warp with 9 shuffles instead of
+// 8 x 5: at the 16, 8 and 4 levels each lane keeps half of its values and
+// trades the other half with its partner, then the 2 and 1 levels add.  Every
+// value is summed over the same lane pairs at every level as warp_tree, and
+// fp32 addition is commutative, so each sum is bit-identical to warp_tree's.
+// Lane L ends up holding the sum of value (L >> 2) & 7.
+__device__ __forceinline__ float warp_tree8(const float (&v)[8], int lane) {
+    const bool b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1;
+    float a[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float keep = b4 ? v[4 + i] : v[i], send = b4 ? v[i] : v[4 + i];
+        a[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+    float b[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const float keep = b3 ? a[2 + i] : a[i], send = b3 ? a[i] : a[2 + i];
+        b[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+    float c = (b2 ? b[1] : b[0]) + __shfl_xor_sync(0xffffffffu, b2 ? b[0] : b[1], 4);
+    c += __shfl_xor_sync(0xffffffffu, c, 2);
+    c += __shfl_xor_sync(0xffffffffu, c, 1);
+    return c;
+}
+
 __device__ __forceinline__ float tree8(const float* s) {
     return ((s[0] + s[1]) + (s[2] + s[3])) + ((s[4] + s[5]) + (s[6] + s[7]));
 }

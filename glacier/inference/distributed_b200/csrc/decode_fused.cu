@@ -14,8 +14,8 @@
 //   1. stages the router [D][E] and x [T][D] in shared memory with two bulk
 //      copies, and computes RMSNorm + router logits + top-k itself, in the
 //      canonical reduction order of router.cu (8 warps, 256 strided fused
-//      partials, xor butterfly, pairwise tree) -- so no barrier is needed and
-//      every CTA holds the same bit-exact expert ids;
+//      partials, xor butterfly, pairwise tree) -- so no grid-wide exchange
+//      is needed and every CTA holds the same bit-exact expert ids;
 //   2. gate/up GEMV + SwiGLU over its balanced share of the (pair, F) rows,
 //      weights streamed by a producer warp through a ring of shared-memory
 //      stages (cp.async.bulk + mbarriers, L2 evict-first);
@@ -35,7 +35,6 @@
 #ifndef GLC_FUSED_MAX_STAGES
 #define GLC_FUSED_MAX_STAGES 8
 #endif
-
 namespace glc {
 
 namespace {
@@ -51,126 +50,130 @@ __device__ __forceinline__ int xs_index(int d, int U) {
     return (((d & 63) >> 2) * (U + 1) + (d >> 6)) * 4 + (d & 3);
 }
 
-// RMSNorm (optional) + router logits of every token, threads 0..255, from the
-// raw input xr [T][D]; the normalised input goes to xs (xs_index layout).
-__device__ void router_logits(const FusedDecodeParams& p, const float* Wr, const float* xr, float* xs,
-                              float* red, float* logit, float* rms_s, int tid) {
+// RMSNorm scale of every token, threads 0..255, from the raw input xr [T][D]:
+// canonical sum of squares (256 strided fused partials, warp butterfly,
+// pairwise tree over the 8 warp sums), then 1 / sqrt(ss / D + 1e-5).
+__device__ void router_rms(const FusedDecodeParams& p, const float* xr, float* red, float* rms_s, int tid) {
     const int warp = tid >> 5, lane = tid & 31;
-    const int D = p.D, E = p.E, U = D >> 6;
-    for (int t = 0; t < p.T; ++t) {
-        const float* xt = xr + (size_t)t * D;
-        float rms = 1.0f;
-        if (p.rmsnorm) {
-            float a = 0.f;
+    const int D = p.D, T = p.T;
+    float a[kFusedMaxTokens];
+#pragma unroll
+    for (int t = 0; t < kFusedMaxTokens; ++t) a[t] = 0.f;
 #pragma unroll 4
-            for (int d = tid; d < D; d += kRouterWidth) a = fmaf(xt[d], xt[d], a);
-            a = warp_tree(a);
-            if (lane == 0) red[warp] = a;
-            named_bar_sync(2, kRouterWidth);
-            if (tid == 0) {
-                const float ss = tree8(red);
-                rms_s[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), 1e-5f)));
+    for (int d = tid; d < D; d += kRouterWidth) {
+#pragma unroll
+        for (int t = 0; t < kFusedMaxTokens; ++t)
+            if (t < T) {
+                const float v = xr[(size_t)t * D + d];
+                a[t] = fmaf(v, v, a[t]);
             }
-            named_bar_sync(2, kRouterWidth);
-            rms = rms_s[t];
+    }
+#pragma unroll
+    for (int t = 0; t < kFusedMaxTokens; ++t)
+        if (t < T) {
+            const float v = warp_tree(a[t]);
+            if (lane == 0) red[t * 8 + warp] = v;
         }
+    named_bar_sync(2, kRouterWidth);
+    if (tid < T) rms_s[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tree8(red + tid * 8), (float)D), 1e-5f)));
+    named_bar_sync(2, kRouterWidth);
+}
+
+// Router logits of every token, threads 0..255, in the canonical order of
+// router.cu (256 strided fused partials over the normalised input, warp
+// butterfly, pairwise tree over the 8 warp sums), eight experts per pass; the
+// first pass also writes the normalised input to xs (xs_index layout).
+__device__ void router_logits(const FusedDecodeParams& p, const float* Wr, const float* xr, float* xs,
+                              float* red, float* logit, const float* rms_s, int tid) {
+    const int warp = tid >> 5, lane = tid & 31;
+    const int D = p.D, E = p.E, T = p.T, U = D >> 6;
+    // At E = 8 rows are 32 B apart across lanes; lanes 4..7 of each 8 read
+    // their second half first so one 16-byte read covers all banks.
+    const int h = (E == 8) ? ((lane >> 2) & 1) : 0;
+    for (int t = 0; t < T; ++t) {
+        const float* xt = xr + (size_t)t * D;
+        float* xo = xs + (size_t)t * (D + 64);
+        const float rms = p.rmsnorm ? rms_s[t] : 1.0f;
         for (int e0 = 0; e0 < E; e0 += 8) {
             float acc[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) acc[e] = 0.f;
             if ((E & 3) == 0 && e0 + 8 <= E) {
-                // Two 16-byte reads of the 32 bytes e0..e0+7 of the router row.
-                // At E = 8 rows are 32 B apart across lanes; lanes 4..7 of each
-                // 8 read their second half first so one read covers all banks.
-                const int h = (E == 8) ? ((lane >> 2) & 1) : 0;
 #pragma unroll 4
                 for (int d = tid; d < D; d += kRouterWidth) {
                     const float raw = xt[d];
                     const float xv = p.rmsnorm ? __fmul_rn(raw, rms) : raw;
+                    if (e0 == 0) xo[xs_index(d, U)] = xv;
                     const float4* wr = reinterpret_cast<const float4*>(Wr + (size_t)d * E + e0);
                     const float4 f = wr[h], g = wr[h ^ 1];
-                    const float4 a = h ? g : f, b = h ? f : g;
-                    acc[0] = fmaf(xv, a.x, acc[0]); acc[1] = fmaf(xv, a.y, acc[1]);
-                    acc[2] = fmaf(xv, a.z, acc[2]); acc[3] = fmaf(xv, a.w, acc[3]);
-                    acc[4] = fmaf(xv, b.x, acc[4]); acc[5] = fmaf(xv, b.y, acc[5]);
-                    acc[6] = fmaf(xv, b.z, acc[6]); acc[7] = fmaf(xv, b.w, acc[7]);
+                    const float4 lo = h ? g : f, hi = h ? f : g;
+                    acc[0] = fmaf(xv, lo.x, acc[0]); acc[1] = fmaf(xv, lo.y, acc[1]);
+                    acc[2] = fmaf(xv, lo.z, acc[2]); acc[3] = fmaf(xv, lo.w, acc[3]);
+                    acc[4] = fmaf(xv, hi.x, acc[4]); acc[5] = fmaf(xv, hi.y, acc[5]);
+                    acc[6] = fmaf(xv, hi.z, acc[6]); acc[7] = fmaf(xv, hi.w, acc[7]);
                 }
             } else {
                 for (int d = tid; d < D; d += kRouterWidth) {
                     const float raw = xt[d];
                     const float xv = p.rmsnorm ? __fmul_rn(raw, rms) : raw;
+                    if (e0 == 0) xo[xs_index(d, U)] = xv;
                     const float* wr = Wr + (size_t)d * E + e0;
 #pragma unroll
                     for (int e = 0; e < 8; ++e)
                         if (e0 + e < E) acc[e] = fmaf(xv, wr[e], acc[e]);
                 }
             }
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const float v = warp_tree(acc[e]);
-                if (lane == 0) red[warp * 8 + e] = v;
-            }
+            const float v = warp_tree8(acc, lane);
+            if ((lane & 3) == 0) red[((lane >> 2) & 7) * 8 + warp] = v;
             named_bar_sync(2, kRouterWidth);
-            if (tid < 8 && e0 + tid < E) {
-                float s[8];
-#pragma unroll
-                for (int w = 0; w < 8; ++w) s[w] = red[w * 8 + tid];
-                logit[t * E + e0 + tid] = tree8(s);
-            }
+            if (tid < 8 && e0 + tid < E) logit[t * E + e0 + tid] = tree8(red + tid * 8);
             named_bar_sync(2, kRouterWidth);
         }
-        float* xo = xs + (size_t)t * (D + 64);
-        for (int d = tid; d < D; d += kRouterWidth) xo[xs_index(d, U)] = p.rmsnorm ? __fmul_rn(xt[d], rms) : xt[d];
     }
 }
 
-// Top-k of one token by one warp (E <= 64: lane l holds experts l and l+32),
-// then softmax weights: the selection order, tie rule (lower index wins; NaN
-// logits count as -inf) and the sequential fp32 sums are those of the router
-// kernel in router.cu, so ids and weights are bit-identical to it.
+// Top-k of token t by one warp (E <= 64: lane l ranks experts l and l+32),
+// then the softmax weights.  An expert's rank is the number of experts ahead
+// of it in the order (logit descending, lower index first on ties, NaN as
+// -inf), so the experts of rank < k come out in the order of the router
+// kernel's repeated arg-max in router.cu; the weights use the same expf
+// arguments and the same sequential fp32 sums, so ids and weights are
+// bit-identical to it.  ex holds E floats of scratch.
 __device__ void topk_token_warp(const FusedDecodeParams& p, const float* l, int t, int* s_ids, float* s_w,
-                                int lane) {
+                                float* ex, int lane) {
     const int E = p.E, k = p.k;
     const int e0 = lane, e1 = lane + 32;
-    float v0 = -INFINITY, v1 = -INFINITY;
-    bool a0 = e0 < E, a1 = e1 < E;  // still selectable
-    if (a0) v0 = isnan(l[e0]) ? -INFINITY : l[e0];
-    if (a1) v1 = isnan(l[e1]) ? -INFINITY : l[e1];
-    int first = -1;
-    for (int j = 0; j < k; ++j) {
-        // lane candidate: its better selectable entry (lower index on ties)
-        int bi = a0 ? e0 : (a1 ? e1 : 1 << 30);
-        float bv = a0 ? v0 : (a1 ? v1 : -INFINITY);
-        if (a0 && a1 && v1 > v0) { bi = e1; bv = v1; }
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-            // an index of 1<<30 marks "nothing selectable"; it never beats a real entry
-            const bool take = (oi < (1 << 30)) && (bi == (1 << 30) || ov > bv || (ov == bv && oi < bi));
-            if (take) { bv = ov; bi = oi; }
-        }
-        if (bi == e0) a0 = false;
-        if (bi == e1) a1 = false;
-        if (lane == 0) s_ids[t * k + j] = bi;
-        if (j == 0) first = bi;
+    const float v0 = (e0 < E && !isnan(l[e0])) ? l[e0] : -INFINITY;
+    const float v1 = (e1 < E && !isnan(l[e1])) ? l[e1] : -INFINITY;
+    int r0 = 0, r1 = 0;
+    for (int e = 0; e < E; ++e) {
+        const float v = isnan(l[e]) ? -INFINITY : l[e];
+        r0 += (v > v0 || (v == v0 && e < e0)) ? 1 : 0;
+        r1 += (v > v1 || (v == v1 && e < e1)) ? 1 : 0;
     }
+    if (e0 < E && r0 < k) s_ids[t * k + r0] = e0;
+    if (e1 < E && r1 < k) s_ids[t * k + r1] = e1;
     __syncwarp();
+    const int first = s_ids[t * k];
+    const float mx = isnan(l[first]) ? -INFINITY : l[first];
+    if (e0 < E) ex[e0] = expf(l[e0] - mx);
+    if (e1 < E) ex[e1] = expf(l[e1] - mx);
+    __syncwarp();
+    float den = 0.f;
     if (lane == 0) {
-        const float mx = isnan(l[first]) ? -INFINITY : l[first];
-        float den = 0.f;
         if (p.renorm) {
-            for (int j = 0; j < k; ++j) den += expf(l[s_ids[t * k + j]] - mx);
+            for (int j = 0; j < k; ++j) den += ex[s_ids[t * k + j]];
         } else {
-            for (int e = 0; e < E; ++e) den += expf(l[e] - mx);
+            for (int e = 0; e < E; ++e) den += ex[e];
         }
-        for (int j = 0; j < k; ++j) s_w[t * k + j] = expf(l[s_ids[t * k + j]] - mx) / den;
     }
+    den = __shfl_sync(0xffffffffu, den, 0);
+    if (lane < k) s_w[t * k + lane] = ex[s_ids[t * k + lane]] / den;
 }
 
 __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(const __grid_constant__ FusedDecodeParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ int s_ok;
+    __shared__ int s_ok, s_okx, s_okw;
     float* xs = reinterpret_cast<float*>(smem + p.off_xs);
     float* pgu = reinterpret_cast<float*>(smem + p.off_pgu);
     float* pdn = reinterpret_cast<float*>(smem + p.off_pdn);
@@ -183,6 +186,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
     const int S = p.stages;
     uint64_t* empty = full + S;
     uint64_t* xbar = empty + S;
+    uint64_t* wbar = xbar + 1;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int T = p.T, D = p.D, F = p.F, k = p.k, P = T * k;
@@ -194,28 +198,48 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
             mbar_init(&empty[s], kFusedConsumerWarps);
         }
         mbar_init(xbar, 1);
+        mbar_init(wbar, 1);
         fence_mbar_init();
-        s_ok = 1;
+        s_ok = s_okx = s_okw = 1;
     }
     __syncthreads();
 
-    // ---- 1. stage the router and x in the (still idle) stage ring; RMSNorm,
-    // logits, top-k (every CTA)
+    // ---- 1. stage x and the router in the (still idle) stage ring, each with
+    // its own barrier so the sum of squares runs while the router lands; then
+    // RMSNorm, logits and top-k (every CTA)
     const uint32_t wb = (uint32_t)D * p.E * 4u;  // a multiple of 1024
     const float* xraw = reinterpret_cast<const float*>(smem + wb);
     if (tid == 0) {
         const uint32_t xb = (uint32_t)T * D * 4u;
-        mbar_arrive_expect_tx(xbar, xb + wb);
-        bulk_g2s_nohint(smem, p.Wr, wb, xbar);
+        mbar_arrive_expect_tx(xbar, xb);
         bulk_g2s_nohint(smem + wb, p.x, xb, xbar);
+        mbar_arrive_expect_tx(wbar, wb);
+        bulk_g2s_nohint(smem, p.Wr, wb, wbar);
     }
-    if (!mbar_wait(xbar, 0, p.err, kDevTimeoutFull)) s_ok = 0;
+    // this CTA's rows, independent of the routing: computed while the copies fly
+    const long long gu_total = (long long)P * F, dn_total = (long long)T * D;
+    const int g0 = (int)(gu_total * blockIdx.x / gridDim.x);
+    const int g1 = (int)(gu_total * (blockIdx.x + 1) / gridDim.x);
+    const int q0 = (int)(dn_total * blockIdx.x / gridDim.x);
+    const int q1 = (int)(dn_total * (blockIdx.x + 1) / gridDim.x);
+    const int rbG = (D >> 8) * 144, rbD = (F >> 8) * 144;
+    if (tid < kRouterWidth) {
+        // Each wait's outcome goes through its own flag and a barrier of the
+        // 256 router threads, so all of them take the same branch.
+        if (!mbar_wait(xbar, 0, p.err, kDevTimeoutFull)) s_okx = 0;
+        named_bar_sync(2, kRouterWidth);
+        const bool okx = s_okx != 0;
+        if (okx && p.rmsnorm) router_rms(p, xraw, red, rms_s, tid);
+        if (okx && !mbar_wait(wbar, 0, p.err, kDevTimeoutFull)) s_okw = 0;
+        named_bar_sync(2, kRouterWidth);
+        if (okx && s_okw != 0)
+            router_logits(p, reinterpret_cast<const float*>(smem), xraw, xs, red, logit, rms_s, tid);
+        else if (tid == 0)
+            s_ok = 0;
+    }
     __syncthreads();
     const bool staged = s_ok != 0;
-    if (staged && tid < kRouterWidth)
-        router_logits(p, reinterpret_cast<const float*>(smem), xraw, xs, red, logit, rms_s, tid);
-    __syncthreads();
-    if (staged && warp < T) topk_token_warp(p, logit + warp * p.E, warp, s_ids, s_w, lane);
+    if (staged && warp < T) topk_token_warp(p, logit + warp * p.E, warp, s_ids, s_w, red + warp * 64, lane);
     __syncthreads();
     if (!staged) return;  // uniform: every thread read the same s_ok
     if (blockIdx.x == 0) {
@@ -229,13 +253,6 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
                 p.xin[i] = xs[(size_t)t * (D + 64) + xs_index(d, D >> 6)];
             }
     }
-
-    const long long gu_total = (long long)P * F, dn_total = (long long)T * D;
-    const int g0 = (int)(gu_total * blockIdx.x / gridDim.x);
-    const int g1 = (int)(gu_total * (blockIdx.x + 1) / gridDim.x);
-    const int q0 = (int)(dn_total * blockIdx.x / gridDim.x);
-    const int q1 = (int)(dn_total * (blockIdx.x + 1) / gridDim.x);
-    const int rbG = (D >> 8) * 144, rbD = (F >> 8) * 144;
 
     if (warp == kFusedConsumerWarps) {
         // ------------------------------------------------------ producer warp
@@ -411,13 +428,13 @@ int fused_decode_configure(FusedDecodeParams& p, int num_sms, size_t smem_limit,
     const size_t o_xs = o;    o = align16(o + (size_t)T * (D + 64) * 4);
     const size_t o_pgu = o;   o = align16(o + (size_t)gu_rows * 2 * gu_nsegw * 4);
     const size_t o_pdn = o;   o = align16(o + (size_t)dn_rows * k * dn_nsegw * 4);
-    const size_t o_red = o;   o = align16(o + 64 * 4);
+    const size_t o_red = o;   o = align16(o + (size_t)kFusedMaxTokens * 64 * 4);
     const size_t o_logit = o; o = align16(o + (size_t)T * E * 4);
     const size_t o_rms = o;   o = align16(o + (size_t)T * 4);
     const size_t o_ids = o;   o = align16(o + (size_t)P * 4);
     const size_t o_w = o;     o = align16(o + (size_t)P * 4);
     const size_t o_bars = o;
-    const size_t fixed = o + (2 * GLC_FUSED_MAX_STAGES + 1) * 8;
+    const size_t fixed = o + (2 * GLC_FUSED_MAX_STAGES + 2) * 8;
     if (fixed >= smem_limit) return -1;
     int S = (int)((smem_limit - fixed) / slot);
     if (S > GLC_FUSED_MAX_STAGES) S = GLC_FUSED_MAX_STAGES;
@@ -438,7 +455,7 @@ int fused_decode_configure(FusedDecodeParams& p, int num_sms, size_t smem_limit,
     p.off_ids = (int)(ring + o_ids);
     p.off_w = (int)(ring + o_w);
     p.off_bars = (int)(ring + o_bars);
-    *smem_bytes = ring + o_bars + (2 * (size_t)S + 1) * 8;
+    *smem_bytes = ring + o_bars + (2 * (size_t)S + 2) * 8;
     *grid = g;
     return 0;
 }
