@@ -99,6 +99,10 @@ struct glc_moe {
     float* ones = nullptr;     // [T*k] unit combine weights (per-row expert outputs)
     int* ep_keys = nullptr;    // [T*k] destination-rank keys of the expert-parallel dispatch
     int* err = nullptr;        // [0] device error word; [2..3] grid-barrier counter (u64) of the fused decode kernel
+    // err, ids, wts and out are carved from one result block, in that order,
+    // so the host-buffer forward returns all of them with one copy
+    uint8_t* res = nullptr;
+    size_t res_off_ids = 0, res_off_w = 0, res_off_out = 0, res_bytes = 0;
     // batched (T > 1) path
     glc::DispatchPlan plan{};
     int plan_gmax = 0;
@@ -108,7 +112,7 @@ struct glc_moe {
     float* ysort = nullptr;     // [T*k][D]
     // pinned host staging
     float* h_x = nullptr;
-    float* h_out = nullptr;
+    uint8_t* h_res = nullptr;  // pinned copy of the result block
     int* h_ids = nullptr;
     float* h_w = nullptr;
     // optional per-kernel CUDA-event timing of the last forward (launch order)
@@ -373,16 +377,24 @@ int glc_moe_create(const glc_moe_desc* desc, glc_moe** out) {
         return cleanup(fail(GLC_ERR_CUDA, "cudaStreamCreate failed"));
     ALLOC(h->x, sizeof(float) * T * D);
     ALLOC(h->xin, sizeof(float) * T * D);
-    ALLOC(h->out, sizeof(float) * T * D);
     ALLOC(h->act, sizeof(float) * T * k * F);
     if (Fs) ALLOC(h->act_sh, sizeof(float) * T * Fs);
-    ALLOC(h->wts, sizeof(float) * T * k);
     ALLOC(h->gate_out, sizeof(float) * T);
-    ALLOC(h->ids, sizeof(int) * T * k);
     ALLOC(h->zeros_i, sizeof(int) * T);
     ALLOC(h->ones, sizeof(float) * T * k);
     ALLOC(h->ep_keys, sizeof(int) * T * k);
-    ALLOC(h->err, 4 * sizeof(int));
+    {
+        auto a16 = [](size_t v) { return (v + 15) & ~size_t(15); };
+        h->res_off_ids = a16(4 * sizeof(int));
+        h->res_off_w = a16(h->res_off_ids + sizeof(int) * T * k);
+        h->res_off_out = a16(h->res_off_w + sizeof(float) * T * k);
+        h->res_bytes = h->res_off_out + sizeof(float) * T * D;
+        ALLOC(h->res, h->res_bytes);
+        h->err = reinterpret_cast<int*>(h->res);
+        h->ids = reinterpret_cast<int*>(h->res + h->res_off_ids);
+        h->wts = reinterpret_cast<float*>(h->res + h->res_off_w);
+        h->out = reinterpret_cast<float*>(h->res + h->res_off_out);
+    }
     {
         const size_t P = T * k;
         const int E = d.num_experts;
@@ -412,7 +424,7 @@ int glc_moe_create(const glc_moe_desc* desc, glc_moe** out) {
         return cleanup(fail(GLC_ERR_CUDA, "initialising the unit weights failed"));
     cudaMemset(h->err, 0, 4 * sizeof(int));
     if (cudaMallocHost(&h->h_x, sizeof(float) * T * D) != cudaSuccess ||
-        cudaMallocHost(&h->h_out, sizeof(float) * T * D) != cudaSuccess ||
+        cudaMallocHost(&h->h_res, h->res_bytes) != cudaSuccess ||
         cudaMallocHost(&h->h_ids, sizeof(int) * T * k) != cudaSuccess ||
         cudaMallocHost(&h->h_w, sizeof(float) * T * k) != cudaSuccess)
         return cleanup(fail(GLC_ERR_OOM, "cudaMallocHost failed"));
@@ -430,14 +442,14 @@ int glc_moe_destroy(glc_moe* h) {
         if (e) cudaEventDestroy(e);
     if (h->graph_exec) cudaGraphExecDestroy(h->graph_exec);
     if (h->graph) cudaGraphDestroy(h->graph);
-    cudaFree(h->x); cudaFree(h->xin); cudaFree(h->out); cudaFree(h->act); cudaFree(h->act_sh);
-    cudaFree(h->wts); cudaFree(h->gate_out); cudaFree(h->ids); cudaFree(h->zeros_i); cudaFree(h->err);
+    cudaFree(h->x); cudaFree(h->xin); cudaFree(h->act); cudaFree(h->act_sh);
+    cudaFree(h->gate_out); cudaFree(h->zeros_i); cudaFree(h->res);
     cudaFree(h->ones); cudaFree(h->ep_keys);
     cudaFree(h->plan.counts); cudaFree(h->plan.offsets); cudaFree(h->plan.perm); cudaFree(h->plan.inv);
     cudaFree(h->plan.grp_first); cudaFree(h->plan.grp_e); cudaFree(h->plan.grp_ntok); cudaFree(h->plan.grp_N);
     cudaFree(h->plan.grp_pos0); cudaFree(h->plan.grp_units); cudaFree(h->plan.meta);
     cudaFree(h->btiles); cudaFree(h->rscale); cudaFree(h->ysort);
-    cudaFreeHost(h->h_x); cudaFreeHost(h->h_out); cudaFreeHost(h->h_ids); cudaFreeHost(h->h_w);
+    cudaFreeHost(h->h_x); cudaFreeHost(h->h_res); cudaFreeHost(h->h_ids); cudaFreeHost(h->h_w);
     if (h->stream) cudaStreamDestroy(h->stream);
     h->disposed = 1;
     delete h;
@@ -803,11 +815,16 @@ int glc_moe_forward(glc_moe* h, int32_t layer, const float* x, int32_t T, uint32
     CUDA_TRY(cudaMemcpyAsync(h->x, x, sizeof(float) * (size_t)T * D, cudaMemcpyHostToDevice, st));
     rc = glc_moe_forward_dev(h, layer, h->x, T, flags, h->out, nullptr, nullptr, st);
     if (rc) return rc;
-    CUDA_TRY(cudaMemcpyAsync(out, h->out, sizeof(float) * (size_t)T * D, cudaMemcpyDeviceToHost, st));
-    if (ids_out) CUDA_TRY(cudaMemcpyAsync(ids_out, h->ids, sizeof(int) * (size_t)T * k, cudaMemcpyDeviceToHost, st));
-    if (w_out) CUDA_TRY(cudaMemcpyAsync(w_out, h->wts, sizeof(float) * (size_t)T * k, cudaMemcpyDeviceToHost, st));
+    // One copy back: the error word, expert ids, combine weights and output
+    // are adjacent in the result block (no separate round trip for the error).
+    CUDA_TRY(cudaMemcpyAsync(h->h_res, h->res, h->res_off_out + sizeof(float) * (size_t)T * D,
+                             cudaMemcpyDeviceToHost, st));
     CUDA_TRY(cudaStreamSynchronize(st));
-    return check_device_error(h);
+    if (reinterpret_cast<const int*>(h->h_res)[0] != 0) return check_device_error(h);
+    std::memcpy(out, h->h_res + h->res_off_out, sizeof(float) * (size_t)T * D);
+    if (ids_out) std::memcpy(ids_out, h->h_res + h->res_off_ids, sizeof(int) * (size_t)T * k);
+    if (w_out) std::memcpy(w_out, h->h_res + h->res_off_w, sizeof(float) * (size_t)T * k);
+    return GLC_OK;
 }
 
 int glc_moe_graph_build(glc_moe* h, int32_t layer, const float* x, int32_t T, uint32_t flags, float* out) {
