@@ -133,14 +133,12 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(self.samples)}
 
 
-def result_block_bytes(T, D, k, max_tokens):
-    """Bytes the host-buffer forward copies back per call: one copy of the
-    handle's result block (error words, expert ids and combine weights sized
-    for max_tokens, each 16-byte aligned, then the T x D output)."""
-    a16 = lambda v: (v + 15) // 16 * 16
-    off_w = a16(16 + 4 * max_tokens * k)
-    off_out = a16(off_w + 4 * max_tokens * k)
-    return off_out + 4 * T * D
+def host_result_bytes(T, D, k):
+    """Bytes that cross from the device to the host per decode call of the
+    host-buffer forward: the kernel writes the T x D output, the expert ids and
+    the combine weights into mapped host memory, plus the 16-byte completion
+    and error words."""
+    return 4 * T * D + 8 * T * k + 16
 
 
 def make_tokens(w, n):
@@ -371,7 +369,7 @@ def run_ours(args, w):
                                     "note": "same step as three launches (q4k_gemv_kernel x2 + router), "
                                             "event marks between launches"}},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": T * D * 4,
-                    "d2h_bytes_per_step": result_block_bytes(T, D, w["k"], max(T, BATCH_TOKENS)), "steps": e2e_steps,
+                    "d2h_bytes_per_step": host_result_bytes(T, D, w["k"]), "steps": e2e_steps,
                     "api": "glc_moe_forward (host buffers, synchronous)"},
             "gpu_launches": args.steps,
             "clocks": clocks,

@@ -10,6 +10,8 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
+#include <chrono>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -80,6 +82,10 @@ int set_last_error(int code, const char* msg) {
 }
 }  // namespace glc
 
+// Device words at the head of a handle's result block: error word, grid-barrier
+// counter and completion counter of the fused decode kernel.
+constexpr int kErrWords = 8;
+
 struct glc_moe {
     glc_moe_desc d{};
     int num_sms = 0;
@@ -98,7 +104,7 @@ struct glc_moe {
     int* zeros_i = nullptr;    // [T] expert id 0 for the shared expert
     float* ones = nullptr;     // [T*k] unit combine weights (per-row expert outputs)
     int* ep_keys = nullptr;    // [T*k] destination-rank keys of the expert-parallel dispatch
-    int* err = nullptr;        // [0] device error word; [2..3] grid-barrier counter (u64) of the fused decode kernel
+    int* err = nullptr;        // [0] device error word; [2..3] grid-barrier counter (u64), [4..5] completion counter (u64) of the fused decode kernel
     // err, ids, wts and out are carved from one result block, in that order,
     // so the host-buffer forward returns all of them with one copy
     uint8_t* res = nullptr;
@@ -112,7 +118,13 @@ struct glc_moe {
     float* ysort = nullptr;     // [T*k][D]
     // pinned host staging
     float* h_x = nullptr;
-    uint8_t* h_res = nullptr;  // pinned copy of the result block
+    uint8_t* h_res = nullptr;  // pinned (and mapped) copy of the result block
+    uint8_t* d_res_map = nullptr;  // device address of h_res
+    // mapped completion words of the fused decode launch the host-buffer
+    // forward waits on: [0] epoch of the last finished launch, [1] its error word
+    unsigned long long* h_sig = nullptr;
+    unsigned long long* d_sig_map = nullptr;
+    unsigned long long host_epoch = 0;
     int* h_ids = nullptr;
     float* h_w = nullptr;
     // optional per-kernel CUDA-event timing of the last forward (launch order)
@@ -154,8 +166,11 @@ int check_device_error(glc_moe* h) {
     int code = 0;
     CUDA_TRY(cudaMemcpy(&code, h->err, sizeof(int), cudaMemcpyDeviceToHost));
     if (code != 0) {
-        // also clears the grid-barrier counter, which a launch that gave up may leave mid-count
-        cudaMemset(h->err, 0, 4 * sizeof(int));
+        // also clears the fused kernel's barrier and completion counters, which a
+        // launch that gave up may leave mid-count, and the host's matching epoch
+        cudaMemset(h->err, 0, kErrWords * sizeof(int));
+        h->host_epoch = 0;
+        if (h->h_sig) h->h_sig[0] = h->h_sig[1] = 0;
         return fail(GLC_ERR_TIMEOUT, "device-side wait gave up (code %d)", code);
     }
     return GLC_OK;
@@ -385,7 +400,7 @@ int glc_moe_create(const glc_moe_desc* desc, glc_moe** out) {
     ALLOC(h->ep_keys, sizeof(int) * T * k);
     {
         auto a16 = [](size_t v) { return (v + 15) & ~size_t(15); };
-        h->res_off_ids = a16(4 * sizeof(int));
+        h->res_off_ids = a16(kErrWords * sizeof(int));
         h->res_off_w = a16(h->res_off_ids + sizeof(int) * T * k);
         h->res_off_out = a16(h->res_off_w + sizeof(float) * T * k);
         h->res_bytes = h->res_off_out + sizeof(float) * T * D;
@@ -422,12 +437,20 @@ int glc_moe_create(const glc_moe_desc* desc, glc_moe** out) {
     cudaMemset(h->zeros_i, 0, sizeof(int) * T);
     if (glc::fill_launch(h->ones, T * k, 1.0f, h->stream) != cudaSuccess)
         return cleanup(fail(GLC_ERR_CUDA, "initialising the unit weights failed"));
-    cudaMemset(h->err, 0, 4 * sizeof(int));
+    cudaMemset(h->err, 0, kErrWords * sizeof(int));
     if (cudaMallocHost(&h->h_x, sizeof(float) * T * D) != cudaSuccess ||
-        cudaMallocHost(&h->h_res, h->res_bytes) != cudaSuccess ||
+        cudaHostAlloc(&h->h_res, h->res_bytes, cudaHostAllocMapped) != cudaSuccess ||
+        cudaHostAlloc(&h->h_sig, 64, cudaHostAllocMapped) != cudaSuccess ||
         cudaMallocHost(&h->h_ids, sizeof(int) * T * k) != cudaSuccess ||
         cudaMallocHost(&h->h_w, sizeof(float) * T * k) != cudaSuccess)
         return cleanup(fail(GLC_ERR_OOM, "cudaMallocHost failed"));
+    h->h_sig[0] = h->h_sig[1] = 0;
+    if (cudaHostGetDevicePointer(reinterpret_cast<void**>(&h->d_res_map), h->h_res, 0) != cudaSuccess ||
+        cudaHostGetDevicePointer(reinterpret_cast<void**>(&h->d_sig_map), h->h_sig, 0) != cudaSuccess) {
+        h->d_res_map = nullptr;  // no mapped host memory: the host-buffer forward copies instead
+        h->d_sig_map = nullptr;
+        cudaGetLastError();
+    }
     if (cudaDeviceSynchronize() != cudaSuccess) return cleanup(fail(GLC_ERR_CUDA, "device sync failed"));
     *out = h;
     return GLC_OK;
@@ -449,7 +472,7 @@ int glc_moe_destroy(glc_moe* h) {
     cudaFree(h->plan.grp_first); cudaFree(h->plan.grp_e); cudaFree(h->plan.grp_ntok); cudaFree(h->plan.grp_N);
     cudaFree(h->plan.grp_pos0); cudaFree(h->plan.grp_units); cudaFree(h->plan.meta);
     cudaFree(h->btiles); cudaFree(h->rscale); cudaFree(h->ysort);
-    cudaFreeHost(h->h_x); cudaFreeHost(h->h_res); cudaFreeHost(h->h_ids); cudaFreeHost(h->h_w);
+    cudaFreeHost(h->h_x); cudaFreeHost(h->h_res); cudaFreeHost(h->h_sig); cudaFreeHost(h->h_ids); cudaFreeHost(h->h_w);
     if (h->stream) cudaStreamDestroy(h->stream);
     h->disposed = 1;
     delete h;
@@ -632,6 +655,42 @@ int glc_routed_topk(glc_moe* h, int32_t layer, const float* x, const int32_t* id
     return check_device_error(h);
 }
 
+namespace {
+
+// The whole-layer fused decode launch serves this call (T tokens, flags).
+bool fused_applies(const glc_moe* h, int T, uint32_t flags) {
+    const bool grouped = (flags & GLC_FWD_BATCHED) ? true : (flags & GLC_FWD_DECODE) ? false : (T > 1);
+    return !grouped && !(flags & GLC_FWD_UNFUSED) && h->d.shared_ffn_dim == 0;
+}
+
+// Fused-kernel parameters of a layer; the caller sets x, resid and out.
+glc::FusedDecodeParams fused_params(glc_moe* h, const LayerDev* L, int T, uint32_t flags) {
+    const int D = h->d.hidden_dim, F = h->d.expert_ffn_dim;
+    glc::FusedDecodeParams fp{};
+    fp.Wr = L->router;
+    fp.gate = L->gate;
+    fp.up = L->up;
+    fp.down = L->down;
+    fp.gu_expert_bytes = (long long)F * rowbytes(D);
+    fp.dn_expert_bytes = (long long)D * rowbytes(F);
+    fp.act = h->act;
+    fp.xin = nullptr;
+    fp.ids = h->ids;
+    fp.w = h->wts;
+    fp.bar = reinterpret_cast<unsigned long long*>(h->err + 2);
+    fp.err = h->err;
+    fp.T = T;
+    fp.D = D;
+    fp.F = F;
+    fp.E = h->d.num_experts;
+    fp.k = h->d.top_k;
+    fp.renorm = h->d.renormalize;
+    fp.rmsnorm = (flags & GLC_FWD_RMSNORM) ? 1 : 0;
+    return fp;
+}
+
+}  // namespace
+
 int glc_moe_forward_dev(glc_moe* h, int32_t layer, const float* x, int32_t T, uint32_t flags, float* out,
                         int32_t* ids_out, float* w_out, void* stream) {
     int rc = check_handle(h);
@@ -648,33 +707,13 @@ int glc_moe_forward_dev(glc_moe* h, int32_t layer, const float* x, int32_t T, ui
     // T == 1 (decode): dequant-fused GEMVs; T > 1: grouped tensor-core GEMMs.
     const bool grouped = (flags & GLC_FWD_BATCHED) ? true : (flags & GLC_FWD_DECODE) ? false : (T > 1);
     const float* resid = (flags & GLC_FWD_RESIDUAL) ? x : nullptr;
-    if (!grouped && !(flags & GLC_FWD_UNFUSED) && h->d.shared_ffn_dim == 0) {
+    if (fused_applies(h, T, flags)) {
         // Whole layer in one persistent launch when it fits (few tokens, router
         // and input small enough to stage in shared memory).
-        const int F = h->d.expert_ffn_dim;
-        glc::FusedDecodeParams fp{};
+        glc::FusedDecodeParams fp = fused_params(h, L, T, flags);
         fp.x = x;
-        fp.Wr = L->router;
         fp.resid = resid;
-        fp.gate = L->gate;
-        fp.up = L->up;
-        fp.down = L->down;
-        fp.gu_expert_bytes = (long long)F * rowbytes(D);
-        fp.dn_expert_bytes = (long long)D * rowbytes(F);
-        fp.act = h->act;
         fp.out = out;
-        fp.xin = nullptr;
-        fp.ids = h->ids;
-        fp.w = h->wts;
-        fp.bar = reinterpret_cast<unsigned long long*>(h->err + 2);
-        fp.err = h->err;
-        fp.T = T;
-        fp.D = D;
-        fp.F = F;
-        fp.E = E;
-        fp.k = k;
-        fp.renorm = h->d.renormalize;
-        fp.rmsnorm = (flags & GLC_FWD_RMSNORM) ? 1 : 0;
         h->n_marks = 0;
         mark(h, st);
         const cudaError_t e = glc::fused_decode_launch(fp, h->num_sms, st);
@@ -812,6 +851,47 @@ int glc_moe_forward(glc_moe* h, int32_t layer, const float* x, int32_t T, uint32
     if (T > h->d.max_tokens) return fail(GLC_ERR_INVALID_ARG, "T=%d exceeds max_tokens=%d", T, h->d.max_tokens);
     const int D = h->d.hidden_dim, k = h->d.top_k;
     cudaStream_t st = h->stream;
+    if (h->d_res_map && !h->profiling && fused_applies(h, T, flags)) {
+        LayerDev* L = layer_of(h, layer);
+        if (!L->loaded) return fail(GLC_ERR_STATE, "layer %d has no weights", layer);
+        // The kernel writes its outputs into mapped host memory and its last
+        // CTA writes the launch's epoch to a mapped word: no copy back and no
+        // stream synchronisation.
+        CUDA_TRY(cudaMemcpyAsync(h->x, x, sizeof(float) * (size_t)T * D, cudaMemcpyHostToDevice, st));
+        glc::FusedDecodeParams fp = fused_params(h, L, T, flags);
+        fp.x = h->x;
+        fp.resid = (flags & GLC_FWD_RESIDUAL) ? h->x : nullptr;
+        fp.out = reinterpret_cast<float*>(h->d_res_map + h->res_off_out);
+        fp.ids = reinterpret_cast<int*>(h->d_res_map + h->res_off_ids);
+        fp.w = reinterpret_cast<float*>(h->d_res_map + h->res_off_w);
+        fp.done_ctr = reinterpret_cast<unsigned long long*>(h->err + 4);
+        fp.host_done = h->d_sig_map;
+        fp.host_err = reinterpret_cast<int*>(h->d_sig_map + 1);
+        fp.epoch = h->host_epoch + 1;
+        const cudaError_t e = glc::fused_decode_launch(fp, h->num_sms, st);
+        if (e == cudaSuccess) {
+            h->host_epoch = fp.epoch;
+            const volatile unsigned long long* done = h->h_sig;
+            const auto t0 = std::chrono::steady_clock::now();
+            bool finished = true;
+            for (uint32_t n = 0; *done != fp.epoch; ++n)
+                if ((n & 1023u) == 1023u && std::chrono::steady_clock::now() - t0 > std::chrono::seconds(30)) {
+                    finished = false;
+                    break;
+                }
+            std::atomic_thread_fence(std::memory_order_acquire);
+            if (!finished || reinterpret_cast<const volatile int*>(h->h_sig + 1)[0] != 0) {
+                CUDA_TRY(cudaStreamSynchronize(st));
+                rc = check_device_error(h);
+                return rc ? rc : fail(GLC_ERR_TIMEOUT, "fused decode launch did not report its completion");
+            }
+            std::memcpy(out, h->h_res + h->res_off_out, sizeof(float) * (size_t)T * D);
+            if (ids_out) std::memcpy(ids_out, h->h_res + h->res_off_ids, sizeof(int) * (size_t)T * k);
+            if (w_out) std::memcpy(w_out, h->h_res + h->res_off_w, sizeof(float) * (size_t)T * k);
+            return GLC_OK;
+        }
+        if (e != cudaErrorNotSupported) return fail(GLC_ERR_CUDA, "fused decode launch: %s", cudaGetErrorString(e));
+    }
     CUDA_TRY(cudaMemcpyAsync(h->x, x, sizeof(float) * (size_t)T * D, cudaMemcpyHostToDevice, st));
     rc = glc_moe_forward_dev(h, layer, h->x, T, flags, h->out, nullptr, nullptr, st);
     if (rc) return rc;

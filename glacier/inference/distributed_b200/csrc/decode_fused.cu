@@ -216,6 +216,22 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
         mbar_arrive_expect_tx(wbar, wb);
         bulk_g2s_nohint(smem, p.Wr, wb, wbar);
     }
+    // Every CTA reports its end when the caller waits on host memory (see
+    // FusedDecodeParams::done_ctr): its writes become visible system-wide
+    // first, and the CTA that completes the count publishes the error word
+    // and then the epoch.
+    auto signal_done = [&]() {
+        if (p.done_ctr && tid == 0) {
+            __threadfence_system();
+            const unsigned long long prev = atomicAdd(p.done_ctr, 1ull);
+            if (prev + 1 == p.epoch * gridDim.x) {
+                __threadfence();
+                *reinterpret_cast<volatile int*>(p.host_err) = *reinterpret_cast<volatile int*>(p.err);
+                __threadfence_system();
+                *reinterpret_cast<volatile unsigned long long*>(p.host_done) = p.epoch;
+            }
+        }
+    };
     // this CTA's rows, independent of the routing: computed while the copies fly
     const long long gu_total = (long long)P * F, dn_total = (long long)T * D;
     const int g0 = (int)(gu_total * blockIdx.x / gridDim.x);
@@ -241,7 +257,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
     const bool staged = s_ok != 0;
     if (staged && warp < T) topk_token_warp(p, logit + warp * p.E, warp, s_ids, s_w, red + warp * 64, lane);
     __syncthreads();
-    if (!staged) return;  // uniform: every thread read the same s_ok
+    if (!staged) {  // uniform: every thread read the same s_ok
+        signal_done();
+        return;
+    }
     if (blockIdx.x == 0) {
         if (tid < P) {
             p.ids[tid] = s_ids[tid];
@@ -345,7 +364,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
         if (!gok) s_ok = 0;
     }
     named_bar_sync(1, NT);
-    if (!s_ok) return;
+    if (!s_ok) {
+        signal_done();
+        return;
+    }
 
     {  // ---- 4. down projection, all k slots of each row, then the combine
         const int nsegw = p.dn_nsegw, G = p.dn_G;
@@ -381,7 +403,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
     }
     if (!ok) s_ok = 0;
     named_bar_sync(1, NT);
-    if (!s_ok) return;
+    if (!s_ok) {
+        signal_done();
+        return;
+    }
     {
         const int nsegw = p.dn_nsegw;
         for (int lr = tid; lr < q1 - q0; lr += NT) {
@@ -396,6 +421,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
             }
             p.out[o] = acc;
         }
+    }
+    if (p.done_ctr) {
+        named_bar_sync(1, NT);  // every consumer's output written before the CTA reports
+        signal_done();
     }
 }
 

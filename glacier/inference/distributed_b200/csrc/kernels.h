@@ -84,6 +84,15 @@ struct FusedDecodeParams {
     float* w;             // [T][k] combine weights
     unsigned long long* bar;  // grid-barrier arrival counter (8-byte aligned), zero at first use
     int* err;
+    // Host-visible completion, for a caller that waits on host memory instead
+    // of the stream: when done_ctr is set, every CTA adds 1 to it as it
+    // finishes, and the one that completes the count epoch * grid copies *err
+    // to *host_err and then writes epoch to *host_done (both mapped host
+    // memory; out/ids/w may be mapped host memory too).
+    unsigned long long* done_ctr;
+    unsigned long long* host_done;
+    int* host_err;
+    unsigned long long epoch;
     int T, D, F, E, k, renorm, rmsnorm;
     // filled by fused_decode_configure
     int gu_nsegw, gu_G, gu_R, dn_nsegw, dn_G, dn_R, dn_split, stages, slot_bytes;
