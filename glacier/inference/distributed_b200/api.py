@@ -32,6 +32,21 @@ def _ptr(a: np.ndarray | None):
     return None if a is None else a.ctypes.data_as(C.c_void_p)
 
 
+CUDA_STREAM_LEGACY = 1  # cudaStreamLegacy
+
+
+def torch_stream_handle(stream=None) -> int:
+    """cudaStream_t of a torch stream (default: the current one) for the C ABI.
+
+    torch's default stream has the handle 0, which the handle-based *_dev entry
+    points read as "the handle's own stream" (a non-blocking stream that does
+    not order with the default stream); it is passed as cudaStreamLegacy
+    instead, so work stays ordered with torch's own operations."""
+    import torch
+    s = (stream if stream is not None else torch.cuda.current_stream()).cuda_stream
+    return s if s != 0 else CUDA_STREAM_LEGACY
+
+
 def q4k_row_bytes(k: int) -> int:
     return int(lib().glc_q4k_row_bytes(int(k)))
 

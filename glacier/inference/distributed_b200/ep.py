@@ -28,7 +28,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
-from .api import GpuExpertStageWorker
+from .api import GpuExpertStageWorker, torch_stream_handle
 
 
 class CudaExpertShard:
@@ -45,7 +45,7 @@ class CudaExpertShard:
 
     @staticmethod
     def _stream() -> int:
-        return torch.cuda.current_stream().cuda_stream
+        return torch_stream_handle()
 
     def route(self, layer: int, x: torch.Tensor, flags: int):
         T, D = x.shape

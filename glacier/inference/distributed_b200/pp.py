@@ -15,7 +15,7 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 
-from .api import FusedActivationHeader, QuantizationKernels, WirePrecisionMode
+from .api import FusedActivationHeader, QuantizationKernels, WirePrecisionMode, torch_stream_handle
 
 
 class CudaWireCodec:
@@ -28,14 +28,14 @@ class CudaWireCodec:
         out = torch.empty(T * QuantizationKernels.GetPackedTokenBytes(mode, D), dtype=torch.uint8,
                           device=x.device)
         QuantizationKernels.quantize_dev(mode, x.data_ptr(), T, D, out.data_ptr(),
-                                         torch.cuda.current_stream().cuda_stream)
+                                         torch_stream_handle())
         return out
 
     @staticmethod
     def dequantize(mode: int, payload: torch.Tensor, T: int, D: int) -> torch.Tensor:
         out = torch.empty(T, D, dtype=torch.float32, device=payload.device)
         QuantizationKernels.dequantize_dev(mode, payload.data_ptr(), T, D, out.data_ptr(),
-                                           torch.cuda.current_stream().cuda_stream)
+                                           torch_stream_handle())
         return out
 
 

@@ -10,7 +10,11 @@
  *     functions take DEVICE pointers and a cudaStream_t passed as void*, and
  *     return without synchronising the stream.
  *   - The library never frees caller memory, never calls exit() and never traps.
- *   - A glc_moe handle owns one device and one stream. Calls on one handle must
+ *   - A glc_moe handle owns one device and one stream. On the glc_moe_*_dev
+ *     entry points a NULL stream selects the handle's own (non-blocking)
+ *     stream; a caller working on the legacy default stream passes
+ *     cudaStreamLegacy.  Entry points without a handle use the stream as
+ *     given (NULL is the legacy default stream).  Calls on one handle must
  *     be serialised by the caller (the reference serialises GPU work with
  *     lock(_gpuLock), GpuFirstExpertStageWorker.cs:447). Handles on different
  *     devices are independent.

@@ -71,7 +71,8 @@ def test_fused_mixtral_full_size_repeat_and_graph(cuda, glc, oracle):
     for x in xs:
         xd.copy_(torch.from_numpy(x))
         od.zero_()
-        w.graph_launch(torch.cuda.current_stream().cuda_stream)
+        from glacier.inference.distributed_b200.api import torch_stream_handle
+        w.graph_launch(torch_stream_handle())
         torch.cuda.synchronize()
         so, _, _, _ = _run(w, x, 3 | UNFUSED)
         assert np.array_equal(od.cpu().numpy(), so)

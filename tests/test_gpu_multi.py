@@ -37,8 +37,12 @@ def _free_port() -> int:
 
 
 def _run(rank, world, port, fn, errq):
+    import faulthandler
     import torch
     import torch.distributed as dist
+    # a rank that is still running after 180 s prints every thread's stack and
+    # exits, so a stuck collective or wait shows where it is instead of hanging
+    faulthandler.dump_traceback_later(180, exit=True)
     try:
         os.environ["MASTER_ADDR"] = "127.0.0.1"
         os.environ["MASTER_PORT"] = str(port)
@@ -66,7 +70,7 @@ def _spawn(fn, world=2):
     for p in procs:
         p.start()
     for p in procs:
-        p.join(timeout=600)
+        p.join(timeout=300)
     errs = []
     while not errq.empty():
         errs.append(errq.get())

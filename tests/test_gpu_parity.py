@@ -31,7 +31,8 @@ def dev(torch, a):
 
 
 def stream(torch):
-    return torch.cuda.current_stream().cuda_stream
+    from glacier.inference.distributed_b200.api import torch_stream_handle
+    return torch_stream_handle()
 
 
 def make_layer(oracle, seed, D, F, E, k, renorm=True, Fs=0):
