@@ -3,9 +3,9 @@ Glacier.Inference.Distributed: Q4_K expert GEMV / grouped GEMM, router,
 dispatch, SwiGLU, weighted combine and the INT8 stage-boundary wire codec,
 behind the C ABI in include/glacier_b200.h."""
 from ._lib import GlcError, LIB_PATH, lib  # noqa: F401
-from .api import (FusedActivationHeader, GpuExpertStageWorker, QuantizationKernels,  # noqa: F401
-                  WirePrecisionMode, device_count, dispatch_plan_dev, gemv_q4k_dev,
-                  q4k_row_bytes, router_topk_dev)
+from .api import (Communicator, FusedActivationHeader, GpuExpertStageWorker,  # noqa: F401
+                  QuantizationKernels, WirePrecisionMode, device_count, dispatch_plan_dev,
+                  gemv_q4k_dev, q4k_row_bytes, router_topk_dev, torch_stream_handle)
 # ep / pp import torch.distributed; they are imported on use:
 #   from glacier.inference.distributed_b200.ep import ExpertParallelStageWorker, CudaExpertShard
 #   from glacier.inference.distributed_b200.pp import StageBoundaryLink, CudaWireCodec

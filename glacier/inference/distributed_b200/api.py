@@ -162,6 +162,13 @@ class GpuExpertStageWorker:
         check(lib().glc_moe_forward_dev(self._handle(), layer, x_ptr, T, flags, out_ptr, ids_ptr,
                                         w_ptr, stream))
 
+
+    def ep_forward_dev(self, comm: "Communicator", layer: int, x_ptr: int, T: int, flags: int, out_ptr: int,
+                       ids_ptr: int | None = None, w_ptr: int | None = None, stream: int | None = None) -> None:
+        """The expert-parallel layer over ``comm`` (glc_moe_ep_forward): this worker
+        holds expert shard comm.rank of comm.nranks; device pointers."""
+        check(lib().glc_moe_ep_forward(self._handle(), comm._handle(), layer, x_ptr, T, flags, out_ptr,
+                                       ids_ptr, w_ptr, stream))
     def graph_build(self, layer: int, x_ptr: int, T: int, flags: int, out_ptr: int) -> None:
         check(lib().glc_moe_graph_build(self._handle(), layer, x_ptr, T, flags, out_ptr))
 
@@ -297,3 +304,63 @@ class FusedActivationHeader:
 
     def get_payload_byte_count(self) -> int:
         return int(lib().glc_fused_header_payload_bytes(C.byref(self._c())))
+
+
+def _load_torch_nccl_first() -> None:
+    """The library loads NCCL by soname ("libnccl.so.2") at its first
+    communicator call, and a process holds one library per soname: if torch is
+    installed, it is imported first so that its own NCCL is the one loaded
+    (loading the system one first would leave torch without the newer NCCL
+    symbols it needs)."""
+    try:
+        import torch  # noqa: F401
+    except ImportError:
+        pass
+
+
+class Communicator:
+    """The NCCL communicator of the C ABI (``glc_comm_*``), for hosts that have
+    no ``torch.distributed``: one process per GPU; rank 0 makes the id with
+    ``unique_id()``, the host hands the bytes to every rank, and each rank
+    constructs ``Communicator(uid, nranks, rank, device)`` (collective)."""
+
+    @staticmethod
+    def unique_id() -> bytes:
+        _load_torch_nccl_first()
+        buf = (C.c_uint8 * _lib.GLC_COMM_ID_BYTES)()
+        check(lib().glc_comm_unique_id(buf))
+        return bytes(buf)
+
+    def __init__(self, uid: bytes, nranks: int, rank: int, device: int):
+        self._h = None
+        if len(uid) != _lib.GLC_COMM_ID_BYTES:
+            raise GlcError(-1, "communicator id must be 128 bytes")
+        _load_torch_nccl_first()
+        buf = (C.c_uint8 * _lib.GLC_COMM_ID_BYTES).from_buffer_copy(uid)
+        h = C.c_void_p()
+        check(lib().glc_comm_create(buf, nranks, rank, device, C.byref(h)))
+        self._h = h
+        self.nranks, self.rank, self.device = nranks, rank, device
+
+    def _handle(self) -> C.c_void_p:
+        if self._h is None:
+            raise GlcError(-5, "communicator was destroyed")
+        return self._h
+
+    def pp_send(self, peer: int, header: "FusedActivationHeader", x_ptr: int, stream=None) -> None:
+        """Stage boundary: quantise x [T][D] (from the header) on the GPU and send
+        the header and the payload to ``peer``."""
+        check(lib().glc_pp_send(self._handle(), peer, C.byref(header._c()), x_ptr, stream))
+
+    def pp_recv(self, peer: int, x_ptr: int, max_tokens: int, hidden_dim: int,
+                stream=None) -> "FusedActivationHeader":
+        """Receive a header and its payload from ``peer`` and dequantise into x [T][hidden_dim]."""
+        h = _lib.FusedHeader()
+        check(lib().glc_pp_recv(self._handle(), peer, C.byref(h), x_ptr, max_tokens, hidden_dim, stream))
+        return FusedActivationHeader(h.sequence_id, h.token_index, h.layer_index, h.hidden_dim,
+                                     h.precision_mode, h.flags, h.scale, h.batch_tokens)
+
+    def dispose(self) -> None:
+        if self._h is not None:
+            lib().glc_comm_destroy(self._h)
+            self._h = None

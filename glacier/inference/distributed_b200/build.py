@@ -21,7 +21,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-ffp-contract=off",
           "-I", CSRC, "-I", INCLUDE, "--expt-relaxed-constexpr"]
 SOURCES = ["api.cu", "gemv_q4k.cu", "decode_fused.cu", "router.cu", "wire.cu", "prefill.cu", "grouped_mma.cu",
-           "noalloc.cu", "ep.cu", "synth.cpp"]
+           "noalloc.cu", "ep.cu", "comm.cu", "synth.cpp"]
 HEADERS = ["common.cuh", "gemv_lane.cuh", "kernels.h", "synth.h"]
 
 
@@ -44,7 +44,7 @@ def build(force: bool = False) -> str:
         objs = list(ex.map(lambda s: _compile(s, force), SOURCES))
     if force or not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs):
         tmp = LIB + ".tmp"
-        subprocess.check_call([NVCC, *ARCH, "-shared", "-o", tmp, *objs])
+        subprocess.check_call([NVCC, *ARCH, "-shared", "-o", tmp, *objs, "-ldl"])
         os.replace(tmp, LIB)
     return LIB
 

@@ -842,6 +842,94 @@ int glc_moe_combine_dev(glc_moe* h, int32_t layer, const float* y_back, const in
     return GLC_OK;
 }
 
+int glc_moe_ep_forward(glc_moe* h, glc_comm* c, int32_t layer, const float* x, int32_t T, uint32_t flags,
+                       float* out, int32_t* ids_out, float* w_out, void* stream) {
+    int rc = check_handle(h);
+    if (rc) return rc;
+    if (!c) return fail(GLC_ERR_INVALID_ARG, "null communicator");
+    const int world = glc::comm_world(c), rank = glc::comm_rank(c);
+    const int E = h->d.num_experts, El = local_experts(h);
+    if (E % world || El * world != E || h->d.expert_begin != rank * El)
+        return fail(GLC_ERR_STATE, "the handle must hold expert shard %d of %d (experts [%d, %d))", rank, world,
+                    rank * (E / world), (rank + 1) * (E / world));
+    if (T < 0 || T > h->d.max_tokens) return fail(GLC_ERR_INVALID_ARG, "T=%d outside [0, max_tokens=%d]", T, h->d.max_tokens);
+    if (T > 0 && (!x || !out)) return fail(GLC_ERR_INVALID_ARG, "null activation pointer");
+    LayerDev* L = layer_of(h, layer);
+    if (!L->loaded) return fail(GLC_ERR_STATE, "layer %d has no weights", layer);
+    cudaStream_t st = stream ? (cudaStream_t)stream : h->stream;
+    const int D = h->d.hidden_dim, k = h->d.top_k, P = T * k;
+    const size_t row = sizeof(float) * (size_t)D;
+    auto scratch = [&](int slot, size_t bytes) { return glc::comm_scratch(c, slot, bytes ? bytes : 16); };
+    // communicator scratch slots 2.. (0 and 1 hold stage-boundary payloads)
+    float* xin = static_cast<float*>(scratch(2, (size_t)T * row));
+    int32_t* ids = static_cast<int32_t*>(scratch(3, sizeof(int32_t) * P));
+    float* w = static_cast<float*>(scratch(4, sizeof(float) * P));
+    int32_t* counts = static_cast<int32_t*>(scratch(5, sizeof(int32_t) * (3 * (size_t)world + 1)));
+    int32_t* perm = static_cast<int32_t*>(scratch(6, sizeof(int32_t) * P));
+    int32_t* inv = static_cast<int32_t*>(scratch(7, sizeof(int32_t) * P));
+    float* send_rows = static_cast<float*>(scratch(8, (size_t)P * row));
+    int32_t* send_ids = static_cast<int32_t*>(scratch(9, sizeof(int32_t) * P));
+    if (!xin || !ids || !w || !counts || !perm || !inv || !send_rows || !send_ids)
+        return fail(GLC_ERR_OOM, "expert-parallel scratch");
+    int32_t* rcounts = counts + world;
+    int32_t* offsets = counts + 2 * world;
+    if (T > 0) {
+        rc = glc_moe_route_dev(h, layer, x, T, flags, xin, ids, w, st);
+        if (rc) return rc;
+        rc = glc_moe_ep_dispatch_dev(h, xin, ids, T, world, counts, offsets, perm, inv, send_rows, send_ids, st);
+        if (rc) return rc;
+    } else {
+        CUDA_TRY(cudaMemsetAsync(counts, 0, sizeof(int32_t) * world, st));
+    }
+    // pair counts per destination rank -> per source rank, read on the host to size the exchange
+    rc = glc::comm_alltoall_i32(c, counts, rcounts, st);
+    if (rc) return rc;
+    int32_t* hc = glc::comm_host_counts(c);
+    CUDA_TRY(cudaMemcpyAsync(hc, counts, sizeof(int32_t) * 2 * world, cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaStreamSynchronize(st));
+    std::vector<size_t> so(world), sn(world), ro(world), rn(world);
+    size_t ns = 0, nr = 0;
+    for (int p = 0; p < world; ++p) {
+        so[p] = ns; sn[p] = (size_t)hc[p]; ns += sn[p];
+        ro[p] = nr; rn[p] = (size_t)hc[world + p]; nr += rn[p];
+    }
+    if (ns != (size_t)P) return fail(GLC_ERR_STATE, "dispatch counted %zu pairs, expected %d", ns, P);
+    const size_t R = nr;
+    float* recv_rows = static_cast<float*>(scratch(10, R * row));
+    int32_t* recv_ids = static_cast<int32_t*>(scratch(11, sizeof(int32_t) * R));
+    float* y = static_cast<float*>(scratch(12, R * row));
+    float* y_back = static_cast<float*>(scratch(13, (size_t)P * row));
+    if (!recv_rows || !recv_ids || !y || !y_back) return fail(GLC_ERR_OOM, "expert-parallel scratch");
+    auto scaled = [](const std::vector<size_t>& v, size_t f) {
+        std::vector<size_t> o(v.size());
+        for (size_t i = 0; i < v.size(); ++i) o[i] = v[i] * f;
+        return o;
+    };
+    const auto soR = scaled(so, row), snR = scaled(sn, row), roR = scaled(ro, row), rnR = scaled(rn, row);
+    const auto soI = scaled(so, 4), snI = scaled(sn, 4), roI = scaled(ro, 4), rnI = scaled(rn, 4);
+    rc = glc::comm_alltoallv(c, send_rows, soR.data(), snR.data(), recv_rows, roR.data(), rnR.data(), st);
+    if (rc) return rc;
+    rc = glc::comm_alltoallv(c, send_ids, soI.data(), snI.data(), recv_ids, roI.data(), rnI.data(), st);
+    if (rc) return rc;
+    // this rank's experts on every row it received, in chunks of the handle's pair slots
+    const size_t cap = (size_t)h->d.max_tokens * k;
+    for (size_t r0 = 0; r0 < R; r0 += cap) {
+        const int n = (int)std::min(cap, R - r0);
+        rc = glc_moe_experts_dev(h, layer, recv_rows + r0 * D, recv_ids + r0, n, flags, y + r0 * D, st);
+        if (rc) return rc;
+    }
+    // expert outputs back to the ranks the rows came from, in their send order
+    rc = glc::comm_alltoallv(c, y, roR.data(), rnR.data(), y_back, soR.data(), snR.data(), st);
+    if (rc) return rc;
+    if (T > 0) {
+        rc = glc_moe_combine_dev(h, layer, y_back, inv, w, T, (flags & GLC_FWD_RESIDUAL) ? x : nullptr, xin, out, st);
+        if (rc) return rc;
+        if (ids_out) CUDA_TRY(cudaMemcpyAsync(ids_out, ids, sizeof(int32_t) * P, cudaMemcpyDeviceToDevice, st));
+        if (w_out) CUDA_TRY(cudaMemcpyAsync(w_out, w, sizeof(float) * P, cudaMemcpyDeviceToDevice, st));
+    }
+    return GLC_OK;
+}
+
 int glc_moe_forward(glc_moe* h, int32_t layer, const float* x, int32_t T, uint32_t flags, float* out,
                     int32_t* ids_out, float* w_out) {
     int rc = check_handle(h);

@@ -5,6 +5,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+struct glc_comm;  // NCCL communicator of the C ABI (comm.cu)
+
 namespace glc {
 
 constexpr int kMaxDevices = 64;
@@ -164,5 +166,14 @@ cudaError_t wire_dequantize_launch(int mode, const uint8_t* in, int T, int D, fl
                                    cudaStream_t stream);
 
 int set_last_error(int code, const char* msg);
+
+// ---------------------------------------------------------------- communicator (comm.cu)
+int comm_world(const glc_comm* c);
+int comm_rank(const glc_comm* c);
+int32_t* comm_host_counts(glc_comm* c);  // pinned [2 * world]
+void* comm_scratch(glc_comm* c, int slot, size_t bytes);
+int comm_alltoall_i32(glc_comm* c, const int32_t* send, int32_t* recv, cudaStream_t st);
+int comm_alltoallv(glc_comm* c, const void* send, const size_t* soff, const size_t* scnt, void* recv,
+                   const size_t* roff, const size_t* rcnt, cudaStream_t st);
 
 }  // namespace glc

@@ -257,6 +257,41 @@ int glc_fused_header_write(const glc_fused_header* h, uint8_t* out32);
 int glc_fused_header_read(const uint8_t* in32, glc_fused_header* h);
 int32_t glc_fused_header_payload_bytes(const glc_fused_header* h);
 
+/* ---- Multi-GPU plumbing for hosts without torch.distributed (the C# host):
+ *      an NCCL communicator inside the library (NCCL is loaded at first use).
+ *      One process per GPU; the host moves the 128-byte id from one rank to
+ *      the others (its own channel), then every rank calls glc_comm_create.
+ *      NCCL is opened by soname ("libnccl.so.2"): a process that also loads
+ *      another NCCL user (e.g. torch, with its own NCCL) loads that one first. ---- */
+#define GLC_COMM_ID_BYTES 128
+typedef struct glc_comm glc_comm;
+int glc_comm_unique_id(uint8_t* id_out);
+int glc_comm_create(const uint8_t* id, int32_t nranks, int32_t rank, int32_t device, glc_comm** out);
+int glc_comm_destroy(glc_comm* c);
+
+/* Stage boundary, replacing the socket transport of a FusedActivationHeader and
+ * its wire payload (FusedSocketTransport.cs:51-135, DistributedClusterSession.cs:1123):
+ * glc_pp_send quantises x [T][D] on the GPU in hdr->precision_mode (T =
+ * hdr->batch_tokens, 0 meaning 1; D = hdr->hidden_dim) and sends the 32-byte
+ * header and the payload to `peer`; glc_pp_recv receives the header, sizes the
+ * payload with GetPayloadByteCount (FusedActivationHeader.cs:109-125),
+ * receives and dequantises it into x_out [T][hidden_dim] (T <= max_tokens).
+ * Device pointers; NULL stream = the communicator's stream.  glc_pp_recv reads
+ * the header on the host, so it returns after the header has arrived. */
+int glc_pp_send(glc_comm* c, int32_t peer, const glc_fused_header* hdr, const float* x, void* stream);
+int glc_pp_recv(glc_comm* c, int32_t peer, glc_fused_header* hdr_out, float* x_out, int32_t max_tokens,
+                int32_t hidden_dim, void* stream);
+
+/* The expert-parallel layer in one call (the steps of the glc_moe_*_dev
+ * functions above with the exchanges over `c`): h holds expert shard
+ * comm_rank of comm_world (expert_begin = rank * E / world), every rank calls
+ * it with its own T tokens (T may differ), and out [T][D], ids_out [T][k],
+ * w_out [T][k] equal the single-GPU layer's bit for bit.  Device pointers
+ * (ids_out, w_out may be NULL); NULL stream = the handle's stream.  Reads the
+ * per-rank pair counts on the host once per call. */
+int glc_moe_ep_forward(glc_moe* h, glc_comm* c, int32_t layer, const float* x, int32_t T, uint32_t flags,
+                       float* out, int32_t* ids_out, float* w_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
