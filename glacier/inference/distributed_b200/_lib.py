@@ -68,6 +68,7 @@ _SIGNATURES = {
     "glc_moe_set_profiling": (C.c_int, [vp, i32]),
     "glc_moe_kernel_times": (C.c_int, [vp, C.POINTER(C.c_float), i32, C.POINTER(C.c_int32)]),
     "glc_moe_poll_error": (C.c_int, [vp]),
+    "glc_moe_debug_stall": (C.c_int, [vp, i32, C.c_int64]),
     "glc_expert_forward": (C.c_int, [vp, i32, i32, vp, vp]),
     "glc_expert_forward_dev": (C.c_int, [vp, i32, i32, vp, vp, vp]),
     "glc_routed_topk": (C.c_int, [vp, i32, vp, vp, vp, i32, vp]),

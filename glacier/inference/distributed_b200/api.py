@@ -125,6 +125,12 @@ class GpuExpertStageWorker:
     def poll_error(self) -> None:
         check(lib().glc_moe_poll_error(self._handle()))
 
+    def debug_stall(self, cta: int, wait_limit_ns: int) -> None:
+        """Failure-detection test hook: the next fused decode launch leaves CTA
+        ``cta`` out of its grid barrier with every wait limited to
+        ``wait_limit_ns``; that launch reports GLC_ERR_TIMEOUT."""
+        check(lib().glc_moe_debug_stall(self._handle(), cta, wait_limit_ns))
+
     # -- operator API -----------------------------------------------------
     def process_activation(self, layer: int, expert_id: int, x: np.ndarray) -> np.ndarray:
         x = np.ascontiguousarray(x, np.float32)

@@ -125,6 +125,9 @@ struct glc_moe {
     unsigned long long* h_sig = nullptr;
     unsigned long long* d_sig_map = nullptr;
     unsigned long long host_epoch = 0;
+    // failure-detection test hook (glc_moe_debug_stall), consumed by the next fused launch
+    int debug_stall_cta = 0;           // CTA index + 1, 0 = none
+    long long debug_wait_limit_ns = 0;
     int* h_ids = nullptr;
     float* h_w = nullptr;
     // optional per-kernel CUDA-event timing of the last forward (launch order)
@@ -573,6 +576,16 @@ int glc_moe_kernel_times(glc_moe* h, float* ms, int32_t max_kernels, int32_t* n_
     return GLC_OK;
 }
 
+int glc_moe_debug_stall(glc_moe* h, int32_t cta, int64_t wait_limit_ns) {
+    int rc = check_handle(h);
+    if (rc) return rc;
+    if (cta < 0 || cta >= h->num_sms) return fail(GLC_ERR_INVALID_ARG, "CTA %d outside the grid of %d", cta, h->num_sms);
+    if (wait_limit_ns <= 0) return fail(GLC_ERR_INVALID_ARG, "the wait limit must be positive");
+    h->debug_stall_cta = cta + 1;
+    h->debug_wait_limit_ns = wait_limit_ns;
+    return GLC_OK;
+}
+
 int glc_moe_poll_error(glc_moe* h) {
     int rc = check_handle(h);
     if (rc) return rc;
@@ -686,6 +699,10 @@ glc::FusedDecodeParams fused_params(glc_moe* h, const LayerDev* L, int T, uint32
     fp.k = h->d.top_k;
     fp.renorm = h->d.renormalize;
     fp.rmsnorm = (flags & GLC_FWD_RMSNORM) ? 1 : 0;
+    fp.stall_cta = h->debug_stall_cta;
+    fp.wait_limit_ns = h->debug_wait_limit_ns;
+    h->debug_stall_cta = 0;  // one launch only
+    h->debug_wait_limit_ns = 0;
     return fp;
 }
 

@@ -63,13 +63,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait: returns false (and records `code` in *err) if the phase does
 // not complete within kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
+                                          uint64_t limit_ns = kWaitLimitNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     while (true) {
         for (int i = 0; i < 32; ++i)
             if (mbar_try_wait(bar, parity)) return true;
-        if (global_timer_ns() - t0 > kWaitLimitNs) break;
+        if (global_timer_ns() - t0 > limit_ns) break;
     }
     if (err) atomicExch(err, code);
     return false;
@@ -171,14 +172,15 @@ __device__ __forceinline__ unsigned long long atom_add_acq_rel_gpu_u64(unsigned 
 // synchronised; the caller synchronises them again afterwards.  Waits at most
 // kWaitLimitNs, then records kDevTimeoutGrid and returns false (the host must
 // then clear the counter before the next launch).
-__device__ __forceinline__ bool grid_barrier(unsigned long long* ctr, unsigned nblocks, int* err) {
+__device__ __forceinline__ bool grid_barrier(unsigned long long* ctr, unsigned nblocks, int* err,
+                                             uint64_t limit_ns = kWaitLimitNs) {
     __threadfence();
     const unsigned long long prev = atom_add_acq_rel_gpu_u64(ctr, 1ull);
     const unsigned long long target = (prev / nblocks + 1) * nblocks;
     if (prev + 1 == target) return true;
     const uint64_t t0 = global_timer_ns();
     while (ld_acquire_gpu_u64(ctr) < target) {
-        if (global_timer_ns() - t0 > kWaitLimitNs) {
+        if (global_timer_ns() - t0 > limit_ns) {
             if (err) atomicExch(err, kDevTimeoutGrid);
             return false;
         }

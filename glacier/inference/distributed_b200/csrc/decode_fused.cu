@@ -190,6 +190,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int T = p.T, D = p.D, F = p.F, k = p.k, P = T * k;
+    const uint64_t lim = p.wait_limit_ns > 0 ? (uint64_t)p.wait_limit_ns : kWaitLimitNs;
     const int slot = p.slot_bytes;
 
     if (tid == 0) {
@@ -242,11 +243,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
     if (tid < kRouterWidth) {
         // Each wait's outcome goes through its own flag and a barrier of the
         // 256 router threads, so all of them take the same branch.
-        if (!mbar_wait(xbar, 0, p.err, kDevTimeoutFull)) s_okx = 0;
+        if (!mbar_wait(xbar, 0, p.err, kDevTimeoutFull, lim)) s_okx = 0;
         named_bar_sync(2, kRouterWidth);
         const bool okx = s_okx != 0;
         if (okx && p.rmsnorm) router_rms(p, xraw, red, rms_s, tid);
-        if (okx && !mbar_wait(wbar, 0, p.err, kDevTimeoutFull)) s_okw = 0;
+        if (okx && !mbar_wait(wbar, 0, p.err, kDevTimeoutFull, lim)) s_okw = 0;
         named_bar_sync(2, kRouterWidth);
         if (okx && s_okw != 0)
             router_logits(p, reinterpret_cast<const float*>(smem), xraw, xs, red, logit, rms_s, tid);
@@ -258,6 +259,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
     if (staged && warp < T) topk_token_warp(p, logit + warp * p.E, warp, s_ids, s_w, red + warp * 64, lane);
     __syncthreads();
     if (!staged) {  // uniform: every thread read the same s_ok
+        if (tid == 0) {  // the staging copies land (bounded) before the CTA exits
+            mbar_wait(xbar, 0, nullptr, 0, lim);
+            mbar_wait(wbar, 0, nullptr, 0, lim);
+        }
         signal_done();
         return;
     }
@@ -279,11 +284,12 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
             fence_proxy_async_smem();  // router reads of the ring before bulk writes into it
             const uint64_t pol = l2_evict_first_policy();
             bool ok = true;
+            int issued = 0;  // stages issued so far
             const int nxt = for_each_stage_rows(F, 1, p.gu_R, g0, g1, 0, [&](int sidx, int seg, int, int rin, int nr, int) {
                 if (!ok) return;
                 const int buf = sidx % S;
                 const uint32_t ph = (uint32_t)(sidx / S) & 1u;
-                if (!mbar_wait(&empty[buf], ph ^ 1u, p.err, kDevTimeoutEmpty)) { ok = false; return; }
+                if (!mbar_wait(&empty[buf], ph ^ 1u, p.err, kDevTimeoutEmpty, lim)) { ok = false; return; }
                 const int e = clamp_expert(s_ids[seg], p.E);
                 const size_t off = (size_t)e * p.gu_expert_bytes + (size_t)rin * rbG;
                 const uint32_t bytes = (uint32_t)(nr * rbG);
@@ -291,6 +297,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
                 mbar_arrive_expect_tx(&full[buf], 2u * bytes);
                 bulk_g2s(dst, p.gate + off, bytes, &full[buf], pol);
                 bulk_g2s(dst + (size_t)p.gu_R * rbG, p.up + off, bytes, &full[buf], pol);
+                issued = sidx + 1;
             });
             // Down-projection stages: with the slot-split layout a stage holds the
             // same dn_R rows of all k selected experts (one copy each), else dn_R
@@ -300,7 +307,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
                 if (!ok) return;
                 const int buf = sidx % S;
                 const uint32_t ph = (uint32_t)(sidx / S) & 1u;
-                if (!mbar_wait(&empty[buf], ph ^ 1u, p.err, kDevTimeoutEmpty)) { ok = false; return; }
+                if (!mbar_wait(&empty[buf], ph ^ 1u, p.err, kDevTimeoutEmpty, lim)) { ok = false; return; }
                 const uint32_t bytes = (uint32_t)(nr * rbD);
                 mbar_arrive_expect_tx(&full[buf], bytes * ncp);
                 for (int c = 0; c < ncp; ++c) {
@@ -308,7 +315,14 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
                     bulk_g2s(smem + (size_t)buf * slot + (size_t)c * p.dn_R * rbD,
                              p.down + (size_t)e * p.dn_expert_bytes + (size_t)rin * rbD, bytes, &full[buf], pol);
                 }
+                issued = sidx + 1;
             });
+            if (!ok) {
+                // gave up waiting: the copies of the last stages issued land
+                // (bounded) before this warp, and so the CTA, can exit
+                for (int st = issued > S ? issued - S : 0; st < issued; ++st)
+                    mbar_wait(&full[st % S], (uint32_t)(st / S) & 1u, nullptr, 0, lim);
+            }
         }
         return;
     }
@@ -335,7 +349,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
             }
             const int buf = sidx % S;
             const uint32_t ph = (uint32_t)(sidx / S) & 1u;
-            if (!mbar_wait(&full[buf], ph, p.err, kDevTimeoutFull)) { ok = false; return; }
+            if (!mbar_wait(&full[buf], ph, p.err, kDevTimeoutFull, lim)) { ok = false; return; }
             if (wact)
                 consume_stage(smem + (size_t)buf * slot, nr, p.gu_R, 2, G, grp, rbG, sb, c, active, xr, lane,
                               [&](int i, int m, float v) { pgu[((size_t)(lr0 + i) * 2 + m) * nsegw + segw] = v; });
@@ -360,8 +374,12 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
     // ---- 3. publish the activations grid-wide (every CTA arrives, even after
     // a local timeout, so the others are not held for the full wait limit)
     if (tid == 0) {
-        const bool gok = grid_barrier(p.bar, gridDim.x, p.err);
-        if (!gok) s_ok = 0;
+        if ((int)blockIdx.x == p.stall_cta - 1) {
+            s_ok = 0;  // failure-detection test: this CTA stays out of the barrier
+        } else {
+            const bool gok = grid_barrier(p.bar, gridDim.x, p.err, lim);
+            if (!gok) s_ok = 0;
+        }
     }
     named_bar_sync(1, NT);
     if (!s_ok) {
@@ -392,7 +410,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
             }
             const int buf = sidx % S;
             const uint32_t ph = (uint32_t)(sidx / S) & 1u;
-            if (!mbar_wait(&full[buf], ph, p.err, kDevTimeoutFull)) { ok = false; return; }
+            if (!mbar_wait(&full[buf], ph, p.err, kDevTimeoutFull, lim)) { ok = false; return; }
             const uint8_t* st = smem + (size_t)buf * slot + (p.dn_split ? (size_t)j * p.dn_R * rbD : 0);
             if (wact)
                 consume_stage(st, nr, p.dn_R, 1, Gs, gs, rbD, sb, c, active, xr, lane,

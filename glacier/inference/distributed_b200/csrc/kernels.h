@@ -95,6 +95,12 @@ struct FusedDecodeParams {
     unsigned long long* host_done;
     int* host_err;
     unsigned long long epoch;
+    // Failure-detection tests: wait_limit_ns > 0 replaces the 4 s limit of every
+    // device-side wait of the launch, and CTA stall_cta - 1 (stall_cta > 0;
+    // 0 = none) stays out of the grid barrier, so the other CTAs' wait there
+    // runs out and is reported.
+    long long wait_limit_ns;
+    int stall_cta;
     int T, D, F, E, k, renorm, rmsnorm;
     // filled by fused_decode_configure
     int gu_nsegw, gu_G, gu_R, dn_nsegw, dn_G, dn_R, dn_split, stages, slot_bytes;

@@ -125,6 +125,13 @@ int glc_moe_kernel_times(glc_moe* h, float* ms, int32_t max_kernels, int32_t* n_
 /* Reads and clears the device error word of the handle (GLC_ERR_TIMEOUT when a
  * bounded device-side wait gave up during an asynchronous _dev call). */
 int glc_moe_poll_error(glc_moe* h);
+/* Failure-detection test hook: the next fused decode launch of this handle
+ * leaves CTA `cta` out of its grid barrier and gives every device-side wait of
+ * the launch `wait_limit_ns` instead of 4 s, so the other CTAs' wait runs out;
+ * that launch reports GLC_ERR_TIMEOUT (the host-buffer forward, or
+ * glc_moe_poll_error) and clears the device words, after which the handle
+ * works normally.  One launch only. */
+int glc_moe_debug_stall(glc_moe* h, int32_t cta, int64_t wait_limit_ns);
 
 /* ---- per-expert stage worker: IInferenceStageWorker.ProcessActivation
  *      (IInferenceStageWorker.cs:43; zero-alloc overload CpuWarmExpertPoolWorker.cs:232).
