@@ -45,11 +45,15 @@ __device__ __forceinline__ void quant_block32(const float4 (&t)[8], int (&dst)[1
 #pragma unroll
     for (int i = 0; i < 32; ++i) { mx = fmaxf(mx, fabsf(v[i])); s += v[i]; }
     const float inv = mx > 0.f ? 32767.0f / mx : 0.f;
+    // Round to nearest even without a float-to-int conversion (a low-rate
+    // pipe that a whole CTA quantising at once would queue on): adding
+    // 1.5 * 2^23 to |v * inv| <= 32767 leaves the rounded integer in the low
+    // 16 bits of the sum's bit pattern, the same value __float2int_rn gives.
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-        const int q0 = __float2int_rn(v[2 * i] * inv);
-        const int q1 = __float2int_rn(v[2 * i + 1] * inv);
-        dst[i] = (q0 & 0xFFFF) | (q1 << 16);
+        const float t0 = __fadd_rn(__fmul_rn(v[2 * i], inv), 12582912.0f);
+        const float t1 = __fadd_rn(__fmul_rn(v[2 * i + 1], inv), 12582912.0f);
+        dst[i] = (int)__byte_perm(__float_as_uint(t0), __float_as_uint(t1), 0x5410);
     }
     scale = mx * (1.0f / 32767.0f);
     sum = s;
