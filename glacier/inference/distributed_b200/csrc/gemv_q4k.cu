@@ -23,11 +23,12 @@
 #include "gemv_lane.cuh"
 #include "kernels.h"
 
-// Pipeline shape knobs (bytes of the stage ring, stage count bound, L2
-// streaming hint).  A stage holds one pass of four row-units per warp.
-#ifndef GLC_GEMV_RING_BYTES
-#define GLC_GEMV_RING_BYTES (192 * 1024)
-#endif
+// Pipeline shape knobs (stage count bound, L2 streaming hint).  A stage holds
+// one pass of four row-units per warp; the ring takes as many stages as the
+// shared-memory opt-in limit leaves room for after the partial sums, up to the
+// bound.  At the Mixtral shapes a stage is 64.5 KB, so that is 3 stages: with
+// 2, one stage loads while the other is consumed and the copies in flight
+// cover only half the latency-bandwidth product of an SM.
 #ifndef GLC_GEMV_MAX_STAGES
 #define GLC_GEMV_MAX_STAGES 8
 #endif
@@ -180,20 +181,17 @@ int gemv_configure(GemvParams& p, int num_sms, size_t smem_limit, size_t* smem_b
     const int rowBytes = (p.K >> 8) * 144;
     p.stage_rows = stage_rows_for(NM, G);  // one pass of four row-units per warp
     const size_t stage_bytes = (size_t)NM * p.stage_rows * rowBytes;
-    int S = (int)((size_t)GLC_GEMV_RING_BYTES / stage_bytes);
-    S = S < 2 ? 2 : (S > GLC_GEMV_MAX_STAGES ? GLC_GEMV_MAX_STAGES : S);
     const long long total = (long long)p.nseg * p.rows;
     int range_cap = (int)(16384 / (NMP * nsegw * 4));
     int g = num_sms;
     if ((total + g - 1) / g > range_cap) g = (int)((total + range_cap - 1) / range_cap);
     if (g > total) g = (int)total;
-    size_t bytes = (size_t)S * stage_bytes + 2 * S * sizeof(uint64_t) +
-                   (size_t)((total + g - 1) / g) * NMP * nsegw * sizeof(float);
-    while (bytes > smem_limit && S > 2) {
-        --S;
-        bytes -= stage_bytes + 2 * sizeof(uint64_t);
-    }
-    if (bytes > smem_limit) return -1;
+    const size_t part_bytes = (size_t)((total + g - 1) / g) * NMP * nsegw * sizeof(float);
+    const size_t per_stage = stage_bytes + 2 * sizeof(uint64_t);
+    if (smem_limit < part_bytes + 2 * per_stage) return -1;
+    int S = (int)((smem_limit - part_bytes) / per_stage);
+    if (S > GLC_GEMV_MAX_STAGES) S = GLC_GEMV_MAX_STAGES;
+    const size_t bytes = (size_t)S * per_stage + part_bytes;
     p.stages = S;
     *smem_bytes = bytes;
     *grid = g;
