@@ -11,7 +11,8 @@ Workload (one "step" = one decode token through one MoE layer):
 
   ours       : the sm_100a decode-layer kernel (router, gate/up GEMV + SwiGLU,
                grid barrier, down GEMV + weighted combine + residual, all in
-               one persistent launch), replayed as one CUDA graph per step;
+               one persistent launch), one launch per step through
+               glc_moe_forward_dev on the step's resident token buffer;
                16 input tokens rotate so consecutive steps route to different
                experts; the 793 MB expert working set is > L2.
   reference  : the CPU port of the reference's CPU path (CpuWarmExpertPoolWorker
@@ -20,7 +21,9 @@ Workload (one "step" = one decode token through one MoE layer):
                (.NET) with its mat-vec in an un-vendored package and cannot run.
 
 Multi-GPU (torchrun): each rank runs its own decode stream on its own GPU
-(weak scaling, replicas of the layer, no data-path collective yet).
+(weak scaling, replicas of the layer: the headline value); the line also
+carries an expert-parallel leg (experts split over the ranks, NCCL
+all-to-all dispatch and combine around the grouped tensor-core experts).
 """
 from __future__ import annotations
 
