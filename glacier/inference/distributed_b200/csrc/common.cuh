@@ -169,12 +169,15 @@ __device__ __forceinline__ unsigned long long atom_add_acq_rel_gpu_u64(unsigned 
 // prev / nblocks, which completes when the counter reaches the next multiple
 // of nblocks.  One atomic round trip to arrive, polling to leave, no reset.
 // Called by ONE thread per CTA after the CTA's participating threads have
-// synchronised; the caller synchronises them again afterwards.  Waits at most
-// kWaitLimitNs, then records kDevTimeoutGrid and returns false (the host must
-// then clear the counter before the next launch).
+// synchronised; the caller synchronises them again afterwards.  No separate
+// fences: the arrival is a release at gpu scope (acq_rel atomic) and the poll
+// an acquire, and the CTA barriers on either side carry the other threads'
+// writes before the release and their reads after the acquire (causality
+// order is transitive across the CTA barrier).  Waits at most kWaitLimitNs,
+// then records kDevTimeoutGrid and returns false (the host must then clear
+// the counter before the next launch).
 __device__ __forceinline__ bool grid_barrier(unsigned long long* ctr, unsigned nblocks, int* err,
                                              uint64_t limit_ns = kWaitLimitNs) {
-    __threadfence();
     const unsigned long long prev = atom_add_acq_rel_gpu_u64(ctr, 1ull);
     const unsigned long long target = (prev / nblocks + 1) * nblocks;
     if (prev + 1 == target) return true;
@@ -186,7 +189,6 @@ __device__ __forceinline__ bool grid_barrier(unsigned long long* ctr, unsigned n
         }
         __nanosleep(32);  // keeps the pollers from crowding out the last arrivals at the counter's L2 slice
     }
-    __threadfence();
     return true;
 }
 
