@@ -187,6 +187,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
     uint64_t* empty = full + S;
     uint64_t* xbar = empty + S;
     uint64_t* wbar = xbar + 1;
+    uint64_t* go_bar = wbar + 1;  // the producer has issued its first ring's worth of stages
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int T = p.T, D = p.D, F = p.F, k = p.k, P = T * k;
@@ -200,6 +201,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
         }
         mbar_init(xbar, 1);
         mbar_init(wbar, 1);
+        mbar_init(go_bar, 1);
         fence_mbar_init();
         s_ok = s_okx = s_okw = 1;
     }
@@ -298,7 +300,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
                 bulk_g2s(dst, p.gate + off, bytes, &full[buf], pol);
                 bulk_g2s(dst + (size_t)p.gu_R * rbG, p.up + off, bytes, &full[buf], pol);
                 issued = sidx + 1;
+                if (sidx == S - 1) mbar_arrive(go_bar);
             });
+            if (issued < S) mbar_arrive(go_bar);  // fewer stages than the ring, or gave up
             // Down-projection stages: with the slot-split layout a stage holds the
             // same dn_R rows of all k selected experts (one copy each), else dn_R
             // rows of one expert.
@@ -340,6 +344,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
         const int sb = active ? (u >> 2) : 0, c = u & 3;
         XRegs xr;
         int cur = -1;
+        // The consumers' input loads start once the producer's first copies
+        // are out: their shared-memory traffic would otherwise hold up the
+        // producer's barrier and copy operations at the start of the stream.
+        if (!mbar_wait(go_bar, 0, p.err, kDevTimeoutFull, lim)) ok = false;
         nxt = for_each_stage_rows(F, 1, p.gu_R, g0, g1, 0, [&](int sidx, int seg, int, int, int nr, int lr0) {
             if (!ok) return;
             const int t = seg / k;
@@ -481,7 +489,7 @@ int fused_decode_configure(FusedDecodeParams& p, int num_sms, size_t smem_limit,
     const size_t o_ids = o;   o = align16(o + (size_t)P * 4);
     const size_t o_w = o;     o = align16(o + (size_t)P * 4);
     const size_t o_bars = o;
-    const size_t fixed = o + (2 * GLC_FUSED_MAX_STAGES + 2) * 8;
+    const size_t fixed = o + (2 * GLC_FUSED_MAX_STAGES + 3) * 8;
     if (fixed >= smem_limit) return -1;
     int S = (int)((smem_limit - fixed) / slot);
     if (S > GLC_FUSED_MAX_STAGES) S = GLC_FUSED_MAX_STAGES;
@@ -502,7 +510,7 @@ int fused_decode_configure(FusedDecodeParams& p, int num_sms, size_t smem_limit,
     p.off_ids = (int)(ring + o_ids);
     p.off_w = (int)(ring + o_w);
     p.off_bars = (int)(ring + o_bars);
-    *smem_bytes = ring + o_bars + (2 * (size_t)S + 2) * 8;
+    *smem_bytes = ring + o_bars + (2 * (size_t)S + 3) * 8;
     *grid = g;
     return 0;
 }
