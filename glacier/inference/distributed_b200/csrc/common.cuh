@@ -76,6 +76,36 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     return false;
 }
 
+// Bounded wait that polls with the non-suspending test_wait.  For kernels
+// whose waiting warps have no working neighbours to take issue slots from
+// (every consumer waits on the same stage): a thread suspended in try_wait
+// resumes measurably later than the phase completes.  Same bound and error
+// reporting as mbar_wait.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, int* err, int code,
+                                               uint64_t limit_ns = kWaitLimitNs) {
+    if (mbar_test_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (true) {
+        for (int i = 0; i < 32; ++i)
+            if (mbar_test_wait(bar, parity)) return true;
+        if (global_timer_ns() - t0 > limit_ns) break;
+    }
+    if (err) atomicExch(err, code);
+    return false;
+}
+
 // Bounded wait for threads that share their SM sub-partition with warps doing
 // the real work: between polls the thread sleeps `ns` nanoseconds instead of
 // spinning, so it does not take issue slots from them.  Same bound and error

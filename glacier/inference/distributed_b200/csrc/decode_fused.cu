@@ -146,7 +146,8 @@ __device__ void topk_token_warp(const FusedDecodeParams& p, const float* l, int 
     const float v0 = (e0 < E && !isnan(l[e0])) ? l[e0] : -INFINITY;
     const float v1 = (e1 < E && !isnan(l[e1])) ? l[e1] : -INFINITY;
     int r0 = 0, r1 = 0;
-    for (int e = 0; e < E; ++e) {
+#pragma unroll 8
+    for (int e = 0; e < E; ++e) {  // unrolled: the shared-memory reads overlap
         const float v = isnan(l[e]) ? -INFINITY : l[e];
         r0 += (v > v0 || (v == v0 && e < e0)) ? 1 : 0;
         r1 += (v > v1 || (v == v1 && e < e1)) ? 1 : 0;
@@ -162,8 +163,10 @@ __device__ void topk_token_warp(const FusedDecodeParams& p, const float* l, int 
     float den = 0.f;
     if (lane == 0) {
         if (p.renorm) {
+#pragma unroll 4
             for (int j = 0; j < k; ++j) den += ex[s_ids[t * k + j]];
         } else {
+#pragma unroll 8
             for (int e = 0; e < E; ++e) den += ex[e];
         }
     }
@@ -242,14 +245,20 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
     const int q0 = (int)(dn_total * blockIdx.x / gridDim.x);
     const int q1 = (int)(dn_total * (blockIdx.x + 1) / gridDim.x);
     const int rbG = (D >> 8) * 144, rbD = (F >> 8) * 144;
+    // The residual this thread adds in the final combine, loaded now so its
+    // latency is not on the launch's last step (rows q0 + tid, one per thread
+    // when the CTA has no more rows than consumer threads).
+    constexpr int NT = kFusedConsumerWarps * 32;
+    float resid0 = 0.f;
+    if (p.resid && tid < NT && tid < q1 - q0) resid0 = __ldg(p.resid + (size_t)q0 + tid);
     if (tid < kRouterWidth) {
         // Each wait's outcome goes through its own flag and a barrier of the
         // 256 router threads, so all of them take the same branch.
-        if (!mbar_wait(xbar, 0, p.err, kDevTimeoutFull, lim)) s_okx = 0;
+        if (!mbar_wait_spin(xbar, 0, p.err, kDevTimeoutFull, lim)) s_okx = 0;
         named_bar_sync(2, kRouterWidth);
         const bool okx = s_okx != 0;
         if (okx && p.rmsnorm) router_rms(p, xraw, red, rms_s, tid);
-        if (okx && !mbar_wait(wbar, 0, p.err, kDevTimeoutFull, lim)) s_okw = 0;
+        if (okx && !mbar_wait_spin(wbar, 0, p.err, kDevTimeoutFull, lim)) s_okw = 0;
         named_bar_sync(2, kRouterWidth);
         if (okx && s_okw != 0)
             router_logits(p, reinterpret_cast<const float*>(smem), xraw, xs, red, logit, rms_s, tid);
@@ -262,8 +271,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
     __syncthreads();
     if (!staged) {  // uniform: every thread read the same s_ok
         if (tid == 0) {  // the staging copies land (bounded) before the CTA exits
-            mbar_wait(xbar, 0, nullptr, 0, lim);
-            mbar_wait(wbar, 0, nullptr, 0, lim);
+            mbar_wait_spin(xbar, 0, nullptr, 0, lim);
+            mbar_wait_spin(wbar, 0, nullptr, 0, lim);
         }
         signal_done();
         return;
@@ -291,7 +300,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
                 if (!ok) return;
                 const int buf = sidx % S;
                 const uint32_t ph = (uint32_t)(sidx / S) & 1u;
-                if (!mbar_wait(&empty[buf], ph ^ 1u, p.err, kDevTimeoutEmpty, lim)) { ok = false; return; }
+                if (!mbar_wait_spin(&empty[buf], ph ^ 1u, p.err, kDevTimeoutEmpty, lim)) { ok = false; return; }
                 const int e = clamp_expert(s_ids[seg], p.E);
                 const size_t off = (size_t)e * p.gu_expert_bytes + (size_t)rin * rbG;
                 const uint32_t bytes = (uint32_t)(nr * rbG);
@@ -311,7 +320,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
                 if (!ok) return;
                 const int buf = sidx % S;
                 const uint32_t ph = (uint32_t)(sidx / S) & 1u;
-                if (!mbar_wait(&empty[buf], ph ^ 1u, p.err, kDevTimeoutEmpty, lim)) { ok = false; return; }
+                if (!mbar_wait_spin(&empty[buf], ph ^ 1u, p.err, kDevTimeoutEmpty, lim)) { ok = false; return; }
                 const uint32_t bytes = (uint32_t)(nr * rbD);
                 mbar_arrive_expect_tx(&full[buf], bytes * ncp);
                 for (int c = 0; c < ncp; ++c) {
@@ -325,14 +334,13 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
                 // gave up waiting: the copies of the last stages issued land
                 // (bounded) before this warp, and so the CTA, can exit
                 for (int st = issued > S ? issued - S : 0; st < issued; ++st)
-                    mbar_wait(&full[st % S], (uint32_t)(st / S) & 1u, nullptr, 0, lim);
+                    mbar_wait_spin(&full[st % S], (uint32_t)(st / S) & 1u, nullptr, 0, lim);
             }
         }
         return;
     }
 
     // ---------------------------------------------------------- consumer warps
-    constexpr int NT = kFusedConsumerWarps * 32;
     bool ok = true;
     int nxt;
     {  // ---- 2. gate/up + SwiGLU
@@ -347,7 +355,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
         // The consumers' input loads start once the producer's first copies
         // are out: their shared-memory traffic would otherwise hold up the
         // producer's barrier and copy operations at the start of the stream.
-        if (!mbar_wait(go_bar, 0, p.err, kDevTimeoutFull, lim)) ok = false;
+        if (!mbar_wait_spin(go_bar, 0, p.err, kDevTimeoutFull, lim)) ok = false;
         nxt = for_each_stage_rows(F, 1, p.gu_R, g0, g1, 0, [&](int sidx, int seg, int, int, int nr, int lr0) {
             if (!ok) return;
             const int t = seg / k;
@@ -357,7 +365,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
             }
             const int buf = sidx % S;
             const uint32_t ph = (uint32_t)(sidx / S) & 1u;
-            if (!mbar_wait(&full[buf], ph, p.err, kDevTimeoutFull, lim)) { ok = false; return; }
+            if (!mbar_wait_spin(&full[buf], ph, p.err, kDevTimeoutFull, lim)) { ok = false; return; }
             if (wact)
                 consume_stage(smem + (size_t)buf * slot, nr, p.gu_R, 2, G, grp, rbG, sb, c, active, xr, lane,
                               [&](int i, int m, float v) { pgu[((size_t)(lr0 + i) * 2 + m) * nsegw + segw] = v; });
@@ -418,7 +426,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
             }
             const int buf = sidx % S;
             const uint32_t ph = (uint32_t)(sidx / S) & 1u;
-            if (!mbar_wait(&full[buf], ph, p.err, kDevTimeoutFull, lim)) { ok = false; return; }
+            if (!mbar_wait_spin(&full[buf], ph, p.err, kDevTimeoutFull, lim)) { ok = false; return; }
             const uint8_t* st = smem + (size_t)buf * slot + (p.dn_split ? (size_t)j * p.dn_R * rbD : 0);
             if (wact)
                 consume_stage(st, nr, p.dn_R, 1, Gs, gs, rbD, sb, c, active, xr, lane,
@@ -438,7 +446,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
         for (int lr = tid; lr < q1 - q0; lr += NT) {
             const int g = q0 + lr, t = g / D, rin = g - t * D;
             const size_t o = (size_t)t * D + rin;
-            float acc = p.resid ? p.resid[o] : 0.f;
+            float acc = p.resid ? (lr == tid ? resid0 : p.resid[o]) : 0.f;
             const float* pp = pdn + (size_t)lr * k * nsegw;
             for (int jj = 0; jj < k; ++jj) {
                 float s = 0.f;

@@ -79,7 +79,7 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
                 if (!ok) return;
                 const int buf = sidx % S;
                 const uint32_t ph = (uint32_t)(sidx / S) & 1u;
-                if (!mbar_wait(&empty[buf], ph ^ 1u, p.err, kDevTimeoutEmpty)) { ok = false; return; }
+                if (!mbar_wait_spin(&empty[buf], ph ^ 1u, p.err, kDevTimeoutEmpty)) { ok = false; return; }
                 const uint8_t* srcA;
                 const uint8_t* srcB = nullptr;
                 if (p.mode == kGemvPlain) {
@@ -127,7 +127,7 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
         }
         const int buf = sidx % S;
         const uint32_t ph = (uint32_t)(sidx / S) & 1u;
-        if (!mbar_wait(&full[buf], ph, p.err, kDevTimeoutFull)) { ok = false; return; }
+        if (!mbar_wait_spin(&full[buf], ph, p.err, kDevTimeoutFull)) { ok = false; return; }
         const uint8_t* st = smem + (size_t)buf * stage_bytes;
         consume_stage(st, nr, R, NM, G, grp, rowBytes, sb, c, active, xr, lane, [&](int i, int m, float v) {
             const int slot = (p.mode == kGemvDownCombine) ? j : m;
