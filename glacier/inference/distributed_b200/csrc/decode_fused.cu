@@ -224,17 +224,18 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
     }
     // Every CTA reports its end when the caller waits on host memory (see
     // FusedDecodeParams::done_ctr): its writes become visible system-wide
-    // first, and the CTA that completes the count publishes the error word
-    // and then the epoch.
+    // first, and the CTA that completes a multiple of the grid size publishes
+    // the error word and then the launch's epoch (count / grid), so the
+    // launch needs no per-call parameter and can be replayed from a graph.
     auto signal_done = [&]() {
         if (p.done_ctr && tid == 0) {
             __threadfence_system();
             const unsigned long long prev = atomicAdd(p.done_ctr, 1ull);
-            if (prev + 1 == p.epoch * gridDim.x) {
+            if ((prev + 1) % gridDim.x == 0) {
                 __threadfence();
                 *reinterpret_cast<volatile int*>(p.host_err) = *reinterpret_cast<volatile int*>(p.err);
                 __threadfence_system();
-                *reinterpret_cast<volatile unsigned long long*>(p.host_done) = p.epoch;
+                *reinterpret_cast<volatile unsigned long long*>(p.host_done) = (prev + 1) / gridDim.x;
             }
         }
     };

@@ -88,13 +88,13 @@ struct FusedDecodeParams {
     int* err;
     // Host-visible completion, for a caller that waits on host memory instead
     // of the stream: when done_ctr is set, every CTA adds 1 to it as it
-    // finishes, and the one that completes the count epoch * grid copies *err
-    // to *host_err and then writes epoch to *host_done (both mapped host
-    // memory; out/ids/w may be mapped host memory too).
+    // finishes, and the one that completes a multiple of the grid size copies
+    // *err to *host_err and then writes the launch's epoch (the count over the
+    // grid size: launches since the counter was last cleared) to *host_done
+    // (both mapped host memory; out/ids/w may be mapped host memory too).
     unsigned long long* done_ctr;
     unsigned long long* host_done;
     int* host_err;
-    unsigned long long epoch;
     // Failure-detection tests: wait_limit_ns > 0 replaces the 4 s limit of every
     // device-side wait of the launch, and CTA stall_cta - 1 (stall_cta > 0;
     // 0 = none) stays out of the grid barrier, so the other CTAs' wait there
