@@ -19,6 +19,11 @@
 //   * Epilogues: plain store; gate/up pair -> SwiGLU act = silu(g)*u; down rows
 //     of the k experts of a token -> weighted combine acc = (y*w)+acc in k order
 //     (+ residual), i.e. AccumulatorStageWorker.AccumulateWeightedExpert.
+//   * Down projection, when top-k divides the warp-group count: every stage
+//     holds the same rows of all k selected experts (one copy each) and warp
+//     group g computes slot g % k, keeping that slot's activations in
+//     registers for the whole launch (no reload mid-stream, no half-empty
+//     stage at each slot's end).  Each row's reduction order is unchanged.
 #include "common.cuh"
 #include "gemv_lane.cuh"
 #include "kernels.h"
@@ -38,18 +43,22 @@
 
 namespace glc {
 
-template <class F>
+template <bool SPLIT, class F>
 __device__ __forceinline__ void for_each_stage(const GemvParams& p, int r0, int r1, F&& f) {
-    for_each_stage_rows(p.rows, (p.mode == kGemvDownCombine) ? p.kslots : 1, p.stage_rows, r0, r1, 0, f);
+    for_each_stage_rows(p.rows, (p.mode == kGemvDownCombine && !SPLIT) ? p.kslots : 1, p.stage_rows, r0, r1, 0, f);
 }
 
+// SPLIT: the slot-split down layout (p.split), a separate instantiation so
+// the other modes keep their code unchanged.
+template <bool SPLIT>
 __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __grid_constant__ GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int NM = (p.mode == kGemvGateUp) ? 2 : 1;
     const int NMP = (p.mode == kGemvGateUp) ? 2 : (p.mode == kGemvDownCombine ? p.kslots : 1);
+    const int NCP = SPLIT ? p.kslots : 1;  // expert copies per stage
     const int rowBytes = (p.K >> 8) * 144;
     const int R = p.stage_rows;
-    const int stage_bytes = NM * R * rowBytes;
+    const int stage_bytes = NM * NCP * R * rowBytes;
     const int S = p.stages;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);
     uint64_t* empty = full + S;
@@ -75,7 +84,7 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
         if (lane == 0) {
             const uint64_t pol = GLC_GEMV_L2_HINT ? l2_evict_first_policy() : 0ull;
             bool ok = true;
-            for_each_stage(p, r0, r1, [&](int sidx, int seg, int j, int rin, int nr, int) {
+            for_each_stage<SPLIT>(p, r0, r1, [&](int sidx, int seg, int j, int rin, int nr, int) {
                 if (!ok) return;
                 const int buf = sidx % S;
                 const uint32_t ph = (uint32_t)(sidx / S) & 1u;
@@ -88,12 +97,24 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
                     const int e = clamp_expert(__ldg(p.ids + seg), p.num_experts);
                     srcA = p.A + (size_t)e * p.expert_bytes + (size_t)rin * rowBytes;
                     srcB = p.B + (size_t)e * p.expert_bytes + (size_t)rin * rowBytes;
-                } else {
+                } else if (!SPLIT) {
                     const int e = clamp_expert(__ldg(p.ids + seg * p.kslots + j), p.num_experts);
                     srcA = p.A + (size_t)e * p.expert_bytes + (size_t)rin * rowBytes;
+                } else {
+                    srcA = nullptr;  // one copy per slot below
                 }
                 const uint32_t bytes = (uint32_t)(nr * rowBytes);
                 uint8_t* dst = smem + (size_t)buf * stage_bytes;
+                if (SPLIT) {
+                    mbar_arrive_expect_tx(&full[buf], bytes * NCP);
+                    for (int c = 0; c < NCP; ++c) {
+                        const int e = clamp_expert(__ldg(p.ids + seg * p.kslots + c), p.num_experts);
+                        const uint8_t* src = p.A + (size_t)e * p.expert_bytes + (size_t)rin * rowBytes;
+                        if (GLC_GEMV_L2_HINT) bulk_g2s(dst + (size_t)c * R * rowBytes, src, bytes, &full[buf], pol);
+                        else bulk_g2s_nohint(dst + (size_t)c * R * rowBytes, src, bytes, &full[buf]);
+                    }
+                    return;
+                }
                 mbar_arrive_expect_tx(&full[buf], bytes * NM);
                 if (GLC_GEMV_L2_HINT) {
                     bulk_g2s(dst, srcA, bytes, &full[buf], pol);
@@ -109,7 +130,11 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
 
     // ---------------------------------------------------------- consumer warps
     const int nsegw = p.nsegw;
-    const int segw = warp % nsegw, grp = warp / nsegw, G = NW / nsegw;
+    const int segw = warp % nsegw, grp0 = warp / nsegw, G0 = NW / nsegw;
+    // slot-split layout: group grp0 works on slot js of every stage, as group
+    // grp of G per slot
+    const int js = SPLIT ? grp0 % p.kslots : 0;
+    const int G = SPLIT ? G0 / p.kslots : G0, grp = SPLIT ? grp0 / p.kslots : grp0;
     const int U = (p.K >> 8) * 4;
     const int u = segw * 32 + lane;
     const bool active = u < U;
@@ -117,10 +142,11 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
     XRegs xr;
     int cur_x = -1;
     bool ok = true;
-    for_each_stage(p, r0, r1, [&](int sidx, int seg, int j, int, int nr, int lr0) {
+    for_each_stage<SPLIT>(p, r0, r1, [&](int sidx, int seg, int j, int, int nr, int lr0) {
         if (!ok) return;
+        const int jj = SPLIT ? js : j;
         const int xid = (p.mode == kGemvPlain) ? 0
-                        : (p.mode == kGemvGateUp ? seg / p.kslots : seg * p.kslots + j);
+                        : (p.mode == kGemvGateUp ? seg / p.kslots : seg * p.kslots + jj);
         if (xid != cur_x) {
             load_x<kXGlobalRO>(xr, reinterpret_cast<const float4*>(p.x + (size_t)xid * p.K) + 16 * u, 1, active);
             cur_x = xid;
@@ -128,9 +154,9 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
         const int buf = sidx % S;
         const uint32_t ph = (uint32_t)(sidx / S) & 1u;
         if (!mbar_wait_spin(&full[buf], ph, p.err, kDevTimeoutFull)) { ok = false; return; }
-        const uint8_t* st = smem + (size_t)buf * stage_bytes;
+        const uint8_t* st = smem + (size_t)buf * stage_bytes + (SPLIT ? (size_t)js * R * rowBytes : 0);
         consume_stage(st, nr, R, NM, G, grp, rowBytes, sb, c, active, xr, lane, [&](int i, int m, float v) {
-            const int slot = (p.mode == kGemvDownCombine) ? j : m;
+            const int slot = (p.mode == kGemvDownCombine) ? jj : m;
             part[((size_t)(lr0 + i) * NMP + slot) * nsegw + segw] = v;
         });
         __syncwarp();
@@ -179,8 +205,10 @@ int gemv_configure(GemvParams& p, int num_sms, size_t smem_limit, size_t* smem_b
     const int NM = (p.mode == kGemvGateUp) ? 2 : 1;
     const int NMP = (p.mode == kGemvGateUp) ? 2 : (p.mode == kGemvDownCombine ? p.kslots : 1);
     const int rowBytes = (p.K >> 8) * 144;
-    p.stage_rows = stage_rows_for(NM, G);  // one pass of four row-units per warp
-    const size_t stage_bytes = (size_t)NM * p.stage_rows * rowBytes;
+    p.split = (p.mode == kGemvDownCombine && p.kslots > 1 && G % p.kslots == 0) ? 1 : 0;
+    const int NCP = p.split ? p.kslots : 1;
+    p.stage_rows = stage_rows_for(NM, p.split ? G / p.kslots : G);  // one pass of four row-units per warp
+    const size_t stage_bytes = (size_t)NM * NCP * p.stage_rows * rowBytes;
     const long long total = (long long)p.nseg * p.rows;
     int range_cap = (int)(16384 / (NMP * nsegw * 4));
     int g = num_sms;
@@ -209,14 +237,19 @@ cudaError_t gemv_launch(const GemvParams& p0, int num_sms, cudaStream_t stream) 
     if (smem_optin[dev] == 0) {
         int v = 0;
         cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-        cudaError_t e = cudaFuncSetAttribute(q4k_gemv_kernel,
+        cudaError_t e = cudaFuncSetAttribute(q4k_gemv_kernel<false>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, v);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(q4k_gemv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, v);
         if (e != cudaSuccess) return e;
         smem_optin[dev] = v;
     }
     const size_t smem_limit = (size_t)smem_optin[dev];
     if (gemv_configure(p, num_sms, smem_limit, &smem, &grid) != 0) return cudaErrorInvalidValue;
-    q4k_gemv_kernel<<<grid, (p.nw + 1) * 32, smem, stream>>>(p);
+    if (p.split)
+        q4k_gemv_kernel<true><<<grid, (p.nw + 1) * 32, smem, stream>>>(p);
+    else
+        q4k_gemv_kernel<false><<<grid, (p.nw + 1) * 32, smem, stream>>>(p);
     return cudaGetLastError();
 }
 

@@ -39,8 +39,10 @@ struct GemvParams {
     float* y;
     int* err;          // device error word (bounded waits)
     int accumulate;    // down: start from the existing y instead of resid / 0
-    // filled by gemv_configure
-    int nsegw, nw, stage_rows, stages;
+    // filled by gemv_configure; split: down mode with the slot-split stage
+    // layout (every stage holds the same stage_rows rows of all kslots
+    // experts, warp group g computes slot g % kslots)
+    int nsegw, nw, stage_rows, stages, split;
 };
 
 int gemv_configure(GemvParams& p, int num_sms, size_t smem_limit, size_t* smem_bytes, int* grid);
