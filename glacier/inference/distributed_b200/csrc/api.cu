@@ -137,10 +137,15 @@ struct glc_moe {
     // captured decode step
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t graph_exec = nullptr;
-    // the host-buffer forward's replayed step (copy of h_x + fused launch) and its shape
-    cudaGraphExec_t fwd_exec = nullptr;
-    int fwd_layer = -1, fwd_T = 0;
-    uint32_t fwd_flags = 0;
+    // the host-buffer forward's replayed steps (copy of h_x + fused launch),
+    // one per (layer, T, flags) shape seen, replaced round robin when full
+    struct FwdGraph {
+        cudaGraphExec_t exec = nullptr;
+        int layer = -1, T = 0;
+        uint32_t flags = 0;
+    };
+    std::vector<FwdGraph> fwd_graphs;
+    size_t fwd_next = 0;
 };
 
 namespace {
@@ -472,7 +477,8 @@ int glc_moe_destroy(glc_moe* h) {
         if (e) cudaEventDestroy(e);
     if (h->graph_exec) cudaGraphExecDestroy(h->graph_exec);
     if (h->graph) cudaGraphDestroy(h->graph);
-    if (h->fwd_exec) cudaGraphExecDestroy(h->fwd_exec);
+    for (auto& g : h->fwd_graphs)
+        if (g.exec) cudaGraphExecDestroy(g.exec);
     cudaFree(h->x); cudaFree(h->xin); cudaFree(h->act); cudaFree(h->act_sh);
     cudaFree(h->gate_out); cudaFree(h->zeros_i); cudaFree(h->res);
     cudaFree(h->ones); cudaFree(h->ep_keys);
@@ -986,9 +992,13 @@ int glc_moe_forward(glc_moe* h, int32_t layer, const float* x, int32_t T, uint32
             fp.host_err = reinterpret_cast<int*>(h->d_sig_map + 1);
             return fp;
         };
-        const bool replay = !debug && h->fwd_exec && h->fwd_layer == layer && h->fwd_T == T && h->fwd_flags == flags;
+        cudaGraphExec_t cached = nullptr;
+        if (!debug)
+            for (const auto& g : h->fwd_graphs)
+                if (g.layer == layer && g.T == T && g.flags == flags) cached = g.exec;
+        const bool replay = cached != nullptr;
         if (replay) {
-            CUDA_TRY(cudaGraphLaunch(h->fwd_exec, st));
+            CUDA_TRY(cudaGraphLaunch(cached, st));
         } else {
             CUDA_TRY(cudaMemcpyAsync(h->x, h->h_x, xbytes, cudaMemcpyHostToDevice, st));
             const cudaError_t e = glc::fused_decode_launch(host_params(), h->num_sms, st);
@@ -1018,24 +1028,28 @@ int glc_moe_forward(glc_moe* h, int32_t layer, const float* x, int32_t T, uint32
         if (!replay && !debug) {
             // capture this shape for the next calls (the launch above did the
             // first-use set-up, which is not capturable); on any failure the
-            // calls simply stay eager
-            if (h->fwd_exec) { cudaGraphExecDestroy(h->fwd_exec); h->fwd_exec = nullptr; }
+            // calls of this shape simply stay eager
             cudaGraph_t g = nullptr;
+            cudaGraphExec_t exec = nullptr;
             if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
                 const glc::FusedDecodeParams fp = host_params();
                 const bool ok = cudaMemcpyAsync(h->x, h->h_x, xbytes, cudaMemcpyHostToDevice, st) == cudaSuccess &&
                                 glc::fused_decode_launch(fp, h->num_sms, st) == cudaSuccess;
-                if (cudaStreamEndCapture(st, &g) == cudaSuccess && ok &&
-                    cudaGraphInstantiate(&h->fwd_exec, g, 0) == cudaSuccess) {
-                    h->fwd_layer = layer;
-                    h->fwd_T = T;
-                    h->fwd_flags = flags;
-                } else {
-                    h->fwd_exec = nullptr;
-                }
+                if (cudaStreamEndCapture(st, &g) != cudaSuccess || !ok || cudaGraphInstantiate(&exec, g, 0) != cudaSuccess)
+                    exec = nullptr;
                 if (g) cudaGraphDestroy(g);
             }
             cudaGetLastError();
+            if (exec) {
+                constexpr size_t kMaxFwdGraphs = 64;
+                if (h->fwd_graphs.size() < kMaxFwdGraphs) {
+                    h->fwd_graphs.push_back({exec, layer, T, flags});
+                } else {
+                    auto& slot = h->fwd_graphs[h->fwd_next++ % kMaxFwdGraphs];
+                    cudaGraphExecDestroy(slot.exec);
+                    slot = {exec, layer, T, flags};
+                }
+            }
         }
         return GLC_OK;
     }
