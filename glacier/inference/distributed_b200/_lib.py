@@ -77,6 +77,9 @@ _SIGNATURES = {
     "glc_moe_graph_build": (C.c_int, [vp, i32, vp, i32, C.c_uint32, vp]),
     "glc_moe_graph_launch": (C.c_int, [vp, vp]),
     "glc_gemv_q4k_dev": (C.c_int, [vp, vp, vp, i32, i32, vp]),
+    "glc_attn_workspace_bytes": (C.c_int, [i32, i32, i32, C.POINTER(C.c_uint64)]),
+    "glc_attn_decode_dev": (C.c_int, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, C.c_float, vp, vp,
+                                      C.c_uint64, vp]),
     "glc_router_topk_dev": (C.c_int, [vp, vp, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp]),
     "glc_dispatch_plan_dev": (C.c_int, [vp, i32, i32, vp, vp, vp, vp, vp]),
     "glc_dispatch_plan_noalloc_dev": (C.c_int, [vp, i32, i32, vp, vp, vp, vp, vp]),

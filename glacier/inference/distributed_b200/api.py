@@ -215,6 +215,22 @@ def gemv_q4k_dev(W_ptr: int, x_ptr: int, y_ptr: int, K: int, N: int, stream: int
     check(lib().glc_gemv_q4k_dev(W_ptr, x_ptr, y_ptr, K, N, stream))
 
 
+def attn_workspace_bytes(n_heads: int, n_kv_heads: int, max_len: int) -> int:
+    n = C.c_uint64(0)
+    check(lib().glc_attn_workspace_bytes(n_heads, n_kv_heads, max_len, C.byref(n)))
+    return int(n.value)
+
+
+def attn_decode_dev(q_ptr: int, k_new_ptr: int, v_new_ptr: int, k_cache_ptr: int, v_cache_ptr: int,
+                    n_heads: int, n_kv_heads: int, max_len: int, pos: int, rope_theta: float, out_ptr: int,
+                    work_ptr: int, work_bytes: int, head_dim: int = 128, stream: int | None = None) -> None:
+    """Decode attention of one token at position ``pos`` (glc_attn_decode_dev):
+    RoPE on q and the new key, the new key and value stored as fp16 in row
+    ``pos`` of the caches, grouped-query attention over positions 0..pos."""
+    check(lib().glc_attn_decode_dev(q_ptr, k_new_ptr, v_new_ptr, k_cache_ptr, v_cache_ptr, n_heads, n_kv_heads,
+                                    head_dim, max_len, pos, rope_theta, out_ptr, work_ptr, work_bytes, stream))
+
+
 def dispatch_plan_dev(ids_ptr, P, E, counts_ptr, offsets_ptr, perm_ptr, inv_ptr, stream=None):
     check(lib().glc_dispatch_plan_dev(ids_ptr, P, E, counts_ptr, offsets_ptr, perm_ptr, inv_ptr, stream))
 

@@ -1101,6 +1101,49 @@ int glc_moe_graph_launch(glc_moe* h, void* stream) {
     return GLC_OK;
 }
 
+int glc_attn_workspace_bytes(int32_t n_heads, int32_t n_kv_heads, int32_t max_len, uint64_t* bytes) {
+    if (!bytes) return fail(GLC_ERR_INVALID_ARG, "null pointer");
+    if (n_heads <= 0 || n_kv_heads <= 0 || max_len <= 0 || n_heads % n_kv_heads)
+        return fail(GLC_ERR_INVALID_ARG, "bad attention shape (%d heads, %d KV heads, max_len %d)", n_heads,
+                    n_kv_heads, max_len);
+    *bytes = glc::attn_workspace_bytes(n_heads, n_kv_heads, max_len);
+    return GLC_OK;
+}
+
+int glc_attn_decode_dev(const float* q, const float* k_new, const float* v_new, void* k_cache, void* v_cache,
+                        int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t max_len, int32_t pos,
+                        float rope_theta, float* out, void* workspace, uint64_t workspace_bytes, void* stream) {
+    if (!q || !k_new || !v_new || !k_cache || !v_cache || !out || !workspace)
+        return fail(GLC_ERR_INVALID_ARG, "null pointer");
+    if (head_dim != 128) return fail(GLC_ERR_UNSUPPORTED, "head_dim %d (only 128)", head_dim);
+    if (n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || n_heads / n_kv_heads > glc::kAttnMaxGroup)
+        return fail(GLC_ERR_UNSUPPORTED, "%d heads over %d KV heads (a multiple, at most %d per KV head)", n_heads,
+                    n_kv_heads, glc::kAttnMaxGroup);
+    if (max_len <= 0 || pos < 0 || pos >= max_len)
+        return fail(GLC_ERR_INVALID_ARG, "position %d outside the cache (max_len %d)", pos, max_len);
+    if (!(rope_theta > 0.f)) return fail(GLC_ERR_INVALID_ARG, "rope_theta must be positive");
+    if (((uintptr_t)k_cache | (uintptr_t)v_cache | (uintptr_t)workspace) & 15u)
+        return fail(GLC_ERR_INVALID_ARG, "caches and workspace must be 16-byte aligned");
+    if (workspace_bytes < glc::attn_workspace_bytes(n_heads, n_kv_heads, max_len))
+        return fail(GLC_ERR_INVALID_ARG, "workspace of %llu bytes is too small", (unsigned long long)workspace_bytes);
+    glc::AttnParams p{};
+    p.q = q;
+    p.k_new = k_new;
+    p.v_new = v_new;
+    p.k_cache = static_cast<uint16_t*>(k_cache);
+    p.v_cache = static_cast<uint16_t*>(v_cache);
+    p.out = out;
+    p.work = static_cast<float*>(workspace);
+    p.n_heads = n_heads;
+    p.n_kv_heads = n_kv_heads;
+    p.head_dim = head_dim;
+    p.max_len = max_len;
+    p.pos = pos;
+    p.theta = rope_theta;
+    CUDA_TRY(glc::attn_decode_launch(p, (cudaStream_t)stream));
+    return GLC_OK;
+}
+
 int glc_gemv_q4k_dev(const void* W, const float* x, float* y, int32_t K, int32_t N, void* stream) {
     if (!W || !x || !y) return fail(GLC_ERR_INVALID_ARG, "null pointer");
     if (N <= 0 || K <= 0) return fail(GLC_ERR_INVALID_ARG, "K and N must be positive");

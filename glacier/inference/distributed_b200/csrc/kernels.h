@@ -46,6 +46,23 @@ struct GemvParams {
 };
 
 int gemv_configure(GemvParams& p, int num_sms, size_t smem_limit, size_t* smem_bytes, int* grid);
+
+// Decode attention of one token over fp16 K/V caches (attention.cu).
+constexpr int kAttnMaxGroup = 8;  // query heads per KV head
+struct AttnParams {
+    const float* q;        // [n_heads][head_dim] before rotation
+    const float* k_new;    // [n_kv_heads][head_dim] before rotation
+    const float* v_new;    // [n_kv_heads][head_dim]
+    uint16_t* k_cache;     // fp16 [n_kv_heads][max_len][head_dim] (rotated keys), row pos written
+    uint16_t* v_cache;     // fp16 [n_kv_heads][max_len][head_dim], row pos written
+    float* out;            // [n_heads][head_dim]
+    float* work;           // attn_workspace_bytes()
+    int n_heads, n_kv_heads, head_dim, max_len, pos;
+    float theta;
+    int nchunks;           // set by attn_decode_launch
+};
+size_t attn_workspace_bytes(int n_heads, int n_kv_heads, int max_len);
+cudaError_t attn_decode_launch(AttnParams p, cudaStream_t stream);
 cudaError_t gemv_launch(const GemvParams& p, int num_sms, cudaStream_t stream);
 
 // Router: gate GEMV + softmax + top-k (+ renormalise) with optional RMSNorm

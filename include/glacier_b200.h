@@ -170,6 +170,24 @@ int glc_moe_graph_launch(glc_moe* h, void* stream);
  *      (call shape CpuWarmExpertPoolWorker.cs:379). K % 256 != 0 -> GLC_ERR_UNSUPPORTED. ---- */
 int glc_gemv_q4k_dev(const void* W, const float* x, float* y, int32_t K, int32_t N, void* stream);
 
+/* ---- decode attention of one token (the attention half of a decode stage;
+ *      caller side IClusterStageModel.ForwardStage, IClusterStageModel.cs:19,
+ *      body external in the reference, Program.cs:1390).  Device pointers:
+ *      q [n_heads][128], k_new / v_new [n_kv_heads][128] fp32 before rotation;
+ *      k_cache / v_cache fp16 [n_kv_heads][max_len][128] (16-byte aligned).
+ *      RoPE (rotate-half pairs (i, i+64), frequencies theta^(-2i/128)) at
+ *      position pos rotates q and k_new; row pos of the caches receives the
+ *      rotated k and v as fp16; out [n_heads][128] = softmax(q.K^T/sqrt(128)) V
+ *      over positions 0..pos, query head h reading KV head h / (n_heads /
+ *      n_kv_heads).  head_dim must be 128; n_heads a multiple of n_kv_heads,
+ *      at most 8 query heads per KV head; 0 <= pos < max_len.  workspace:
+ *      glc_attn_workspace_bytes(n_heads, n_kv_heads, max_len) bytes of device
+ *      memory, 16-byte aligned.  Two launches on `stream`. ---- */
+int glc_attn_workspace_bytes(int32_t n_heads, int32_t n_kv_heads, int32_t max_len, uint64_t* bytes);
+int glc_attn_decode_dev(const float* q, const float* k_new, const float* v_new, void* k_cache, void* v_cache,
+                        int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t max_len, int32_t pos,
+                        float rope_theta, float* out, void* workspace, uint64_t workspace_bytes, void* stream);
+
 /* ---- router alone (for tests and for callers that route elsewhere) ---- */
 int glc_router_topk_dev(const float* x, const float* router_w, int32_t T, int32_t D, int32_t E,
                         int32_t k, int32_t renormalize, int32_t rmsnorm, float* xin_out,
