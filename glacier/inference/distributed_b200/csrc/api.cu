@@ -1121,6 +1121,7 @@ int glc_attn_decode_dev(const float* q, const float* k_new, const float* v_new, 
                     n_kv_heads, glc::kAttnMaxGroup);
     if (max_len <= 0 || pos < 0 || pos >= max_len)
         return fail(GLC_ERR_INVALID_ARG, "position %d outside the cache (max_len %d)", pos, max_len);
+    if (max_len > glc::kAttnMaxLen) return fail(GLC_ERR_UNSUPPORTED, "max_len %d (at most %d)", max_len, glc::kAttnMaxLen);
     if (!(rope_theta > 0.f)) return fail(GLC_ERR_INVALID_ARG, "rope_theta must be positive");
     if (((uintptr_t)k_cache | (uintptr_t)v_cache | (uintptr_t)workspace) & 15u)
         return fail(GLC_ERR_INVALID_ARG, "caches and workspace must be 16-byte aligned");

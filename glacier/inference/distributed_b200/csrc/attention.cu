@@ -17,9 +17,12 @@
 // stages its chunk in shared memory (K rows padded to 272 B so the per-position
 // 16-byte reads are conflict-free), computes the G x 64 scores, the chunk's
 // softmax statistics and unnormalised output, and writes them to a workspace;
-// a second launch merges the chunks per query head (flash-decoding).  The CTA
-// whose chunk holds pos builds the new rows from the inputs (fp16-rounded as
-// stored) instead of reading them, and writes them to the caches.
+// a second launch, one CTA per query head, merges the chunks (flash-decoding).
+// Merging in the last CTA of each KV head instead (an atomic count) measured
+// slower: 8 CTAs then merge 5 heads each on the critical path.  The CTA whose
+// chunk holds pos builds the new rows from the inputs (fp16-rounded as stored)
+// instead of reading them, and writes them to the caches.  Each thread issues
+// all its row loads before storing any, so a CTA's 32 KB are in flight at once.
 #include <cuda_fp16.h>
 
 #include "common.cuh"
@@ -34,13 +37,13 @@ constexpr int kChunk = 64;      // positions per CTA
 constexpr int kKStride = 136;   // halves per staged K row (272 B)
 constexpr int kAttnThreads = 128;
 
-// RoPE of pair i (0..63) at position pos: cos and sin of pos * theta^(-2i/128).
+// RoPE of pair i (0..63) at position pos: cos and sin of pos * theta^(-2i/128),
+// the angle formed and reduced to [-pi, pi] in double, then sincosf.
 __device__ __forceinline__ void rope_cs(int pos, float theta, int i, float& c, float& s) {
     const double inv = exp(-(double)(2 * i) / (double)kHd * log((double)theta));
-    double sd, cd;
-    sincos((double)pos * inv, &sd, &cd);
-    c = (float)cd;
-    s = (float)sd;
+    double ang = (double)pos * inv;
+    ang -= 6.283185307179586 * rint(ang * 0.15915494309189535);
+    sincosf((float)ang, &s, &c);
 }
 
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_split_kernel(const AttnParams p) {
@@ -54,6 +57,20 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_split_kernel(const A
     const int G = p.n_heads / p.n_kv_heads;
     const int L = p.pos + 1;
     const int p0 = chunk * kChunk, np = min(kChunk, L - p0);
+    // the chunk's K and V rows already in the cache, all loads in flight first
+    const size_t head_off = (size_t)g * p.max_len * kHd;
+    const int nold = min(np, p.pos - p0);
+    constexpr int kLd = kChunk * (kHd / 8) / kAttnThreads;  // 16-byte loads per thread and matrix
+    uint4 kr[kLd], vr[kLd];
+#pragma unroll
+    for (int j = 0; j < kLd; ++j) {
+        const int idx = tid + j * kAttnThreads, r = idx / (kHd / 8), c8 = idx - r * (kHd / 8);
+        if (r < nold) {
+            const size_t src = head_off + (size_t)(p0 + r) * kHd + c8 * 8;
+            kr[j] = __ldg(reinterpret_cast<const uint4*>(p.k_cache + src));
+            vr[j] = __ldg(reinterpret_cast<const uint4*>(p.v_cache + src));
+        }
+    }
     if (tid < kHd / 2) rope_cs(p.pos, p.theta, tid, cs_c[tid], cs_s[tid]);
     __syncthreads();
 
@@ -66,15 +83,15 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_split_kernel(const A
         qs[h * kHd + i] = (a * cs_c[i] - b * cs_s[i]) * scale;
         qs[h * kHd + i + kHd / 2] = (b * cs_c[i] + a * cs_s[i]) * scale;
     }
-    // the chunk's K and V rows; the row of pos comes from the inputs
-    const size_t head_off = (size_t)g * p.max_len * kHd;
-    const int nold = min(np, p.pos - p0);  // rows already in the cache
-    for (int idx = tid; idx < nold * (kHd / 8); idx += kAttnThreads) {
-        const int r = idx / (kHd / 8), c8 = idx - r * (kHd / 8);
-        const size_t src = head_off + (size_t)(p0 + r) * kHd + c8 * 8;
-        *reinterpret_cast<uint4*>(ks + r * kKStride + c8 * 8) = __ldg(reinterpret_cast<const uint4*>(p.k_cache + src));
-        *reinterpret_cast<uint4*>(vs + r * kHd + c8 * 8) = __ldg(reinterpret_cast<const uint4*>(p.v_cache + src));
+#pragma unroll
+    for (int j = 0; j < kLd; ++j) {
+        const int idx = tid + j * kAttnThreads, r = idx / (kHd / 8), c8 = idx - r * (kHd / 8);
+        if (r < nold) {
+            *reinterpret_cast<uint4*>(ks + r * kKStride + c8 * 8) = kr[j];
+            *reinterpret_cast<uint4*>(vs + r * kHd + c8 * 8) = vr[j];
+        }
     }
+    // the row of pos comes from the inputs
     if (p.pos >= p0 && p.pos < p0 + kChunk && tid < kHd / 2) {
         const int r = p.pos - p0, i = tid;
         const float* kn = p.k_new + (size_t)g * kHd;
@@ -177,26 +194,45 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_split_kernel(const A
     }
 }
 
-// Merge of the chunks of query head blockIdx.x: thread t -> dimension t.
+// Merge of the chunks of query head blockIdx.x (flash-decoding): warp 0 turns
+// the chunks' (max, sum) statistics into weights exp(m_c - M) / sum_c l_c
+// exp(m_c - M); then thread t sums dimension t over the chunks, the partials
+// read independently (at most 64 chunks).
 __global__ void __launch_bounds__(kAttnThreads) attn_combine_kernel(const AttnParams p) {
+    __shared__ float wts[kChunk];
     const int hq = blockIdx.x, tid = threadIdx.x;
     const int G = p.n_heads / p.n_kv_heads, g = hq / G, h = hq - g * G;
-    const float* base = p.work + (size_t)g * p.nchunks * G * (kHd + 2) + (size_t)h * (kHd + 2);
     const size_t cstride = (size_t)G * (kHd + 2);
-    float M = -INFINITY;
-    for (int c = 0; c < p.nchunks; ++c) M = fmaxf(M, base[c * cstride + kHd]);
-    float l = 0.f, acc = 0.f;
-    for (int c = 0; c < p.nchunks; ++c) {
-        const float* w = base + c * cstride;
-        const float f = __expf(w[kHd] - M);
-        l = fmaf(w[kHd + 1], f, l);
-        acc = fmaf(w[tid], f, acc);
+    const float* bh = p.work + (size_t)g * p.nchunks * cstride + (size_t)h * (kHd + 2);
+    if (tid < 32) {
+        const int lane = tid;
+        const float m0 = lane < p.nchunks ? __ldg(bh + lane * cstride + kHd) : -INFINITY;
+        const float m1 = lane + 32 < p.nchunks ? __ldg(bh + (lane + 32) * cstride + kHd) : -INFINITY;
+        const float l0 = lane < p.nchunks ? __ldg(bh + lane * cstride + kHd + 1) : 0.f;
+        const float l1 = lane + 32 < p.nchunks ? __ldg(bh + (lane + 32) * cstride + kHd + 1) : 0.f;
+        float M = fmaxf(m0, m1);
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        const float f0 = lane < p.nchunks ? __expf(m0 - M) : 0.f;
+        const float f1 = lane + 32 < p.nchunks ? __expf(m1 - M) : 0.f;
+        float l = l0 * f0 + l1 * f1;
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        wts[lane] = f0 / l;
+        wts[lane + 32] = f1 / l;
     }
-    p.out[(size_t)hq * kHd + tid] = acc / l;
+    __syncthreads();
+    float acc = 0.f;
+#pragma unroll 8
+    for (int c = 0; c < p.nchunks; ++c) acc = fmaf(__ldg(bh + c * cstride + tid), wts[c], acc);
+    p.out[(size_t)hq * kHd + tid] = acc;
 }
+
 
 }  // namespace
 
+// Partials [n_kv_heads][chunks][G][130] floats: a chunk's 128 unnormalised
+// outputs, its score maximum and its sum of exponentials.
 size_t attn_workspace_bytes(int n_heads, int n_kv_heads, int max_len) {
     const int G = n_kv_heads > 0 ? n_heads / n_kv_heads : 0;
     const int nchunks = (max_len + kChunk - 1) / kChunk;
@@ -206,7 +242,7 @@ size_t attn_workspace_bytes(int n_heads, int n_kv_heads, int max_len) {
 cudaError_t attn_decode_launch(AttnParams p, cudaStream_t stream) {
     if (p.head_dim != kHd || p.n_kv_heads <= 0 || p.n_heads % p.n_kv_heads) return cudaErrorInvalidValue;
     const int G = p.n_heads / p.n_kv_heads;
-    if (G > kAttnMaxGroup || p.pos < 0 || p.pos >= p.max_len) return cudaErrorInvalidValue;
+    if (G > kAttnMaxGroup || p.pos < 0 || p.pos >= p.max_len || p.max_len > kAttnMaxLen) return cudaErrorInvalidValue;
     p.nchunks = (p.pos + 1 + kChunk - 1) / kChunk;
     attn_decode_split_kernel<<<dim3(p.n_kv_heads, p.nchunks), kAttnThreads, 0, stream>>>(p);
     attn_combine_kernel<<<p.n_heads, kAttnThreads, 0, stream>>>(p);

@@ -48,7 +48,8 @@ struct GemvParams {
 int gemv_configure(GemvParams& p, int num_sms, size_t smem_limit, size_t* smem_bytes, int* grid);
 
 // Decode attention of one token over fp16 K/V caches (attention.cu).
-constexpr int kAttnMaxGroup = 8;  // query heads per KV head
+constexpr int kAttnMaxGroup = 8;    // query heads per KV head
+constexpr int kAttnMaxLen = 4096;   // cache rows: 64 chunks of 64 positions, merged by one warp
 struct AttnParams {
     const float* q;        // [n_heads][head_dim] before rotation
     const float* k_new;    // [n_kv_heads][head_dim] before rotation

@@ -180,7 +180,7 @@ int glc_gemv_q4k_dev(const void* W, const float* x, float* y, int32_t K, int32_t
  *      rotated k and v as fp16; out [n_heads][128] = softmax(q.K^T/sqrt(128)) V
  *      over positions 0..pos, query head h reading KV head h / (n_heads /
  *      n_kv_heads).  head_dim must be 128; n_heads a multiple of n_kv_heads,
- *      at most 8 query heads per KV head; 0 <= pos < max_len.  workspace:
+ *      at most 8 query heads per KV head; 0 <= pos < max_len <= 4096.  workspace:
  *      glc_attn_workspace_bytes(n_heads, n_kv_heads, max_len) bytes of device
  *      memory, 16-byte aligned.  Two launches on `stream`. ---- */
 int glc_attn_workspace_bytes(int32_t n_heads, int32_t n_kv_heads, int32_t max_len, uint64_t* bytes);

@@ -28,7 +28,7 @@ def run(torch, glc, q, k, v, kc, vc, pos):
     dvc = torch.from_numpy(vc.view(np.uint16).copy()).cuda()
     out = torch.empty(Hq, 128, device="cuda")
     nb = glc.attn_workspace_bytes(Hq, Hkv, L)
-    ws = torch.empty(nb, dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(nb, dtype=torch.uint8, device="cuda")
     glc.attn_decode_dev(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dkc.data_ptr(), dvc.data_ptr(), Hq, Hkv, L,
                         pos, THETA, out.data_ptr(), ws.data_ptr(), nb, stream=1)
     torch.cuda.synchronize()
@@ -66,7 +66,7 @@ def test_sequential_decode_steps(cuda, glc):
     dkc = torch.zeros(Hkv, L, 128, dtype=torch.int16, device="cuda")
     dvc = torch.zeros(Hkv, L, 128, dtype=torch.int16, device="cuda")
     nb = glc.attn_workspace_bytes(Hq, Hkv, L)
-    ws = torch.empty(nb, dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(nb, dtype=torch.uint8, device="cuda")
     out = torch.empty(Hq, 128, device="cuda")
     for pos in range(70):
         q = rng.standard_normal((Hq, 128)).astype(np.float32)
@@ -92,5 +92,7 @@ def test_attention_rejects_bad_arguments(cuda, glc):
         glc.attn_decode_dev(p, p, p, p, p, 16, 1, 16, 0, THETA, p, p, 1 << 20, stream=1)
     with pytest.raises(glc.GlcError):  # position outside the cache
         glc.attn_decode_dev(p, p, p, p, p, 8, 8, 16, 16, THETA, p, p, 1 << 20, stream=1)
+    with pytest.raises(glc.GlcError):  # cache longer than the kernel merges
+        glc.attn_decode_dev(p, p, p, p, p, 8, 8, 8192, 3, THETA, p, p, 1 << 20, stream=1)
     with pytest.raises(glc.GlcError):  # workspace too small
         glc.attn_decode_dev(p, p, p, p, p, 8, 8, 16, 3, THETA, p, p, 16, stream=1)
