@@ -152,6 +152,8 @@ class GpuExpertStageWorker:
         return out
 
     def forward(self, layer: int, x: np.ndarray, flags: int = 0):
+        """The MoE layer on host buffers (glc_moe_forward): returns (out [T][D],
+        expert ids [T][k], combine weights [T][k])."""
         x = np.ascontiguousarray(x, np.float32)
         if x.ndim == 1:
             x = x[None, :]
@@ -168,13 +170,13 @@ class GpuExpertStageWorker:
         check(lib().glc_moe_forward_dev(self._handle(), layer, x_ptr, T, flags, out_ptr, ids_ptr,
                                         w_ptr, stream))
 
-
     def ep_forward_dev(self, comm: "Communicator", layer: int, x_ptr: int, T: int, flags: int, out_ptr: int,
                        ids_ptr: int | None = None, w_ptr: int | None = None, stream: int | None = None) -> None:
         """The expert-parallel layer over ``comm`` (glc_moe_ep_forward): this worker
         holds expert shard comm.rank of comm.nranks; device pointers."""
         check(lib().glc_moe_ep_forward(self._handle(), comm._handle(), layer, x_ptr, T, flags, out_ptr,
                                        ids_ptr, w_ptr, stream))
+
     def graph_build(self, layer: int, x_ptr: int, T: int, flags: int, out_ptr: int) -> None:
         check(lib().glc_moe_graph_build(self._handle(), layer, x_ptr, T, flags, out_ptr))
 

@@ -150,7 +150,11 @@ int glc_routed_topk(glc_moe* h, int32_t layer, const float* x, const int32_t* id
 /* ---- full MoE layer for T tokens: router (gate GEMV + softmax + top-k +
  *      renormalise), dispatch, experts, combine. x, out: fp32 [T][D]; ids_out
  *      int32 [T][k], w_out fp32 [T][k] (either may be NULL).  T == 1 runs the
- *      decode path (dequant-fused GEMV kernels); T > 1 the batched path. ---- */
+ *      decode path (dequant-fused GEMV kernels); T > 1 the batched path.
+ *      Host-buffer form: for shapes the fused decode launch takes, the first
+ *      call of each (layer, T, flags) captures the input copy and the launch
+ *      into a graph that later calls replay (up to 64 shapes per handle,
+ *      replaced round robin); results are the same either way. ---- */
 int glc_moe_forward(glc_moe* h, int32_t layer, const float* x, int32_t T, uint32_t flags,
                     float* out, int32_t* ids_out, float* w_out);
 int glc_moe_forward_dev(glc_moe* h, int32_t layer, const float* x, int32_t T, uint32_t flags,
