@@ -427,6 +427,7 @@ def measure_batched(torch, worker, w, stream, args):
     out = torch.empty(T, D, device="cuda")
     s = stream.cuda_stream
     reps = max(10, min(200, args.steps // 100))
+    reps = (reps + 3) // 4 * 4
     with torch.cuda.stream(stream):
         for i in range(3):
             worker.forward_dev(0, xs[i % 4].data_ptr(), T, w["flags"], out.data_ptr(), stream=s)
@@ -437,7 +438,24 @@ def measure_batched(torch, worker, w, stream, args):
             worker.forward_dev(0, xs[i % 4].data_ptr(), T, w["flags"], out.data_ptr(), stream=s)
         e1.record(stream)
         torch.cuda.synchronize()
+        ms_direct = e0.elapsed_time(e1) / reps
+    # as the decode leg: four batches (the four inputs) captured in one CUDA
+    # graph and replayed
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(4):
+            worker.forward_dev(0, xs[i].data_ptr(), T, w["flags"], out.data_ptr(), stream=s)
+    with torch.cuda.stream(stream):
+        graph.replay()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for i in range(reps // 4):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / reps
+    del graph
+    with torch.cuda.stream(stream):
         worker.set_profiling(True)
         kt = []
         for i in range(reps):
@@ -453,6 +471,8 @@ def measure_batched(torch, worker, w, stream, args):
     gu = kt[3] if len(kt) > 3 else float("nan")
     dn = kt[5] if len(kt) > 5 else float("nan")
     return {"workload": "mixtral8x7b_moe_layer_prefill_64", "tokens": T, "ms_per_batch": ms,
+            "ms_per_batch_direct_launches": ms_direct,
+            "submission": "4 batches captured in one CUDA graph and replayed (direct launches beside it)",
             "tokens_per_s": T / (ms * 1e-3), "weight_bytes": weight_bytes,
             "layer_gbs": weight_bytes / (ms * 1e-3) / 1e9,
             "grouped_gateup_gbs": (2 * w["E"] * w["F"] * q4k_row_bytes(D)) / (gu * 1e-3) / 1e9,
