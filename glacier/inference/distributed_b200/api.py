@@ -342,6 +342,91 @@ def _load_torch_nccl_first() -> None:
         pass
 
 
+class DynamicPrecisionSwitcher:
+    """Wire precision of a stage-boundary send, chosen per message
+    (DynamicPrecisionSwitcher, DynamicPrecisionSwitcher.cs:10-178): a forced
+    mode wins; decode keeps FP16, except under link congestion (smoothed
+    round-trip time above ``congestion_latency_threshold_ms``) where it backs
+    off to INT8, unless the sequence is deeper than ``deep_context_threshold``
+    (FP16 protects the attention logits there); prefill batches of at least
+    ``prefill_batch_threshold`` tokens, or any batch under congestion, use
+    INT8, smaller ones FP16.  The round-trip time is an exponential moving
+    average (factor ``ema_alpha``) whose first sample sets it directly; before
+    any sample it reads 0.5 ms.  Every change of the selected mode counts as
+    a switch.  On NVLink the round trip is the host-measured time of a
+    send/recv pair; the thresholds keep the reference's defaults."""
+
+    def __init__(self, forced_precision: int | None = None):
+        self.forced_precision = forced_precision
+        self.prefill_batch_threshold = 32
+        self.congestion_latency_threshold_ms = 2.5
+        self.deep_context_threshold = 16384
+        self.ema_alpha = 0.2
+        self._ema_ms = -1.0
+        self._last = forced_precision if forced_precision is not None else WirePrecisionMode.FP16
+        self._switches = 0
+
+    @property
+    def current_ema_latency_ms(self) -> float:
+        return self._ema_ms if self._ema_ms > 0.0 else 0.5
+
+    @property
+    def last_selected_precision(self) -> int:
+        return self._last
+
+    @property
+    def total_switches(self) -> int:
+        return self._switches
+
+    def update_measured_latency(self, rtt_ms: float) -> None:
+        if rtt_ms <= 0.0:
+            return
+        if self._ema_ms <= 0.0:
+            self._ema_ms = rtt_ms
+        else:
+            self._ema_ms = (1.0 - self.ema_alpha) * self._ema_ms + self.ema_alpha * rtt_ms
+
+    record_rtt = update_measured_latency
+
+    def select_precision(self, batch_size: int, sequence_position: int = 0, is_decode: bool = False,
+                         override_rtt_ms: float | None = None) -> int:
+        if self.forced_precision is not None:
+            self._last = self.forced_precision
+            return self.forced_precision
+        rtt = override_rtt_ms if override_rtt_ms is not None else self.current_ema_latency_ms
+        congested = rtt > self.congestion_latency_threshold_ms
+        if is_decode:
+            if sequence_position > self.deep_context_threshold:
+                mode = WirePrecisionMode.FP16
+            else:
+                mode = WirePrecisionMode.INT8_Symmetric if congested else WirePrecisionMode.FP16
+        elif batch_size >= self.prefill_batch_threshold or congested:
+            mode = WirePrecisionMode.INT8_Symmetric
+        else:
+            mode = WirePrecisionMode.FP16
+        if mode != self._last:
+            self._switches += 1
+            self._last = mode
+        return mode
+
+    @staticmethod
+    def select_optimal_wire_precision(batch_size: int, is_decode: bool, lan_latency_ms: float,
+                                      forced_override: int | None = None) -> int:
+        """The static form (DynamicPrecisionSwitcher.cs:153-164)."""
+        if forced_override is not None:
+            return forced_override
+        if is_decode:
+            return WirePrecisionMode.FP16
+        if lan_latency_ms > 2.5:
+            return WirePrecisionMode.INT8_Symmetric
+        return WirePrecisionMode.INT8_Symmetric if batch_size >= 32 else WirePrecisionMode.FP16
+
+    def reset(self) -> None:
+        self._ema_ms = -1.0
+        self._switches = 0
+        self._last = self.forced_precision if self.forced_precision is not None else WirePrecisionMode.FP16
+
+
 class Communicator:
     """The NCCL communicator of the C ABI (``glc_comm_*``), for hosts that have
     no ``torch.distributed``: one process per GPU; rank 0 makes the id with

@@ -43,13 +43,19 @@ class StageBoundaryLink:
     """Sends activations to the next pipeline stage and receives them from the
     previous one.  ``send``/``recv`` must be paired across the two ranks."""
 
-    def __init__(self, codec=None, group=None):
+    def __init__(self, codec=None, group=None, switcher=None):
         self.codec = codec if codec is not None else CudaWireCodec()
         self.group = group
+        self.switcher = switcher  # optional DynamicPrecisionSwitcher: picks the mode when send gets none
 
-    def send(self, x: torch.Tensor, dst: int, mode: int = WirePrecisionMode.INT8_Symmetric, *,
-             sequence_id: int = 0, token_index: int = 0, layer_index: int = 0, flags: int = 0) -> None:
+    def send(self, x: torch.Tensor, dst: int, mode: int | None = WirePrecisionMode.INT8_Symmetric, *,
+             sequence_id: int = 0, token_index: int = 0, layer_index: int = 0, flags: int = 0,
+             sequence_position: int = 0, is_decode: bool = False) -> None:
         T, D = x.shape
+        if mode is None:
+            if self.switcher is None:
+                raise ValueError("send without a mode needs a DynamicPrecisionSwitcher")
+            mode = self.switcher.select_precision(T, sequence_position, is_decode)
         payload = self.codec.quantize(mode, x)
         hdr = FusedActivationHeader(sequence_id, token_index, layer_index, D, mode, flags, 1.0, T)
         raw = torch.frombuffer(bytearray(hdr.write_to()), dtype=torch.uint8).to(x.device)

@@ -181,3 +181,29 @@ def _pp_case(rank, world):
 
 def test_stage_boundary_link_two_ranks():
     _spawn(_pp_case)
+
+
+def _pp_switcher_case(rank, world):
+    from oracle import oracle as o
+    from glacier.inference.distributed_b200 import DynamicPrecisionSwitcher, WirePrecisionMode
+    from glacier.inference.distributed_b200.pp import StageBoundaryLink
+    o.build()
+    sw = DynamicPrecisionSwitcher()
+    link = StageBoundaryLink(OracleCodec(o), switcher=sw)
+    # (tokens, decode?, round-trip ms) -> the mode the switcher picks and the header carries
+    cases = [(1, True, 0.4, WirePrecisionMode.FP16), (64, False, 0.4, WirePrecisionMode.INT8_Symmetric),
+             (8, False, 0.4, WirePrecisionMode.FP16), (1, True, 9.0, WirePrecisionMode.INT8_Symmetric)]
+    for i, (T, decode, rtt, want_mode) in enumerate(cases):
+        x = o.fill_normal(90 + i, 1, 1.0, T * 256).reshape(T, 256)
+        if rank == 0:
+            sw.update_measured_latency(rtt) if i < 3 else [sw.update_measured_latency(rtt) for _ in range(30)]
+            link.send(torch.from_numpy(x), 1, None, sequence_position=100, is_decode=decode)
+        else:
+            hdr, back = link.recv(0, "cpu")
+            assert hdr.precision_mode == want_mode and hdr.batch_tokens == T
+            want = o.wire_dequantize(want_mode, np.asarray(o.wire_quantize(want_mode, x)), T, 256)
+            assert np.array_equal(back.numpy(), want)
+
+
+def test_stage_boundary_link_picks_modes_with_the_switcher():
+    _spawn(_pp_switcher_case)
