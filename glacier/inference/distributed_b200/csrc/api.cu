@@ -183,6 +183,8 @@ int check_device_error(glc_moe* h) {
         cudaMemset(h->err, 0, kErrWords * sizeof(int));
         h->host_epoch = 0;
         if (h->h_sig) h->h_sig[0] = h->h_sig[1] = 0;
+        if (code == glc::kDevBadArg)
+            return fail(GLC_ERR_INVALID_ARG, "a kernel rejected its arguments (device code %d)", code);
         return fail(GLC_ERR_TIMEOUT, "device-side wait gave up (code %d)", code);
     }
     return GLC_OK;

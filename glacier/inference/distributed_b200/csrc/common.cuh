@@ -7,16 +7,9 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
-namespace glc {
+#include "kernels.h"  // device error codes
 
-// Device-side error codes written to the per-handle error word.
-enum : int {
-    kDevOk = 0,
-    kDevTimeoutFull = 1,   // consumer gave up waiting for a stage to land
-    kDevTimeoutEmpty = 2,  // producer gave up waiting for a stage to be released
-    kDevBadArg = 3,
-    kDevTimeoutGrid = 4,   // a CTA gave up waiting at a grid-wide barrier
-};
+namespace glc {
 
 // Upper bound on any device-side wait, in nanoseconds of %globaltimer.
 constexpr uint64_t kWaitLimitNs = 4000000000ull;
@@ -120,6 +113,18 @@ __device__ __forceinline__ bool mbar_wait_backoff(uint64_t* bar, uint32_t parity
     }
     if (err) atomicExch(err, code);
     return false;
+}
+
+// Called by a producer thread before it returns, on every path: waits
+// (bounded, suspending polls, nothing recorded) until the copies of the last
+// min(issued, S) stages of a ring of S stages (stage i on full[i % S], phase
+// i / S) have landed, so the CTA can never exit with bulk copies still writing
+// into its shared memory -- also when the consumers abandon the ring (a
+// timed-out grid barrier) while the producer has issued everything.  On the
+// normal path those phases completed long ago and every wait returns at once.
+__device__ __forceinline__ void drain_issued_stages(uint64_t* full, int S, int issued, uint64_t limit_ns) {
+    for (int st = issued > S ? issued - S : 0; st < issued; ++st)
+        mbar_wait(&full[st % S], (uint32_t)(st / S) & 1u, nullptr, 0, limit_ns);
 }
 
 // 1-D bulk copy global -> shared, completion counted on `bar` in bytes.

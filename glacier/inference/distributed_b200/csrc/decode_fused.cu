@@ -331,12 +331,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
                 }
                 issued = sidx + 1;
             });
-            if (!ok) {
-                // gave up waiting: the copies of the last stages issued land
-                // (bounded) before this warp, and so the CTA, can exit
-                for (int st = issued > S ? issued - S : 0; st < issued; ++st)
-                    mbar_wait_spin(&full[st % S], (uint32_t)(st / S) & 1u, nullptr, 0, lim);
-            }
+            // On every path (this warp gave up, the consumers abandoned the
+            // ring after a failed grid barrier, or normal completion) the
+            // copies of the last stages issued land before this warp, and so
+            // the CTA, can exit.
+            drain_issued_stages(full, S, issued, lim);
         }
         return;
     }

@@ -84,11 +84,13 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
         if (lane == 0) {
             const uint64_t pol = GLC_GEMV_L2_HINT ? l2_evict_first_policy() : 0ull;
             bool ok = true;
+            int issued = 0;  // stages issued so far
             for_each_stage<SPLIT>(p, r0, r1, [&](int sidx, int seg, int j, int rin, int nr, int) {
                 if (!ok) return;
                 const int buf = sidx % S;
                 const uint32_t ph = (uint32_t)(sidx / S) & 1u;
                 if (!mbar_wait_spin(&empty[buf], ph ^ 1u, p.err, kDevTimeoutEmpty)) { ok = false; return; }
+                issued = sidx + 1;
                 const uint8_t* srcA;
                 const uint8_t* srcB = nullptr;
                 if (p.mode == kGemvPlain) {
@@ -124,6 +126,8 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
                     if (NM == 2) bulk_g2s_nohint(dst + (size_t)R * rowBytes, srcB, bytes, &full[buf]);
                 }
             });
+            // the copies in flight land before this warp, and so the CTA, exits
+            drain_issued_stages(full, S, issued, kWaitLimitNs);
         }
         return;
     }

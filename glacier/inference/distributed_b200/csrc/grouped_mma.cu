@@ -291,7 +291,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint64_t* a_empty = a_full + kAUnits;
     uint64_t* acc_full = a_empty + kAUnits;
     uint64_t* acc_empty = acc_full + 1;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
+    uint64_t* mma_drain = acc_empty + 1;  // one per MMA issuer: its MMAs done before an early exit
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_drain + 2);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nm = p.nm;
@@ -315,6 +316,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         mbar_init(acc_full, 2);
         mbar_init(acc_empty, 4);
+        mbar_init(&mma_drain[0], 1);
+        mbar_init(&mma_drain[1], 1);
         fence_mbar_init();
     }
     if (warp == 9) {
@@ -347,6 +350,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     if (nm == 2) tma_load_2d(rdst + kRawTile, &tmB, s * 144, row0, &raw_full[stg]);
                 }
             }
+            // the tiles in flight land before the CTA can exit (also when the
+            // dequantisers abandoned the ring after a failed wait)
+            drain_issued_stages(raw_full, S, it, kWaitLimitNs);
         }
     } else if (warp == 15) {
         // ------------------------------------------------------------ B tiles
@@ -366,6 +372,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                    &b_full[stg]);
                 }
             }
+            drain_issued_stages(b_full, kBStages, it, kWaitLimitNs);
         }
     } else if (warp >= 1 && warp <= 8) {
         // ------------------------------------------------------- dequantise
@@ -467,6 +474,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     tc_commit(&b_empty[stg]);
                 }
                 if (ok) tc_commit(acc_full);
+            }
+            if (!ok) {
+                // gave up: every MMA this thread issued completes before the
+                // CTA frees its tensor memory and exits
+                tc_commit(&mma_drain[v]);
+                mbar_wait(&mma_drain[v], 0, nullptr, 0, kWaitLimitNs);
             }
         }
     } else {

@@ -9,6 +9,16 @@ struct glc_comm;  // NCCL communicator of the C ABI (comm.cu)
 
 namespace glc {
 
+// Device-side error codes written to the per-handle error word.
+enum : int {
+    kDevOk = 0,
+    kDevTimeoutFull = 1,   // consumer gave up waiting for a stage to land
+    kDevTimeoutEmpty = 2,  // producer gave up waiting for a stage to be released
+    kDevBadArg = 3,
+    kDevTimeoutGrid = 4,   // a CTA gave up waiting at a grid-wide barrier
+};
+
+
 constexpr int kMaxDevices = 64;
 #ifndef GLC_GEMV_WARPS
 #define GLC_GEMV_WARPS 15

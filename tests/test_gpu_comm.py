@@ -30,6 +30,9 @@ def _need_two_gpus():
 
 def _run(rank, world, uid, fn, errq):
     import faulthandler
+    # No NVLink multicast objects: a rank that the watchdog below ends must not
+    # leave memory bound to one (NCCL reads this when the communicator opens).
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     faulthandler.dump_traceback_later(180, exit=True)
     try:
         sys.path.insert(0, REPO)
