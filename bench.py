@@ -12,9 +12,10 @@ Workload (one "step" = one decode token through one MoE layer):
   ours       : the sm_100a decode-layer kernel (router, gate/up GEMV + SwiGLU,
                grid barrier, down GEMV + weighted combine + residual, all in
                one persistent launch), one launch per step through
-               glc_moe_forward_dev on the step's resident token buffer,
-               16 consecutive steps captured in one CUDA graph that the timed
-               region replays (as a serving loop would);
+               glc_moe_forward_dev on the step's resident token buffer;
+               the timed steps are captured in CUDA graphs that the timed
+               region replays (as a serving loop would): one graph of all
+               the steps up to 512, else graphs of 16 steps + a remainder;
                16 input tokens rotate so consecutive steps route to different
                experts; the 793 MB expert working set is > L2.
   reference  : the CPU port of the reference's CPU path (CpuWarmExpertPoolWorker
@@ -46,6 +47,7 @@ sys.path.insert(0, REPO)
 WORKLOAD = dict(name="mixtral8x7b_moe_layer_decode", D=4096, F=14336, E=8, k=2, T=1, seed=20241201,
                 flags=3)  # GLC_FWD_RMSNORM | GLC_FWD_RESIDUAL
 N_TOKENS = 16
+MAX_ONE_GRAPH = 512  # timed steps captured as one graph up to this many
 BATCH_TOKENS = 64  # the 64-token batch of the same layer (grouped tensor-core path)
 METRIC = "MoE-layer decode tokens/s & Q4_K expert GEMV HBM GB/s vs 8 TB/s, 1/2/4/8 GPU"
 UNIT = "tokens/s"
@@ -147,6 +149,14 @@ def host_result_bytes(T, D, k):
     return 4 * T * D + 8 * T * k + 16
 
 
+def workload_config(w, world):
+    """The config both arms print (same keys and values for the same run)."""
+    return {"workload": w["name"], "hidden": w["D"], "ffn": w["F"], "experts": w["E"], "top_k": w["k"],
+            "tokens_per_step": w["T"], "weights": "Q4_K",
+            "parallelism": f"replica x{world}" if world > 1 else "single",
+            "l2": "inputs larger than L2: 793 MB expert working set, 16 rotating tokens"}
+
+
 def make_tokens(w, n):
     rng = np.random.default_rng(w["seed"])
     return rng.standard_normal((n, w["T"], w["D"])).astype(np.float32)
@@ -210,8 +220,7 @@ def run_reference(args, w):
         "ms_per_step": 1000.0 / value,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q4k-f32",
         "data": "synthetic (seeded generator; no checkpoint offline)",
-        "config": {"workload": w["name"], "hidden": w["D"], "ffn": w["F"], "experts": w["E"],
-                   "top_k": w["k"], "tokens_per_step": w["T"], "weights": "Q4_K"},
+        "config": workload_config(w, int(os.environ.get("WORLD_SIZE", "1"))),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": nthreads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -233,6 +242,9 @@ def run_ours(args, w):
     if world > 1:
         import datetime
         import torch.distributed as dist
+        # no NVLink multicast objects: a rank that dies must not leave memory
+        # bound to one (the exchanges here are point-to-point all-to-alls)
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     from glacier.inference import distributed_b200 as glc
@@ -251,40 +263,67 @@ def run_ours(args, w):
     def step(i):
         worker.forward_dev(0, tokens[i % N_TOKENS].data_ptr(), T, w["flags"], out.data_ptr(), stream=s)
 
-    with torch.cuda.stream(stream):
-        for i in range(args.warmup):
+    # A serving loop replays captured launches.  Up to MAX_ONE_GRAPH steps are
+    # one CUDA graph of exactly `steps` consecutive decode steps (one layer
+    # launch each, token buffers i % 16); more steps replay a graph of 16
+    # steps and one graph of the remainder.  Every timed step is a
+    # graph-replayed launch and every graph is replayed once before timing.
+    for i in range(2):  # first launches (function attributes, tensor maps) outside any capture
+        with torch.cuda.stream(stream):
             step(i)
     torch.cuda.synchronize()
-    worker.poll_error()
-    # A serving loop replays captured launches: one CUDA graph holds N_TOKENS
-    # consecutive decode steps (one layer launch each, token buffers 0..15) and
-    # the timed region replays it, plus direct launches for a remainder.
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        for i in range(N_TOKENS):
-            step(i)
+
+    def capture(n):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(n):
+                step(i)
+        return g
+
+    if args.steps <= MAX_ONE_GRAPH:
+        plan = [(capture(args.steps), 1)]
+    else:
+        plan = [(capture(N_TOKENS), args.steps // N_TOKENS)]
+        if args.steps % N_TOKENS:
+            plan.append((capture(args.steps % N_TOKENS), 1))
+    warm_graph = capture(N_TOKENS)  # for the extra warm-up below
     with torch.cuda.stream(stream):
-        graph.replay()
+        for g, _ in plan:
+            g.replay()
     torch.cuda.synchronize()
     worker.poll_error()
 
-    def timed_steps(n):
-        for _ in range(n // N_TOKENS):
-            graph.replay()
-        for i in range(n % N_TOKENS):
-            step(i)
+    def replay_steps():
+        for g, reps in plan:
+            for _ in range(reps):
+                g.replay()
 
     sampler = ClockSampler(local) if rank == 0 else None
     if sampler:
         sampler.start()
         time.sleep(0.3)
+    # The W warm-up steps run right before the timed region (after the clock
+    # sampler's start-up pause), then the same launches keep the GPU busy for
+    # ~30 ms more (40 replays of 16 steps), so the timed steps do not start on
+    # a GPU that idled.
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i)
+        for _ in range(40):
+            warm_graph.replay()
+    torch.cuda.synchronize()
+    worker.poll_error()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
     with torch.cuda.stream(stream):
+        # an untimed spin kernel (~100 us) ahead of the start event, so the
+        # first timed launch is already queued when the event fires and the
+        # host's launch latency stays out of the timed region
+        torch.cuda._sleep(200000)
         ev0.record(stream)
-        timed_steps(args.steps)
+        replay_steps()
         ev1.record(stream)
     torch.cuda.synchronize()
     if dist:
@@ -352,6 +391,11 @@ def run_ours(args, w):
     del C
 
     batched = measure_batched(torch, worker, w, stream, args) if not args.skip_batched else None
+    qwen = None
+    if not args.skip_qwen:
+        worker.dispose()  # the Qwen layer (1.1 GB) gets the device to itself
+        worker = None
+        qwen = measure_qwen(torch, glc, args, stream, rank == 0 and world == 1 and not args.skip_cpu_baseline)
     ep_leg = measure_ep(torch, dist, glc, w, stream, args, world, rank, local) if dist else None
 
     cpu_baseline = None
@@ -369,12 +413,10 @@ def run_ours(args, w):
             "warmup": args.warmup, "ms_per_step": ms_total / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "q4k-int16dp-f32",
             "data": "synthetic (seeded generator; no checkpoint offline)",
-            "config": {"workload": w["name"], "hidden": D, "ffn": w["F"], "experts": w["E"],
-                       "top_k": w["k"], "tokens_per_step_per_gpu": T, "weights": "Q4_K",
-                       "parallelism": f"replica x{world}" if world > 1 else "single",
-                       "l2": "inputs larger than L2: 793 MB expert working set, 16 rotating tokens",
-                       "submission": "one fused layer launch per step (glc_moe_forward_dev) on the step's resident token buffer, "
-                                     "16 consecutive steps captured in one CUDA graph and replayed"},
+            "config": workload_config(w, world),
+            "submission": "one fused layer launch per step (glc_moe_forward_dev) on the step's resident token "
+                          "buffer; the timed steps are one replayed CUDA graph of all of them (up to 512 steps; "
+                          "more: graphs of 16 steps plus one of the remainder), no direct launch is timed",
             "roofline": {"bound": "hbm", "kernel": "moe_decode_fused_kernel (router + gate/up+SwiGLU + "
                                                       "down+combine, one launch per step)",
                          "achieved": layer_gbs, "peak": peak, "unit": "GB/s", "frac": layer_gbs / peak,
@@ -407,10 +449,13 @@ def run_ours(args, w):
             line["cpu_baseline"] = cpu_baseline
         if batched:
             line["batched_64"] = batched
+        if qwen:
+            line["qwen2_57b"] = qwen
         if ep_leg is not None:
             line["ep"] = ep_leg
         print(json.dumps(line), flush=True)
-    worker.dispose()
+    if worker is not None:
+        worker.dispose()
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -481,6 +526,116 @@ def measure_batched(torch, worker, w, stream, args):
             "kernel_ms": {n: float(v) for n, v in zip(names, kt)}}
 
 
+QWEN = dict(name="qwen2_57b_a14b_moe_layer", D=3584, F=2560, E=64, k=8, Fs=20480, seed=20241202, flags=3)
+QWEN_T = (1, 16, 256)
+
+
+def qwen_host_layer(glc, w, worker):
+    """Host copies of the config's weights for the CPU port: the routed experts
+    and router read back from the device, the shared expert from the same
+    seeded generator (byte-identical to the device's, tested)."""
+    from cuda.bindings import runtime as rt
+    from oracle import oracle as o
+    D, F, E, Fs = w["D"], w["F"], w["E"], w["Fs"]
+    gb, db = E * F * q4k_row_bytes(D), E * D * q4k_row_bytes(F)
+    L = {}
+    for key, ptr, n in zip(("gate", "up", "down", "router"), worker.layer_device_ptrs(0), (gb, gb, db, 4 * D * E)):
+        buf = np.empty(n, np.uint8)
+        err, = rt.cudaMemcpy(buf.ctypes.data, ptr, n, rt.cudaMemcpyKind.cudaMemcpyDeviceToHost)
+        if int(err) != 0:
+            raise RuntimeError(f"device-to-host copy of {key} failed: {err}")
+        L[key] = buf if key != "router" else buf.view(np.float32)
+    L["sh_gate"] = o.synth_q4k(w["seed"], o.expert_tag(65535, 0), Fs, D)
+    L["sh_up"] = o.synth_q4k(w["seed"], o.expert_tag(65535, 1), Fs, D)
+    L["sh_down"] = o.synth_q4k(w["seed"], o.expert_tag(65535, 2), D, Fs)
+    L["sh_gate_vec"] = o.fill_normal(w["seed"], 3, 0.02, D)
+    return o, L
+
+
+def measure_qwen(torch, glc, args, stream, want_cpu):
+    """Qwen2-57B-A14B-shaped MoE layer (hidden 3584, 64 experts top-8 softmax
+    without renormalisation, SwiGLU experts 3584->2560->3584, a sigmoid-gated
+    shared expert 3584->20480->3584, all Q4_K) at token batches of 1, 16 and
+    256: device time per call (four rotating input batches captured in one CUDA
+    graph and replayed), tokens/s, and the HBM roofline of the whole layer
+    call, with algorithmic bytes = distinct experts the batch touches (counted
+    from the ids the call returns) x 15,482,880 B + the shared expert's
+    123,863,040 B + the router + activations."""
+    w = QWEN
+    D, F, E, k, Fs = w["D"], w["F"], w["E"], w["k"], w["Fs"]
+    worker = glc.GpuExpertStageWorker(D, F, E, k, shared_ffn_dim=Fs, renormalize=False, max_tokens=max(QWEN_T))
+    worker.synth_layer(0, w["seed"])
+    s = stream.cuda_stream
+    peak, _ = peaks()
+    expert_bytes = 2 * F * q4k_row_bytes(D) + D * q4k_row_bytes(F)
+    shared_bytes = 2 * Fs * q4k_row_bytes(D) + D * q4k_row_bytes(Fs)
+    legs = {}
+    rng = np.random.default_rng(w["seed"])
+    for T in QWEN_T:
+        xs = [torch.from_numpy(rng.standard_normal((T, D)).astype(np.float32)).cuda() for _ in range(4)]
+        out = torch.empty(T, D, device="cuda")
+        ids = [torch.empty(T, k, dtype=torch.int32, device="cuda") for _ in range(4)]
+        wts = torch.empty(T, k, device="cuda")
+        with torch.cuda.stream(stream):
+            for i in range(4):
+                worker.forward_dev(0, xs[i].data_ptr(), T, w["flags"], out.data_ptr(), ids[i].data_ptr(),
+                                   wts.data_ptr(), stream=s)
+        torch.cuda.synchronize()
+        worker.poll_error()
+        distinct = [len(np.unique(t.cpu().numpy())) for t in ids]
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(4):
+                worker.forward_dev(0, xs[i].data_ptr(), T, w["flags"], out.data_ptr(), stream=s)
+        reps = max(5, min(100, int(2000 // (1 + T // 4))))
+        with torch.cuda.stream(stream):
+            graph.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda._sleep(200000)
+            e0.record(stream)
+            for _ in range(reps):
+                graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / (4 * reps)
+        del graph
+        worker.poll_error()
+        # launches per call and each kernel's share, from the event marks
+        worker.set_profiling(True)
+        with torch.cuda.stream(stream):
+            worker.forward_dev(0, xs[0].data_ptr(), T, w["flags"], out.data_ptr(), stream=s)
+            torch.cuda.synchronize()
+        kt = worker.kernel_times_ms()
+        worker.set_profiling(False)
+        act_bytes = 4 * T * D * 3 + 4 * T * k * (2 * F) + 4 * T * 2 * Fs
+        alg = float(np.mean(distinct)) * expert_bytes + shared_bytes + 4 * D * E + 4 * D + act_bytes
+        gbs = alg / (ms * 1e-3) / 1e9
+        legs[f"T{T}"] = {"workload": f"qwen2_57b_moe_layer_T{T}", "tokens": T, "ms_per_call": ms,
+                         "tokens_per_s": T / (ms * 1e-3), "distinct_experts_mean": float(np.mean(distinct)),
+                         "algorithmic_bytes": alg, "achieved_gbs": gbs, "peak_gbs": peak, "frac": gbs / peak,
+                         "launches_per_call": len(kt), "kernel_ms": [round(v, 4) for v in kt],
+                         "submission": "4 calls (rotating inputs) captured in one CUDA graph and replayed"}
+    cpu = None
+    if want_cpu:
+        o, L = qwen_host_layer(glc, w, worker)
+        nthreads = os.cpu_count() or 1
+        x = make_tokens(dict(w, T=1), 4)
+        outh = np.empty(D, np.float32)
+        n, t0 = 0, time.perf_counter()
+        while n < 2 or time.perf_counter() - t0 < args.cpu_seconds / 3:
+            o.lib().oc_cpu_moe_token_shared_fast(L["gate"], L["up"], L["down"], L["router"], L["sh_gate"],
+                                                 L["sh_up"], L["sh_down"], L["sh_gate_vec"], D, F, E, k, Fs, 0,
+                                                 w["flags"], x[n % 4][0], outh, nthreads)
+            n += 1
+        el = time.perf_counter() - t0
+        cpu = {"value": n / el, "unit": UNIT, "cores": nthreads, "kind": "port",
+               "sample": f"{n} tokens one at a time in {el:.1f} s through the CPU port of the reference CPU "
+                         f"path (routed experts + shared expert), same layer"}
+    worker.dispose()
+    return {"legs": legs, "cpu_baseline": cpu}
+
+
 EP_TOKENS = 8  # decode tokens per rank in the expert-parallel leg
 
 
@@ -534,6 +689,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--skip-cpu-baseline", action="store_true")
     ap.add_argument("--skip-batched", action="store_true")
+    ap.add_argument("--skip-qwen", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -68,6 +68,10 @@ struct LayerDev {
     alignas(64) uint8_t tmap_gate[128];
     alignas(64) uint8_t tmap_up[128];
     alignas(64) uint8_t tmap_down[128];
+    // the shared expert's ([Fs][D/256*144] gate/up, [D][Fs/256*144] down)
+    alignas(64) uint8_t tmap_sh_gate[128];
+    alignas(64) uint8_t tmap_sh_up[128];
+    alignas(64) uint8_t tmap_sh_down[128];
     bool tmaps = false;
 };
 
@@ -85,6 +89,9 @@ int set_last_error(int code, const char* msg) {
 // Device words at the head of a handle's result block: error word, grid-barrier
 // counter and completion counter of the fused decode kernel.
 constexpr int kErrWords = 8;
+// K slices of the shared expert's batched down projection: enough 128-row x
+// slice work items to cover the SMs when a few token groups give few tiles.
+constexpr int kShSlicesMax = 8;
 
 struct glc_moe {
     glc_moe_desc d{};
@@ -100,6 +107,7 @@ struct glc_moe {
     float* act_sh = nullptr;   // [T][Fs]
     float* wts = nullptr;      // [T*k]
     float* gate_out = nullptr; // [T]
+    float* route_logits = nullptr;  // [T][E+1] logits and shared gate of the wide decode kernel
     int* ids = nullptr;        // [T*k]
     int* zeros_i = nullptr;    // [T] expert id 0 for the shared expert
     float* ones = nullptr;     // [T*k] unit combine weights (per-row expert outputs)
@@ -116,6 +124,12 @@ struct glc_moe {
     size_t btiles_bytes = 0;
     float* rscale = nullptr;    // [T*k]
     float* ysort = nullptr;     // [T*k][D]
+    // the shared expert on the batched path: all T tokens as one expert's
+    // groups, its down projection in K slices (partial planes summed by the combine)
+    glc::DispatchPlan plan_sh{};
+    int plan_sh_gmax = 0;
+    float* rscale_sh = nullptr;  // [T]
+    float* ysh = nullptr;        // [kShSlicesMax][T][D]
     // pinned host staging
     float* h_x = nullptr;
     uint8_t* h_res = nullptr;  // pinned (and mapped) copy of the result block
@@ -275,14 +289,62 @@ int make_layer_tmaps(glc_moe* h, LayerDev& L) {
         glc::make_q4k_tensor_map(L.tmap_up, L.up, (long long)El * F, (int)rowbytes(D)) ||
         glc::make_q4k_tensor_map(L.tmap_down, L.down, (long long)El * D, (int)rowbytes(F)))
         return fail(GLC_ERR_CUDA, "cuTensorMapEncodeTiled failed for the expert tensors");
+    const int Fs = h->d.shared_ffn_dim;
+    if (Fs > 0 && (glc::make_q4k_tensor_map(L.tmap_sh_gate, L.sh_gate, Fs, (int)rowbytes(D)) ||
+                   glc::make_q4k_tensor_map(L.tmap_sh_up, L.sh_up, Fs, (int)rowbytes(D)) ||
+                   glc::make_q4k_tensor_map(L.tmap_sh_down, L.sh_down, D, (int)rowbytes(Fs))))
+        return fail(GLC_ERR_CUDA, "cuTensorMapEncodeTiled failed for the shared expert");
     L.tmaps = true;
+    return GLC_OK;
+}
+
+// The shared expert of a batched call (T > 1) on the grouped tensor-core
+// path: all T tokens are one expert's groups, so its weights are read once
+// per launch whatever T is; the down projection (few 128-row tiles at small
+// T) is split into K slices to fill the SMs.  Leaves the slice planes in
+// h->ysh (their count in *slices) for the combine to add with the gate.
+int run_shared_grouped(glc_moe* h, LayerDev* L, const float* xin, int T, int* slices, cudaStream_t st) {
+    const int D = h->d.hidden_dim, Fs = h->d.shared_ffn_dim;
+    if (!L->sh_gate || !L->tmaps) return fail(GLC_ERR_STATE, "layer has no shared expert tensor maps");
+    CUDA_TRY(glc::dispatch_plan_launch(h->zeros_i, T, 1, h->plan_sh, st));
+    mark(h, st);
+    CUDA_TRY(glc::split_rows_launch(xin, T, D, 1, 1, h->plan_sh, h->btiles, h->rscale_sh, st));
+    mark(h, st);
+    const int gsh = (T + glc::kGroupTokens - 1) / glc::kGroupTokens;
+    glc::GroupedParams sg{};
+    sg.K = D;
+    sg.rows_per_e = Fs;
+    sg.nm = 2;
+    sg.num_experts = 1;
+    sg.plan = h->plan_sh;
+    sg.btiles = h->btiles;
+    sg.rscale = h->rscale_sh;
+    sg.out = h->act_sh;
+    sg.err = h->err;
+    CUDA_TRY(glc::grouped_launch(L->tmap_sh_gate, L->tmap_sh_up, sg, gsh * (Fs / 128), h->num_sms, st));
+    mark(h, st);
+    CUDA_TRY(glc::split_rows_launch(h->act_sh, T, Fs, 1, 0, h->plan_sh, h->btiles, h->rscale_sh, st));
+    mark(h, st);
+    const int tiles = gsh * (D / 128);
+    const int n = std::min(std::min(kShSlicesMax, Fs / 256), std::max(1, (h->num_sms + tiles - 1) / tiles));
+    glc::GroupedParams sd = sg;
+    sd.K = Fs;
+    sd.rows_per_e = D;
+    sd.nm = 1;
+    sd.out = h->ysh;
+    sd.ksplit = n;
+    sd.part_stride = (long long)T * D;
+    CUDA_TRY(glc::grouped_launch(L->tmap_sh_down, nullptr, sd, tiles * n, h->num_sms, st));
+    mark(h, st);
+    *slices = n;
     return GLC_OK;
 }
 
 // Batched path (T > 1): dispatch plan, fp16 hi/lo operand tiles, grouped
 // tcgen05 GEMMs (gate/up + SwiGLU, then down), k-ordered weighted combine.
 int run_experts_grouped(glc_moe* h, LayerDev* L, const float* xin, int T, int k, const int* ids,
-                        const float* wts, const float* resid, float* out, cudaStream_t st) {
+                        const float* wts, const float* resid, float* out, cudaStream_t st, bool with_shared) {
+    int rc = GLC_OK;
     const int D = h->d.hidden_dim, F = h->d.expert_ffn_dim, E = local_experts(h);
     const int P = T * k;
     if (!L->tmaps) return fail(GLC_ERR_STATE, "layer has no tensor maps");
@@ -312,7 +374,15 @@ int run_experts_grouped(glc_moe* h, LayerDev* L, const float* xin, int T, int k,
     dn.out = h->ysort;
     CUDA_TRY(glc::grouped_launch(L->tmap_down, nullptr, dn, gmax * (D / 128), h->num_sms, st));
     mark(h, st);
-    CUDA_TRY(glc::combine_launch(h->ysort, T, D, k, h->plan.inv, wts, resid, out, st));
+    const float* ysh = nullptr;
+    int slices = 1;
+    if (with_shared && h->d.shared_ffn_dim > 0) {
+        rc = run_shared_grouped(h, L, xin, T, &slices, st);
+        if (rc) return rc;
+        ysh = h->ysh;
+    }
+    CUDA_TRY(glc::combine_launch(h->ysort, T, D, k, h->plan.inv, wts, resid, out, st, ysh, slices,
+                                 (long long)T * D, h->gate_out));
     mark(h, st);
     return GLC_OK;
 }
@@ -409,6 +479,7 @@ int glc_moe_create(const glc_moe_desc* desc, glc_moe** out) {
     ALLOC(h->act, sizeof(float) * T * k * F);
     if (Fs) ALLOC(h->act_sh, sizeof(float) * T * Fs);
     ALLOC(h->gate_out, sizeof(float) * T);
+    ALLOC(h->route_logits, sizeof(float) * T * (d.num_experts + 1));
     ALLOC(h->zeros_i, sizeof(int) * T);
     ALLOC(h->ones, sizeof(float) * T * k);
     ALLOC(h->ep_keys, sizeof(int) * T * k);
@@ -443,6 +514,25 @@ int glc_moe_create(const glc_moe_desc* desc, glc_moe** out) {
         // B tiles: sum_g N_g <= 2 * (P + 7 * groups) rows, 512 B per row per 256 of K
         const size_t units = 2 * (P + 7 * (size_t)gmax);
         h->btiles_bytes = units * 512 * (size_t)(std::max(D, F) / 256);
+        if (Fs) {  // the shared expert's tiles (T tokens, K up to Fs) reuse the same buffer
+            const int gsh = glc::plan_max_groups((int)T, 1);
+            const size_t units_sh = 2 * (T + 7 * (size_t)gsh);
+            h->btiles_bytes = std::max(h->btiles_bytes, units_sh * 512 * (size_t)(std::max(D, Fs) / 256));
+            h->plan_sh_gmax = gsh;
+            ALLOC(h->plan_sh.counts, sizeof(int));
+            ALLOC(h->plan_sh.offsets, sizeof(int) * 2);
+            ALLOC(h->plan_sh.perm, sizeof(int) * T);
+            ALLOC(h->plan_sh.inv, sizeof(int) * T);
+            ALLOC(h->plan_sh.grp_first, sizeof(int));
+            ALLOC(h->plan_sh.grp_e, sizeof(int) * gsh);
+            ALLOC(h->plan_sh.grp_ntok, sizeof(int) * gsh);
+            ALLOC(h->plan_sh.grp_N, sizeof(int) * gsh);
+            ALLOC(h->plan_sh.grp_pos0, sizeof(int) * gsh);
+            ALLOC(h->plan_sh.grp_units, sizeof(int) * gsh);
+            ALLOC(h->plan_sh.meta, sizeof(int) * 2);
+            ALLOC(h->rscale_sh, sizeof(float) * T);
+            ALLOC(h->ysh, sizeof(float) * kShSlicesMax * T * D);
+        }
         ALLOC(h->btiles, h->btiles_bytes);
         ALLOC(h->rscale, sizeof(float) * P);
         ALLOC(h->ysort, sizeof(float) * P * D);
@@ -482,12 +572,16 @@ int glc_moe_destroy(glc_moe* h) {
     for (auto& g : h->fwd_graphs)
         if (g.exec) cudaGraphExecDestroy(g.exec);
     cudaFree(h->x); cudaFree(h->xin); cudaFree(h->act); cudaFree(h->act_sh);
-    cudaFree(h->gate_out); cudaFree(h->zeros_i); cudaFree(h->res);
+    cudaFree(h->gate_out); cudaFree(h->route_logits); cudaFree(h->zeros_i); cudaFree(h->res);
     cudaFree(h->ones); cudaFree(h->ep_keys);
     cudaFree(h->plan.counts); cudaFree(h->plan.offsets); cudaFree(h->plan.perm); cudaFree(h->plan.inv);
     cudaFree(h->plan.grp_first); cudaFree(h->plan.grp_e); cudaFree(h->plan.grp_ntok); cudaFree(h->plan.grp_N);
     cudaFree(h->plan.grp_pos0); cudaFree(h->plan.grp_units); cudaFree(h->plan.meta);
     cudaFree(h->btiles); cudaFree(h->rscale); cudaFree(h->ysort);
+    cudaFree(h->plan_sh.counts); cudaFree(h->plan_sh.offsets); cudaFree(h->plan_sh.perm); cudaFree(h->plan_sh.inv);
+    cudaFree(h->plan_sh.grp_first); cudaFree(h->plan_sh.grp_e); cudaFree(h->plan_sh.grp_ntok);
+    cudaFree(h->plan_sh.grp_N); cudaFree(h->plan_sh.grp_pos0); cudaFree(h->plan_sh.grp_units);
+    cudaFree(h->plan_sh.meta); cudaFree(h->rscale_sh); cudaFree(h->ysh);
     cudaFreeHost(h->h_x); cudaFreeHost(h->h_res); cudaFreeHost(h->h_sig); cudaFreeHost(h->h_ids); cudaFreeHost(h->h_w);
     if (h->stream) cudaStreamDestroy(h->stream);
     h->disposed = 1;
@@ -686,7 +780,7 @@ namespace {
 // The whole-layer fused decode launch serves this call (T tokens, flags).
 bool fused_applies(const glc_moe* h, int T, uint32_t flags) {
     const bool grouped = (flags & GLC_FWD_BATCHED) ? true : (flags & GLC_FWD_DECODE) ? false : (T > 1);
-    return !grouped && !(flags & GLC_FWD_UNFUSED) && h->d.shared_ffn_dim == 0;
+    return !grouped && !(flags & GLC_FWD_UNFUSED);
 }
 
 // Fused-kernel parameters of a layer; the caller sets x, resid and out.
@@ -704,6 +798,15 @@ glc::FusedDecodeParams fused_params(glc_moe* h, const LayerDev* L, int T, uint32
     fp.ids = h->ids;
     fp.w = h->wts;
     fp.bar = reinterpret_cast<unsigned long long*>(h->err + 2);
+    // the wide kernel (shared expert, or a router too large to stage)
+    fp.route_bar = reinterpret_cast<unsigned long long*>(h->err + 6);
+    fp.route_logits = h->route_logits;
+    fp.Fs = h->d.shared_ffn_dim > 0 ? h->d.shared_ffn_dim : 0;
+    fp.sh_gate = L->sh_gate;
+    fp.sh_up = L->sh_up;
+    fp.sh_down = L->sh_down;
+    fp.sh_gate_vec = L->sh_gate_vec;
+    fp.act_sh = h->act_sh;
     fp.err = h->err;
     fp.T = T;
     fp.D = D;
@@ -773,10 +876,10 @@ int glc_moe_forward_dev(glc_moe* h, int32_t layer, const float* x, int32_t T, ui
     mark(h, st);
     CUDA_TRY(glc::router_launch(rp, st));
     mark(h, st);
-    rc = grouped ? run_experts_grouped(h, L, h->xin, T, k, h->ids, h->wts, resid, out, st)
+    rc = grouped ? run_experts_grouped(h, L, h->xin, T, k, h->ids, h->wts, resid, out, st, true)
                  : run_experts(h, L, h->xin, T, k, h->ids, h->wts, resid, out, st);
     if (rc) return rc;
-    if (h->d.shared_ffn_dim > 0) {
+    if (h->d.shared_ffn_dim > 0 && !grouped) {  // the grouped path ran it already
         rc = run_shared_expert(h, L, h->xin, T, out, st);
         if (rc) return rc;
     }
@@ -849,7 +952,7 @@ int glc_moe_experts_dev(glc_moe* h, int32_t layer, const float* rows, const int3
     const bool grouped = (flags & GLC_FWD_BATCHED) ? true : (flags & GLC_FWD_DECODE) ? false : (R > 1);
     h->n_marks = 0;
     mark(h, st);
-    return grouped ? run_experts_grouped(h, L, rows, R, 1, h->ids, h->ones, nullptr, y_out, st)
+    return grouped ? run_experts_grouped(h, L, rows, R, 1, h->ids, h->ones, nullptr, y_out, st, false)
                    : run_experts(h, L, rows, R, 1, h->ids, h->ones, nullptr, y_out, st);
 }
 
@@ -862,10 +965,21 @@ int glc_moe_combine_dev(glc_moe* h, int32_t layer, const float* y_back, const in
     if (T > h->d.max_tokens) return fail(GLC_ERR_INVALID_ARG, "T=%d exceeds max_tokens=%d", T, h->d.max_tokens);
     LayerDev* L = layer_of(h, layer);
     cudaStream_t st = stream ? (cudaStream_t)stream : h->stream;
-    CUDA_TRY(glc::combine_launch(y_back, T, h->d.hidden_dim, h->d.top_k, inv, w, resid, out, st));
     if (h->d.shared_ffn_dim > 0) {
         if (!L->loaded) return fail(GLC_ERR_STATE, "layer %d has no weights", layer);
         if (!xin) return fail(GLC_ERR_INVALID_ARG, "the shared expert needs xin");
+    }
+    if (h->d.shared_ffn_dim > 0 && T > 1) {
+        // batched: the shared expert on the grouped path, added by the combine
+        int slices = 1;
+        rc = run_shared_grouped(h, L, xin, T, &slices, st);
+        if (rc) return rc;
+        CUDA_TRY(glc::combine_launch(y_back, T, h->d.hidden_dim, h->d.top_k, inv, w, resid, out, st, h->ysh, slices,
+                                     (long long)T * h->d.hidden_dim, h->gate_out));
+        return GLC_OK;
+    }
+    CUDA_TRY(glc::combine_launch(y_back, T, h->d.hidden_dim, h->d.top_k, inv, w, resid, out, st));
+    if (h->d.shared_ffn_dim > 0) {
         rc = run_shared_expert(h, L, xin, T, out, st);
         if (rc) return rc;
     }

@@ -524,6 +524,8 @@ int fused_decode_configure(FusedDecodeParams& p, int num_sms, size_t smem_limit,
 }
 
 cudaError_t fused_decode_launch(const FusedDecodeParams& p0, int num_sms, cudaStream_t stream) {
+    // a shared expert, or a router too large to stage: the wide kernel
+    if (p0.Fs > 0) return wide_decode_launch(p0, num_sms, stream);
     FusedDecodeParams p = p0;
     static int smem_optin[kMaxDevices] = {0};
     int dev = 0;
@@ -542,7 +544,8 @@ cudaError_t fused_decode_launch(const FusedDecodeParams& p0, int num_sms, cudaSt
     }
     size_t smem = 0;
     int grid = 0;
-    if (fused_decode_configure(p, num_sms, (size_t)smem_optin[dev], &smem, &grid) != 0) return cudaErrorNotSupported;
+    if (fused_decode_configure(p, num_sms, (size_t)smem_optin[dev], &smem, &grid) != 0)
+        return wide_decode_launch(p0, num_sms, stream);  // cudaErrorNotSupported when that does not fit either
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kFusedThreads);

@@ -273,6 +273,23 @@ __device__ __forceinline__ void epilogue_item(uint32_t trow, int nm, int ntok, c
     }
 }
 
+// Work item -> (group g, 128-row tile mt, K slice ks) and the K slice's
+// super-blocks [s0, s1).  The K slice is the fastest-varying index; every
+// role of the CTA walks the same items in the same order.
+struct ItemCoords {
+    int g, mt, ks, s0, s1;
+};
+__device__ __forceinline__ ItemCoords item_coords(int item, int mtiles, int ksplit, int nsb) {
+    ItemCoords c;
+    c.ks = item % ksplit;
+    const int r = item / ksplit;
+    c.g = r / mtiles;
+    c.mt = r - c.g * mtiles;
+    c.s0 = (int)((long long)nsb * c.ks / ksplit);
+    c.s1 = (int)((long long)nsb * (c.ks + 1) / ksplit);
+    return c;
+}
+
 __global__ void __launch_bounds__(kTcThreads, 1)
     grouped_q4k_mma_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                            const __grid_constant__ GroupedParams p, int stages) {
@@ -299,7 +316,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int nsb = p.K >> 8;
     const int mtiles = p.rows_per_e >> 7;
     const int ngroups = p.plan.meta[0];
-    const int nitems = ngroups * mtiles;
+    const int ksplit = p.ksplit > 0 ? p.ksplit : 1;
+    const int nitems = ngroups * mtiles * ksplit;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -337,10 +355,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             bool ok = true;
             int it = 0;
             for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
-                const int g = item / mtiles, mt = item - g * mtiles;
-                const int e = p.plan.grp_e[g];
-                const int row0 = e * p.rows_per_e + mt * 128;
-                for (int s = 0; s < nsb; ++s, ++it) {
+                const ItemCoords ic = item_coords(item, mtiles, ksplit, nsb);
+                const int e = p.plan.grp_e[ic.g];
+                const int row0 = e * p.rows_per_e + ic.mt * 128;
+                for (int s = ic.s0; s < ic.s1; ++s, ++it) {
                     const int stg = it % S;
                     const uint32_t ph = (uint32_t)(it / S) & 1u;
                     if (!mbar_wait_backoff(&raw_empty[stg], ph ^ 1u, p.err, kDevTimeoutEmpty, kPollNs)) { ok = false; break; }
@@ -360,10 +378,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             bool ok = true;
             int it = 0;
             for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
-                const int g = item / mtiles;
-                const int N = p.plan.grp_N[g];
-                const uint8_t* bsrc = p.btiles + (size_t)p.plan.grp_units[g] * 512u * nsb;
-                for (int s = 0; s < nsb; ++s, ++it) {
+                const ItemCoords ic = item_coords(item, mtiles, ksplit, nsb);
+                const int N = p.plan.grp_N[ic.g];
+                const uint8_t* bsrc = p.btiles + (size_t)p.plan.grp_units[ic.g] * 512u * nsb;
+                for (int s = ic.s0; s < ic.s1; ++s, ++it) {
                     const int stg = it % kBStages;
                     const uint32_t ph = (uint32_t)(it / kBStages) & 1u;
                     if (!mbar_wait_backoff(&b_empty[stg], ph ^ 1u, p.err, kDevTimeoutEmpty, kPollNs)) { ok = false; break; }
@@ -384,7 +402,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         bool ok = true;
         int it = 0, u = 0;                     // super-block and unit counters over all items
         for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
-            for (int s = 0; s < nsb && ok; ++s, ++it) {
+            const ItemCoords ic = item_coords(item, mtiles, ksplit, nsb);
+            for (int s = ic.s0; s < ic.s1 && ok; ++s, ++it) {
                 const int stg = it % S;
                 const uint32_t ph = (uint32_t)(it / S) & 1u;
                 if (!mbar_wait(&raw_full[stg], ph, p.err, kDevTimeoutFull)) { ok = false; break; }
@@ -440,13 +459,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const int upsb = (nm == 2) ? 2 : 1;
             const uint32_t dcol = tmem + 64u * (uint32_t)v;
             for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x, ++icount) {
-                const int g = item / mtiles;
-                const int N = p.plan.grp_N[g];
+                const ItemCoords ic = item_coords(item, mtiles, ksplit, nsb);
+                const int N = p.plan.grp_N[ic.g];
                 const uint32_t idesc = idesc_f16(N);
                 const uint32_t cstride = (uint32_t)N * 128u;  // bytes between the 4 K chunks of the B tile
                 if (!mbar_wait_backoff(acc_empty, ((uint32_t)icount & 1u) ^ 1u, p.err, kDevTimeoutEmpty, kPollNs)) { ok = false; break; }
                 tc_fence_after();
-                for (int s = 0; s < nsb && ok; ++s, ++it) {
+                for (int s = ic.s0; s < ic.s1 && ok; ++s, ++it) {
                     const int stg = it % kBStages;
                     const uint32_t ph = (uint32_t)(it / kBStages) & 1u;
                     if (!mbar_wait_backoff(&b_full[stg], ph, p.err, kDevTimeoutFull, kPollNs)) { ok = false; break; }
@@ -461,7 +480,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         }
                         tc_fence_after();
                         const int hh = (nm == 2) ? j : v;  // K half of the super-block
-                        const bool first = (s == 0) && (nm == 1 || j == 0);
+                        const bool first = (s == ic.s0) && (nm == 1 || j == 0);
                         const uint32_t acol = tmem + kAccCols + 128u * (uint32_t)slot + 64u * (uint32_t)v;
 #pragma unroll
                         for (int kk = 0; kk < 8; ++kk) {
@@ -490,13 +509,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         bool ok = true;
         int icount = 0;
         for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x, ++icount) {
-            const int g = item / mtiles, mt = item - g * mtiles;
+            const ItemCoords ic = item_coords(item, mtiles, ksplit, nsb);
+            const int g = ic.g, mt = ic.mt;
             const int N = p.plan.grp_N[g];
             const int ntok = p.plan.grp_ntok[g];
             const int pos0 = p.plan.grp_pos0[g];
             if (!mbar_wait_backoff(acc_full, (uint32_t)icount & 1u, p.err, kDevTimeoutFull, kPollNs)) { ok = false; break; }
             tc_fence_after();
-            float* o = p.out + (size_t)pos0 * p.rows_per_e + (size_t)mt * 128 + row;
+            // a K slice writes its partial sums to its own plane of the output
+            float* o = p.out + (size_t)ic.ks * (size_t)p.part_stride + (size_t)pos0 * p.rows_per_e +
+                       (size_t)mt * 128 + row;
             const float* rs = p.rscale + pos0;
             switch (N) {  // hi columns [0, N/2), lo columns [N/2, N) of each accumulator
                 case 16: epilogue_item<8>(trow, nm, ntok, rs, o, p.rows_per_e, acc_empty, lane); break;
@@ -543,6 +565,8 @@ int make_q4k_tensor_map(void* tmap64, const void* base, long long rows, int row_
 cudaError_t grouped_launch(const void* tmapA, const void* tmapB, const GroupedParams& p, int max_items, int num_sms,
                            cudaStream_t st) {
     if ((p.K & 255) || (p.rows_per_e & 127) || (p.nm != 1 && p.nm != 2)) return cudaErrorInvalidValue;
+    // K slices only for the plain projection (the SwiGLU epilogue needs whole sums)
+    if (p.ksplit < 1 || (p.ksplit > 1 && p.nm != 1) || p.ksplit > (p.K >> 8)) return cudaErrorInvalidValue;
     static int optin[kMaxDevices] = {0};
     int dev = 0;
     cudaGetDevice(&dev);

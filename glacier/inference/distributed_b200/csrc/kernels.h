@@ -132,9 +132,25 @@ struct FusedDecodeParams {
     long long wait_limit_ns;
     int stall_cta;
     int T, D, F, E, k, renorm, rmsnorm;
+    // Qwen2-MoE shared expert (Fs > 0): rows [Fs][D/256*144] gate/up,
+    // [D][Fs/256*144] down, gate vector [D]; act_sh [T][Fs] scratch.  A layer
+    // with a shared expert, or whose router does not fit the shared-memory
+    // staging, runs the wide kernel (decode_wide.cu), which also needs
+    // route_logits [T][E+1] scratch and a second grid-barrier counter.
+    const uint8_t* sh_gate;
+    const uint8_t* sh_up;
+    const uint8_t* sh_down;
+    const float* sh_gate_vec;
+    int Fs;
+    float* act_sh;
+    float* route_logits;
+    unsigned long long* route_bar;
     // filled by fused_decode_configure
     int gu_nsegw, gu_G, gu_R, dn_nsegw, dn_G, dn_R, dn_split, stages, slot_bytes;
     int off_xs, off_pgu, off_pdn, off_red, off_logit, off_rms, off_ids, off_w, off_bars;
+    // wide kernel: down-phase lane layout (units of 64 weights per routed slot
+    // / shared row, warps covering them, partial-sum slots per output row)
+    int wide, dn_Ur, dn_Pr, dn_nwr, dn_Us, dn_nws, dn_row_parts;
 };
 // Returns 0 and fills the launch shape when the layer fits the fused kernel
 // (T <= kFusedMaxTokens, E <= 64, router and input staged in shared memory),
@@ -142,6 +158,9 @@ struct FusedDecodeParams {
 int fused_decode_configure(FusedDecodeParams& p, int num_sms, size_t smem_limit, size_t* smem_bytes, int* grid);
 // Returns cudaErrorNotSupported when the layer does not fit (see above).
 cudaError_t fused_decode_launch(const FusedDecodeParams& p, int num_sms, cudaStream_t stream);
+// The wide kernel (decode_wide.cu): same contract.
+int wide_decode_configure(FusedDecodeParams& p, int num_sms, size_t smem_limit, size_t* smem_bytes, int* grid);
+cudaError_t wide_decode_launch(const FusedDecodeParams& p, int num_sms, cudaStream_t stream);
 
 // ---------------------------------------------------------------- batched path
 constexpr int kGroupTokens = 32;  // tokens per MMA group (N = 2*roundup8(ntok) <= 64)
@@ -166,8 +185,11 @@ cudaError_t dispatch_plan_launch(const int* ids, int P, int E, const DispatchPla
 // B tiles: per group, per super-block s of K: [4 chunks][N rows][128 B] SWIZZLE_128B.
 cudaError_t split_rows_launch(const float* src, int P, int K, int kslots, int src_is_token,
                               const DispatchPlan& plan, uint8_t* btiles, float* rscale, cudaStream_t st);
+// out[t] = (resid|0) + sum_j y[inv[t,j]] * w[t,j] in j order, then, with ysh,
+// + (sum of ysh's K-slice planes) * sg[t] (the shared expert).
 cudaError_t combine_launch(const float* y, int T, int D, int k, const int* inv, const float* w,
-                           const float* resid, float* out, cudaStream_t st);
+                           const float* resid, float* out, cudaStream_t st, const float* ysh = nullptr,
+                           int ysh_slices = 1, long long ysh_stride = 0, const float* sg = nullptr);
 
 // Grouped expert GEMM on tcgen05 tensor cores (weights dequantised into TMEM).
 struct GroupedParams {
@@ -178,8 +200,10 @@ struct GroupedParams {
     DispatchPlan plan;
     const uint8_t* btiles;
     const float* rscale;  // [P] power-of-two row scales of the B operand
-    float* out;           // nm=2: act [P][F]; nm=1: y [P][D]
+    float* out;           // nm=2: act [P][F]; nm=1: y [P][D] (K slice ks: out + ks * part_stride)
     int* err;
+    int ksplit = 1;       // nm=1 only: K split into ksplit slices of whole super-blocks,
+    long long part_stride = 0;  // each writing partial sums to its own plane (elements apart)
 };
 // Tensor maps are built once per weight tensor (2-D [rows][rowBytes] uint8, box 144 x 128).
 int make_q4k_tensor_map(void* tmap64, const void* base, long long rows, int row_bytes);

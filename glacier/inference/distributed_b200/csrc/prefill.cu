@@ -140,15 +140,31 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict
     }
 }
 
+// Shared expert term of the combine (Qwen2-MoE): acc = (ysh * sg[t]) + acc
+// after the routed slots, ysh the sum of nslices K-slice planes (slice order).
+struct SharedCombine {
+    const float* ysh;  // [nslices][T][D] or nullptr
+    int nslices;
+    long long stride;  // elements between planes
+    const float* sg;   // [T] sigmoid gate values
+};
+
 __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ y, int D, int k,
                                                       const int* __restrict__ inv, const float* __restrict__ w,
-                                                      const float* __restrict__ resid, float* __restrict__ out) {
+                                                      const float* __restrict__ resid, float* __restrict__ out,
+                                                      SharedCombine sh) {
     const int t = blockIdx.x;
     for (int d = threadIdx.x; d < D; d += 256) {
         float acc = resid ? resid[(size_t)t * D + d] : 0.f;
         for (int j = 0; j < k; ++j) {
             const int pos = inv[t * k + j];
             acc = __fadd_rn(__fmul_rn(y[(size_t)pos * D + d], w[t * k + j]), acc);
+        }
+        if (sh.ysh) {
+            const float* ys = sh.ysh + (size_t)t * D + d;
+            float v = ys[0];
+            for (int s = 1; s < sh.nslices; ++s) v = __fadd_rn(v, ys[(size_t)s * sh.stride]);
+            acc = __fadd_rn(__fmul_rn(v, sh.sg[t]), acc);
         }
         out[(size_t)t * D + d] = acc;
     }
@@ -168,9 +184,11 @@ cudaError_t split_rows_launch(const float* src, int P, int K, int kslots, int sr
 }
 
 cudaError_t combine_launch(const float* y, int T, int D, int k, const int* inv, const float* w, const float* resid,
-                           float* out, cudaStream_t st) {
+                           float* out, cudaStream_t st, const float* ysh, int ysh_slices, long long ysh_stride,
+                           const float* sg) {
     if (T <= 0) return cudaSuccess;
-    combine_kernel<<<T, 256, 0, st>>>(y, D, k, inv, w, resid, out);
+    if (ysh && (ysh_slices < 1 || !sg)) return cudaErrorInvalidValue;
+    combine_kernel<<<T, 256, 0, st>>>(y, D, k, inv, w, resid, out, SharedCombine{ysh, ysh_slices, ysh_stride, sg});
     return cudaGetLastError();
 }
 

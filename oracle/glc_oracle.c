@@ -443,6 +443,23 @@ void oc_cpu_moe_token_fast(const uint8_t* gate_exps, const uint8_t* up_exps,
     }
     free(xin); free(y);
 }
+/* The same token with a Qwen2-MoE shared expert (Fs rows, sigmoid gate over
+ * the normalised input) after the routed experts: out += sigmoid(xin.g) * y_s,
+ * the routed part as above (CPU port, rows split over nthreads). */
+void oc_cpu_moe_token_shared_fast(const uint8_t* gate_exps, const uint8_t* up_exps, const uint8_t* down_exps,
+                                  const float* router_w, const uint8_t* sh_gate, const uint8_t* sh_up,
+                                  const uint8_t* sh_down, const float* sh_gate_vec, int D, int F, int E, int k,
+                                  int Fs, int renorm, int flags, const float* x, float* out, int nthreads) {
+    oc_cpu_moe_token_fast(gate_exps, up_exps, down_exps, router_w, D, F, E, k, renorm, flags, x, out, nthreads);
+    float* xin = (float*)malloc(sizeof(float) * (size_t)D);
+    float* y = (float*)malloc(sizeof(float) * (size_t)D);
+    if (flags & 1) oc_rmsnorm(x, xin, D); else memcpy(xin, x, sizeof(float) * (size_t)D);
+    const float s = oc_dot_canonical(xin, sh_gate_vec, D, 1);
+    const float sg = 1.0f / (1.0f + expf(-s));
+    oc_cpu_expert_forward_fast(sh_gate, sh_up, sh_down, D, Fs, xin, y, nthreads);
+    axpy_unfused(out, y, sg, D);
+    free(xin); free(y);
+}
 
 /* ------------------------------------------------------------------------ */
 /* Wire codecs (QuantizationKernels.cs).                                     */

@@ -76,6 +76,10 @@ void oc_cpu_moe_token_fast(const uint8_t* gate_exps, const uint8_t* up_exps,
                            const uint8_t* down_exps, const float* router_w, int D, int F, int E,
                            int k, int renorm, int flags, const float* x, float* out,
                            int nthreads);
+void oc_cpu_moe_token_shared_fast(const uint8_t* gate_exps, const uint8_t* up_exps, const uint8_t* down_exps,
+                                  const float* router_w, const uint8_t* sh_gate, const uint8_t* sh_up,
+                                  const uint8_t* sh_down, const float* sh_gate_vec, int D, int F, int E, int k,
+                                  int Fs, int renorm, int flags, const float* x, float* out, int nthreads);
 
 /* ---- wire codecs (QuantizationKernels) ---- */
 int oc_wire_token_bytes(int mode, int dim);

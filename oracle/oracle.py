@@ -76,6 +76,9 @@ def lib():
                                                   C.c_int]),
             "oc_cpu_moe_token_fast": (None, [u8p, u8p, u8p, f32p, C.c_int, C.c_int, C.c_int,
                                              C.c_int, C.c_int, C.c_int, f32p, f32p, C.c_int]),
+            "oc_cpu_moe_token_shared_fast": (None, [u8p, u8p, u8p, f32p, u8p, u8p, u8p, f32p, C.c_int,
+                                                    C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                                    f32p, f32p, C.c_int]),
             "oc_wire_token_bytes": (C.c_int, [C.c_int, C.c_int]),
             "oc_quantize_int8": (C.c_float, [f32p, C.c_int, u8p]),
             "oc_dequantize_int8": (None, [u8p, C.c_int, f32p]),
