@@ -107,7 +107,7 @@ struct glc_moe {
     float* act_sh = nullptr;   // [T][Fs]
     float* wts = nullptr;      // [T*k]
     float* gate_out = nullptr; // [T]
-    float* route_logits = nullptr;  // [T][E+1] logits and shared gate of the wide decode kernel
+    unsigned long long* route_slots = nullptr;  // [T][E+1][8] epoch-tagged partial logits of the wide decode kernel
     int* ids = nullptr;        // [T*k]
     int* zeros_i = nullptr;    // [T] expert id 0 for the shared expert
     float* ones = nullptr;     // [T*k] unit combine weights (per-row expert outputs)
@@ -195,6 +195,8 @@ int check_device_error(glc_moe* h) {
         // also clears the fused kernel's barrier and completion counters, which a
         // launch that gave up may leave mid-count, and the host's matching epoch
         cudaMemset(h->err, 0, kErrWords * sizeof(int));
+        // the wide kernel's launch counter restarts, so its tagged slots must too
+        cudaMemset(h->route_slots, 0, sizeof(unsigned long long) * h->d.max_tokens * (h->d.num_experts + 1) * 8);
         h->host_epoch = 0;
         if (h->h_sig) h->h_sig[0] = h->h_sig[1] = 0;
         if (code == glc::kDevBadArg)
@@ -479,7 +481,7 @@ int glc_moe_create(const glc_moe_desc* desc, glc_moe** out) {
     ALLOC(h->act, sizeof(float) * T * k * F);
     if (Fs) ALLOC(h->act_sh, sizeof(float) * T * Fs);
     ALLOC(h->gate_out, sizeof(float) * T);
-    ALLOC(h->route_logits, sizeof(float) * T * (d.num_experts + 1));
+    ALLOC(h->route_slots, sizeof(unsigned long long) * T * (d.num_experts + 1) * 8);
     ALLOC(h->zeros_i, sizeof(int) * T);
     ALLOC(h->ones, sizeof(float) * T * k);
     ALLOC(h->ep_keys, sizeof(int) * T * k);
@@ -572,7 +574,7 @@ int glc_moe_destroy(glc_moe* h) {
     for (auto& g : h->fwd_graphs)
         if (g.exec) cudaGraphExecDestroy(g.exec);
     cudaFree(h->x); cudaFree(h->xin); cudaFree(h->act); cudaFree(h->act_sh);
-    cudaFree(h->gate_out); cudaFree(h->route_logits); cudaFree(h->zeros_i); cudaFree(h->res);
+    cudaFree(h->gate_out); cudaFree(h->route_slots); cudaFree(h->zeros_i); cudaFree(h->res);
     cudaFree(h->ones); cudaFree(h->ep_keys);
     cudaFree(h->plan.counts); cudaFree(h->plan.offsets); cudaFree(h->plan.perm); cudaFree(h->plan.inv);
     cudaFree(h->plan.grp_first); cudaFree(h->plan.grp_e); cudaFree(h->plan.grp_ntok); cudaFree(h->plan.grp_N);
@@ -800,7 +802,7 @@ glc::FusedDecodeParams fused_params(glc_moe* h, const LayerDev* L, int T, uint32
     fp.bar = reinterpret_cast<unsigned long long*>(h->err + 2);
     // the wide kernel (shared expert, or a router too large to stage)
     fp.route_bar = reinterpret_cast<unsigned long long*>(h->err + 6);
-    fp.route_logits = h->route_logits;
+    fp.route_slots = h->route_slots;
     fp.Fs = h->d.shared_ffn_dim > 0 ? h->d.shared_ffn_dim : 0;
     fp.sh_gate = L->sh_gate;
     fp.sh_up = L->sh_up;

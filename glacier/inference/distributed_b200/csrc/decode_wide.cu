@@ -10,23 +10,28 @@
 // plus the shared expert of the model code.
 //
 // Layout of one launch (one CTA per SM, all resident, 16 warps):
-//   warp 15 (router): CTA c < E computes the logit of expert c for every
-//     token, CTA E the shared-expert gate, in the canonical reduction order of
-//     router.cu (256 strided fused partials -- here 8 virtual warps of one
-//     real warp, each lane running 8 of the partial chains -- a xor
-//     butterfly per virtual warp, a pairwise tree over the 8), and stores it
-//     in route_logits; every CTA's router warp then meets at a grid-wide
-//     arrival counter, reads all logits, ranks the experts (ties to the lower
-//     index, NaN as -inf) and forms the softmax weights exactly as router.cu,
-//     so ids and weights are bit-identical to it.
+//   warp 15 (router): CTAs 2c and 2c + 1 compute the logit of expert c (the
+//     shared-expert gate as column E) for every token in the canonical
+//     reduction order of router.cu (256 strided fused partials -- here
+//     virtual warps of one real warp, each lane running 4 of the partial
+//     chains -- a xor butterfly per virtual warp, a pairwise tree over the
+//     8), publishing the 8 virtual-warp sums as epoch-tagged 64-bit slots;
+//     every CTA's router warp reads them (one memory round trip), ranks the
+//     experts (ties to the lower index, NaN as -inf) and forms the softmax
+//     weights exactly as router.cu, so ids and weights are bit-identical to it.
+//     Its router column is loaded before the weight stream fills the memory
+//     system: under a saturated stream every later memory round trip costs
+//     several microseconds.
 //   warp 14 (producer): streams this CTA's share of the SHARED expert's
 //     gate/up rows first -- they do not depend on the routing, so the weight
 //     stream starts at once and the routing is hidden behind it -- then,
 //     once its router warp has the ids, its share of the routed experts'
 //     gate/up rows, then the down-projection rows.  cp.async.bulk into a ring
 //     of shared-memory stages on mbarriers, L2 evict-first, no multicast.
-//   warps 0..13 (consumers): RMSNorm of the input, gate/up GEMV + SwiGLU (the
-//     lane math of gemv_lane.cuh), activations to global memory; grid
+//   warps 0..13 (consumers): gate/up GEMV of the raw input (the lane math of
+//     gemv_lane.cuh quantises each 32-block by its own maximum, so the norm
+//     scale factors out of every row sum and is applied in the SwiGLU
+//     epilogue), activations to global memory; grid
 //     barrier; down projection: every output row is read as k routed slots
 //     of F/64 lane units each plus the shared row of Fs/64 units, one lane per
 //     unit (Qwen2-57B: 8 x 40 = 320 = 10 warps, and 320 for the shared row),
@@ -56,31 +61,6 @@ __device__ __forceinline__ int xs_index_w(int d, int U) {
     return (((d & 63) >> 2) * (U + 1) + (d >> 6)) * 4 + (d & 3);
 }
 
-// Canonical sum over d of f(d) for one token with ONE warp: lane l runs the
-// partial chains of the 8 "threads" l + 32w (w = 0..7) of the 256-thread
-// order (d = tid, tid + 256, ... in increasing d, fused multiply-adds), each
-// virtual warp's partials are reduced by the xor butterfly (warp_tree8 keeps
-// every value on the same lane pairs as warp_tree), and the 8 sums by tree8.
-// Every lane returns the result.
-template <class Term>
-__device__ __forceinline__ float canonical_warp_sum(int D, int lane, Term&& term) {
-    float a[8];
-#pragma unroll
-    for (int w = 0; w < 8; ++w) a[w] = 0.f;
-    for (int d0 = 0; d0 < D; d0 += kRouterThreadsC) {
-#pragma unroll
-        for (int w = 0; w < 8; ++w) {
-            const int d = d0 + 32 * w + lane;
-            if (d < D) a[w] = term(d, a[w]);
-        }
-    }
-    const float v = warp_tree8(a, lane);  // lane L: sum of virtual warp (L >> 2) & 7
-    float s[8];
-#pragma unroll
-    for (int w = 0; w < 8; ++w) s[w] = __shfl_sync(0xffffffffu, v, 4 * w);
-    return tree8(s);
-}
-
 __device__ __forceinline__ float rms_scale(float ss, int D) {
     return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), 1e-5f)));
 }
@@ -103,6 +83,8 @@ __global__ void __launch_bounds__(kWThreads, 1) moe_decode_wide_kernel(const __g
     uint64_t* empty = full + S;
     uint64_t* route_mb = empty + S;  // the router warp's ids are in shared memory
     uint64_t* go_bar = route_mb + 1;  // the producer has issued its first ring's worth of stages
+    uint64_t* xbar = go_bar + 1;      // the raw input has landed in shared memory
+    float* xraw = reinterpret_cast<float*>(smem + p.off_red);  // [T][D] raw input
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int T = p.T, D = p.D, F = p.F, Fs = p.Fs, k = p.k, E = p.E;
@@ -117,9 +99,14 @@ __global__ void __launch_bounds__(kWThreads, 1) moe_decode_wide_kernel(const __g
         }
         mbar_init(route_mb, 1);
         mbar_init(go_bar, 1);
+        mbar_init(xbar, 1);
         fence_mbar_init();
         s_ok = 1;
         s_route_ok = 1;
+        // the layer input in one bulk copy (the RMSNorm and the router read it)
+        const uint32_t xb = (uint32_t)(p.T * p.D * 4);
+        mbar_arrive_expect_tx(xbar, xb);
+        bulk_g2s_nohint(xraw, p.x, xb, xbar);
     }
     __syncthreads();
 
@@ -147,81 +134,173 @@ __global__ void __launch_bounds__(kWThreads, 1) moe_decode_wide_kernel(const __g
 
     if (warp == kWRouter) {
         // ------------------------------------------------------- router warp
+        // Two CTAs per router column (expert c, or the shared gate as column
+        // E): CTA 2c + h computes the partial sums of the 4 virtual warps
+        // 4h .. 4h + 3 of the canonical 256-thread order (thread tid = 32 w +
+        // lane runs d = tid, tid + 256, ... increasing, fused multiply-adds),
+        // each reduced by the xor butterfly, and publishes them tagged with
+        // the launch's epoch; every router warp then reads the 8 virtual-warp
+        // sums of every column and adds them by the pairwise tree -- the
+        // logits of router.cu bit for bit.  The router column is loaded before
+        // the weight stream fills the memory system; the RMSNorm scale comes
+        // from the staged input in shared memory.
         const bool has_gate = Fs > 0 && p.sh_gate_vec != nullptr;
-        const int col = b;  // expert col (col < E) or the shared gate (col == E)
-        if (col < E || (col == E && has_gate)) {
-            for (int t = 0; t < T; ++t) {
-                const float* xt = p.x + (size_t)t * D;
-                float rms = 1.0f;
-                if (p.rmsnorm)
-                    rms = rms_scale(canonical_warp_sum(D, lane, [&](int d, float a) {
-                                        const float v = __ldg(xt + d);
-                                        return fmaf(v, v, a);
-                                    }), D);
-                const float* wc = col < E ? p.Wr + col : p.sh_gate_vec;
-                const size_t ws = col < E ? (size_t)E : 1;
-                const float lg = canonical_warp_sum(D, lane, [&](int d, float a) {
-                    const float raw = __ldg(xt + d);
-                    const float xv = p.rmsnorm ? __fmul_rn(raw, rms) : raw;
-                    return fmaf(xv, __ldg(wc + (size_t)d * ws), a);
-                });
-                if (lane == 0) p.route_logits[(size_t)t * (E + 1) + col] = lg;
-            }
-        }
-        __syncwarp();
+        const int ncols = E + (has_gate ? 1 : 0);
+        const int col = b >> 1, half = b & 1;
+        unsigned long long prev = 0;
+        if (lane == 0) prev = atomicAdd(p.route_bar, 1ull);
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        const unsigned long long epoch = (prev / (unsigned long long)G + 1ull) & 0xFFFFFFFFull;
         bool rok = true;
-        if (lane == 0) rok = grid_barrier(p.route_bar, gridDim.x, p.err, lim);
-        rok = __shfl_sync(0xffffffffu, rok ? 1 : 0, 0) != 0;
-        if (rok) {
-            for (int t = 0; t < T; ++t) {
-                const float* lg = p.route_logits + (size_t)t * (E + 1);
-                const int ea = lane, eb = lane + 32;
-                const float la = ea < E ? __ldcg(lg + ea) : 0.f, lb = eb < E ? __ldcg(lg + eb) : 0.f;
-                const float va = (ea < E && !isnan(la)) ? la : -INFINITY;
-                const float vb = (eb < E && !isnan(lb)) ? lb : -INFINITY;
-                int ra = 0, rb = 0;
-                for (int e = 0; e < E; ++e) {
-                    const float le = __shfl_sync(0xffffffffu, e < 32 ? la : lb, e & 31);
-                    const float v = isnan(le) ? -INFINITY : le;
-                    ra += (v > va || (v == va && e < ea)) ? 1 : 0;
-                    rb += (v > vb || (v == vb && e < eb)) ? 1 : 0;
-                }
-                if (ea < E && ra < k) s_rank[ra] = ea;
-                if (eb < E && rb < k) s_rank[rb] = eb;
-                __syncwarp();
-                const int first = s_rank[0];
-                const float lf = first < 32 ? __shfl_sync(0xffffffffu, la, first) : __shfl_sync(0xffffffffu, lb, first - 32);
-                const float mx = isnan(lf) ? -INFINITY : lf;
-                if (ea < E) s_ex[ea] = expf(la - mx);
-                if (eb < E) s_ex[eb] = expf(lb - mx);
-                __syncwarp();
-                float den = 0.f;
-                if (lane == 0) {
-                    if (p.renorm) {
-                        for (int j = 0; j < k; ++j) den += s_ex[s_rank[j]];
-                    } else {
-#pragma unroll 8
-                        for (int e = 0; e < E; ++e) den += s_ex[e];
+        if (col < ncols) {
+            constexpr int kRS = 14;  // d-steps of 256 held in registers per batch
+            const float* wc = col < E ? p.Wr + col : p.sh_gate_vec;
+            const size_t ws = col < E ? (size_t)E : 1;
+            const int nsteps = D >> 8;
+            float a[kFusedMaxTokens][4];
+#pragma unroll
+            for (int t = 0; t < kFusedMaxTokens; ++t)
+#pragma unroll
+                for (int w = 0; w < 4; ++w) a[t][w] = 0.f;
+            float rms[kFusedMaxTokens];
+            for (int s0 = 0; s0 < nsteps; s0 += kRS) {
+                float wv[kRS][4];
+#pragma unroll
+                for (int s = 0; s < kRS; ++s)
+#pragma unroll
+                    for (int w = 0; w < 4; ++w) {
+                        const int d = (s0 + s) * 256 + 32 * (4 * half + w) + lane;
+                        wv[s][w] = (s0 + s < nsteps) ? __ldg(wc + (size_t)d * ws) : 0.f;
+                    }
+                if (s0 == 0) {
+                    // the input has landed: RMSNorm scale of every token, canonical
+                    if (!mbar_wait(xbar, 0, p.err, kDevTimeoutFull, lim)) { rok = false; break; }
+#pragma unroll
+                    for (int t = 0; t < kFusedMaxTokens; ++t) {
+                        rms[t] = 1.0f;
+                        if (t < T && p.rmsnorm) {
+                            float q[8];
+#pragma unroll
+                            for (int w = 0; w < 8; ++w) q[w] = 0.f;
+                            for (int s = 0; s < nsteps; ++s)
+#pragma unroll
+                                for (int w = 0; w < 8; ++w) {
+                                    const float v = xraw[(size_t)t * D + s * 256 + 32 * w + lane];
+                                    q[w] = fmaf(v, v, q[w]);
+                                }
+                            const float v = warp_tree8(q, lane);
+                            float sw[8];
+#pragma unroll
+                            for (int w = 0; w < 8; ++w) sw[w] = __shfl_sync(0xffffffffu, v, 4 * w);
+                            rms[t] = rms_scale(tree8(sw), D);
+                        }
                     }
                 }
-                den = __shfl_sync(0xffffffffu, den, 0);
-                if (lane < k) {
-                    const int id = s_rank[lane];
-                    const float wv = s_ex[id] / den;
-                    s_ids[t * k + lane] = id;
-                    s_w[t * k + lane] = wv;
-                    if (b == 0) {
-                        p.ids[t * k + lane] = id;
-                        p.w[t * k + lane] = wv;
-                    }
-                }
-                if (lane == 0)
-                    s_sg[t] = has_gate ? 1.0f / (1.0f + expf(-__ldcg(lg + E))) : 0.f;
-                __syncwarp();
+#pragma unroll
+                for (int s = 0; s < kRS; ++s)
+                    if (s0 + s < nsteps)
+#pragma unroll
+                        for (int t = 0; t < kFusedMaxTokens; ++t)
+                            if (t < T)
+#pragma unroll
+                                for (int w = 0; w < 4; ++w) {
+                                    const float raw = xraw[(size_t)t * D + (s0 + s) * 256 + 32 * (4 * half + w) + lane];
+                                    const float xv = p.rmsnorm ? __fmul_rn(raw, rms[t]) : raw;
+                                    a[t][w] = fmaf(xv, wv[s][w], a[t][w]);
+                                }
             }
-        } else if (lane == 0) {
-            s_route_ok = 0;
+            if (rok) {
+#pragma unroll
+                for (int t = 0; t < kFusedMaxTokens; ++t)
+                    if (t < T) {
+                        // zeros in values 4..7: lanes 4w (w < 4) hold virtual warp 4 half + w's sum
+                        const float a8[8] = {a[t][0], a[t][1], a[t][2], a[t][3], 0.f, 0.f, 0.f, 0.f};
+                        const float v = warp_tree8(a8, lane);
+                        if ((lane & 3) == 0 && lane < 16) {
+                            const unsigned long long tagged = (epoch << 32) | (unsigned long long)__float_as_uint(v);
+                            unsigned long long* slot_p =
+                                p.route_slots + ((size_t)t * (E + 1) + col) * 8 + 4 * half + (lane >> 2);
+                            asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(slot_p), "l"(tagged) : "memory");
+                        }
+                    }
+            }
         }
+        // every column's 8 partial sums of this launch, then the top-k.  Each
+        // 64-bit slot holds the epoch and the value together, so relaxed
+        // loads suffice, and all of a lane's columns are polled in one loop
+        // (one memory round trip when they are ready).
+        const uint64_t t0 = global_timer_ns();
+        for (int t = 0; t < T && rok; ++t) {
+            const int ca = lane, cb = lane + 32;
+            const unsigned long long* base = p.route_slots + (size_t)t * (E + 1) * 8;
+            const bool wa = ca < E, wb = cb < E, wg = lane == 0 && has_gate;
+            float sa[8], sb[8], sg8[8];
+            bool got = false;
+            while (true) {
+                bool all = true;
+#pragma unroll
+                for (int w = 0; w < 8; ++w) {
+                    unsigned long long va = 0, vb = 0, vg = 0;
+                    if (wa) asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(va) : "l"(base + (size_t)ca * 8 + w) : "memory");
+                    if (wb) asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(vb) : "l"(base + (size_t)cb * 8 + w) : "memory");
+                    if (wg) asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(vg) : "l"(base + (size_t)E * 8 + w) : "memory");
+                    all = all && (!wa || (va >> 32) == epoch) && (!wb || (vb >> 32) == epoch) && (!wg || (vg >> 32) == epoch);
+                    sa[w] = __uint_as_float((uint32_t)va);
+                    sb[w] = __uint_as_float((uint32_t)vb);
+                    sg8[w] = __uint_as_float((uint32_t)vg);
+                }
+                if (all) { got = true; break; }
+                if (global_timer_ns() - t0 > lim) break;
+            }
+            if (!__all_sync(0xffffffffu, got)) {
+                if (lane == 0) atomicExch(p.err, kDevTimeoutGrid);
+                rok = false;
+                break;
+            }
+            const float la = wa ? tree8(sa) : 0.f, lb = wb ? tree8(sb) : 0.f, lg = wg ? tree8(sg8) : 0.f;
+            const int ea = ca, eb = cb;
+            const float va = (ea < E && !isnan(la)) ? la : -INFINITY;
+            const float vb = (eb < E && !isnan(lb)) ? lb : -INFINITY;
+            int ra = 0, rb = 0;
+            for (int e = 0; e < E; ++e) {
+                const float le = __shfl_sync(0xffffffffu, e < 32 ? la : lb, e & 31);
+                const float v = isnan(le) ? -INFINITY : le;
+                ra += (v > va || (v == va && e < ea)) ? 1 : 0;
+                rb += (v > vb || (v == vb && e < eb)) ? 1 : 0;
+            }
+            if (ea < E && ra < k) s_rank[ra] = ea;
+            if (eb < E && rb < k) s_rank[rb] = eb;
+            __syncwarp();
+            const int first = s_rank[0];
+            const float lf = first < 32 ? __shfl_sync(0xffffffffu, la, first) : __shfl_sync(0xffffffffu, lb, first - 32);
+            const float mx = isnan(lf) ? -INFINITY : lf;
+            if (ea < E) s_ex[ea] = expf(la - mx);
+            if (eb < E) s_ex[eb] = expf(lb - mx);
+            __syncwarp();
+            float den = 0.f;
+            if (lane == 0) {
+                if (p.renorm) {
+                    for (int j = 0; j < k; ++j) den += s_ex[s_rank[j]];
+                } else {
+#pragma unroll 8
+                    for (int e = 0; e < E; ++e) den += s_ex[e];
+                }
+            }
+            den = __shfl_sync(0xffffffffu, den, 0);
+            if (lane < k) {
+                const int id = s_rank[lane];
+                const float wv = s_ex[id] / den;
+                s_ids[t * k + lane] = id;
+                s_w[t * k + lane] = wv;
+                if (b == 0) {
+                    p.ids[t * k + lane] = id;
+                    p.w[t * k + lane] = wv;
+                }
+            }
+            if (lane == 0) s_sg[t] = has_gate ? 1.0f / (1.0f + expf(-lg)) : 0.f;
+            __syncwarp();
+        }
+        if (!rok && lane == 0) s_route_ok = 0;
         __syncwarp();
         if (lane == 0) mbar_arrive(route_mb);
         return;
@@ -298,40 +377,16 @@ __global__ void __launch_bounds__(kWThreads, 1) moe_decode_wide_kernel(const __g
     }
 
     // -------------------------------------------------------- consumer warps
-    // RMSNorm scale of every token (canonical: 256 strided partials, warp
-    // butterfly, pairwise tree) and the normalised input in the padded
-    // chunk-major layout the gate/up lanes read.
+    // The RAW input in the padded chunk-major layout the gate/up lanes read:
+    // the lanes quantise it per 32-block (scale-free, so x and x * rms give
+    // the same integers up to rounding) and the RMSNorm scale, a factor of
+    // every gate/up row sum, is applied in the SwiGLU epilogue -- the weight
+    // stream does not wait for the norm.
     {
         const int U = D >> 6;
-        if (tid < kRouterThreadsC) {
-            float a[kFusedMaxTokens];
-#pragma unroll
-            for (int t = 0; t < kFusedMaxTokens; ++t) a[t] = 0.f;
-            if (p.rmsnorm) {
-                for (int d = tid; d < D; d += kRouterThreadsC)
-#pragma unroll
-                    for (int t = 0; t < kFusedMaxTokens; ++t)
-                        if (t < T) {
-                            const float v = __ldg(p.x + (size_t)t * D + d);
-                            a[t] = fmaf(v, v, a[t]);
-                        }
-#pragma unroll
-                for (int t = 0; t < kFusedMaxTokens; ++t)
-                    if (t < T) {
-                        const float v = warp_tree(a[t]);
-                        if (lane == 0) s_red[t * 8 + warp] = v;
-                    }
-            }
-        }
-        named_bar_sync(1, kWNT);
-        if (tid < T) s_rms[tid] = p.rmsnorm ? rms_scale(tree8(s_red + tid * 8), D) : 1.0f;
-        named_bar_sync(1, kWNT);
-        for (int i = tid; i < T * D; i += kWNT) {
-            const int t = i / D, d = i - t * D;
-            const float raw = __ldg(p.x + i);
-            xs[(size_t)t * (D + 64) + xs_index_w(d, U)] = p.rmsnorm ? __fmul_rn(raw, s_rms[t]) : raw;
-            if (b == 0 && p.xin) p.xin[i] = p.rmsnorm ? __fmul_rn(raw, s_rms[t]) : raw;
-        }
+        if (!mbar_wait_spin(xbar, 0, p.err, kDevTimeoutFull, lim)) s_ok = 0;
+        for (int t = 0; t < T; ++t)
+            for (int d = tid; d < D; d += kWNT) xs[(size_t)t * (D + 64) + xs_index_w(d, U)] = xraw[(size_t)t * D + d];
         named_bar_sync(1, kWNT);
     }
     // residual of this thread's first output row, loaded ahead of the end
@@ -371,7 +426,31 @@ __global__ void __launch_bounds__(kWThreads, 1) moe_decode_wide_kernel(const __g
                                   [&](int sidx, int seg, int, int, int nr, int lr0) { consume(sidx, seg / k, nr, nsh + lr0); });
     }
     if (!ok) s_ok = 0;
+    // RMSNorm scale of every token (canonical: 256 strided partials, warp
+    // butterfly, pairwise tree), from the staged input
+    if (tid < kRouterThreadsC && p.rmsnorm) {
+        float a[kFusedMaxTokens];
+#pragma unroll
+        for (int t = 0; t < kFusedMaxTokens; ++t) a[t] = 0.f;
+        for (int d = tid; d < D; d += kRouterThreadsC)
+#pragma unroll
+            for (int t = 0; t < kFusedMaxTokens; ++t)
+                if (t < T) {
+                    const float v = xraw[(size_t)t * D + d];
+                    a[t] = fmaf(v, v, a[t]);
+                }
+#pragma unroll
+        for (int t = 0; t < kFusedMaxTokens; ++t)
+            if (t < T) {
+                const float v = warp_tree(a[t]);
+                if (lane == 0) s_red[t * 8 + warp] = v;
+            }
+    }
     named_bar_sync(1, kWNT);
+    if (tid < T) s_rms[tid] = p.rmsnorm ? rms_scale(tree8(s_red + tid * 8), D) : 1.0f;
+    named_bar_sync(1, kWNT);
+    if (b == 0 && p.xin)
+        for (int i = tid; i < T * D; i += kWNT) p.xin[i] = p.rmsnorm ? __fmul_rn(xraw[i], s_rms[i / D]) : xraw[i];
     {
         const int nsegw = p.gu_nsegw;
         const int nrow = nsh + (r1 - r0);
@@ -379,6 +458,9 @@ __global__ void __launch_bounds__(kWThreads, 1) moe_decode_wide_kernel(const __g
             const float* pp = pgu + (size_t)lr * 2 * nsegw;
             float gs = 0.f, us = 0.f;
             for (int q = 0; q < nsegw; ++q) { gs += pp[q]; us += pp[nsegw + q]; }
+            const int tok = lr < nsh ? (sh0 + lr) / Fs : (r0 + (lr - nsh)) / F / k;
+            gs = __fmul_rn(gs, s_rms[tok]);  // the row sums of the raw input, scaled by the norm
+            us = __fmul_rn(us, s_rms[tok]);
             const float a = (gs / (1.0f + expf(-gs))) * us;
             if (lr < nsh) {
                 const int g = sh0 + lr, t = g / Fs, rin = g - t * Fs;
@@ -409,6 +491,18 @@ __global__ void __launch_bounds__(kWThreads, 1) moe_decode_wide_kernel(const __g
     }
 
     const int PR = p.dn_row_parts;
+    // The shared row's lanes: unit L of Fs / 64 (its activations are loaded
+    // when its sub-phase starts: holding both sets of activations at once
+    // would not fit the registers).
+    const int Us = p.dn_Us;
+    const int Ls = warp * 32 + lane;
+    const bool act_s = Fs > 0 && warp < p.dn_nws && Ls < Us;
+    XRegs xr_s;
+    int cur_s = -1;
+    auto load_shared_x = [&](int t) {
+        load_x<kXGlobalCG>(xr_s, reinterpret_cast<const float4*>(p.act_sh + (size_t)t * Fs) + (act_s ? Ls : 0), Us, act_s);
+        cur_s = t;
+    };
     {  // ---- down projection, routed slots: lane unit L -> slot L / Ur, unit L % Ur
         const int Ur = p.dn_Ur, Pr = p.dn_Pr;
         const int L = warp * 32 + lane;
@@ -458,25 +552,16 @@ __global__ void __launch_bounds__(kWThreads, 1) moe_decode_wide_kernel(const __g
         });
     }
     if (Fs > 0) {  // ---- down projection, the shared row: lane unit L of Fs / 64
-        const int Us = p.dn_Us;
-        const int L = warp * 32 + lane;
         const bool wact = warp < p.dn_nws;
-        const bool active = wact && L < Us;
-        const int sb = active ? (L >> 2) : 0, c = L & 3;
-        XRegs xr;
-        int cur = -1;
+        const int sb = act_s ? (Ls >> 2) : 0, c = Ls & 3;
         for_each_stage_rows(D, 1, p.dn_R, q0, q1, nxt, [&](int sidx, int t, int, int, int nr, int lr0) {
             if (!ok) return;
-            if (t != cur) {
-                load_x<kXGlobalCG>(xr, reinterpret_cast<const float4*>(p.act_sh + (size_t)t * Fs) + (active ? L : 0), Us,
-                                   active);
-                cur = t;
-            }
+            if (t != cur_s) load_shared_x(t);
             const int buf = sidx % S;
             const uint32_t ph = (uint32_t)(sidx / S) & 1u;
             if (!mbar_wait_spin(&full[buf], ph, p.err, kDevTimeoutFull, lim)) { ok = false; return; }
             if (wact)
-                consume_stage(smem + (size_t)buf * slot, nr, p.dn_R, 1, 1, 0, rbS, sb, c, active, xr, lane,
+                consume_stage(smem + (size_t)buf * slot, nr, p.dn_R, 1, 1, 0, rbS, sb, c, act_s, xr_s, lane,
                               [&](int i, int, float v) { pdn[(size_t)(lr0 + i) * PR + k * p.dn_Pr + warp] = v; });
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[buf]);
@@ -522,14 +607,13 @@ size_t align16w(size_t v) { return (v + 15) & ~size_t(15); }
 int wide_decode_configure(FusedDecodeParams& p, int num_sms, size_t smem_limit, size_t* smem_bytes, int* grid) {
     const int T = p.T, D = p.D, F = p.F, E = p.E, k = p.k, Fs = p.Fs;
     if (T < 1 || T > kFusedMaxTokens || E < 1 || E > 64 || k < 1 || k > kWMaxK || k > E) return -1;
-    if (D <= 0 || F <= 0 || (D & 255) || (F & 255) || Fs < 0 || (Fs & 255) || num_sms < E + 1) return -1;
-    if (!p.gate || !p.up || !p.down || !p.act || !p.out || !p.ids || !p.w || !p.bar || !p.route_bar || !p.route_logits)
+    if (D <= 0 || F <= 0 || (D & 255) || (F & 255) || Fs < 0 || (Fs & 255) || num_sms < 2 * (E + 1)) return -1;
+    if (!p.gate || !p.up || !p.down || !p.act || !p.out || !p.ids || !p.w || !p.bar || !p.route_bar || !p.route_slots)
         return -1;
     if (Fs > 0 && (!p.sh_gate || !p.sh_up || !p.sh_down || !p.sh_gate_vec || !p.act_sh)) return -1;
     // gate/up lanes: D/64 units per row, whole warps per row
     const int gu_nsegw = ((D >> 6) + 31) / 32;
     if (gu_nsegw > kWConsumerWarps) return -1;
-    const int gu_G = kWConsumerWarps / gu_nsegw;
     // down lanes: k slots of F/64 units (each slot at least a warp wide, so a
     // warp holds parts of at most two slots) and the shared row's Fs/64 units
     const int Ur = F >> 6, Us = Fs >> 6;
@@ -540,22 +624,43 @@ int wide_decode_configure(FusedDecodeParams& p, int num_sms, size_t smem_limit, 
     for (int j = 0; j < k; ++j) Pr = std::max(Pr, (j * Ur + Ur - 1) / 32 - (j * Ur) / 32 + 1);
     const int row_parts = k * Pr + (Fs > 0 ? nws : 0);
     const int rbG = (D >> 8) * 144, rbD = (F >> 8) * 144, rbS = (Fs >> 8) * 144;
-    const int gu_R = stage_rows_for(2, gu_G);
     const int dn_R = 4;  // one pass of four row units per warp (one warp group)
-    const size_t slot = std::max({(size_t)2 * gu_R * rbG, (size_t)k * dn_R * rbD, (size_t)dn_R * rbS});
+    const size_t dn_stage = std::max((size_t)k * dn_R * rbD, (size_t)dn_R * rbS);
     const int g = num_sms;
     const long long gu_rows = ((long long)T * Fs + g - 1) / g + ((long long)T * k * F + g - 1) / g;
     const long long dn_rows = ((long long)T * D + g - 1) / g;
     size_t o = 0;
     const size_t o_xs = o;  o = align16w(o + (size_t)T * (D + 64) * 4);
+    const size_t o_x = o;   o = align16w(o + (size_t)T * D * 4);
     const size_t o_pgu = o; o = align16w(o + (size_t)gu_rows * 2 * gu_nsegw * 4);
     const size_t o_pdn = o; o = align16w(o + (size_t)dn_rows * row_parts * 4);
     const size_t o_bars = o;
-    const size_t fixed = o + (2 * 8 + 2) * 8;
+    const size_t fixed = o + (2 * 8 + 4) * 8;
     if (fixed >= smem_limit) return -1;
-    int S = (int)((smem_limit - fixed) / slot);
-    if (S > 8) S = 8;
-    if (S < 2) return -1;
+    // Warp groups of the gate/up phase: more groups make bigger stages, fewer
+    // make more of them in the same shared memory.  The weight stream of each
+    // phase is bounded by the bytes it keeps in flight (all stages but the one
+    // being consumed), so pick the group count that minimises
+    // sum over phases of phase bytes / bytes in flight.
+    const double gu_bytes = (double)T * (Fs + (double)k * F) * 2 * rbG;
+    const double dn_bytes = (double)T * D * ((double)k * rbD + (Fs > 0 ? rbS : 0));
+    int gu_G = 0, S = 0;
+    size_t slot = 0;
+    double best = 0.0;
+    for (int Gc = kWConsumerWarps / gu_nsegw; Gc >= 1; --Gc) {
+        const size_t gu_stage = (size_t)2 * stage_rows_for(2, Gc) * rbG;
+        const size_t sl = std::max(gu_stage, dn_stage);
+        int Sc = (int)((smem_limit - fixed) / sl);
+        if (Sc > 8) Sc = 8;
+        if (Sc < 2) continue;
+        const double cost = gu_bytes / ((double)(Sc - 1) * gu_stage) + dn_bytes / ((double)(Sc - 1) * dn_stage);
+        if (gu_G == 0 || cost < best * 0.98) {
+            gu_G = Gc; S = Sc; slot = sl; best = cost;
+        }
+    }
+    if (gu_G == 0) return -1;
+    if (((uintptr_t)p.x & 15u) || ((size_t)T * D * 4) >= (1u << 20)) return -1;  // one bulk copy of the input
+    const int gu_R = stage_rows_for(2, gu_G);
     const size_t ring = (size_t)S * slot;
     p.wide = 1;
     p.gu_nsegw = gu_nsegw; p.gu_G = gu_G; p.gu_R = gu_R;
@@ -564,10 +669,11 @@ int wide_decode_configure(FusedDecodeParams& p, int num_sms, size_t smem_limit, 
     p.stages = S;
     p.slot_bytes = (int)slot;
     p.off_xs = (int)(ring + o_xs);
+    p.off_red = (int)(ring + o_x);
     p.off_pgu = (int)(ring + o_pgu);
     p.off_pdn = (int)(ring + o_pdn);
     p.off_bars = (int)(ring + o_bars);
-    *smem_bytes = ring + o_bars + (2 * (size_t)S + 2) * 8;
+    *smem_bytes = ring + o_bars + (2 * (size_t)S + 4) * 8;
     *grid = g;
     return 0;
 }

@@ -136,14 +136,15 @@ struct FusedDecodeParams {
     // [D][Fs/256*144] down, gate vector [D]; act_sh [T][Fs] scratch.  A layer
     // with a shared expert, or whose router does not fit the shared-memory
     // staging, runs the wide kernel (decode_wide.cu), which also needs
-    // route_logits [T][E+1] scratch and a second grid-barrier counter.
+    // route_slots [T][E+1][8] scratch (epoch-tagged partial logits, cleared
+    // together with route_bar) and route_bar, a launch counter.
     const uint8_t* sh_gate;
     const uint8_t* sh_up;
     const uint8_t* sh_down;
     const float* sh_gate_vec;
     int Fs;
     float* act_sh;
-    float* route_logits;
+    unsigned long long* route_slots;
     unsigned long long* route_bar;
     // filled by fused_decode_configure
     int gu_nsegw, gu_G, gu_R, dn_nsegw, dn_G, dn_R, dn_split, stages, slot_bytes;
