@@ -396,7 +396,7 @@ def run_ours(args, w):
         worker.dispose()  # the Qwen layer (1.1 GB) gets the device to itself
         worker = None
         qwen = measure_qwen(torch, glc, args, stream, rank == 0 and world == 1 and not args.skip_cpu_baseline)
-    ep_leg = measure_ep(torch, dist, glc, w, stream, args, world, rank, local) if dist else None
+    ep_leg = measure_ep(torch, dist, glc, w, stream, args, world, rank, local) if not args.skip_ep else None
 
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.skip_cpu_baseline:
@@ -636,48 +636,126 @@ def measure_qwen(torch, glc, args, stream, want_cpu):
     return {"legs": legs, "cpu_baseline": cpu}
 
 
-EP_TOKENS = 8  # decode tokens per rank in the expert-parallel leg
+EP_TOKENS = 8  # decode tokens per rank in the expert-parallel leg (Mixtral layer)
+EP_QWEN_T = (16, 256)  # tokens per rank of the Qwen2-57B expert-parallel legs
+EP_PHASES = ["route", "dispatch", "exchange_out", "experts", "exchange_back", "combine"]
+
+
+def ep_communicator(glc, dist, world, rank, local):
+    """The C ABI's own NCCL communicator (glc_comm_*): the exchange a host
+    without torch.distributed uses.  torch.distributed only hands rank 0's id
+    to the other ranks."""
+    uid = glc.Communicator.unique_id() if rank == 0 else None
+    if dist:
+        box = [uid]
+        dist.broadcast_object_list(box, src=0)
+        uid = box[0]
+    return glc.Communicator(uid, world, rank, local)
+
+
+def ep_time(torch, dist, shard, comm, xs, T, flags, stream, steps):
+    """Device time per expert-parallel step (max over ranks) and the mean of
+    each phase (route, dispatch, exchange out, experts, exchange back, combine)."""
+    D = xs[0].shape[1]
+    out = torch.empty(T, D, device="cuda")
+    s = stream.cuda_stream
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            shard.ep_forward_dev(comm, 0, xs[i % len(xs)].data_ptr(), T, flags, out.data_ptr(), stream=s)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(steps):
+            shard.ep_forward_dev(comm, 0, xs[i % len(xs)].data_ptr(), T, flags, out.data_ptr(), stream=s)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    shard.set_profiling(True)
+    ph = []
+    with torch.cuda.stream(stream):
+        for i in range(8):
+            shard.ep_forward_dev(comm, 0, xs[i % len(xs)].data_ptr(), T, flags, out.data_ptr(), stream=s)
+            torch.cuda.synchronize()
+            ph.append(shard.kernel_times_ms())
+    shard.set_profiling(False)
+    shard.poll_error()
+    phases = {n: float(v) for n, v in zip(EP_PHASES, np.mean(np.array(ph), axis=0))}
+    return float(t.item()), phases
 
 
 def measure_ep(torch, dist, glc, w, stream, args, world, rank, local):
-    """Expert parallelism over the ranks (NCCL): E / world experts per rank,
-    EP_TOKENS decode tokens per rank through ExpertParallelStageWorker (route,
-    rank-grouped dispatch, all-to-all of counts, rows and expert ids, grouped
-    tensor-core experts on the received rows, reverse all-to-all, k-ordered
-    combine).  Device time per step on the launching stream, max over ranks."""
-    from glacier.inference.distributed_b200.ep import CudaExpertShard, ExpertParallelStageWorker
+    """Expert parallelism through the C ABI (glc_moe_ep_forward, the call a C#
+    host binds: NCCL inside the library, no torch.distributed on the data
+    path): E / world experts per rank, fixed-size dispatch blocks exchanged
+    with one grouped NCCL send/receive each way (no host read of the counts),
+    grouped tensor-core experts on the rows each rank receives, k-ordered
+    combine at home.  Every rank checks its output, ids and weights against
+    its own single-GPU layer on the same tokens; device time per step as the
+    max over ranks, with the per-phase breakdown."""
     D, F, E, k = w["D"], w["F"], w["E"], w["k"]
     epr = E // world
+    comm = ep_communicator(glc, dist, world, rank, local)
+    res = {"exchange": "fixed-size per-rank blocks (worst case T*k rows), one grouped ncclSend/ncclRecv each way, "
+                       "counts read on the device only",
+           "api": "glc_moe_ep_forward (C ABI, communicator glc_comm)"}
+    flags = w["flags"] | GLC_FWD_BATCHED
+    # ---- Mixtral-8x7B layer, EP_TOKENS decode tokens per rank
     T = EP_TOKENS
     shard = glc.GpuExpertStageWorker(D, F, E, k, renormalize=True, device=local, max_tokens=world * T,
                                      expert_begin=rank * epr, expert_count=epr)
     shard.synth_layer(0, w["seed"])
-    ep = ExpertParallelStageWorker(CudaExpertShard(shard))
     rng = np.random.default_rng(w["seed"] + 100 + rank)
-    xs = [torch.from_numpy(rng.standard_normal((T, D)).astype(np.float32)).cuda() for _ in range(4)]
-    flags = w["flags"] | GLC_FWD_BATCHED
+    xh = [rng.standard_normal((T, D)).astype(np.float32) for _ in range(4)]
+    xs = [torch.from_numpy(x).cuda() for x in xh]
+    # parity: this rank's tokens against its own single-GPU layer (batched path)
+    full = glc.GpuExpertStageWorker(D, F, E, k, renormalize=True, device=local, max_tokens=T)
+    full.synth_layer(0, w["seed"])
+    out = torch.empty(T, D, device="cuda")
+    ids = torch.empty(T, k, dtype=torch.int32, device="cuda")
+    wts = torch.empty(T, k, device="cuda")
+    shard.ep_forward_dev(comm, 0, xs[0].data_ptr(), T, flags, out.data_ptr(), ids.data_ptr(), wts.data_ptr())
+    torch.cuda.synchronize()
+    fo, fids, fw = full.forward(0, xh[0], flags)
+    full.dispose()
+    eo = out.cpu().numpy()
+    exact = bool(np.array_equal(eo, fo) and np.array_equal(ids.cpu().numpy(), fids)
+                 and np.array_equal(wts.cpu().numpy(), fw))
+    ok = torch.tensor([1 if exact else 0], device="cuda")
+    if dist:
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
     steps = max(20, min(args.steps // 10, 200))
-    with torch.cuda.stream(stream):
-        for i in range(5):
-            ep.forward(0, xs[i % 4], flags)
-        torch.cuda.synchronize()
-        dist.barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for i in range(steps):
-            ep.forward(0, xs[i % 4], flags)
-        e1.record(stream)
-        torch.cuda.synchronize()
-    dist.barrier()
-    t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
-    shard.poll_error()
+    ms, phases = ep_time(torch, dist, shard, comm, xs, T, flags, stream, steps)
     shard.dispose()
-    return {"workload": f"mixtral8x7b_moe_layer_decode_ep{world}", "experts_per_rank": epr,
-            "tokens_per_rank": T, "ms_per_step": ms, "tokens_per_s": world * T / (ms * 1e-3),
-            "steps": steps, "exchange": "NCCL all_to_all_single (counts, rows, ids; outputs back)",
-            "experts": "grouped tcgen05 kernels on the rows each rank receives"}
+    res["mixtral"] = {"workload": f"mixtral8x7b_moe_layer_decode_ep{world}", "experts_per_rank": epr,
+                      "tokens_per_rank": T, "ms_per_step": ms, "tokens_per_s": world * T / (ms * 1e-3),
+                      "tokens_per_s_per_gpu": T / (ms * 1e-3), "steps": steps, "phases_ms": phases,
+                      "parity": {"bit_exact_vs_single_gpu_all_ranks": bool(ok.item() == 1),
+                                 "reference": "each rank's own single-GPU layer, batched path, same tokens"}}
+    # ---- Qwen2-57B layer, 64 / world experts per rank + the shared expert
+    if not args.skip_qwen:
+        q = QWEN
+        Dq, Fq, Eq, kq, Fsq = q["D"], q["F"], q["E"], q["k"], q["Fs"]
+        eq = Eq // world
+        shard = glc.GpuExpertStageWorker(Dq, Fq, Eq, kq, shared_ffn_dim=Fsq, renormalize=False, device=local,
+                                         max_tokens=world * max(EP_QWEN_T), expert_begin=rank * eq,
+                                         expert_count=eq)
+        shard.synth_layer(0, q["seed"])
+        for Tq in EP_QWEN_T:
+            xs = [torch.from_numpy(rng.standard_normal((Tq, Dq)).astype(np.float32)).cuda() for _ in range(2)]
+            stq = max(5, min(steps, 2000 // Tq))
+            ms, phases = ep_time(torch, dist, shard, comm, xs, Tq, q["flags"] | GLC_FWD_BATCHED, stream, stq)
+            res[f"qwen2_57b_T{Tq}"] = {"workload": f"qwen2_57b_moe_layer_ep{world}_T{Tq}", "experts_per_rank": eq,
+                                        "tokens_per_rank": Tq, "ms_per_step": ms,
+                                        "tokens_per_s": world * Tq / (ms * 1e-3),
+                                        "tokens_per_s_per_gpu": Tq / (ms * 1e-3), "steps": stq,
+                                        "phases_ms": phases}
+        shard.dispose()
+    comm.dispose()
+    return res
 
 
 def main():
@@ -690,6 +768,7 @@ def main():
     ap.add_argument("--skip-cpu-baseline", action="store_true")
     ap.add_argument("--skip-batched", action="store_true")
     ap.add_argument("--skip-qwen", action="store_true")
+    ap.add_argument("--skip-ep", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -147,6 +147,7 @@ struct glc_moe {
     // optional per-kernel CUDA-event timing of the last forward (launch order)
     int profiling = 0;
     int n_marks = 0;
+    int mark_lock = 0;  // > 0: inner steps of a call that records its own phase marks
     cudaEvent_t marks[16] = {};
     // captured decode step
     cudaGraph_t graph = nullptr;
@@ -184,6 +185,12 @@ LayerDev* layer_of(glc_moe* h, int layer) {
 // Records a timing mark on `st` when profiling is enabled (marks[i+1]-marks[i]
 // is the device time of the i-th kernel of the last forward).
 void mark(glc_moe* h, cudaStream_t st) {
+    if (!h->profiling || h->mark_lock || h->n_marks >= 16) return;
+    cudaEventRecord(h->marks[h->n_marks++], st);
+}
+
+// A phase boundary of a call that times its phases rather than its kernels.
+void mark_phase(glc_moe* h, cudaStream_t st) {
     if (!h->profiling || h->n_marks >= 16) return;
     cudaEventRecord(h->marks[h->n_marks++], st);
 }
@@ -344,15 +351,18 @@ int run_shared_grouped(glc_moe* h, LayerDev* L, const float* xin, int T, int* sl
 
 // Batched path (T > 1): dispatch plan, fp16 hi/lo operand tiles, grouped
 // tcgen05 GEMMs (gate/up + SwiGLU, then down), k-ordered weighted combine.
+// count (optional, device memory): the rows actually present of the T given
+// (a batch sized on the device; T is then its upper bound).
 int run_experts_grouped(glc_moe* h, LayerDev* L, const float* xin, int T, int k, const int* ids,
-                        const float* wts, const float* resid, float* out, cudaStream_t st, bool with_shared) {
+                        const float* wts, const float* resid, float* out, cudaStream_t st, bool with_shared,
+                        const int* count = nullptr) {
     int rc = GLC_OK;
     const int D = h->d.hidden_dim, F = h->d.expert_ffn_dim, E = local_experts(h);
     const int P = T * k;
     if (!L->tmaps) return fail(GLC_ERR_STATE, "layer has no tensor maps");
-    CUDA_TRY(glc::dispatch_plan_launch(ids, P, E, h->plan, st));
+    CUDA_TRY(glc::dispatch_plan_launch(ids, P, E, h->plan, st, count));
     mark(h, st);
-    CUDA_TRY(glc::split_rows_launch(xin, P, D, k, 1, h->plan, h->btiles, h->rscale, st));
+    CUDA_TRY(glc::split_rows_launch(xin, P, D, k, 1, h->plan, h->btiles, h->rscale, st, count));
     mark(h, st);
     const int gmax = glc::plan_max_groups(P, E);
     glc::GroupedParams g{};
@@ -367,7 +377,7 @@ int run_experts_grouped(glc_moe* h, LayerDev* L, const float* xin, int T, int k,
     g.err = h->err;
     CUDA_TRY(glc::grouped_launch(L->tmap_gate, L->tmap_up, g, gmax * (F / 128), h->num_sms, st));
     mark(h, st);
-    CUDA_TRY(glc::split_rows_launch(h->act, P, F, k, 0, h->plan, h->btiles, h->rscale, st));
+    CUDA_TRY(glc::split_rows_launch(h->act, P, F, k, 0, h->plan, h->btiles, h->rscale, st, count));
     mark(h, st);
     glc::GroupedParams dn = g;
     dn.K = F;
@@ -384,7 +394,7 @@ int run_experts_grouped(glc_moe* h, LayerDev* L, const float* xin, int T, int k,
         ysh = h->ysh;
     }
     CUDA_TRY(glc::combine_launch(h->ysort, T, D, k, h->plan.inv, wts, resid, out, st, ysh, slices,
-                                 (long long)T * D, h->gate_out));
+                                 (long long)T * D, h->gate_out, count));
     mark(h, st);
     return GLC_OK;
 }
@@ -668,7 +678,7 @@ int glc_moe_set_profiling(glc_moe* h, int32_t enable) {
     if (enable && !h->marks[0])
         for (auto& e : h->marks) CUDA_TRY(cudaEventCreate(&e));
     h->profiling = enable ? 1 : 0;
-    h->n_marks = 0;
+    if (!h->mark_lock) h->n_marks = 0;
     return GLC_OK;
 }
 
@@ -849,7 +859,7 @@ int glc_moe_forward_dev(glc_moe* h, int32_t layer, const float* x, int32_t T, ui
         fp.x = x;
         fp.resid = resid;
         fp.out = out;
-        h->n_marks = 0;
+        if (!h->mark_lock) h->n_marks = 0;
         mark(h, st);
         const cudaError_t e = glc::fused_decode_launch(fp, h->num_sms, st);
         if (e == cudaSuccess) {
@@ -874,7 +884,7 @@ int glc_moe_forward_dev(glc_moe* h, int32_t layer, const float* x, int32_t T, ui
     rp.w = h->wts;
     rp.gate_vec = h->d.shared_ffn_dim > 0 ? L->sh_gate_vec : nullptr;
     rp.gate_out = h->gate_out;
-    h->n_marks = 0;
+    if (!h->mark_lock) h->n_marks = 0;
     mark(h, st);
     CUDA_TRY(glc::router_launch(rp, st));
     mark(h, st);
@@ -952,7 +962,7 @@ int glc_moe_experts_dev(glc_moe* h, int32_t layer, const float* rows, const int3
     CUDA_TRY(glc::localize_ids_launch(expert_ids, R, h->d.expert_begin, local_experts(h), h->ids, st));
     // each row is its own "token" with one slot and unit weight: y = expert(row) exactly
     const bool grouped = (flags & GLC_FWD_BATCHED) ? true : (flags & GLC_FWD_DECODE) ? false : (R > 1);
-    h->n_marks = 0;
+    if (!h->mark_lock) h->n_marks = 0;
     mark(h, st);
     return grouped ? run_experts_grouped(h, L, rows, R, 1, h->ids, h->ones, nullptr, y_out, st, false)
                    : run_experts(h, L, rows, R, 1, h->ids, h->ones, nullptr, y_out, st);
@@ -998,82 +1008,97 @@ int glc_moe_ep_forward(glc_moe* h, glc_comm* c, int32_t layer, const float* x, i
     if (E % world || El * world != E || h->d.expert_begin != rank * El)
         return fail(GLC_ERR_STATE, "the handle must hold expert shard %d of %d (experts [%d, %d))", rank, world,
                     rank * (E / world), (rank + 1) * (E / world));
-    if (T < 0 || T > h->d.max_tokens) return fail(GLC_ERR_INVALID_ARG, "T=%d outside [0, max_tokens=%d]", T, h->d.max_tokens);
-    if (T > 0 && (!x || !out)) return fail(GLC_ERR_INVALID_ARG, "null activation pointer");
     LayerDev* L = layer_of(h, layer);
     if (!L->loaded) return fail(GLC_ERR_STATE, "layer %d has no weights", layer);
     cudaStream_t st = stream ? (cudaStream_t)stream : h->stream;
-    const int D = h->d.hidden_dim, k = h->d.top_k, P = T * k;
+    const int D = h->d.hidden_dim, k = h->d.top_k;
+    // Every rank's batch holds at most Tc = max_tokens / world tokens (the
+    // handle is sized world x the largest per-rank batch), so the most pairs
+    // one rank can send one peer, cap, is the same on every rank: the
+    // exchange is an all-to-all of equal fixed-size blocks whose counts
+    // travel inside them and are used only on the device.  No host read.
+    const int Tc = h->d.max_tokens / world;
+    if (Tc < 1 || (D & 3)) return fail(GLC_ERR_STATE, "max_tokens=%d holds no token per rank of %d", h->d.max_tokens, world);
+    const int cap = Tc * k;
+    // A call that is invalid on this rank still takes part in both exchanges
+    // with no pairs, so its peers do not wait on it; it reports afterwards.
+    int bad = GLC_OK;
+    if (T < 0 || T > Tc)
+        bad = fail(GLC_ERR_INVALID_ARG,
+                   "T=%d outside [0, %d]: an expert-parallel handle's max_tokens is world x the largest per-rank batch",
+                   T, Tc);
+    else if (T > 0 && (!x || !out))
+        bad = fail(GLC_ERR_INVALID_ARG, "null activation pointer");
+    const int Tl = bad ? 0 : T, P = Tl * k;
     const size_t row = sizeof(float) * (size_t)D;
-    auto scratch = [&](int slot, size_t bytes) { return glc::comm_scratch(c, slot, bytes ? bytes : 16); };
-    // communicator scratch slots 2.. (0 and 1 hold stage-boundary payloads)
-    float* xin = static_cast<float*>(scratch(2, (size_t)T * row));
-    int32_t* ids = static_cast<int32_t*>(scratch(3, sizeof(int32_t) * P));
-    float* w = static_cast<float*>(scratch(4, sizeof(float) * P));
-    int32_t* counts = static_cast<int32_t*>(scratch(5, sizeof(int32_t) * (3 * (size_t)world + 1)));
-    int32_t* perm = static_cast<int32_t*>(scratch(6, sizeof(int32_t) * P));
-    int32_t* inv = static_cast<int32_t*>(scratch(7, sizeof(int32_t) * P));
-    float* send_rows = static_cast<float*>(scratch(8, (size_t)P * row));
-    int32_t* send_ids = static_cast<int32_t*>(scratch(9, sizeof(int32_t) * P));
-    if (!xin || !ids || !w || !counts || !perm || !inv || !send_rows || !send_ids)
+    const size_t bb = glc::ep_block_bytes(cap, D);
+    auto scratch = [&](int slot, size_t bytes) { return glc::comm_scratch(c, slot, bytes); };
+    // communicator scratch slots 2.. (0 and 1 hold stage-boundary payloads);
+    // their sizes depend only on the handle and the world, so they are
+    // allocated by the first call and reused
+    float* xin = static_cast<float*>(scratch(2, (size_t)Tc * row));
+    int32_t* ids = static_cast<int32_t*>(scratch(3, sizeof(int32_t) * cap));
+    float* w = static_cast<float*>(scratch(4, sizeof(float) * cap));
+    int32_t* ints = static_cast<int32_t*>(scratch(5, sizeof(int32_t) * (3 * (size_t)cap + 3 * (size_t)world + 2)));
+    uint8_t* send = static_cast<uint8_t*>(scratch(6, (size_t)world * bb));
+    uint8_t* recv = static_cast<uint8_t*>(scratch(7, (size_t)world * bb));
+    float* rows = static_cast<float*>(scratch(8, (size_t)world * cap * row));
+    float* y = static_cast<float*>(scratch(9, (size_t)world * cap * row));
+    float* y_send = static_cast<float*>(scratch(10, (size_t)world * cap * row));
+    float* y_recv = static_cast<float*>(scratch(11, (size_t)world * cap * row));
+    float* y_back = static_cast<float*>(scratch(12, (size_t)cap * row));
+    if (!xin || !ids || !w || !ints || !send || !recv || !rows || !y || !y_send || !y_recv || !y_back)
         return fail(GLC_ERR_OOM, "expert-parallel scratch");
-    int32_t* rcounts = counts + world;
-    int32_t* offsets = counts + 2 * world;
-    if (T > 0) {
-        rc = glc_moe_route_dev(h, layer, x, T, flags, xin, ids, w, st);
+    int32_t* counts = ints;                 // [world] pairs to each rank
+    int32_t* offsets = counts + world;      // [world + 1]
+    int32_t* perm = offsets + world + 1;    // [cap]
+    int32_t* inv = perm + cap;              // [cap]
+    int32_t* src_off = inv + cap;           // [world + 1] received rows per source, prefix
+    glc::DispatchPlan pl = h->plan;  // group-table scratch of the handle, outputs here
+    pl.counts = counts;
+    pl.offsets = offsets;
+    pl.perm = perm;
+    pl.inv = inv;
+    h->n_marks = 0;
+    mark_phase(h, st);
+    struct Lock {
+        glc_moe* h;
+        ~Lock() { h->mark_lock = 0; }
+    } lock{h};
+    h->mark_lock = 1;  // the inner steps record no marks: the phases below do
+    if (P > 0) {
+        rc = glc_moe_route_dev(h, layer, x, Tl, flags, xin, ids, w, st);
         if (rc) return rc;
-        rc = glc_moe_ep_dispatch_dev(h, xin, ids, T, world, counts, offsets, perm, inv, send_rows, send_ids, st);
-        if (rc) return rc;
-    } else {
-        CUDA_TRY(cudaMemsetAsync(counts, 0, sizeof(int32_t) * world, st));
     }
-    // pair counts per destination rank -> per source rank, read on the host to size the exchange
-    rc = glc::comm_alltoall_i32(c, counts, rcounts, st);
-    if (rc) return rc;
-    int32_t* hc = glc::comm_host_counts(c);
-    CUDA_TRY(cudaMemcpyAsync(hc, counts, sizeof(int32_t) * 2 * world, cudaMemcpyDeviceToHost, st));
-    CUDA_TRY(cudaStreamSynchronize(st));
-    std::vector<size_t> so(world), sn(world), ro(world), rn(world);
-    size_t ns = 0, nr = 0;
+    mark_phase(h, st);  // route
+    CUDA_TRY(glc::ep_pack_launch(xin, ids, Tl, D, k, E, world, cap, h->ep_keys, pl, send, st));
+    mark_phase(h, st);  // dispatch into per-rank blocks
+    std::vector<size_t> off(world), cnt(world, bb), off_y(world), cnt_y(world, (size_t)cap * row);
     for (int p = 0; p < world; ++p) {
-        so[p] = ns; sn[p] = (size_t)hc[p]; ns += sn[p];
-        ro[p] = nr; rn[p] = (size_t)hc[world + p]; nr += rn[p];
+        off[p] = (size_t)p * bb;
+        off_y[p] = (size_t)p * cap * row;
     }
-    if (ns != (size_t)P) return fail(GLC_ERR_STATE, "dispatch counted %zu pairs, expected %d", ns, P);
-    const size_t R = nr;
-    float* recv_rows = static_cast<float*>(scratch(10, R * row));
-    int32_t* recv_ids = static_cast<int32_t*>(scratch(11, sizeof(int32_t) * R));
-    float* y = static_cast<float*>(scratch(12, R * row));
-    float* y_back = static_cast<float*>(scratch(13, (size_t)P * row));
-    if (!recv_rows || !recv_ids || !y || !y_back) return fail(GLC_ERR_OOM, "expert-parallel scratch");
-    auto scaled = [](const std::vector<size_t>& v, size_t f) {
-        std::vector<size_t> o(v.size());
-        for (size_t i = 0; i < v.size(); ++i) o[i] = v[i] * f;
-        return o;
-    };
-    const auto soR = scaled(so, row), snR = scaled(sn, row), roR = scaled(ro, row), rnR = scaled(rn, row);
-    const auto soI = scaled(so, 4), snI = scaled(sn, 4), roI = scaled(ro, 4), rnI = scaled(rn, 4);
-    rc = glc::comm_alltoallv(c, send_rows, soR.data(), snR.data(), recv_rows, roR.data(), rnR.data(), st);
+    rc = glc::comm_alltoallv(c, send, off.data(), cnt.data(), recv, off.data(), cnt.data(), st);
     if (rc) return rc;
-    rc = glc::comm_alltoallv(c, send_ids, soI.data(), snI.data(), recv_ids, roI.data(), rnI.data(), st);
+    mark_phase(h, st);  // exchange out
+    CUDA_TRY(glc::ep_unpack_launch(recv, world, cap, D, h->d.expert_begin, El, rows, h->ids, src_off, st));
+    // this rank's experts on every row received, the row count on the device
+    rc = run_experts_grouped(h, L, rows, world * cap, 1, h->ids, h->ones, nullptr, y, st, false, src_off + world);
     if (rc) return rc;
-    // this rank's experts on every row it received, in chunks of the handle's pair slots
-    const size_t cap = (size_t)h->d.max_tokens * k;
-    for (size_t r0 = 0; r0 < R; r0 += cap) {
-        const int n = (int)std::min(cap, R - r0);
-        rc = glc_moe_experts_dev(h, layer, recv_rows + r0 * D, recv_ids + r0, n, flags, y + r0 * D, st);
-        if (rc) return rc;
-    }
-    // expert outputs back to the ranks the rows came from, in their send order
-    rc = glc::comm_alltoallv(c, y, roR.data(), rnR.data(), y_back, soR.data(), snR.data(), st);
+    CUDA_TRY(glc::ep_repack_launch(y, src_off, world, cap, D, y_send, st));
+    mark_phase(h, st);  // experts
+    rc = glc::comm_alltoallv(c, y_send, off_y.data(), cnt_y.data(), y_recv, off_y.data(), cnt_y.data(), st);
     if (rc) return rc;
-    if (T > 0) {
-        rc = glc_moe_combine_dev(h, layer, y_back, inv, w, T, (flags & GLC_FWD_RESIDUAL) ? x : nullptr, xin, out, st);
+    mark_phase(h, st);  // exchange back
+    if (P > 0) {
+        CUDA_TRY(glc::ep_unblock_launch(y_recv, P, cap, D, h->ep_keys, pl, y_back, st));
+        rc = glc_moe_combine_dev(h, layer, y_back, inv, w, Tl, (flags & GLC_FWD_RESIDUAL) ? x : nullptr, xin, out, st);
         if (rc) return rc;
         if (ids_out) CUDA_TRY(cudaMemcpyAsync(ids_out, ids, sizeof(int32_t) * P, cudaMemcpyDeviceToDevice, st));
         if (w_out) CUDA_TRY(cudaMemcpyAsync(w_out, w, sizeof(float) * P, cudaMemcpyDeviceToDevice, st));
     }
-    return GLC_OK;
+    mark_phase(h, st);  // combine
+    return bad;
 }
 
 int glc_moe_forward(glc_moe* h, int32_t layer, const float* x, int32_t T, uint32_t flags, float* out,

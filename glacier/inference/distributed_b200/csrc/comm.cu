@@ -97,6 +97,7 @@ struct glc_comm {
     // device scratch, grown on demand (slot -> buffer)
     std::vector<void*> scratch;
     std::vector<size_t> scratch_bytes;
+    std::vector<void*> retired;  // outgrown scratch, possibly still in use by queued work: freed at destroy
     int32_t* h_counts = nullptr;  // pinned [2 * nranks]: counts sent, counts received
 };
 
@@ -106,8 +107,11 @@ int comm_world(const glc_comm* c) { return c->nranks; }
 int comm_rank(const glc_comm* c) { return c->rank; }
 int32_t* comm_host_counts(glc_comm* c) { return c->h_counts; }
 
-// Device buffer `slot` of at least `bytes`; a buffer that must grow is replaced
-// after the device has finished all work (the old one may still be in use).
+// Device buffer `slot` of at least `bytes`.  The callers' sizes depend only
+// on the handle and the world size, so a slot is allocated by the first call
+// and reused; a buffer that must grow is retired, not freed (work already
+// queued may still use it), and retired buffers are freed when the
+// communicator is destroyed -- no device-wide synchronisation on the way.
 void* comm_scratch(glc_comm* c, int slot, size_t bytes) {
     if ((int)c->scratch.size() <= slot) {
         c->scratch.resize(slot + 1, nullptr);
@@ -115,8 +119,7 @@ void* comm_scratch(glc_comm* c, int slot, size_t bytes) {
     }
     if (c->scratch_bytes[slot] < bytes) {
         if (c->scratch[slot]) {
-            cudaDeviceSynchronize();
-            cudaFree(c->scratch[slot]);
+            c->retired.push_back(c->scratch[slot]);
             c->scratch[slot] = nullptr;
             c->scratch_bytes[slot] = 0;
         }
@@ -202,7 +205,9 @@ int glc_comm_destroy(glc_comm* c) {
     cudaSetDevice(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
     if (c->comm) nccl().CommDestroy(c->comm);
+    cudaDeviceSynchronize();  // work of other streams may still use the scratch
     for (void* p : c->scratch) cudaFree(p);
+    for (void* p : c->retired) cudaFree(p);
     cudaFree(c->d_hdr);
     cudaFreeHost(c->h_hdr);
     cudaFreeHost(c->h_counts);

@@ -54,6 +54,131 @@ __global__ void __launch_bounds__(256) fill_kernel(float* __restrict__ p, int n,
     if (i < n) p[i] = v;
 }
 
+// ---------------------------------------------------------------------------
+// Fixed-capacity exchange blocks (no host read of the counts): the block a
+// rank sends to peer p holds [int32 count | pad to 16 B][int32 expert id x
+// cap, padded to 16 B][fp32 row x cap]; `cap` is the worst case of one rank's
+// pairs to one peer, so every block has the same size on every rank and the
+// all-to-all is one grouped send/receive of equal blocks.
+
+__host__ __device__ inline size_t ep_ids_off() { return 16; }
+__host__ __device__ inline size_t ep_rows_off(int cap) { return 16 + (((size_t)cap * 4 + 15) & ~(size_t)15); }
+size_t ep_block_bytes(int cap, int D) { return ep_rows_off(cap) + (size_t)cap * D * 4; }
+
+// One CTA per send position (or one CTA when there are none): the row and the
+// global expert id of pair perm[pos] into slot pos - offsets[p] of the block
+// for its rank p; block 0 also writes every block's count.
+__global__ void __launch_bounds__(256) ep_pack_kernel(const float* __restrict__ xin, const int* __restrict__ ids, int P,
+                                                      int D, int k, int world, int cap, const int* __restrict__ keys,
+                                                      DispatchPlan plan, uint8_t* __restrict__ blocks, size_t bb) {
+    const int pos = blockIdx.x;
+    if (pos == 0 && threadIdx.x < world)
+        *reinterpret_cast<int*>(blocks + (size_t)threadIdx.x * bb) = P > 0 ? plan.counts[threadIdx.x] : 0;
+    if (pos >= P) return;
+    const int pair = plan.perm[pos];
+    const int p = keys[pair];
+    const int slot = pos - plan.offsets[p];
+    uint8_t* blk = blocks + (size_t)p * bb;
+    const float4* s4 = reinterpret_cast<const float4*>(xin + (size_t)(pair / k) * D);
+    float4* d4 = reinterpret_cast<float4*>(blk + ep_rows_off(cap) + (size_t)slot * D * 4);
+    for (int i = threadIdx.x; i < (D >> 2); i += 256) d4[i] = s4[i];
+    if (threadIdx.x == 0) reinterpret_cast<int*>(blk + ep_ids_off())[slot] = ids[pair];
+}
+
+// Received blocks -> contiguous rows in source order: slot s of source q
+// goes to row R_q + s (R_q = rows of the sources before q); the expert id is
+// localised to this rank's shard [begin, begin + count) (clamped, like
+// GpuFirstExpertStageWorker.ProcessRoutedTopK clamps ids).  CTA (s, q); the
+// first CTA writes the total row count and the source offsets.
+__global__ void __launch_bounds__(256) ep_unpack_kernel(const uint8_t* __restrict__ blocks, size_t bb, int world,
+                                                        int cap, int D, int begin, int count, float* __restrict__ rows,
+                                                        int* __restrict__ local_ids, int* __restrict__ src_off) {
+    __shared__ int s_base, s_n;
+    const int s = blockIdx.x, q = blockIdx.y;
+    if (threadIdx.x == 0) {
+        int base = 0;
+        for (int r = 0; r < q; ++r) base += *reinterpret_cast<const int*>(blocks + (size_t)r * bb);
+        s_base = base;
+        s_n = *reinterpret_cast<const int*>(blocks + (size_t)q * bb);
+        if (s == 0 && q == 0) {
+            int acc = 0;
+            for (int r = 0; r < world; ++r) {
+                src_off[r] = acc;
+                acc += *reinterpret_cast<const int*>(blocks + (size_t)r * bb);
+            }
+            src_off[world] = acc;  // total rows received
+        }
+    }
+    __syncthreads();
+    if (s >= s_n) return;
+    const uint8_t* blk = blocks + (size_t)q * bb;
+    const float4* s4 = reinterpret_cast<const float4*>(blk + ep_rows_off(cap) + (size_t)s * D * 4);
+    float4* d4 = reinterpret_cast<float4*>(rows + (size_t)(s_base + s) * D);
+    for (int i = threadIdx.x; i < (D >> 2); i += 256) d4[i] = s4[i];
+    if (threadIdx.x == 0) {
+        const int e = reinterpret_cast<const int*>(blk + ep_ids_off())[s] - begin;
+        local_ids[s_base + s] = e < 0 ? 0 : (e >= count ? count - 1 : e);
+    }
+}
+
+// Expert outputs back into per-source blocks of rows: y[R_q + s] -> out
+// block q slot s (the order the source sent them in).  CTA (s, q).
+__global__ void __launch_bounds__(256) ep_repack_kernel(const float* __restrict__ y, const int* __restrict__ src_off,
+                                                        int cap, int D, float* __restrict__ out) {
+    const int s = blockIdx.x, q = blockIdx.y;
+    if (s >= src_off[q + 1] - src_off[q]) return;
+    const float4* s4 = reinterpret_cast<const float4*>(y + (size_t)(src_off[q] + s) * D);
+    float4* d4 = reinterpret_cast<float4*>(out + ((size_t)q * cap + s) * D);
+    for (int i = threadIdx.x; i < (D >> 2); i += 256) d4[i] = s4[i];
+}
+
+// This rank's expert outputs, received as per-peer blocks, into send order:
+// y_back[pos] = blocks[p][pos - offsets[p]] with p the rank of pair perm[pos].
+__global__ void __launch_bounds__(256) ep_unblock_kernel(const float* __restrict__ blocks, int cap, int D,
+                                                         const int* __restrict__ keys, DispatchPlan plan,
+                                                         float* __restrict__ y_back) {
+    const int pos = blockIdx.x;
+    const int p = keys[plan.perm[pos]];
+    const int slot = pos - plan.offsets[p];
+    const float4* s4 = reinterpret_cast<const float4*>(blocks + ((size_t)p * cap + slot) * D);
+    float4* d4 = reinterpret_cast<float4*>(y_back + (size_t)pos * D);
+    for (int i = threadIdx.x; i < (D >> 2); i += 256) d4[i] = s4[i];
+}
+
+cudaError_t ep_pack_launch(const float* xin, const int* ids, int T, int D, int k, int num_experts, int world, int cap,
+                           int* keys, const DispatchPlan& plan, uint8_t* blocks, cudaStream_t st) {
+    const int P = T * k;
+    if (world < 1 || world > 64 || num_experts % world || (D & 3) || P > cap) return cudaErrorInvalidValue;
+    if (P > 0) {
+        ep_rank_keys_kernel<<<(P + 255) / 256, 256, 0, st>>>(ids, P, num_experts / world, world, keys);
+        const cudaError_t e = dispatch_plan_launch(keys, P, world, plan, st);
+        if (e != cudaSuccess) return e;
+    }
+    ep_pack_kernel<<<P > 0 ? P : 1, 256, 0, st>>>(xin, ids, P, D, k, world, cap, keys, plan, blocks,
+                                                    ep_block_bytes(cap, D));
+    return cudaGetLastError();
+}
+
+cudaError_t ep_unpack_launch(const uint8_t* blocks, int world, int cap, int D, int begin, int count, float* rows,
+                             int* local_ids, int* src_off, cudaStream_t st) {
+    ep_unpack_kernel<<<dim3(cap, world), 256, 0, st>>>(blocks, ep_block_bytes(cap, D), world, cap, D, begin, count,
+                                                       rows, local_ids, src_off);
+    return cudaGetLastError();
+}
+
+cudaError_t ep_repack_launch(const float* y, const int* src_off, int world, int cap, int D, float* out,
+                             cudaStream_t st) {
+    ep_repack_kernel<<<dim3(cap, world), 256, 0, st>>>(y, src_off, cap, D, out);
+    return cudaGetLastError();
+}
+
+cudaError_t ep_unblock_launch(const float* blocks, int P, int cap, int D, const int* keys, const DispatchPlan& plan,
+                              float* y_back, cudaStream_t st) {
+    if (P <= 0) return cudaSuccess;
+    ep_unblock_kernel<<<P, 256, 0, st>>>(blocks, cap, D, keys, plan, y_back);
+    return cudaGetLastError();
+}
+
 cudaError_t ep_dispatch_launch(const float* xin, const int* ids, int T, int D, int k, int num_experts, int world,
                                int* keys, const DispatchPlan& plan, float* rows, int* row_ids, cudaStream_t st) {
     const int P = T * k;

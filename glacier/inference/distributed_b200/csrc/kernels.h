@@ -182,15 +182,20 @@ struct DispatchPlan {
 };
 inline int plan_max_groups(int P, int E) { return E + P / kGroupTokens + 1; }
 
-cudaError_t dispatch_plan_launch(const int* ids, int P, int E, const DispatchPlan& plan, cudaStream_t st);
+// count (optional, device memory): the pairs actually present, <= P; the
+// split and combine below take the same pointer and skip the rest.
+cudaError_t dispatch_plan_launch(const int* ids, int P, int E, const DispatchPlan& plan, cudaStream_t st,
+                                 const int* count = nullptr);
 // B tiles: per group, per super-block s of K: [4 chunks][N rows][128 B] SWIZZLE_128B.
 cudaError_t split_rows_launch(const float* src, int P, int K, int kslots, int src_is_token,
-                              const DispatchPlan& plan, uint8_t* btiles, float* rscale, cudaStream_t st);
+                              const DispatchPlan& plan, uint8_t* btiles, float* rscale, cudaStream_t st,
+                              const int* count = nullptr);
 // out[t] = (resid|0) + sum_j y[inv[t,j]] * w[t,j] in j order, then, with ysh,
 // + (sum of ysh's K-slice planes) * sg[t] (the shared expert).
 cudaError_t combine_launch(const float* y, int T, int D, int k, const int* inv, const float* w,
                            const float* resid, float* out, cudaStream_t st, const float* ysh = nullptr,
-                           int ysh_slices = 1, long long ysh_stride = 0, const float* sg = nullptr);
+                           int ysh_slices = 1, long long ysh_stride = 0, const float* sg = nullptr,
+                           const int* count = nullptr);
 
 // Grouped expert GEMM on tcgen05 tensor cores (weights dequantised into TMEM).
 struct GroupedParams {
@@ -218,6 +223,20 @@ cudaError_t grouped_launch(const void* tmapA, const void* tmapB, const GroupedPa
 cudaError_t ep_dispatch_launch(const float* xin, const int* ids, int T, int D, int k, int num_experts, int world,
                                int* keys, const DispatchPlan& plan, float* rows, int* row_ids, cudaStream_t st);
 cudaError_t localize_ids_launch(const int* ids, int n, int begin, int count, int* out, cudaStream_t st);
+// Fixed-capacity expert-parallel exchange (ep.cu): per-peer blocks of
+// ep_block_bytes(cap, D) = [count][cap expert ids][cap rows], cap = the most
+// pairs one rank can send one peer, so the all-to-all needs no host read.
+size_t ep_block_bytes(int cap, int D);
+cudaError_t ep_pack_launch(const float* xin, const int* ids, int T, int D, int k, int num_experts, int world, int cap,
+                           int* keys, const DispatchPlan& plan, uint8_t* blocks, cudaStream_t st);
+// rows [world*cap][D] in source order, local expert ids, src_off [world+1]
+// (src_off[world] = rows received, the device count of the expert batch)
+cudaError_t ep_unpack_launch(const uint8_t* blocks, int world, int cap, int D, int begin, int count, float* rows,
+                             int* local_ids, int* src_off, cudaStream_t st);
+cudaError_t ep_repack_launch(const float* y, const int* src_off, int world, int cap, int D, float* out,
+                             cudaStream_t st);
+cudaError_t ep_unblock_launch(const float* blocks, int P, int cap, int D, const int* keys, const DispatchPlan& plan,
+                              float* y_back, cudaStream_t st);
 cudaError_t fill_launch(float* p, int n, float v, cudaStream_t st);
 
 // Wire codec (QuantizationKernels), one CTA per token.

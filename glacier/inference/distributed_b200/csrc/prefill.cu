@@ -17,8 +17,11 @@ namespace glc {
 
 constexpr int kPlanThreads = 1024;
 
+// count (optional, device): the pairs actually present, <= P (a batch sized
+// on the device, e.g. the rows an expert-parallel exchange delivered).
 __global__ void __launch_bounds__(kPlanThreads) dispatch_plan_kernel(const int* __restrict__ ids, int P, int E,
-                                                                     DispatchPlan plan) {
+                                                                     DispatchPlan plan, const int* __restrict__ count) {
+    if (count) P = min(P, *count);
     __shared__ int s_count[64];
     __shared__ int s_off[65];
     __shared__ int s_run[64];
@@ -96,7 +99,9 @@ __global__ void __launch_bounds__(kPlanThreads) dispatch_plan_kernel(const int* 
 // split into fp16 hi + lo and scatter into the group's swizzled B tiles.
 __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict__ src, int K, int kslots,
                                                          int src_is_token, DispatchPlan plan,
-                                                         uint8_t* __restrict__ btiles, float* __restrict__ rscale) {
+                                                         uint8_t* __restrict__ btiles, float* __restrict__ rscale,
+                                                         const int* __restrict__ count) {
+    if (count && (int)blockIdx.x >= *count) return;  // a position past the batch sized on the device
     __shared__ float smax[8];
     const int pos = blockIdx.x, tid = threadIdx.x;
     const int pair = plan.perm[pos];
@@ -152,8 +157,9 @@ struct SharedCombine {
 __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ y, int D, int k,
                                                       const int* __restrict__ inv, const float* __restrict__ w,
                                                       const float* __restrict__ resid, float* __restrict__ out,
-                                                      SharedCombine sh) {
+                                                      SharedCombine sh, const int* __restrict__ count) {
     const int t = blockIdx.x;
+    if (count && t >= *count) return;  // a token past the batch sized on the device
     for (int d = threadIdx.x; d < D; d += 256) {
         float acc = resid ? resid[(size_t)t * D + d] : 0.f;
         for (int j = 0; j < k; ++j) {
@@ -170,25 +176,27 @@ __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ 
     }
 }
 
-cudaError_t dispatch_plan_launch(const int* ids, int P, int E, const DispatchPlan& plan, cudaStream_t st) {
+cudaError_t dispatch_plan_launch(const int* ids, int P, int E, const DispatchPlan& plan, cudaStream_t st,
+                                 const int* count) {
     if (E > 64) return cudaErrorInvalidValue;
-    dispatch_plan_kernel<<<1, kPlanThreads, 0, st>>>(ids, P, E, plan);
+    dispatch_plan_kernel<<<1, kPlanThreads, 0, st>>>(ids, P, E, plan, count);
     return cudaGetLastError();
 }
 
 cudaError_t split_rows_launch(const float* src, int P, int K, int kslots, int src_is_token, const DispatchPlan& plan,
-                              uint8_t* btiles, float* rscale, cudaStream_t st) {
+                              uint8_t* btiles, float* rscale, cudaStream_t st, const int* count) {
     if (P <= 0) return cudaSuccess;
-    split_rows_kernel<<<P, 256, 0, st>>>(src, K, kslots, src_is_token, plan, btiles, rscale);
+    split_rows_kernel<<<P, 256, 0, st>>>(src, K, kslots, src_is_token, plan, btiles, rscale, count);
     return cudaGetLastError();
 }
 
 cudaError_t combine_launch(const float* y, int T, int D, int k, const int* inv, const float* w, const float* resid,
                            float* out, cudaStream_t st, const float* ysh, int ysh_slices, long long ysh_stride,
-                           const float* sg) {
+                           const float* sg, const int* count) {
     if (T <= 0) return cudaSuccess;
     if (ysh && (ysh_slices < 1 || !sg)) return cudaErrorInvalidValue;
-    combine_kernel<<<T, 256, 0, st>>>(y, D, k, inv, w, resid, out, SharedCombine{ysh, ysh_slices, ysh_stride, sg});
+    combine_kernel<<<T, 256, 0, st>>>(y, D, k, inv, w, resid, out, SharedCombine{ysh, ysh_slices, ysh_stride, sg},
+                                      count);
     return cudaGetLastError();
 }
 

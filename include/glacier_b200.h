@@ -314,10 +314,18 @@ int glc_pp_recv(glc_comm* c, int32_t peer, glc_fused_header* hdr_out, float* x_o
 /* The expert-parallel layer in one call (the steps of the glc_moe_*_dev
  * functions above with the exchanges over `c`): h holds expert shard
  * comm_rank of comm_world (expert_begin = rank * E / world), every rank calls
- * it with its own T tokens (T may differ), and out [T][D], ids_out [T][k],
- * w_out [T][k] equal the single-GPU layer's bit for bit.  Device pointers
- * (ids_out, w_out may be NULL); NULL stream = the handle's stream.  Reads the
- * per-rank pair counts on the host once per call. */
+ * it with its own T tokens (T may differ, 0 <= T <= max_tokens / comm_world:
+ * size the handle's max_tokens as world x the largest per-rank batch), and
+ * out [T][D], ids_out [T][k], w_out [T][k] equal the single-GPU layer's
+ * batched path bit for bit (the rows a rank receives are a batch: they run on
+ * the grouped tensor-core experts whatever the decode flag).  Device pointers (ids_out, w_out may be NULL); NULL stream = the
+ * handle's stream.  Asynchronous: the exchanges move fixed-size blocks (the
+ * most pairs one rank can send one peer) whose counts are read on the device
+ * only, so nothing waits on the host.  A rank whose T is out of range still
+ * takes part in both exchanges with no pairs (its peers do not wait on it)
+ * and returns GLC_ERR_INVALID_ARG.  With profiling on, glc_moe_kernel_times
+ * returns the phases: route, dispatch, exchange out, experts, exchange back,
+ * combine. */
 int glc_moe_ep_forward(glc_moe* h, glc_comm* c, int32_t layer, const float* x, int32_t T, uint32_t flags,
                        float* out, int32_t* ids_out, float* w_out, void* stream);
 
