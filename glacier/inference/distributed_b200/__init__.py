@@ -4,7 +4,7 @@ dispatch, SwiGLU, weighted combine, the INT8 stage-boundary wire codec and
 decode attention over an fp16 KV cache, behind the C ABI in
 include/glacier_b200.h."""
 from ._lib import GlcError, LIB_PATH, lib  # noqa: F401
-from .api import (Communicator, DynamicPrecisionSwitcher, FusedActivationHeader, GpuExpertStageWorker,  # noqa: F401
+from .api import (Communicator, DenseStage, DynamicPrecisionSwitcher, FusedActivationHeader, GpuExpertStageWorker,  # noqa: F401
                   QuantizationKernels, WirePrecisionMode, attn_decode_dev, attn_workspace_bytes,
                   device_count, dispatch_plan_dev, gemv_q4k_dev, q4k_row_bytes, router_topk_dev,
                   torch_stream_handle)

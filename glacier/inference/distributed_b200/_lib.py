@@ -44,6 +44,23 @@ class LayerWeights(C.Structure):
     ]
 
 
+class StageDesc(C.Structure):
+    _fields_ = [
+        ("hidden_dim", C.c_int32), ("ffn_dim", C.c_int32), ("n_heads", C.c_int32), ("n_kv_heads", C.c_int32),
+        ("head_dim", C.c_int32), ("layer_begin", C.c_int32), ("layer_count", C.c_int32), ("max_len", C.c_int32),
+        ("rope_theta", C.c_float), ("rms_eps", C.c_float), ("vocab", C.c_int32), ("has_embedding", C.c_int32),
+        ("has_lm_head", C.c_int32), ("device", C.c_int32),
+    ]
+
+
+class DenseLayerWeights(C.Structure):
+    _fields_ = [
+        ("attn_norm", C.c_void_p), ("wq", C.c_void_p), ("wk", C.c_void_p), ("wv", C.c_void_p),
+        ("bq", C.c_void_p), ("bk", C.c_void_p), ("bv", C.c_void_p), ("wo", C.c_void_p),
+        ("ffn_norm", C.c_void_p), ("w_gate", C.c_void_p), ("w_up", C.c_void_p), ("w_down", C.c_void_p),
+    ]
+
+
 class FusedHeader(C.Structure):
     _fields_ = [
         ("sequence_id", C.c_uint64), ("token_index", C.c_int32), ("layer_index", C.c_int32),
@@ -101,6 +118,15 @@ _SIGNATURES = {
     "glc_pp_send": (C.c_int, [vp, i32, C.POINTER(FusedHeader), vp, vp]),
     "glc_pp_recv": (C.c_int, [vp, i32, C.POINTER(FusedHeader), vp, i32, i32, vp]),
     "glc_moe_ep_forward": (C.c_int, [vp, vp, i32, vp, i32, C.c_uint32, vp, vp, vp, vp]),
+    "glc_stage_create": (C.c_int, [vp, C.POINTER(vp)]),
+    "glc_stage_destroy": (C.c_int, [vp]),
+    "glc_stage_load_layer": (C.c_int, [vp, i32, vp]),
+    "glc_stage_load_io": (C.c_int, [vp, vp, vp, vp]),
+    "glc_stage_synth_layer": (C.c_int, [vp, i32, C.c_uint64]),
+    "glc_stage_synth_io": (C.c_int, [vp, C.c_uint64]),
+    "glc_stage_reset": (C.c_int, [vp]),
+    "glc_stage_forward_dev": (C.c_int, [vp, i32, vp, vp, vp, vp, vp, vp]),
+    "glc_stage_poll_error": (C.c_int, [vp]),
 }
 GLC_COMM_ID_BYTES = 128
 

@@ -473,3 +473,68 @@ class Communicator:
         if self._h is not None:
             lib().glc_comm_destroy(self._h)
             self._h = None
+
+
+class DenseStage:
+    """A dense decoder pipeline stage on one GPU, the counterpart of the
+    reference's IClusterStageModel (Pipeline/IClusterStageModel.cs:9-36):
+    layers [layer_begin, layer_begin + layer_count) of a Qwen2-style model with
+    their fp16 KV caches, plus the embedding table on a first stage and the
+    final norm and LM head on a last stage (glc_stage_*)."""
+
+    def __init__(self, hidden_dim: int, ffn_dim: int, n_heads: int, n_kv_heads: int, layer_begin: int,
+                 layer_count: int, max_len: int, rope_theta: float = 1e6, rms_eps: float = 1e-6,
+                 vocab: int = 0, has_embedding: bool = False, has_lm_head: bool = False, device: int = 0):
+        self._h = None
+        self.desc = _lib.StageDesc(hidden_dim, ffn_dim, n_heads, n_kv_heads, 128, layer_begin, layer_count,
+                                   max_len, rope_theta, rms_eps, vocab, int(has_embedding), int(has_lm_head),
+                                   device)
+        h = C.c_void_p()
+        check(lib().glc_stage_create(C.byref(self.desc), C.byref(h)))
+        self._h = h
+        self.hidden_dim, self.vocab = hidden_dim, vocab
+
+    def _handle(self) -> C.c_void_p:
+        if self._h is None:
+            raise GlcError(-5, "stage was disposed")
+        return self._h
+
+    def load_layer(self, layer: int, attn_norm, wq, wk, wv, bq, bk, bv, wo, ffn_norm, w_gate, w_up, w_down) -> None:
+        arrays = [attn_norm, wq, wk, wv, bq, bk, bv, wo, ffn_norm, w_gate, w_up, w_down]
+        arrays = [None if a is None else np.ascontiguousarray(a) for a in arrays]
+        w = _lib.DenseLayerWeights(*[None if a is None else a.ctypes.data for a in arrays])
+        check(lib().glc_stage_load_layer(self._handle(), layer, C.byref(w)))
+
+    def load_io(self, embedding=None, final_norm=None, lm_head=None) -> None:
+        arrays = [None if a is None else np.ascontiguousarray(a) for a in (embedding, final_norm, lm_head)]
+        check(lib().glc_stage_load_io(self._handle(), *[None if a is None else a.ctypes.data for a in arrays]))
+
+    def synth_layer(self, layer: int, seed: int) -> None:
+        check(lib().glc_stage_synth_layer(self._handle(), layer, seed))
+
+    def synth_io(self, seed: int) -> None:
+        check(lib().glc_stage_synth_io(self._handle(), seed))
+
+    def reset_kv_cache(self) -> None:
+        """ResetKvCache (IClusterStageModel.cs:35)."""
+        check(lib().glc_stage_reset(self._handle()))
+
+    def forward_dev(self, pos: int, token_ptr=None, x_in_ptr=None, x_out_ptr=None, logits_ptr=None,
+                    token_out_ptr=None, stream=None) -> None:
+        """ForwardStage (IClusterStageModel.cs:19) on device pointers."""
+        check(lib().glc_stage_forward_dev(self._handle(), pos, token_ptr, x_in_ptr, x_out_ptr, logits_ptr,
+                                          token_out_ptr, stream))
+
+    def poll_error(self) -> None:
+        check(lib().glc_stage_poll_error(self._handle()))
+
+    def dispose(self) -> None:
+        if self._h is not None:
+            lib().glc_stage_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.dispose()
+        except Exception:
+            pass

@@ -1348,8 +1348,12 @@ int glc_dispatch_plan_dev(const int32_t* ids, int32_t P, int32_t E, int32_t* cou
     if (!ids || !counts || !offsets || !perm || !inv) return fail(GLC_ERR_INVALID_ARG, "null pointer");
     if (P < 0 || E <= 0 || E > 64) return fail(GLC_ERR_INVALID_ARG, "P=%d E=%d out of range", P, E);
     const int gmax = glc::plan_max_groups(P, E);
-    int* scratch = nullptr;  // group table, not returned
-    CUDA_TRY(cudaMalloc(&scratch, sizeof(int) * (size_t)(6 * gmax + E + 2)));
+    // The group table (not returned) comes from the stream-ordered pool and
+    // goes back to it behind the kernel: no device-wide synchronisation, and
+    // the call returns without waiting for the stream.
+    cudaStream_t st = (cudaStream_t)stream;
+    int* scratch = nullptr;
+    CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&scratch), sizeof(int) * (size_t)(6 * gmax + E + 2), st));
     glc::DispatchPlan plan{};
     plan.counts = counts;
     plan.offsets = offsets;
@@ -1362,10 +1366,10 @@ int glc_dispatch_plan_dev(const int32_t* ids, int32_t P, int32_t E, int32_t* cou
     plan.grp_units = scratch + 4 * gmax;
     plan.grp_first = scratch + 5 * gmax;
     plan.meta = scratch + 5 * gmax + E;
-    cudaError_t e = glc::dispatch_plan_launch(ids, P, E, plan, (cudaStream_t)stream);
-    if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
-    cudaFree(scratch);
+    const cudaError_t e = glc::dispatch_plan_launch(ids, P, E, plan, st);
+    const cudaError_t f = cudaFreeAsync(scratch, st);
     if (e != cudaSuccess) return fail(GLC_ERR_CUDA, "dispatch plan: %s", cudaGetErrorString(e));
+    if (f != cudaSuccess) return fail(GLC_ERR_CUDA, "dispatch plan scratch: %s", cudaGetErrorString(f));
     return GLC_OK;
 }
 
@@ -1402,16 +1406,20 @@ int glc_wire_quantize(int32_t mode, const float* x, int32_t T, int32_t D, uint8_
         return fail(GLC_ERR_INVALID_ARG, "Destination buffer too small (%zu < %zu)", out_bytes, need);
     if (need == 0) return GLC_OK;
     if (!x || !out) return fail(GLC_ERR_INVALID_ARG, "null pointer");
+    // device buffers from the stream-ordered pool (no device-wide
+    // synchronisation); the host copies make the call synchronous
+    const cudaStream_t st = cudaStreamLegacy;
     float* dx = nullptr;
     uint8_t* dq = nullptr;
-    CUDA_TRY(cudaMalloc(&dx, sizeof(float) * (size_t)T * D));
-    cudaError_t e = cudaMalloc(&dq, need);
-    if (e != cudaSuccess) { cudaFree(dx); return fail(GLC_ERR_OOM, "cudaMalloc failed"); }
-    e = cudaMemcpy(dx, x, sizeof(float) * (size_t)T * D, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = glc::wire_quantize_launch(mode, dx, T, D, dq, nullptr);
-    if (e == cudaSuccess) e = cudaMemcpy(out, dq, need, cudaMemcpyDeviceToHost);
-    cudaFree(dx);
-    cudaFree(dq);
+    CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&dx), sizeof(float) * (size_t)T * D, st));
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&dq), need, st);
+    if (e != cudaSuccess) { cudaFreeAsync(dx, st); return fail(GLC_ERR_OOM, "device buffer: %s", cudaGetErrorString(e)); }
+    e = cudaMemcpyAsync(dx, x, sizeof(float) * (size_t)T * D, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = glc::wire_quantize_launch(mode, dx, T, D, dq, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out, dq, need, cudaMemcpyDeviceToHost, st);
+    cudaFreeAsync(dx, st);
+    cudaFreeAsync(dq, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) return fail(GLC_ERR_CUDA, "wire quantize: %s", cudaGetErrorString(e));
     return GLC_OK;
 }
@@ -1422,16 +1430,18 @@ int glc_wire_dequantize(int32_t mode, const uint8_t* in, size_t in_bytes, int32_
     if (in_bytes < need) return fail(GLC_ERR_INVALID_ARG, "Source buffer too small (%zu < %zu)", in_bytes, need);
     if (need == 0) return GLC_OK;
     if (!in || !out) return fail(GLC_ERR_INVALID_ARG, "null pointer");
+    const cudaStream_t st = cudaStreamLegacy;
     float* dx = nullptr;
     uint8_t* dq = nullptr;
-    CUDA_TRY(cudaMalloc(&dq, need));
-    cudaError_t e = cudaMalloc(&dx, sizeof(float) * (size_t)T * D);
-    if (e != cudaSuccess) { cudaFree(dq); return fail(GLC_ERR_OOM, "cudaMalloc failed"); }
-    e = cudaMemcpy(dq, in, need, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = glc::wire_dequantize_launch(mode, dq, T, D, dx, nullptr);
-    if (e == cudaSuccess) e = cudaMemcpy(out, dx, sizeof(float) * (size_t)T * D, cudaMemcpyDeviceToHost);
-    cudaFree(dx);
-    cudaFree(dq);
+    CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&dq), need, st));
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&dx), sizeof(float) * (size_t)T * D, st);
+    if (e != cudaSuccess) { cudaFreeAsync(dq, st); return fail(GLC_ERR_OOM, "device buffer: %s", cudaGetErrorString(e)); }
+    e = cudaMemcpyAsync(dq, in, need, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = glc::wire_dequantize_launch(mode, dq, T, D, dx, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out, dx, sizeof(float) * (size_t)T * D, cudaMemcpyDeviceToHost, st);
+    cudaFreeAsync(dx, st);
+    cudaFreeAsync(dq, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) return fail(GLC_ERR_CUDA, "wire dequantize: %s", cudaGetErrorString(e));
     return GLC_OK;
 }

@@ -55,11 +55,13 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_split_kernel(const A
 
     const int g = blockIdx.x, chunk = blockIdx.y, tid = threadIdx.x;
     const int G = p.n_heads / p.n_kv_heads;
-    const int L = p.pos + 1;
+    const int pos = p.pos_dev ? *p.pos_dev : p.pos;  // graph replays read the position from device memory
+    if (chunk * kChunk > pos) return;                // a chunk past the position (device-position launches)
+    const int L = pos + 1;
     const int p0 = chunk * kChunk, np = min(kChunk, L - p0);
     // the chunk's K and V rows already in the cache, all loads in flight first
     const size_t head_off = (size_t)g * p.max_len * kHd;
-    const int nold = min(np, p.pos - p0);
+    const int nold = min(np, pos - p0);
     constexpr int kLd = kChunk * (kHd / 8) / kAttnThreads;  // 16-byte loads per thread and matrix
     uint4 kr[kLd], vr[kLd];
 #pragma unroll
@@ -71,7 +73,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_split_kernel(const A
             vr[j] = __ldg(reinterpret_cast<const uint4*>(p.v_cache + src));
         }
     }
-    if (tid < kHd / 2) rope_cs(p.pos, p.theta, tid, cs_c[tid], cs_s[tid]);
+    if (tid < kHd / 2) rope_cs(pos, p.theta, tid, cs_c[tid], cs_s[tid]);
     __syncthreads();
 
     // rotated, scaled queries of this group
@@ -92,8 +94,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_split_kernel(const A
         }
     }
     // the row of pos comes from the inputs
-    if (p.pos >= p0 && p.pos < p0 + kChunk && tid < kHd / 2) {
-        const int r = p.pos - p0, i = tid;
+    if (pos >= p0 && pos < p0 + kChunk && tid < kHd / 2) {
+        const int r = pos - p0, i = tid;
         const float* kn = p.k_new + (size_t)g * kHd;
         const float* vn = p.v_new + (size_t)g * kHd;
         const float a = kn[i], b = kn[i + kHd / 2];
@@ -104,7 +106,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_split_kernel(const A
         ks[r * kKStride + i + kHd / 2] = k1;
         vs[r * kHd + i] = v0;
         vs[r * kHd + i + kHd / 2] = v1;
-        const size_t dst = head_off + (size_t)p.pos * kHd;
+        const size_t dst = head_off + (size_t)pos * kHd;
         p.k_cache[dst + i] = __half_as_ushort(k0);
         p.k_cache[dst + i + kHd / 2] = __half_as_ushort(k1);
         p.v_cache[dst + i] = __half_as_ushort(v0);
@@ -202,19 +204,20 @@ __global__ void __launch_bounds__(kAttnThreads) attn_combine_kernel(const AttnPa
     __shared__ float wts[kChunk];
     const int hq = blockIdx.x, tid = threadIdx.x;
     const int G = p.n_heads / p.n_kv_heads, g = hq / G, h = hq - g * G;
+    const int nact = ((p.pos_dev ? *p.pos_dev : p.pos) + kChunk) / kChunk;  // chunks written (<= p.nchunks)
     const size_t cstride = (size_t)G * (kHd + 2);
     const float* bh = p.work + (size_t)g * p.nchunks * cstride + (size_t)h * (kHd + 2);
     if (tid < 32) {
         const int lane = tid;
-        const float m0 = lane < p.nchunks ? __ldg(bh + lane * cstride + kHd) : -INFINITY;
-        const float m1 = lane + 32 < p.nchunks ? __ldg(bh + (lane + 32) * cstride + kHd) : -INFINITY;
-        const float l0 = lane < p.nchunks ? __ldg(bh + lane * cstride + kHd + 1) : 0.f;
-        const float l1 = lane + 32 < p.nchunks ? __ldg(bh + (lane + 32) * cstride + kHd + 1) : 0.f;
+        const float m0 = lane < nact ? __ldg(bh + lane * cstride + kHd) : -INFINITY;
+        const float m1 = lane + 32 < nact ? __ldg(bh + (lane + 32) * cstride + kHd) : -INFINITY;
+        const float l0 = lane < nact ? __ldg(bh + lane * cstride + kHd + 1) : 0.f;
+        const float l1 = lane + 32 < nact ? __ldg(bh + (lane + 32) * cstride + kHd + 1) : 0.f;
         float M = fmaxf(m0, m1);
 #pragma unroll
         for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-        const float f0 = lane < p.nchunks ? __expf(m0 - M) : 0.f;
-        const float f1 = lane + 32 < p.nchunks ? __expf(m1 - M) : 0.f;
+        const float f0 = lane < nact ? __expf(m0 - M) : 0.f;
+        const float f1 = lane + 32 < nact ? __expf(m1 - M) : 0.f;
         float l = l0 * f0 + l1 * f1;
 #pragma unroll
         for (int o = 16; o >= 1; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
@@ -224,7 +227,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_combine_kernel(const AttnPa
     __syncthreads();
     float acc = 0.f;
 #pragma unroll 8
-    for (int c = 0; c < p.nchunks; ++c) acc = fmaf(__ldg(bh + c * cstride + tid), wts[c], acc);
+    for (int c = 0; c < nact; ++c) acc = fmaf(__ldg(bh + c * cstride + tid), wts[c], acc);
     p.out[(size_t)hq * kHd + tid] = acc;
 }
 
@@ -242,8 +245,11 @@ size_t attn_workspace_bytes(int n_heads, int n_kv_heads, int max_len) {
 cudaError_t attn_decode_launch(AttnParams p, cudaStream_t stream) {
     if (p.head_dim != kHd || p.n_kv_heads <= 0 || p.n_heads % p.n_kv_heads) return cudaErrorInvalidValue;
     const int G = p.n_heads / p.n_kv_heads;
-    if (G > kAttnMaxGroup || p.pos < 0 || p.pos >= p.max_len || p.max_len > kAttnMaxLen) return cudaErrorInvalidValue;
-    p.nchunks = (p.pos + 1 + kChunk - 1) / kChunk;
+    if (G > kAttnMaxGroup || p.max_len > kAttnMaxLen) return cudaErrorInvalidValue;
+    if (!p.pos_dev && (p.pos < 0 || p.pos >= p.max_len)) return cudaErrorInvalidValue;
+    // a device position (0 <= *pos_dev < max_len, the caller's contract) gets
+    // the launch shape of max_len: the same launch serves every position
+    p.nchunks = p.pos_dev ? (p.max_len + kChunk - 1) / kChunk : (p.pos + 1 + kChunk - 1) / kChunk;
     attn_decode_split_kernel<<<dim3(p.n_kv_heads, p.nchunks), kAttnThreads, 0, stream>>>(p);
     attn_combine_kernel<<<p.n_heads, kAttnThreads, 0, stream>>>(p);
     return cudaGetLastError();

@@ -127,6 +127,19 @@ __device__ __forceinline__ void drain_issued_stages(uint64_t* full, int S, int i
         mbar_wait(&full[st % S], (uint32_t)(st / S) & 1u, nullptr, 0, limit_ns);
 }
 
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialisation may start while the kernel before it on the stream is still
+// running: it must call grid_dep_wait() before touching anything that kernel
+// writes (or reads and this one writes); grid_dep_wait returns once that
+// kernel has completed and its memory is visible.  grid_dep_launch_dependents
+// lets the next such kernel be scheduled once every CTA of this one has
+// called it or exited.  Both are no-ops for a kernel launched without the
+// attribute, or without such a dependent.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // 1-D bulk copy global -> shared, completion counted on `bar` in bytes.
 // dst, src 16-byte aligned; bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,

@@ -81,6 +81,10 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
 
     if (warp == NW) {
         // ------------------------------------------------------ producer warp
+        // Launched behind another kernel with programmatic serialisation, the
+        // weight stream of a plain GEMV starts at once (no kernel writes
+        // weights); the other modes first wait for the expert ids.
+        if (p.mode != kGemvPlain) grid_dep_wait();
         if (lane == 0) {
             const uint64_t pol = GLC_GEMV_L2_HINT ? l2_evict_first_policy() : 0ull;
             bool ok = true;
@@ -129,6 +133,8 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
             // the copies in flight land before this warp, and so the CTA, exits
             drain_issued_stages(full, S, issued, kWaitLimitNs);
         }
+        __syncwarp();
+        grid_dep_launch_dependents();
         return;
     }
 
@@ -146,6 +152,7 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
     XRegs xr;
     int cur_x = -1;
     bool ok = true;
+    grid_dep_wait();  // the input is the previous kernel's output
     for_each_stage<SPLIT>(p, r0, r1, [&](int sidx, int seg, int j, int, int nr, int lr0) {
         if (!ok) return;
         const int jj = SPLIT ? js : j;
@@ -167,6 +174,9 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
         if (lane == 0) mbar_arrive(&empty[buf]);
     });
 
+    // the next kernel of the stream may be scheduled once every CTA is here
+    // (it waits for this kernel's completion before it reads the output)
+    grid_dep_launch_dependents();
     named_bar_sync(1, NW * 32);
     if (!ok) return;
 
@@ -250,11 +260,21 @@ cudaError_t gemv_launch(const GemvParams& p0, int num_sms, cudaStream_t stream) 
     }
     const size_t smem_limit = (size_t)smem_optin[dev];
     if (gemv_configure(p, num_sms, smem_limit, &smem, &grid) != 0) return cudaErrorInvalidValue;
-    if (p.split)
-        q4k_gemv_kernel<true><<<grid, (p.nw + 1) * 32, smem, stream>>>(p);
-    else
-        q4k_gemv_kernel<false><<<grid, (p.nw + 1) * 32, smem, stream>>>(p);
-    return cudaGetLastError();
+    // Programmatic stream serialisation: a GEMV behind another kernel starts
+    // on each SM as soon as that kernel's CTA there has left (and a plain
+    // GEMV streams its weights at once), instead of after the whole grid
+    // and a launch gap; the kernel waits before reading what came before.
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3((p.nw + 1) * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return p.split ? cudaLaunchKernelEx(&cfg, q4k_gemv_kernel<true>, p) : cudaLaunchKernelEx(&cfg, q4k_gemv_kernel<false>, p);
 }
 
 }  // namespace glc

@@ -70,7 +70,8 @@ struct AttnParams {
     float* work;           // attn_workspace_bytes()
     int n_heads, n_kv_heads, head_dim, max_len, pos;
     float theta;
-    int nchunks;           // set by attn_decode_launch
+    int nchunks;           // set by attn_decode_launch (workspace layout)
+    const int* pos_dev = nullptr;  // when set, the position is read here (a launch any position can replay)
 };
 size_t attn_workspace_bytes(int n_heads, int n_kv_heads, int max_len);
 cudaError_t attn_decode_launch(AttnParams p, cudaStream_t stream);

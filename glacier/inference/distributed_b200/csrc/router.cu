@@ -197,7 +197,6 @@ static cudaError_t launch_router(const RouterParams& p, cudaStream_t stream) {
 // bit-identical to router_kernel's.  Rank 0 also writes xin and the shared-
 // expert gate.
 constexpr int kWideGroup = 8;     // experts per CTA
-constexpr int kWideMaxCtas = 8;   // cluster size for E = 64 (portable limit)
 
 template <int TB, int UNROLL>
 __global__ void __launch_bounds__(kRouterThreads) router_wide_kernel(const __grid_constant__ RouterParams p) {

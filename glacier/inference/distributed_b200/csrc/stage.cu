@@ -1,0 +1,600 @@
+// stage.cu -- a dense decoder pipeline stage on sm_100a: one token through a
+// range of transformer layers with its KV cache, the counterpart of
+// IClusterStageModel.ForwardStage (Pipeline/IClusterStageModel.cs:19; the
+// reference's stage bodies are its external model package, Program.cs:41-110,
+// 1382-1390) for the Qwen2-style dense layers of a pipeline-parallel model
+// (the reference splits the layer range over LAN nodes, DistributedClusterSession.cs:
+// 775-830, and quantises the activations at every stage boundary, Program.cs:743).
+//
+// Per layer, on the stage's stream:
+//   h   = RMSNorm(x) * w_attn                    (weighted, eps from the descriptor)
+//   qkv = [Wq; Wk; Wv] h + [bq; bk; bv]           (one Q4_K GEMV over the stacked rows)
+//   o   = attention(q, k, v; the layer's fp16 KV cache at pos)   (attention.cu)
+//   x   = x + Wo o                                (GEMV with the residual in its epilogue)
+//   h   = RMSNorm(x) * w_ffn
+//   a   = SiLU(Wgate h) * (Wup h)                 (GEMV gate/up with the SwiGLU epilogue)
+//   x   = x + Wdown a                             (GEMV with the residual)
+// with, on a first stage, x = dequantised row `token` of the Q4_K embedding
+// table and, on a last stage asked for logits, logits = Wlm RMSNorm(x) * w_final
+// and the arg-max token.  The position lives in device memory, so the whole
+// stage step is one CUDA graph replayed for every token (the attention's launch
+// shape does not depend on the position); the GEMVs are programmatically
+// serialised, so each starts streaming its weights as the kernel before it
+// leaves each SM.
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+#include "../../../../include/glacier_b200.h"
+#include "common.cuh"
+#include "kernels.h"
+#include "synth.h"
+
+namespace glc {
+int set_last_error(int code, const char* msg);
+}
+
+namespace {
+
+using glc::grid_dep_launch_dependents;
+using glc::grid_dep_wait;
+using glc::warp_tree;
+
+constexpr int kHeadDim = 128;
+constexpr int kNormThreads = 512;
+
+// y = x * (1 / sqrt(mean(x^2) + eps)) * w (w may be null: no weight).  One
+// CTA; the sum of squares in a fixed order (strided partials, warp butterfly,
+// warp sums in order), so the result is deterministic.
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_w_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                                 int D, float eps, float* __restrict__ y) {
+    __shared__ float red[kNormThreads / 32];
+    __shared__ float s_scale;
+    grid_dep_wait();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float a = 0.f;
+    for (int d = tid; d < D; d += kNormThreads) a = fmaf(x[d], x[d], a);
+    a = warp_tree(a);
+    if (lane == 0) red[warp] = a;
+    __syncthreads();
+    if (tid == 0) {
+        float ss = 0.f;
+        for (int i = 0; i < kNormThreads / 32; ++i) ss += red[i];
+        s_scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), eps)));
+    }
+    __syncthreads();
+    const float r = s_scale;
+    for (int d = tid; d < D; d += kNormThreads) y[d] = w ? __fmul_rn(__fmul_rn(x[d], r), w[d]) : __fmul_rn(x[d], r);
+    grid_dep_launch_dependents();
+}
+
+__global__ void __launch_bounds__(256) bias_add_kernel(float* __restrict__ y, const float* __restrict__ b, int n) {
+    grid_dep_wait();
+    const int i = blockIdx.x * 256 + threadIdx.x;
+    if (i < n) y[i] = __fadd_rn(y[i], b[i]);
+    grid_dep_launch_dependents();
+}
+
+// x[0..D) = dequantised row *token of a Q4_K table [rows][D/256*144]
+// ((d*sc)*q - dmin*m, the GGUF Q4_K values), one thread per weight.
+__global__ void __launch_bounds__(256) q4k_row_kernel(const uint8_t* __restrict__ table, const int* __restrict__ token,
+                                                      int rows, int D, float* __restrict__ x) {
+    grid_dep_wait();
+    const int i = blockIdx.x * 256 + threadIdx.x;
+    if (i >= D) return;
+    int t = *token;
+    t = t < 0 ? 0 : (t >= rows ? rows - 1 : t);
+    const uint8_t* blk = table + (size_t)t * (D / 256) * 144 + (size_t)(i / 256) * 144;
+    const int w = i & 255, c = w >> 6, l = w & 63, j = 2 * c + (l >> 5);
+    const uint8_t* sc = blk + 4;
+    int s, m;
+    if (j < 4) {
+        s = sc[j] & 63;
+        m = sc[j + 4] & 63;
+    } else {
+        s = (sc[j + 4] & 0xF) | ((sc[j - 4] >> 6) << 4);
+        m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+    }
+    const uint8_t qb = blk[16 + 32 * c + (l & 31)];
+    const int q = (l < 32) ? (qb & 0xF) : (qb >> 4);
+    const float d = __half2float(__ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8))));
+    const float dmin = __half2float(__ushort_as_half((unsigned short)(blk[2] | (blk[3] << 8))));
+    // each product rounded, as the GGUF dequantisation does (no contraction)
+    x[i] = __fsub_rn(__fmul_rn(__fmul_rn(d, (float)s), (float)q), __fmul_rn(dmin, (float)m));
+}
+
+// Arg-max of n logits (NaN as -inf, the lower index on ties) into *out.
+__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ v, int n, int* __restrict__ out) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    grid_dep_wait();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = tid; i < n; i += 1024) {
+        const float x = isnan(v[i]) ? -INFINITY : v[i];
+        if (x > best || (x == best && i < bi)) { best = x; bi = i; }
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+    }
+    if (lane == 0) { sv[warp] = best; si[warp] = bi; }
+    __syncthreads();
+    if (tid == 0) {
+        for (int w = 1; w < 32; ++w)
+            if (sv[w] > best || (sv[w] == best && si[w] < bi)) { best = sv[w]; bi = si[w]; }
+        *out = bi == 0x7fffffff ? 0 : bi;
+    }
+}
+
+__global__ void fill_int_kernel(int* p, int v) { *p = v; }
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    return glc::set_last_error(code, buf);
+}
+
+#define CUDA_TRY(call)                                                                          \
+    do {                                                                                        \
+        const cudaError_t e_ = (call);                                                          \
+        if (e_ != cudaSuccess) return fail(GLC_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+    } while (0)
+
+size_t rowbytes(int k) { return (size_t)(k / 256) * 144; }
+
+struct StageLayer {
+    float* attn_norm = nullptr;
+    uint8_t* wqkv = nullptr;  // [(Hq + 2 Hkv) * 128][rowbytes(D)]
+    float* bqkv = nullptr;
+    uint8_t* wo = nullptr;    // [D][rowbytes(Hq * 128)]
+    float* ffn_norm = nullptr;
+    uint8_t* wgate = nullptr;  // [FF][rowbytes(D)]
+    uint8_t* wup = nullptr;
+    uint8_t* wdown = nullptr;  // [D][rowbytes(FF)]
+    uint16_t* kc = nullptr;    // fp16 [Hkv][max_len][128]
+    uint16_t* vc = nullptr;
+    bool loaded = false;
+};
+
+// host-side bytes of each tensor of a layer
+struct Sizes {
+    size_t qkv_rows, wqkv, wo, wgu, wdown, cache;
+};
+
+}  // namespace
+
+struct glc_stage {
+    glc_stage_desc d{};
+    int num_sms = 0;
+    cudaStream_t stream = nullptr;
+    Sizes sz{};
+    std::vector<StageLayer> layers;
+    uint8_t* embed = nullptr;     // Q4_K [vocab][rowbytes(D)] (first stage)
+    float* final_norm = nullptr;  // [D] (last stage)
+    uint8_t* lm_head = nullptr;   // Q4_K [vocab][rowbytes(D)] (last stage)
+    // device workspace
+    float* x = nullptr;      // [D] the stage's residual stream
+    float* h = nullptr;      // [max(D, Hq*128)] normalised input
+    float* qkv = nullptr;    // [(Hq + 2 Hkv) * 128]
+    float* attn = nullptr;   // [Hq * 128]
+    float* act = nullptr;    // [FF]
+    float* logits = nullptr; // [vocab]
+    float* attn_work = nullptr;
+    float* ones = nullptr;   // [1]
+    int* zeros = nullptr;    // [1]
+    int* pos = nullptr;      // the position the next step uses
+    int* token = nullptr;    // input token (first stage) / arg-max token (last stage)
+    int* err = nullptr;
+    // the captured stage step per (embed, logits) variant
+    cudaGraphExec_t graphs[4] = {};
+};
+
+namespace {
+
+int check(glc_stage* h) {
+    if (!h) return fail(GLC_ERR_INVALID_ARG, "null stage handle");
+    return GLC_OK;
+}
+
+// One token through the stage's layers on `st` (position from h->pos).
+int stage_step(glc_stage* h, bool embed, bool logits, cudaStream_t st) {
+    const glc_stage_desc& d = h->d;
+    const int D = d.hidden_dim, FF = d.ffn_dim, Hq = d.n_heads, Hkv = d.n_kv_heads;
+    const int qrows = (Hq + 2 * Hkv) * kHeadDim;
+    if (embed) {
+        q4k_row_kernel<<<(D + 255) / 256, 256, 0, st>>>(h->embed, h->token, d.vocab, D, h->x);
+        CUDA_TRY(cudaGetLastError());
+    }
+    for (int l = 0; l < d.layer_count; ++l) {
+        StageLayer& L = h->layers[l];
+        rmsnorm_w_kernel<<<1, kNormThreads, 0, st>>>(h->x, L.attn_norm, D, d.rms_eps, h->h);
+        CUDA_TRY(cudaGetLastError());
+        glc::GemvParams g{};
+        g.mode = glc::kGemvPlain;
+        g.K = D;
+        g.rows = qrows;
+        g.nseg = 1;
+        g.kslots = 1;
+        g.num_experts = 1;
+        g.A = L.wqkv;
+        g.x = h->h;
+        g.y = h->qkv;
+        g.err = h->err;
+        CUDA_TRY(glc::gemv_launch(g, h->num_sms, st));
+        bias_add_kernel<<<(qrows + 255) / 256, 256, 0, st>>>(h->qkv, L.bqkv, qrows);
+        CUDA_TRY(cudaGetLastError());
+        glc::AttnParams ap{};
+        ap.q = h->qkv;
+        ap.k_new = h->qkv + (size_t)Hq * kHeadDim;
+        ap.v_new = h->qkv + (size_t)(Hq + Hkv) * kHeadDim;
+        ap.k_cache = L.kc;
+        ap.v_cache = L.vc;
+        ap.out = h->attn;
+        ap.work = h->attn_work;
+        ap.n_heads = Hq;
+        ap.n_kv_heads = Hkv;
+        ap.head_dim = kHeadDim;
+        ap.max_len = d.max_len;
+        ap.pos = 0;
+        ap.pos_dev = h->pos;
+        ap.theta = d.rope_theta;
+        CUDA_TRY(glc::attn_decode_launch(ap, st));
+        glc::GemvParams o{};
+        o.mode = glc::kGemvDownCombine;  // x = x + Wo attn (one slot, unit weight)
+        o.K = Hq * kHeadDim;
+        o.rows = D;
+        o.nseg = 1;
+        o.kslots = 1;
+        o.num_experts = 1;
+        o.A = L.wo;
+        o.ids = h->zeros;
+        o.cw = h->ones;
+        o.x = h->attn;
+        o.y = h->x;
+        o.accumulate = 1;
+        o.err = h->err;
+        CUDA_TRY(glc::gemv_launch(o, h->num_sms, st));
+        rmsnorm_w_kernel<<<1, kNormThreads, 0, st>>>(h->x, L.ffn_norm, D, d.rms_eps, h->h);
+        CUDA_TRY(cudaGetLastError());
+        glc::GemvParams gu{};
+        gu.mode = glc::kGemvGateUp;  // act = SiLU(Wgate h) * (Wup h)
+        gu.K = D;
+        gu.rows = FF;
+        gu.nseg = 1;
+        gu.kslots = 1;
+        gu.num_experts = 1;
+        gu.A = L.wgate;
+        gu.B = L.wup;
+        gu.ids = h->zeros;
+        gu.x = h->h;
+        gu.y = h->act;
+        gu.err = h->err;
+        CUDA_TRY(glc::gemv_launch(gu, h->num_sms, st));
+        glc::GemvParams dn = o;  // x = x + Wdown act
+        dn.K = FF;
+        dn.A = L.wdown;
+        dn.x = h->act;
+        CUDA_TRY(glc::gemv_launch(dn, h->num_sms, st));
+    }
+    if (logits) {
+        rmsnorm_w_kernel<<<1, kNormThreads, 0, st>>>(h->x, h->final_norm, D, d.rms_eps, h->h);
+        CUDA_TRY(cudaGetLastError());
+        glc::GemvParams lm{};
+        lm.mode = glc::kGemvPlain;
+        lm.K = D;
+        lm.rows = d.vocab;
+        lm.nseg = 1;
+        lm.kslots = 1;
+        lm.num_experts = 1;
+        lm.A = h->lm_head;
+        lm.x = h->h;
+        lm.y = h->logits;
+        lm.err = h->err;
+        CUDA_TRY(glc::gemv_launch(lm, h->num_sms, st));
+        argmax_kernel<<<1, 1024, 0, st>>>(h->logits, d.vocab, h->token);
+        CUDA_TRY(cudaGetLastError());
+    }
+    return GLC_OK;
+}
+
+void free_stage(glc_stage* h) {
+    for (auto& L : h->layers) {
+        cudaFree(L.attn_norm); cudaFree(L.wqkv); cudaFree(L.bqkv); cudaFree(L.wo); cudaFree(L.ffn_norm);
+        cudaFree(L.wgate); cudaFree(L.wup); cudaFree(L.wdown); cudaFree(L.kc); cudaFree(L.vc);
+    }
+    cudaFree(h->embed); cudaFree(h->final_norm); cudaFree(h->lm_head);
+    cudaFree(h->x); cudaFree(h->h); cudaFree(h->qkv); cudaFree(h->attn); cudaFree(h->act); cudaFree(h->logits);
+    cudaFree(h->attn_work); cudaFree(h->ones); cudaFree(h->zeros); cudaFree(h->pos); cudaFree(h->token);
+    cudaFree(h->err);
+    for (auto& g : h->graphs)
+        if (g) cudaGraphExecDestroy(g);
+    if (h->stream) cudaStreamDestroy(h->stream);
+}
+
+}  // namespace
+
+extern "C" {
+
+int glc_stage_create(const glc_stage_desc* desc, glc_stage** out) {
+    if (!desc || !out) return fail(GLC_ERR_INVALID_ARG, "null argument");
+    *out = nullptr;
+    const glc_stage_desc& d = *desc;
+    if (d.hidden_dim <= 0 || d.ffn_dim <= 0 || d.n_heads <= 0 || d.n_kv_heads <= 0 || d.layer_count <= 0)
+        return fail(GLC_ERR_INVALID_ARG, "dimensions and layer count must be positive");
+    if (d.head_dim != kHeadDim) return fail(GLC_ERR_UNSUPPORTED, "head_dim %d: 128 supported", d.head_dim);
+    if (d.hidden_dim % 256 || d.ffn_dim % 256 || (d.n_heads * kHeadDim) % 256)
+        return fail(GLC_ERR_UNSUPPORTED, "Q4_K needs hidden, ffn and head widths that are multiples of 256");
+    if (d.n_heads % d.n_kv_heads || d.n_heads / d.n_kv_heads > glc::kAttnMaxGroup)
+        return fail(GLC_ERR_UNSUPPORTED, "at most %d query heads per KV head", glc::kAttnMaxGroup);
+    if (d.max_len <= 0 || d.max_len > glc::kAttnMaxLen) return fail(GLC_ERR_INVALID_ARG, "max_len 1..%d", glc::kAttnMaxLen);
+    if ((d.has_embedding || d.has_lm_head) && d.vocab <= 0) return fail(GLC_ERR_INVALID_ARG, "vocab must be positive");
+    CUDA_TRY(cudaSetDevice(d.device));
+    cudaDeviceProp prop;
+    CUDA_TRY(cudaGetDeviceProperties(&prop, d.device));
+    if (prop.major < 10) return fail(GLC_ERR_UNSUPPORTED, "sm_100a required");
+    glc_stage* h = new glc_stage();
+    h->d = d;
+    h->num_sms = prop.multiProcessorCount;
+    const int D = d.hidden_dim, FF = d.ffn_dim, Hq = d.n_heads, Hkv = d.n_kv_heads;
+    h->sz.qkv_rows = (size_t)(Hq + 2 * Hkv) * kHeadDim;
+    h->sz.wqkv = h->sz.qkv_rows * rowbytes(D);
+    h->sz.wo = (size_t)D * rowbytes(Hq * kHeadDim);
+    h->sz.wgu = (size_t)FF * rowbytes(D);
+    h->sz.wdown = (size_t)D * rowbytes(FF);
+    h->sz.cache = (size_t)Hkv * d.max_len * kHeadDim * sizeof(uint16_t);
+    h->layers.resize(d.layer_count);
+    auto bad = [&](const char* what) {
+        free_stage(h);
+        delete h;
+        return fail(GLC_ERR_OOM, "cudaMalloc: %s", what);
+    };
+#define SALLOC(ptr, bytes) \
+    if (cudaMalloc(reinterpret_cast<void**>(&(ptr)), (bytes)) != cudaSuccess) return bad(#ptr)
+    if (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess) return bad("stream");
+    for (auto& L : h->layers) {
+        SALLOC(L.attn_norm, sizeof(float) * D);
+        SALLOC(L.wqkv, h->sz.wqkv);
+        SALLOC(L.bqkv, sizeof(float) * h->sz.qkv_rows);
+        SALLOC(L.wo, h->sz.wo);
+        SALLOC(L.ffn_norm, sizeof(float) * D);
+        SALLOC(L.wgate, h->sz.wgu);
+        SALLOC(L.wup, h->sz.wgu);
+        SALLOC(L.wdown, h->sz.wdown);
+        SALLOC(L.kc, h->sz.cache);
+        SALLOC(L.vc, h->sz.cache);
+        cudaMemset(L.kc, 0, h->sz.cache);
+        cudaMemset(L.vc, 0, h->sz.cache);
+    }
+    if (d.has_embedding) SALLOC(h->embed, (size_t)d.vocab * rowbytes(D));
+    if (d.has_lm_head) {
+        SALLOC(h->final_norm, sizeof(float) * D);
+        SALLOC(h->lm_head, (size_t)d.vocab * rowbytes(D));
+        SALLOC(h->logits, sizeof(float) * d.vocab);
+    }
+    SALLOC(h->x, sizeof(float) * D);
+    SALLOC(h->h, sizeof(float) * std::max(D, Hq * kHeadDim));
+    SALLOC(h->qkv, sizeof(float) * h->sz.qkv_rows);
+    SALLOC(h->attn, sizeof(float) * Hq * kHeadDim);
+    SALLOC(h->act, sizeof(float) * FF);
+    SALLOC(h->attn_work, glc::attn_workspace_bytes(Hq, Hkv, d.max_len));
+    SALLOC(h->ones, sizeof(float));
+    SALLOC(h->zeros, sizeof(int));
+    SALLOC(h->pos, sizeof(int));
+    SALLOC(h->token, sizeof(int));
+    SALLOC(h->err, sizeof(int) * 8);
+#undef SALLOC
+    const float one = 1.0f;
+    cudaMemcpy(h->ones, &one, sizeof(float), cudaMemcpyHostToDevice);
+    cudaMemset(h->zeros, 0, sizeof(int));
+    cudaMemset(h->pos, 0, sizeof(int));
+    cudaMemset(h->token, 0, sizeof(int));
+    cudaMemset(h->err, 0, sizeof(int) * 8);
+    if (cudaDeviceSynchronize() != cudaSuccess) return bad("initialisation");
+    *out = h;
+    return GLC_OK;
+}
+
+int glc_stage_destroy(glc_stage* h) {
+    if (!h) return GLC_OK;
+    cudaSetDevice(h->d.device);
+    if (h->stream) cudaStreamSynchronize(h->stream);
+    free_stage(h);
+    delete h;
+    return GLC_OK;
+}
+
+int glc_stage_load_layer(glc_stage* h, int32_t layer, const glc_dense_layer_weights* w) {
+    int rc = check(h);
+    if (rc) return rc;
+    if (!w || !w->attn_norm || !w->wq || !w->wk || !w->wv || !w->wo || !w->ffn_norm || !w->w_gate || !w->w_up ||
+        !w->w_down)
+        return fail(GLC_ERR_INVALID_ARG, "null weight pointer");
+    if (layer < 0 || layer >= h->d.layer_count) return fail(GLC_ERR_INVALID_ARG, "layer %d out of range", layer);
+    CUDA_TRY(cudaSetDevice(h->d.device));
+    StageLayer& L = h->layers[layer];
+    const int D = h->d.hidden_dim, Hq = h->d.n_heads, Hkv = h->d.n_kv_heads;
+    const size_t rq = (size_t)Hq * kHeadDim * rowbytes(D), rk = (size_t)Hkv * kHeadDim * rowbytes(D);
+    CUDA_TRY(cudaMemcpy(L.attn_norm, w->attn_norm, sizeof(float) * D, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(L.wqkv, w->wq, rq, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(L.wqkv + rq, w->wk, rk, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(L.wqkv + rq + rk, w->wv, rk, cudaMemcpyHostToDevice));
+    const size_t nq = (size_t)Hq * kHeadDim, nk = (size_t)Hkv * kHeadDim;
+    if (w->bq) CUDA_TRY(cudaMemcpy(L.bqkv, w->bq, sizeof(float) * nq, cudaMemcpyHostToDevice));
+    else CUDA_TRY(cudaMemset(L.bqkv, 0, sizeof(float) * nq));
+    if (w->bk) CUDA_TRY(cudaMemcpy(L.bqkv + nq, w->bk, sizeof(float) * nk, cudaMemcpyHostToDevice));
+    else CUDA_TRY(cudaMemset(L.bqkv + nq, 0, sizeof(float) * nk));
+    if (w->bv) CUDA_TRY(cudaMemcpy(L.bqkv + nq + nk, w->bv, sizeof(float) * nk, cudaMemcpyHostToDevice));
+    else CUDA_TRY(cudaMemset(L.bqkv + nq + nk, 0, sizeof(float) * nk));
+    CUDA_TRY(cudaMemcpy(L.wo, w->wo, h->sz.wo, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(L.ffn_norm, w->ffn_norm, sizeof(float) * D, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(L.wgate, w->w_gate, h->sz.wgu, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(L.wup, w->w_up, h->sz.wgu, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(L.wdown, w->w_down, h->sz.wdown, cudaMemcpyHostToDevice));
+    L.loaded = true;
+    return GLC_OK;
+}
+
+int glc_stage_load_io(glc_stage* h, const void* embedding, const float* final_norm, const void* lm_head) {
+    int rc = check(h);
+    if (rc) return rc;
+    CUDA_TRY(cudaSetDevice(h->d.device));
+    const size_t tb = (size_t)h->d.vocab * rowbytes(h->d.hidden_dim);
+    if (h->d.has_embedding) {
+        if (!embedding) return fail(GLC_ERR_INVALID_ARG, "the first stage needs the embedding table");
+        CUDA_TRY(cudaMemcpy(h->embed, embedding, tb, cudaMemcpyHostToDevice));
+    }
+    if (h->d.has_lm_head) {
+        if (!final_norm || !lm_head) return fail(GLC_ERR_INVALID_ARG, "the last stage needs the final norm and LM head");
+        CUDA_TRY(cudaMemcpy(h->final_norm, final_norm, sizeof(float) * h->d.hidden_dim, cudaMemcpyHostToDevice));
+        CUDA_TRY(cudaMemcpy(h->lm_head, lm_head, tb, cudaMemcpyHostToDevice));
+    }
+    return GLC_OK;
+}
+
+// The documented synthetic weights of global layer `layer_begin + layer`:
+// Q4_K matrices from the seeded generator (sigma_d 0.001; tags
+// 200000 + 16 * global_layer + m, m = 0 q, 1 k, 2 v, 3 o, 4 gate, 5 up, 6 down),
+// norms 1 + N(0, 0.02) (tags 200007/200008 + 16 * global_layer), biases N(0, 0.02)
+// (tag 200009 + 16 * global_layer over the stacked q, k, v rows).
+int glc_stage_synth_layer(glc_stage* h, int32_t layer, uint64_t seed) {
+    int rc = check(h);
+    if (rc) return rc;
+    if (layer < 0 || layer >= h->d.layer_count) return fail(GLC_ERR_INVALID_ARG, "layer %d out of range", layer);
+    CUDA_TRY(cudaSetDevice(h->d.device));
+    StageLayer& L = h->layers[layer];
+    const int D = h->d.hidden_dim, FF = h->d.ffn_dim;
+    const uint64_t base = 200000ull + 16ull * (uint64_t)(h->d.layer_begin + layer);
+    const int nt = 16;
+    std::vector<uint8_t> buf(std::max({h->sz.wqkv, h->sz.wo, h->sz.wgu, h->sz.wdown}));
+    const size_t rq = (size_t)h->d.n_heads * kHeadDim, rk = (size_t)h->d.n_kv_heads * kHeadDim;
+    glc::synth_q4k(seed, base + 0, 0.001f, buf.data(), rq * rowbytes(D) / 144, nt);
+    glc::synth_q4k(seed, base + 1, 0.001f, buf.data() + rq * rowbytes(D), rk * rowbytes(D) / 144, nt);
+    glc::synth_q4k(seed, base + 2, 0.001f, buf.data() + (rq + rk) * rowbytes(D), rk * rowbytes(D) / 144, nt);
+    CUDA_TRY(cudaMemcpy(L.wqkv, buf.data(), h->sz.wqkv, cudaMemcpyHostToDevice));
+    glc::synth_q4k(seed, base + 3, 0.001f, buf.data(), h->sz.wo / 144, nt);
+    CUDA_TRY(cudaMemcpy(L.wo, buf.data(), h->sz.wo, cudaMemcpyHostToDevice));
+    glc::synth_q4k(seed, base + 4, 0.001f, buf.data(), h->sz.wgu / 144, nt);
+    CUDA_TRY(cudaMemcpy(L.wgate, buf.data(), h->sz.wgu, cudaMemcpyHostToDevice));
+    glc::synth_q4k(seed, base + 5, 0.001f, buf.data(), h->sz.wgu / 144, nt);
+    CUDA_TRY(cudaMemcpy(L.wup, buf.data(), h->sz.wgu, cudaMemcpyHostToDevice));
+    glc::synth_q4k(seed, base + 6, 0.001f, buf.data(), h->sz.wdown / 144, nt);
+    CUDA_TRY(cudaMemcpy(L.wdown, buf.data(), h->sz.wdown, cudaMemcpyHostToDevice));
+    std::vector<float> v(std::max((size_t)D, h->sz.qkv_rows));
+    glc::synth_normal(seed, base + 7, 0.02f, v.data(), D, 1);
+    for (int i = 0; i < D; ++i) v[i] = 1.0f + v[i];
+    CUDA_TRY(cudaMemcpy(L.attn_norm, v.data(), sizeof(float) * D, cudaMemcpyHostToDevice));
+    glc::synth_normal(seed, base + 8, 0.02f, v.data(), D, 1);
+    for (int i = 0; i < D; ++i) v[i] = 1.0f + v[i];
+    CUDA_TRY(cudaMemcpy(L.ffn_norm, v.data(), sizeof(float) * D, cudaMemcpyHostToDevice));
+    glc::synth_normal(seed, base + 9, 0.02f, v.data(), h->sz.qkv_rows, 1);
+    CUDA_TRY(cudaMemcpy(L.bqkv, v.data(), sizeof(float) * h->sz.qkv_rows, cudaMemcpyHostToDevice));
+    (void)FF;
+    L.loaded = true;
+    return GLC_OK;
+}
+
+// Embedding table (tag 300000), final norm 1 + N(0, 0.02) (tag 300001) and
+// LM head (tag 300002): Q4_K [vocab][D] with sigma_d 0.001.
+int glc_stage_synth_io(glc_stage* h, uint64_t seed) {
+    int rc = check(h);
+    if (rc) return rc;
+    CUDA_TRY(cudaSetDevice(h->d.device));
+    const int D = h->d.hidden_dim;
+    const size_t tb = (size_t)h->d.vocab * rowbytes(D);
+    if (h->d.has_embedding || h->d.has_lm_head) {
+        std::vector<uint8_t> buf(tb);
+        if (h->d.has_embedding) {
+            glc::synth_q4k(seed, 300000, 0.001f, buf.data(), tb / 144, 16);
+            CUDA_TRY(cudaMemcpy(h->embed, buf.data(), tb, cudaMemcpyHostToDevice));
+        }
+        if (h->d.has_lm_head) {
+            glc::synth_q4k(seed, 300002, 0.001f, buf.data(), tb / 144, 16);
+            CUDA_TRY(cudaMemcpy(h->lm_head, buf.data(), tb, cudaMemcpyHostToDevice));
+            std::vector<float> v(D);
+            glc::synth_normal(seed, 300001, 0.02f, v.data(), D, 1);
+            for (int i = 0; i < D; ++i) v[i] = 1.0f + v[i];
+            CUDA_TRY(cudaMemcpy(h->final_norm, v.data(), sizeof(float) * D, cudaMemcpyHostToDevice));
+        }
+    }
+    return GLC_OK;
+}
+
+int glc_stage_reset(glc_stage* h) {
+    int rc = check(h);
+    if (rc) return rc;
+    CUDA_TRY(cudaSetDevice(h->d.device));
+    CUDA_TRY(cudaStreamSynchronize(h->stream));
+    for (auto& L : h->layers) {
+        CUDA_TRY(cudaMemset(L.kc, 0, h->sz.cache));
+        CUDA_TRY(cudaMemset(L.vc, 0, h->sz.cache));
+    }
+    return GLC_OK;
+}
+
+int glc_stage_forward_dev(glc_stage* h, int32_t pos, const int32_t* token, const float* x_in, float* x_out,
+                          float* logits, int32_t* token_out, void* stream) {
+    int rc = check(h);
+    if (rc) return rc;
+    const glc_stage_desc& d = h->d;
+    if (pos < 0 || pos >= d.max_len) return fail(GLC_ERR_INVALID_ARG, "pos %d outside [0, %d)", pos, d.max_len);
+    for (const auto& L : h->layers)
+        if (!L.loaded) return fail(GLC_ERR_STATE, "a layer of the stage has no weights");
+    const bool embed = d.has_embedding && !x_in;
+    const bool head = d.has_lm_head && (logits || token_out);
+    if (!embed && !x_in) return fail(GLC_ERR_INVALID_ARG, "x_in is needed (the stage has no embedding)");
+    if (embed && !token) return fail(GLC_ERR_INVALID_ARG, "token is needed (no x_in)");
+    cudaStream_t st = stream ? (cudaStream_t)stream : h->stream;
+    const size_t xb = sizeof(float) * d.hidden_dim;
+    // the step's inputs: position, token or activation
+    fill_int_kernel<<<1, 1, 0, st>>>(h->pos, pos);
+    CUDA_TRY(cudaGetLastError());
+    if (embed) CUDA_TRY(cudaMemcpyAsync(h->token, token, sizeof(int), cudaMemcpyDeviceToDevice, st));
+    else CUDA_TRY(cudaMemcpyAsync(h->x, x_in, xb, cudaMemcpyDeviceToDevice, st));
+    // the layers: one captured graph per (embed, head) variant, replayed
+    cudaGraphExec_t& g = h->graphs[(embed ? 1 : 0) | (head ? 2 : 0)];
+    if (!g) {
+        // first use of the variant: eager once (function attributes, opt-in
+        // shared memory), then capture it for the next calls
+        rc = stage_step(h, embed, head, st);
+        if (rc) return rc;
+        cudaGraph_t graph = nullptr;
+        if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+            const int crc = stage_step(h, embed, head, st);
+            if (cudaStreamEndCapture(st, &graph) != cudaSuccess || crc != GLC_OK ||
+                cudaGraphInstantiate(&g, graph, 0) != cudaSuccess)
+                g = nullptr;
+            if (graph) cudaGraphDestroy(graph);
+        }
+        cudaGetLastError();
+        // the eager step above already produced this call's outputs
+    } else {
+        CUDA_TRY(cudaGraphLaunch(g, st));
+    }
+    if (x_out) CUDA_TRY(cudaMemcpyAsync(x_out, h->x, xb, cudaMemcpyDeviceToDevice, st));
+    if (head && logits) CUDA_TRY(cudaMemcpyAsync(logits, h->logits, sizeof(float) * d.vocab, cudaMemcpyDeviceToDevice, st));
+    if (head && token_out) CUDA_TRY(cudaMemcpyAsync(token_out, h->token, sizeof(int), cudaMemcpyDeviceToDevice, st));
+    return GLC_OK;
+}
+
+int glc_stage_poll_error(glc_stage* h) {
+    int rc = check(h);
+    if (rc) return rc;
+    int code = 0;
+    CUDA_TRY(cudaMemcpy(&code, h->err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (code) {
+        cudaMemset(h->err, 0, sizeof(int) * 8);
+        return fail(code == glc::kDevBadArg ? GLC_ERR_INVALID_ARG : GLC_ERR_TIMEOUT, "device code %d", code);
+    }
+    return GLC_OK;
+}
+
+}  // extern "C"

@@ -202,7 +202,9 @@ int glc_router_topk_dev(const float* x, const float* router_w, int32_t T, int32_
  *      counts [E], exclusive offsets [E+1], perm [P] (position -> pair, pairs
  *      grouped by expert in ascending pair order) and inv [P] (pair -> position).
  *      The reference has no batching: it runs experts one token at a time
- *      (DistributedPipelineCoordinator.cs:181-206). ---- */
+ *      (DistributedPipelineCoordinator.cs:181-206).  Asynchronous on `stream`;
+ *      its internal group table comes from CUDA's stream-ordered pool
+ *      (cudaMallocAsync / cudaFreeAsync on `stream`). ---- */
 int glc_dispatch_plan_dev(const int32_t* ids, int32_t P, int32_t E, int32_t* counts,
                           int32_t* offsets, int32_t* perm, int32_t* inv, void* stream);
 
@@ -328,6 +330,73 @@ int glc_pp_recv(glc_comm* c, int32_t peer, glc_fused_header* hdr_out, float* x_o
  * combine. */
 int glc_moe_ep_forward(glc_moe* h, glc_comm* c, int32_t layer, const float* x, int32_t T, uint32_t flags,
                        float* out, int32_t* ids_out, float* w_out, void* stream);
+
+/* ---- dense decoder pipeline stage: IClusterStageModel (Pipeline/IClusterStageModel.cs:9-36)
+ *      for Qwen2-style dense layers.  A stage holds layers [layer_begin,
+ *      layer_begin + layer_count) of a model with their fp16 KV caches (the
+ *      reference splits a model's layers over nodes, DistributedClusterSession.cs:
+ *      775-830), plus the embedding table on a first stage and the final norm
+ *      and LM head on a last stage.  One token per call: ForwardStage
+ *      (IClusterStageModel.cs:19). ---- */
+typedef struct glc_stage glc_stage;
+typedef struct glc_stage_desc {
+    int32_t hidden_dim;    /* D (multiple of 256) */
+    int32_t ffn_dim;       /* FF of the SwiGLU feed-forward (multiple of 256) */
+    int32_t n_heads;       /* query heads (n_heads * 128 a multiple of 256) */
+    int32_t n_kv_heads;    /* KV heads (n_heads / n_kv_heads <= 8) */
+    int32_t head_dim;      /* 128 */
+    int32_t layer_begin;   /* first global layer of the stage (names its synthetic weights) */
+    int32_t layer_count;   /* layers held */
+    int32_t max_len;       /* KV cache rows, <= 4096 */
+    float rope_theta;      /* rotate-half RoPE base (1e6 for Qwen2.5) */
+    float rms_eps;         /* RMSNorm epsilon (1e-6 for Qwen2.5) */
+    int32_t vocab;         /* rows of the embedding / LM head tables */
+    int32_t has_embedding; /* first stage: x = dequantised embedding row of the token */
+    int32_t has_lm_head;   /* last stage: logits = LM_head * (RMSNorm(x) * final_norm) */
+    int32_t device;
+} glc_stage_desc;
+/* Host weights of one layer: norms fp32 [D]; wq Q4_K [n_heads*128][D], wk / wv
+ * [n_kv_heads*128][D], wo [D][n_heads*128], w_gate / w_up [FF][D], w_down
+ * [D][FF] (GGUF row layout); biases fp32 (NULL = zero). */
+typedef struct glc_dense_layer_weights {
+    const float* attn_norm;
+    const void* wq;
+    const void* wk;
+    const void* wv;
+    const float* bq;
+    const float* bk;
+    const float* bv;
+    const void* wo;
+    const float* ffn_norm;
+    const void* w_gate;
+    const void* w_up;
+    const void* w_down;
+} glc_dense_layer_weights;
+int glc_stage_create(const glc_stage_desc* desc, glc_stage** out);
+int glc_stage_destroy(glc_stage* h);
+/* layer: index within the stage (0 .. layer_count - 1) */
+int glc_stage_load_layer(glc_stage* h, int32_t layer, const glc_dense_layer_weights* w);
+/* embedding Q4_K [vocab][D] (first stage), final_norm fp32 [D] and lm_head Q4_K
+ * [vocab][D] (last stage); the others may be NULL. */
+int glc_stage_load_io(glc_stage* h, const void* embedding, const float* final_norm, const void* lm_head);
+/* The documented seeded synthetic weights (Q4_K fields as glc_moe_synth_layer
+ * with sigma_d 0.001; norms 1 + N(0, 0.02); biases N(0, 0.02)). */
+int glc_stage_synth_layer(glc_stage* h, int32_t layer, uint64_t seed);
+int glc_stage_synth_io(glc_stage* h, uint64_t seed);
+/* ResetKvCache (IClusterStageModel.cs:35): clears the caches (synchronous). */
+int glc_stage_reset(glc_stage* h);
+/* ForwardStage(token, pos, inputX, outputX, logits, computeLogits): one token
+ * at position pos (0 <= pos < max_len) through the stage's layers, writing
+ * row pos of every layer's KV cache.  Device pointers: x_in [D] (NULL on a
+ * first stage: the embedding row of *token), x_out [D] (NULL = not needed),
+ * logits [vocab] and token_out (the arg-max, lower index on ties) on a last
+ * stage (NULL = not computed).  Asynchronous on `stream` (NULL = the stage's
+ * stream); after the first call of each (embedding, logits) variant the
+ * stage's kernels are replayed from a captured CUDA graph. */
+int glc_stage_forward_dev(glc_stage* h, int32_t pos, const int32_t* token, const float* x_in, float* x_out,
+                          float* logits, int32_t* token_out, void* stream);
+/* Reads and clears the stage's device error word. */
+int glc_stage_poll_error(glc_stage* h);
 
 #ifdef __cplusplus
 }
