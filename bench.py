@@ -398,6 +398,7 @@ def run_ours(args, w):
         worker = None
         qwen = measure_qwen(torch, glc, args, stream, rank == 0 and world == 1 and not args.skip_cpu_baseline)
     ep_leg = measure_ep(torch, dist, glc, w, stream, args, world, rank, local) if not args.skip_ep else None
+    dense = measure_dense(torch, dist, glc, args, stream, world, rank, local) if not args.skip_dense else None
 
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.skip_cpu_baseline:
@@ -454,6 +455,8 @@ def run_ours(args, w):
             line["gemv_isolated"] = gemv
         if qwen:
             line["qwen2_57b"] = qwen
+        if dense is not None:
+            line["dense_pp"] = dense
         if ep_leg is not None:
             line["ep"] = ep_leg
         print(json.dumps(line), flush=True)
@@ -748,6 +751,98 @@ def ep_time(torch, dist, shard, comm, xs, T, flags, stream, steps):
     return float(t.item()), phases
 
 
+DENSE = dict(name="qwen25_14b_decode", D=5120, FF=13824, Hq=40, Hkv=8, layers=48, vocab=152064, max_len=2048,
+             seed=20241203)
+DENSE_SPLITS = {1: [48], 2: [27, 21], 4: [12, 12, 12, 12], 8: [6] * 8}
+DENSE_STEPS = 16
+
+
+def dense_token_bytes(q, pos):
+    """Bytes one token moves through the whole model: every layer's Q4_K
+    matrices, its KV cache rows 0..pos (K and V, fp16), the embedding row and
+    the LM head."""
+    rb = lambda k: q4k_row_bytes(k)
+    D, FF, Hq, Hkv = q["D"], q["FF"], q["Hq"], q["Hkv"]
+    layer = (Hq + 2 * Hkv) * 128 * rb(D) + D * rb(Hq * 128) + 2 * FF * rb(D) + D * rb(FF)
+    kv = 2 * Hkv * (pos + 1) * 128 * 2
+    return q["layers"] * (layer + kv) + q["vocab"] * rb(D) + rb(D)
+
+
+def measure_dense(torch, dist, glc, args, stream, world, rank, local):
+    """Dense decoder decode (Qwen2.5-14B geometry: 48 layers, hidden 5120, FFN
+    13824, 40 query / 8 KV heads, head dim 128, RoPE theta 1e6, vocab 152064,
+    a 2048-position fp16 KV cache, batch 1), greedy: every layer as a
+    DenseStage (glc_stage_forward_dev, one captured graph per stage step).
+    N = 1: the whole model on one GPU.  N > 1: pipeline stages (27:21 at
+    N = 2, even splits at 4 / 8), the activation crossing every boundary as a
+    FusedActivationHeader + symmetric INT8 payload (glc_pp_send / glc_pp_recv,
+    5,124 B per token), the arg-max token handed back from the last stage to
+    the first (glc_comm_send / recv).  Decode steps at the last positions of
+    the cache (attention over up to 2048 rows); device time per token, max
+    over ranks."""
+    q = DENSE
+    split = DENSE_SPLITS.get(world) or [q["layers"] // world] * world
+    begin, count = sum(split[:rank]), split[rank]
+    first, last = rank == 0, rank == world - 1
+    D = q["D"]
+    st = glc.DenseStage(D, q["FF"], q["Hq"], q["Hkv"], begin, count, q["max_len"], 1e6, 1e-6, q["vocab"], first,
+                        last, local)
+    for l in range(count):
+        st.synth_layer(l, q["seed"])
+    st.synth_io(q["seed"])
+    comm = ep_communicator(glc, dist, world, rank, local) if world > 1 else None
+    s = stream.cuda_stream
+    tok = torch.zeros(1, dtype=torch.int32, device="cuda")
+    x = torch.empty(D, device="cuda")
+    hdr = glc.FusedActivationHeader(1, 0, begin + count, D, 2, 0, 1.0, 1)  # INT8 wire
+
+    def step(pos):
+        if first:
+            st.forward_dev(pos, token_ptr=tok.data_ptr(), x_out_ptr=x.data_ptr(),
+                           token_out_ptr=tok.data_ptr() if last else None, stream=s)
+        else:
+            comm.pp_recv(rank - 1, x.data_ptr(), 1, D, s)
+            st.forward_dev(pos, x_in_ptr=x.data_ptr(), x_out_ptr=None if last else x.data_ptr(),
+                           token_out_ptr=tok.data_ptr() if last else None, stream=s)
+        if not last:
+            comm.pp_send(rank + 1, hdr, x.data_ptr(), s)
+        if world > 1 and last:
+            comm.send(0, tok.data_ptr(), 4, s)
+        if world > 1 and first:
+            comm.recv(world - 1, tok.data_ptr(), 4, s)
+
+    p0 = q["max_len"] - DENSE_STEPS - 3
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            step(p0 + i)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(DENSE_STEPS):
+            step(p0 + 3 + i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / DENSE_STEPS], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    st.poll_error()
+    st.dispose()
+    if comm:
+        comm.dispose()
+    peak, _ = peaks()
+    tb = dense_token_bytes(q, q["max_len"] - 1)
+    gbs = tb / (ms * 1e-3) / 1e9
+    return {"workload": f"{q['name']}_pp{world}", "layers": q["layers"], "stage_layers": split,
+            "ms_per_token": ms, "tokens_per_s": 1000.0 / ms, "steps": DENSE_STEPS,
+            "positions": [p0 + 3, p0 + 2 + DENSE_STEPS], "bytes_per_token": tb,
+            "achieved_gbs_whole_model": gbs, "frac_of_one_gpu_peak": gbs / peak,
+            "boundary": "FusedActivationHeader + INT8 payload (5,124 B / token) per stage boundary" if world > 1
+                        else "single GPU", "submission": "one captured graph per stage step, replayed per token"}
+
+
 def measure_ep(torch, dist, glc, w, stream, args, world, rank, local):
     """Expert parallelism through the C ABI (glc_moe_ep_forward, the call a C#
     host binds: NCCL inside the library, no torch.distributed on the data
@@ -830,6 +925,7 @@ def main():
     ap.add_argument("--skip-batched", action="store_true")
     ap.add_argument("--skip-qwen", action="store_true")
     ap.add_argument("--skip-ep", action="store_true")
+    ap.add_argument("--skip-dense", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -118,6 +118,8 @@ _SIGNATURES = {
     "glc_pp_send": (C.c_int, [vp, i32, C.POINTER(FusedHeader), vp, vp]),
     "glc_pp_recv": (C.c_int, [vp, i32, C.POINTER(FusedHeader), vp, i32, i32, vp]),
     "glc_moe_ep_forward": (C.c_int, [vp, vp, i32, vp, i32, C.c_uint32, vp, vp, vp, vp]),
+    "glc_comm_send": (C.c_int, [vp, i32, vp, C.c_size_t, vp]),
+    "glc_comm_recv": (C.c_int, [vp, i32, vp, C.c_size_t, vp]),
     "glc_stage_create": (C.c_int, [vp, C.POINTER(vp)]),
     "glc_stage_destroy": (C.c_int, [vp]),
     "glc_stage_load_layer": (C.c_int, [vp, i32, vp]),

@@ -461,6 +461,13 @@ class Communicator:
         the header and the payload to ``peer``."""
         check(lib().glc_pp_send(self._handle(), peer, C.byref(header._c()), x_ptr, stream))
 
+    def send(self, peer: int, ptr: int, nbytes: int, stream=None) -> None:
+        """Raw bytes of device memory to ``peer`` (glc_comm_send), e.g. a token id."""
+        check(lib().glc_comm_send(self._handle(), peer, ptr, nbytes, stream))
+
+    def recv(self, peer: int, ptr: int, nbytes: int, stream=None) -> None:
+        check(lib().glc_comm_recv(self._handle(), peer, ptr, nbytes, stream))
+
     def pp_recv(self, peer: int, x_ptr: int, max_tokens: int, hidden_dim: int,
                 stream=None) -> "FusedActivationHeader":
         """Receive a header and its payload from ``peer`` and dequantise into x [T][hidden_dim]."""

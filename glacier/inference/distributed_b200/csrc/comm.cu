@@ -268,4 +268,22 @@ int glc_pp_recv(glc_comm* c, int32_t peer, glc_fused_header* hdr_out, float* x_o
     return GLC_OK;
 }
 
+int glc_comm_send(glc_comm* c, int32_t peer, const void* buf, size_t bytes, void* stream) {
+    if (!c || (!buf && bytes)) return fail(GLC_ERR_INVALID_ARG, "null pointer");
+    if (peer < 0 || peer >= c->nranks || peer == c->rank) return fail(GLC_ERR_INVALID_ARG, "bad peer rank");
+    if (!bytes) return GLC_OK;
+    cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    NCCL_TRY(nccl().Send(buf, bytes, ncclUint8, peer, c->comm, st), "ncclSend");
+    return GLC_OK;
+}
+
+int glc_comm_recv(glc_comm* c, int32_t peer, void* buf, size_t bytes, void* stream) {
+    if (!c || (!buf && bytes)) return fail(GLC_ERR_INVALID_ARG, "null pointer");
+    if (peer < 0 || peer >= c->nranks || peer == c->rank) return fail(GLC_ERR_INVALID_ARG, "bad peer rank");
+    if (!bytes) return GLC_OK;
+    cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    NCCL_TRY(nccl().Recv(buf, bytes, ncclUint8, peer, c->comm, st), "ncclRecv");
+    return GLC_OK;
+}
+
 }  // extern "C"

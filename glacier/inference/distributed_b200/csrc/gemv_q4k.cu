@@ -70,6 +70,11 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
     const int r0 = (int)(total * blockIdx.x / gridDim.x);
     const int r1 = (int)(total * (blockIdx.x + 1) / gridDim.x);
 
+    // The next programmatically serialised kernel of the stream may be
+    // launched at once (its blocks take SMs as this grid's leave them, and it
+    // waits for this grid's completion before it reads what this one writes):
+    // its launch is then off the critical path.
+    grid_dep_launch_dependents();
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
@@ -133,8 +138,6 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
             // the copies in flight land before this warp, and so the CTA, exits
             drain_issued_stages(full, S, issued, kWaitLimitNs);
         }
-        __syncwarp();
-        grid_dep_launch_dependents();
         return;
     }
 
@@ -174,9 +177,6 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
         if (lane == 0) mbar_arrive(&empty[buf]);
     });
 
-    // the next kernel of the stream may be scheduled once every CTA is here
-    // (it waits for this kernel's completion before it reads the output)
-    grid_dep_launch_dependents();
     named_bar_sync(1, NW * 32);
     if (!ok) return;
 

@@ -52,6 +52,8 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_w_kernel(const float* __
                                                                  int D, float eps, float* __restrict__ y) {
     __shared__ float red[kNormThreads / 32];
     __shared__ float s_scale;
+    // the next (weight-streaming) GEMV may start on the SMs this CTA leaves free
+    grid_dep_launch_dependents();
     grid_dep_wait();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float a = 0.f;
@@ -67,14 +69,13 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_w_kernel(const float* __
     __syncthreads();
     const float r = s_scale;
     for (int d = tid; d < D; d += kNormThreads) y[d] = w ? __fmul_rn(__fmul_rn(x[d], r), w[d]) : __fmul_rn(x[d], r);
-    grid_dep_launch_dependents();
 }
 
 __global__ void __launch_bounds__(256) bias_add_kernel(float* __restrict__ y, const float* __restrict__ b, int n) {
+    grid_dep_launch_dependents();
     grid_dep_wait();
     const int i = blockIdx.x * 256 + threadIdx.x;
     if (i < n) y[i] = __fadd_rn(y[i], b[i]);
-    grid_dep_launch_dependents();
 }
 
 // x[0..D) = dequantised row *token of a Q4_K table [rows][D/256*144]

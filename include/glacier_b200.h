@@ -310,6 +310,11 @@ int glc_comm_destroy(glc_comm* c);
  * Device pointers; NULL stream = the communicator's stream.  glc_pp_recv reads
  * the header on the host, so it returns after the header has arrived. */
 int glc_pp_send(glc_comm* c, int32_t peer, const glc_fused_header* hdr, const float* x, void* stream);
+/* Raw device bytes to / from `peer` over the communicator (the sampled token
+ * a last stage hands back to the first, DistributedClusterSession.cs:775-830).
+ * Asynchronous on `stream` (NULL = the communicator's stream). */
+int glc_comm_send(glc_comm* c, int32_t peer, const void* buf, size_t bytes, void* stream);
+int glc_comm_recv(glc_comm* c, int32_t peer, void* buf, size_t bytes, void* stream);
 int glc_pp_recv(glc_comm* c, int32_t peer, glc_fused_header* hdr_out, float* x_out, int32_t max_tokens,
                 int32_t hidden_dim, void* stream);
 
