@@ -469,15 +469,16 @@ def run_ours(args, w):
 
 
 def measure_gemv(torch, glc, worker, w, stream):
-    """The stand-alone Q4_K GEMV (glc_gemv_q4k_dev, the MatVecMul drop-in) in
-    isolation: y = W x at K=4096, N=28672 (gate + up rows of one expert pair)
-    and K=14336, N=8192 (down rows of two experts), each over 4 distinct
-    66 MB weight copies (the resident layer's experts: 264 MB rotating, more
-    than L2) in turn.  A CUDA graph of 64 back-to-back launches is replayed
-    (a model's loop of projections); the launches are programmatically
-    serialised, so each starts streaming its weights as the one before
-    leaves each SM.  Per-launch time, GB/s and the fraction of the measured
-    HBM peak; the event-timed single launch beside it."""
+    """The Q4_K GEMV (the MatVecMul drop-in) in isolation: y = W x at K=4096,
+    N=28672 (gate + up rows of one expert pair) and K=14336, N=8192 (down rows
+    of two experts), each over 4 distinct 66 MB weight copies (the resident
+    layer's experts: 264 MB rotating, more than L2) in turn.
+
+    Headline: glc_gemv_q4k_chain_dev, 64 GEMVs in one launch, every GEMV after
+    the first behind a grid-wide wait for the one before (as if it read its
+    output), replayed from a CUDA graph; per-GEMV time = launch time / 64.
+    Beside it: glc_gemv_q4k_dev as a CUDA graph of 64 programmatically
+    serialised launches, and the event-timed single launch."""
     D, F = w["D"], w["F"]
     g, u, d, r = worker.layer_device_ptrs(0)
     gu_bytes, dn_bytes = F * q4k_row_bytes(D), D * q4k_row_bytes(F)  # one expert's matrix
@@ -518,11 +519,36 @@ def measure_gemv(torch, glc, worker, w, stream):
                 torch.cuda.synchronize()
                 single.append(e0.elapsed_time(e1))
         del graph
-        gbs = nbytes / (per * 1e-3) / 1e9
-        res[name] = {"K": K, "N": N, "weight_bytes": nbytes, "ms_per_launch": per, "gbs": gbs, "frac": gbs / peak,
+        # the chain: 64 GEMVs in one launch, each behind a grid-wide wait
+        jobs = [dict(W=copies[i % 4], x=x.data_ptr(), y=y.data_ptr(), K=K, N=N, after_previous=i > 0)
+                for i in range(launches)]
+        with torch.cuda.stream(stream):
+            glc.gemv_q4k_chain_dev(jobs, s)
+            torch.cuda.synchronize()
+            cgraph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(cgraph, stream=stream):
+                glc.gemv_q4k_chain_dev(jobs, s)
+            cgraph.replay()
+            torch.cuda.synchronize()
+            torch.cuda._sleep(200000)
+            e0.record(stream)
+            for _ in range(4):
+                cgraph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            per_chain = e0.elapsed_time(e1) / (4 * launches)
+        del cgraph
+        glc.gemv_poll_error()
+        gbs = nbytes / (per_chain * 1e-3) / 1e9
+        res[name] = {"K": K, "N": N, "weight_bytes": nbytes, "ms_per_gemv": per_chain, "gbs": gbs,
+                     "frac": gbs / peak,
+                     "submission": f"glc_gemv_q4k_chain_dev: {launches} GEMVs over 4 rotating copies in one launch, "
+                                   "each behind a grid-wide wait for the one before; CUDA graph replayed",
+                     "separate_launches": {"ms_per_launch": per, "frac": nbytes / (per * 1e-3) / 1e9 / peak,
+                                           "submission": f"glc_gemv_q4k_dev: CUDA graph of {launches} "
+                                                         "programmatically serialised launches, replayed"},
                      "single_launch_ms_median": float(np.median(single)),
-                     "single_launch_frac": nbytes / (float(np.median(single)) * 1e-3) / 1e9 / peak,
-                     "submission": f"CUDA graph of {launches} launches over 4 rotating copies, replayed"}
+                     "single_launch_frac": nbytes / (float(np.median(single)) * 1e-3) / 1e9 / peak}
     return res
 
 

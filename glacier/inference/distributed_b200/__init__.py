@@ -6,7 +6,8 @@ include/glacier_b200.h."""
 from ._lib import GlcError, LIB_PATH, lib  # noqa: F401
 from .api import (Communicator, DenseStage, DynamicPrecisionSwitcher, FusedActivationHeader, GpuExpertStageWorker,  # noqa: F401
                   QuantizationKernels, WirePrecisionMode, attn_decode_dev, attn_workspace_bytes,
-                  device_count, dispatch_plan_dev, gemv_q4k_dev, q4k_row_bytes, router_topk_dev,
+                  device_count, dispatch_plan_dev, gemv_poll_error, gemv_q4k_chain_dev, gemv_q4k_dev,
+                  q4k_row_bytes, router_topk_dev,
                   torch_stream_handle)
 # ep / pp import torch.distributed; they are imported on use:
 #   from glacier.inference.distributed_b200.ep import ExpertParallelStageWorker, CudaExpertShard

@@ -61,6 +61,17 @@ class DenseLayerWeights(C.Structure):
     ]
 
 
+class GemvJob(C.Structure):
+    _fields_ = [
+        ("W", C.c_void_p), ("W_up", C.c_void_p), ("x", C.c_void_p), ("y", C.c_void_p), ("norm_w", C.c_void_p),
+        ("norm_eps", C.c_float), ("K", C.c_int32), ("N", C.c_int32), ("op", C.c_int32),
+        ("after_previous", C.c_int32),
+    ]
+
+
+GLC_GEMV_SET, GLC_GEMV_ADD, GLC_GEMV_GATE_UP = 0, 1, 2
+
+
 class FusedHeader(C.Structure):
     _fields_ = [
         ("sequence_id", C.c_uint64), ("token_index", C.c_int32), ("layer_index", C.c_int32),
@@ -94,6 +105,8 @@ _SIGNATURES = {
     "glc_moe_graph_build": (C.c_int, [vp, i32, vp, i32, C.c_uint32, vp]),
     "glc_moe_graph_launch": (C.c_int, [vp, vp]),
     "glc_gemv_q4k_dev": (C.c_int, [vp, vp, vp, i32, i32, vp]),
+    "glc_gemv_q4k_chain_dev": (C.c_int, [C.POINTER(GemvJob), i32, vp]),
+    "glc_gemv_poll_error": (C.c_int, []),
     "glc_attn_workspace_bytes": (C.c_int, [i32, i32, i32, C.POINTER(C.c_uint64)]),
     "glc_attn_decode_dev": (C.c_int, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, C.c_float, vp, vp,
                                       C.c_uint64, vp]),

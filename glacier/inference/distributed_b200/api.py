@@ -217,6 +217,25 @@ def gemv_q4k_dev(W_ptr: int, x_ptr: int, y_ptr: int, K: int, N: int, stream: int
     check(lib().glc_gemv_q4k_dev(W_ptr, x_ptr, y_ptr, K, N, stream))
 
 
+def gemv_q4k_chain_dev(jobs, stream: int | None = None) -> None:
+    """A chain of MatVecMul calls in one launch (glc_gemv_q4k_chain_dev).
+    ``jobs``: dicts with W, x, y (device pointers), K, N and optionally op
+    ("set" | "add" | "gate_up"), W_up, norm_w, norm_eps, after_previous."""
+    ops = {"set": _lib.GLC_GEMV_SET, "add": _lib.GLC_GEMV_ADD, "gate_up": _lib.GLC_GEMV_GATE_UP}
+    arr = (_lib.GemvJob * len(jobs))()
+    for a, j in zip(arr, jobs):
+        a.W, a.W_up, a.x, a.y = j["W"], j.get("W_up"), j["x"], j["y"]
+        a.norm_w, a.norm_eps = j.get("norm_w"), float(j.get("norm_eps", 0.0))
+        a.K, a.N, a.op = int(j["K"]), int(j["N"]), ops[j.get("op", "set")]
+        a.after_previous = int(bool(j.get("after_previous", False)))
+    check(lib().glc_gemv_q4k_chain_dev(arr, len(jobs), stream))
+
+
+def gemv_poll_error() -> None:
+    """Raises GlcError when a bounded device-side wait of a GEMV gave up."""
+    check(lib().glc_gemv_poll_error())
+
+
 def attn_workspace_bytes(n_heads: int, n_kv_heads: int, max_len: int) -> int:
     n = C.c_uint64(0)
     check(lib().glc_attn_workspace_bytes(n_heads, n_kv_heads, max_len, C.byref(n)))

@@ -20,7 +20,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-ffp-contract=off",
           "-I", CSRC, "-I", INCLUDE, "--expt-relaxed-constexpr"]
-SOURCES = ["api.cu", "gemv_q4k.cu", "decode_fused.cu", "decode_wide.cu", "router.cu", "wire.cu", "prefill.cu", "grouped_mma.cu",
+SOURCES = ["api.cu", "gemv_q4k.cu", "gemv_chain.cu", "decode_fused.cu", "decode_wide.cu", "router.cu", "wire.cu", "prefill.cu", "grouped_mma.cu",
            "noalloc.cu", "ep.cu", "comm.cu", "attention.cu", "stage.cu", "synth.cpp"]
 HEADERS = ["common.cuh", "gemv_lane.cuh", "kernels.h", "synth.h"]
 

@@ -1288,23 +1288,46 @@ int glc_attn_decode_dev(const float* q, const float* k_new, const float* v_new, 
     return GLC_OK;
 }
 
+// Per-device state of the raw GEMV entry points: the device error word of
+// their bounded waits and the chain kernel's grid-barrier counter.
+struct GemvDeviceState {
+    int* err = nullptr;
+    unsigned long long* bar = nullptr;
+    int num_sms = 0;
+};
+
+static int gemv_state(GemvDeviceState** out) {
+    static GemvDeviceState st[glc::kMaxDevices];
+    static std::mutex mu;
+    int dev = 0;
+    CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= glc::kMaxDevices) return fail(GLC_ERR_INVALID_ARG, "device %d out of range", dev);
+    std::lock_guard<std::mutex> lk(mu);
+    GemvDeviceState& s = st[dev];
+    if (!s.err) {
+        CUDA_TRY(cudaDeviceGetAttribute(&s.num_sms, cudaDevAttrMultiProcessorCount, dev));
+        int* e = nullptr;
+        unsigned long long* b = nullptr;
+        CUDA_TRY(cudaMalloc(&e, sizeof(int)));
+        if (cudaMalloc(&b, sizeof(unsigned long long)) != cudaSuccess) {
+            cudaFree(e);
+            return fail(GLC_ERR_OOM, "GEMV device state");
+        }
+        CUDA_TRY(cudaMemset(e, 0, sizeof(int)));
+        CUDA_TRY(cudaMemset(b, 0, sizeof(unsigned long long)));
+        s.bar = b;
+        s.err = e;
+    }
+    *out = &s;
+    return GLC_OK;
+}
+
 int glc_gemv_q4k_dev(const void* W, const float* x, float* y, int32_t K, int32_t N, void* stream) {
     if (!W || !x || !y) return fail(GLC_ERR_INVALID_ARG, "null pointer");
     if (N <= 0 || K <= 0) return fail(GLC_ERR_INVALID_ARG, "K and N must be positive");
     if (K % 256) return fail(GLC_ERR_UNSUPPORTED, "Dimension %d is not a multiple of 256 for quantization Q4_K.", K);
-    static int* err_words[glc::kMaxDevices] = {nullptr};
-    static std::mutex mu;
-    int dev = 0;
-    CUDA_TRY(cudaGetDevice(&dev));
-    {
-        std::lock_guard<std::mutex> lk(mu);
-        if (!err_words[dev]) {
-            CUDA_TRY(cudaMalloc(&err_words[dev], sizeof(int)));
-            CUDA_TRY(cudaMemset(err_words[dev], 0, sizeof(int)));
-        }
-    }
-    int nsm = 0;
-    CUDA_TRY(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+    GemvDeviceState* st = nullptr;
+    if (int rc = gemv_state(&st)) return rc;
     glc::GemvParams p{};
     p.mode = glc::kGemvPlain;
     p.K = K;
@@ -1315,9 +1338,64 @@ int glc_gemv_q4k_dev(const void* W, const float* x, float* y, int32_t K, int32_t
     p.A = (const uint8_t*)W;
     p.x = x;
     p.y = y;
-    p.err = err_words[dev];
-    CUDA_TRY(glc::gemv_launch(p, nsm, (cudaStream_t)stream));
+    p.err = st->err;
+    CUDA_TRY(glc::gemv_launch(p, st->num_sms, (cudaStream_t)stream));
     return GLC_OK;
+}
+
+static_assert(GLC_GEMV_SET == glc::kChainSet && GLC_GEMV_ADD == glc::kChainAdd &&
+                  GLC_GEMV_GATE_UP == glc::kChainGateUp,
+              "the chain ops of the C ABI and of the kernel share their values");
+
+int glc_gemv_q4k_chain_dev(const glc_gemv_job* jobs, int32_t n, void* stream) {
+    if (!jobs) return fail(GLC_ERR_INVALID_ARG, "null pointer");
+    if (n <= 0 || n > glc::kMaxChainJobs) return fail(GLC_ERR_INVALID_ARG, "%d jobs (1..%d)", n, glc::kMaxChainJobs);
+    GemvDeviceState* st = nullptr;
+    if (int rc = gemv_state(&st)) return rc;
+    glc::GemvChainParams p{};
+    for (int j = 0; j < n; ++j) {
+        const glc_gemv_job& a = jobs[j];
+        if (!a.W || !a.x || !a.y) return fail(GLC_ERR_INVALID_ARG, "job %d: null pointer", j);
+        if (a.K <= 0 || a.N <= 0) return fail(GLC_ERR_INVALID_ARG, "job %d: K and N must be positive", j);
+        if (a.K % 256)
+            return fail(GLC_ERR_UNSUPPORTED, "job %d: dimension %d is not a multiple of 256 for quantization Q4_K.", j,
+                        a.K);
+        if (a.op != GLC_GEMV_SET && a.op != GLC_GEMV_ADD && a.op != GLC_GEMV_GATE_UP)
+            return fail(GLC_ERR_INVALID_ARG, "job %d: unknown op %d", j, a.op);
+        if (a.op == GLC_GEMV_GATE_UP && !a.W_up) return fail(GLC_ERR_INVALID_ARG, "job %d: GATE_UP needs W_up", j);
+        if (((uintptr_t)a.x | (uintptr_t)a.norm_w) & 15u)
+            return fail(GLC_ERR_INVALID_ARG, "job %d: x and norm_w must be 16-byte aligned", j);
+        if (a.norm_w && !(a.norm_eps >= 0.f)) return fail(GLC_ERR_INVALID_ARG, "job %d: bad norm_eps", j);
+        glc::GemvJob& b = p.jobs[j];
+        b.A = (const uint8_t*)a.W;
+        b.B = (const uint8_t*)a.W_up;
+        b.x = a.x;
+        b.y = a.y;
+        b.norm_w = a.norm_w;
+        b.norm_eps = a.norm_eps;
+        b.K = a.K;
+        b.N = a.N;
+        b.op = a.op;  // GLC_GEMV_* and glc::GemvChainOp share their values
+        b.after_previous = a.after_previous ? 1 : 0;
+    }
+    p.njobs = n;
+    p.bar = st->bar;
+    p.err = st->err;
+    CUDA_TRY(glc::gemv_chain_launch(p, st->num_sms, (cudaStream_t)stream));
+    return GLC_OK;
+}
+
+int glc_gemv_poll_error(void) {
+    GemvDeviceState* st = nullptr;
+    if (int rc = gemv_state(&st)) return rc;
+    CUDA_TRY(cudaDeviceSynchronize());
+    int code = 0;
+    CUDA_TRY(cudaMemcpy(&code, st->err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (code == 0) return GLC_OK;
+    // a wait that gave up leaves the barrier counter short of a whole instance
+    CUDA_TRY(cudaMemset(st->err, 0, sizeof(int)));
+    CUDA_TRY(cudaMemset(st->bar, 0, sizeof(unsigned long long)));
+    return fail(GLC_ERR_TIMEOUT, "device-side wait of a GEMV gave up (code %d)", code);
 }
 
 int glc_router_topk_dev(const float* x, const float* router_w, int32_t T, int32_t D, int32_t E, int32_t k,

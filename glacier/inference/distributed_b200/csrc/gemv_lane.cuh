@@ -83,6 +83,44 @@ __device__ __forceinline__ void load_x(XRegs& r, const float4* xp, int stride, b
     r.sB16 = sB * 0.0625f;
 }
 
+// load_x of a row-major input that is RMSNorm'd with weights w: the lane's
+// values are x * w (w read at the same float4 indices) and ss receives the
+// lane's sum of the raw x^2 (in element order), from which the caller forms
+// the norm's scale.
+template <int SRC>
+__device__ __forceinline__ void load_x_norm(XRegs& r, const float4* xp, const float4* wp, bool active, float& ss) {
+    ss = 0.f;
+    if (!active) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) r.xa[i] = r.xb[i] = 0;
+        r.sA = r.sB16 = r.sumA = r.sumB = 0.f;
+        return;
+    }
+    // one 32-block at a time (x and w of a block: 64 registers)
+#pragma unroll
+    for (int blk = 0; blk < 2; ++blk) {
+        float4 t[8], w[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) t[i] = ldx4<SRC>(xp + 8 * blk + i);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w[i] = __ldg(wp + 8 * blk + i);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            ss = fmaf(t[i].x, t[i].x, ss); ss = fmaf(t[i].y, t[i].y, ss);
+            ss = fmaf(t[i].z, t[i].z, ss); ss = fmaf(t[i].w, t[i].w, ss);
+            t[i] = make_float4(__fmul_rn(t[i].x, w[i].x), __fmul_rn(t[i].y, w[i].y), __fmul_rn(t[i].z, w[i].z),
+                               __fmul_rn(t[i].w, w[i].w));
+        }
+        if (blk == 0) {
+            quant_block32(t, r.xa, r.sA, r.sumA);
+        } else {
+            float sB;
+            quant_block32(t, r.xb, sB, r.sumB);
+            r.sB16 = sB * 0.0625f;
+        }
+    }
+}
+
 // Float index of element w (0..63) of unit u in the chunk-major layout.
 __device__ __forceinline__ int chunk_major_index(int u, int w, int U) { return ((w >> 2) * U + u) * 4 + (w & 3); }
 

@@ -48,9 +48,9 @@ __device__ __forceinline__ void for_each_stage(const GemvParams& p, int r0, int 
     for_each_stage_rows(p.rows, (p.mode == kGemvDownCombine && !SPLIT) ? p.kslots : 1, p.stage_rows, r0, r1, 0, f);
 }
 
-// SPLIT: the slot-split down layout (p.split), a separate instantiation so
-// the other modes keep their code unchanged.
-template <bool SPLIT>
+// SPLIT: the slot-split down layout (p.split); NORM: the folded RMSNorm
+// (p.norm_w); separate instantiations so the other modes keep their code.
+template <bool SPLIT, bool NORM>
 __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __grid_constant__ GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int NM = (p.mode == kGemvGateUp) ? 2 : 1;
@@ -63,6 +63,7 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);
     uint64_t* empty = full + S;
     float* part = reinterpret_cast<float*>(empty + S);
+    float* nss = reinterpret_cast<float*>(smem + p.nss_off);  // [nsegw] sums of x^2 (norm_w set)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int NW = p.nw;
@@ -162,7 +163,15 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
         const int xid = (p.mode == kGemvPlain) ? 0
                         : (p.mode == kGemvGateUp ? seg / p.kslots : seg * p.kslots + jj);
         if (xid != cur_x) {
-            load_x<kXGlobalRO>(xr, reinterpret_cast<const float4*>(p.x + (size_t)xid * p.K) + 16 * u, 1, active);
+            if constexpr (NORM) {  // one segment: xid is 0
+                float ss;
+                load_x_norm<kXGlobalRO>(xr, reinterpret_cast<const float4*>(p.x) + 16 * u,
+                                        reinterpret_cast<const float4*>(p.norm_w) + 16 * u, active, ss);
+                ss = warp_tree(ss);
+                if (grp0 == 0 && lane == 0) nss[segw] = ss;
+            } else {
+                load_x<kXGlobalRO>(xr, reinterpret_cast<const float4*>(p.x + (size_t)xid * p.K) + 16 * u, 1, active);
+            }
             cur_x = xid;
         }
         const int buf = sidx % S;
@@ -181,6 +190,12 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
     if (!ok) return;
 
     // ------------------------------------------------------------ epilogue
+    float rinv = 1.0f;
+    if constexpr (NORM) {
+        float ss = 0.f;
+        for (int q = 0; q < nsegw; ++q) ss += nss[q];
+        rinv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)p.K), p.norm_eps)));
+    }
     const int nrows = r1 - r0;
     for (int lr = threadIdx.x; lr < nrows; lr += NW * 32) {
         const int g = r0 + lr;
@@ -189,10 +204,14 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
         if (p.mode == kGemvPlain) {
             float s = 0.f;
             for (int q = 0; q < nsegw; ++q) s += pp[q];
-            p.y[rin] = s;
+            p.y[rin] = NORM ? __fmul_rn(s, rinv) : s;
         } else if (p.mode == kGemvGateUp) {
             float gs = 0.f, us = 0.f;
             for (int q = 0; q < nsegw; ++q) { gs += pp[q]; us += pp[nsegw + q]; }
+            if constexpr (NORM) {
+                gs = __fmul_rn(gs, rinv);
+                us = __fmul_rn(us, rinv);
+            }
             p.y[(size_t)seg * p.rows + rin] = (gs / (1.0f + expf(-gs))) * us;
         } else {
             const size_t o = (size_t)seg * p.rows + rin;
@@ -228,13 +247,16 @@ int gemv_configure(GemvParams& p, int num_sms, size_t smem_limit, size_t* smem_b
     int g = num_sms;
     if ((total + g - 1) / g > range_cap) g = (int)((total + range_cap - 1) / range_cap);
     if (g > total) g = (int)total;
-    const size_t part_bytes = (size_t)((total + g - 1) / g) * NMP * nsegw * sizeof(float);
+    if (p.norm_w && (p.nseg != 1 || p.mode == kGemvDownCombine)) return -1;
+    // the per-CTA row sums, then the norm's per-segment sums of squares
+    const size_t part_bytes = (size_t)((total + g - 1) / g) * NMP * nsegw * sizeof(float) + 32 * sizeof(float);
     const size_t per_stage = stage_bytes + 2 * sizeof(uint64_t);
     if (smem_limit < part_bytes + 2 * per_stage) return -1;
     int S = (int)((smem_limit - part_bytes) / per_stage);
     if (S > GLC_GEMV_MAX_STAGES) S = GLC_GEMV_MAX_STAGES;
     const size_t bytes = (size_t)S * per_stage + part_bytes;
     p.stages = S;
+    p.nss_off = (int)(bytes - 32 * sizeof(float));
     *smem_bytes = bytes;
     *grid = g;
     return 0;
@@ -251,10 +273,12 @@ cudaError_t gemv_launch(const GemvParams& p0, int num_sms, cudaStream_t stream) 
     if (smem_optin[dev] == 0) {
         int v = 0;
         cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-        cudaError_t e = cudaFuncSetAttribute(q4k_gemv_kernel<false>,
+        cudaError_t e = cudaFuncSetAttribute(q4k_gemv_kernel<false, false>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, v);
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(q4k_gemv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, v);
+            e = cudaFuncSetAttribute(q4k_gemv_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, v);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(q4k_gemv_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, v);
         if (e != cudaSuccess) return e;
         smem_optin[dev] = v;
     }
@@ -274,7 +298,9 @@ cudaError_t gemv_launch(const GemvParams& p0, int num_sms, cudaStream_t stream) 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return p.split ? cudaLaunchKernelEx(&cfg, q4k_gemv_kernel<true>, p) : cudaLaunchKernelEx(&cfg, q4k_gemv_kernel<false>, p);
+    if (p.split) return cudaLaunchKernelEx(&cfg, q4k_gemv_kernel<true, false>, p);
+    if (p.norm_w) return cudaLaunchKernelEx(&cfg, q4k_gemv_kernel<false, true>, p);
+    return cudaLaunchKernelEx(&cfg, q4k_gemv_kernel<false, false>, p);
 }
 
 }  // namespace glc

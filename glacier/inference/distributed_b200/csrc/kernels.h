@@ -49,17 +49,48 @@ struct GemvParams {
     float* y;
     int* err;          // device error word (bounded waits)
     int accumulate;    // down: start from the existing y instead of resid / 0
+    // plain / gate-up with one segment: when set, the input is RMSNorm(x) *
+    // norm_w; the lanes take x * norm_w and the epilogue scales each row sum
+    // by 1 / sqrt(mean(x^2) + norm_eps), the sum of squares formed by every
+    // CTA in the same order
+    const float* norm_w = nullptr;
+    float norm_eps = 0.f;
     // filled by gemv_configure; split: down mode with the slot-split stage
     // layout (every stage holds the same stage_rows rows of all kslots
     // experts, warp group g computes slot g % kslots)
     int nsegw, nw, stage_rows, stages, split;
+    int nss_off;  // shared-memory byte offset of the norm's sums of squares
 };
 
 int gemv_configure(GemvParams& p, int num_sms, size_t smem_limit, size_t* smem_bytes, int* grid);
 
+// A chain of Q4_K GEMVs in one persistent launch (gemv_chain.cu).
+enum GemvChainOp : int { kChainSet = 0, kChainAdd = 1, kChainGateUp = 2 };
+constexpr int kMaxChainJobs = 64;
+struct GemvJob {
+    const uint8_t* A;      // Q4_K [N][K/256*144] (gate rows for kChainGateUp)
+    const uint8_t* B;      // up rows (kChainGateUp)
+    const float* x;        // [K]
+    float* y;              // [N]
+    const float* norm_w;   // nullptr, or the input is RMSNorm(x) * norm_w
+    float norm_eps;
+    int K, N, op;
+    int after_previous;    // x may be an earlier job's output: grid-wide barrier first
+};
+struct GemvChainParams {
+    GemvJob jobs[kMaxChainJobs];
+    int njobs;
+    unsigned long long* bar;  // grid barrier counter (grows only; one counter per grid size)
+    int* err;                 // device error word (bounded waits)
+    // filled by gemv_chain_configure
+    int stages, slot_bytes, part_floats;
+};
+int gemv_chain_configure(GemvChainParams& p, int grid, size_t smem_limit, size_t* smem_bytes);
+cudaError_t gemv_chain_launch(GemvChainParams p, int num_sms, cudaStream_t stream);
+
 // Decode attention of one token over fp16 K/V caches (attention.cu).
 constexpr int kAttnMaxGroup = 8;    // query heads per KV head
-constexpr int kAttnMaxLen = 4096;   // cache rows: 64 chunks of 64 positions, merged by one warp
+constexpr int kAttnMaxLen = 32768;  // cache rows (at most 4096 positions per CTA of an 8-CTA cluster)
 struct AttnParams {
     const float* q;        // [n_heads][head_dim] before rotation
     const float* k_new;    // [n_kv_heads][head_dim] before rotation
@@ -67,11 +98,17 @@ struct AttnParams {
     uint16_t* k_cache;     // fp16 [n_kv_heads][max_len][head_dim] (rotated keys), row pos written
     uint16_t* v_cache;     // fp16 [n_kv_heads][max_len][head_dim], row pos written
     float* out;            // [n_heads][head_dim]
-    float* work;           // attn_workspace_bytes()
+    float* work;           // attn_workspace_bytes() (reserved)
     int n_heads, n_kv_heads, head_dim, max_len, pos;
     float theta;
-    int nchunks;           // set by attn_decode_launch (workspace layout)
-    const int* pos_dev = nullptr;  // when set, the position is read here (a launch any position can replay)
+    // When set, the position is read here (a launch any position can replay).
+    // The kernel reads it before it waits for the kernel it is launched
+    // behind, so the word must be written before that kernel starts.
+    const int* pos_dev = nullptr;
+    // optional biases added to q, k_new and v_new as they are read
+    const float* bq = nullptr;
+    const float* bk = nullptr;
+    const float* bv = nullptr;
 };
 size_t attn_workspace_bytes(int n_heads, int n_kv_heads, int max_len);
 cudaError_t attn_decode_launch(AttnParams p, cudaStream_t stream);

@@ -7,20 +7,26 @@
 // 775-830, and quantises the activations at every stage boundary, Program.cs:743).
 //
 // Per layer, on the stage's stream:
-//   h   = RMSNorm(x) * w_attn                    (weighted, eps from the descriptor)
-//   qkv = [Wq; Wk; Wv] h + [bq; bk; bv]           (one Q4_K GEMV over the stacked rows)
-//   o   = attention(q, k, v; the layer's fp16 KV cache at pos)   (attention.cu)
-//   x   = x + Wo o                                (GEMV with the residual in its epilogue)
-//   h   = RMSNorm(x) * w_ffn
-//   a   = SiLU(Wgate h) * (Wup h)                 (GEMV gate/up with the SwiGLU epilogue)
-//   x   = x + Wdown a                             (GEMV with the residual)
+//   qkv = [Wq; Wk; Wv] (RMSNorm(x) * w_attn)      (one Q4_K GEMV over the stacked
+//         rows; the weighted RMSNorm is folded in: the lanes take x * w_attn
+//         and the epilogue scales by the norm's 1 / rms, which every CTA forms)
+//   o   = attention(q + bq, k + bk, v + bv; the layer's fp16 KV cache at pos)
+//         (attention.cu; the biases are added as it reads its inputs)
+//   x   = x + Wo o                                (GEMV, residual in the epilogue)
+//   a   = SiLU(Wgate h) * (Wup h), h = RMSNorm(x) * w_ffn   (gate/up GEMV, the
+//         norm folded in the same way, SwiGLU epilogue)
+//   x   = x + Wdown a                             (GEMV, residual in the epilogue)
 // with, on a first stage, x = dequantised row `token` of the Q4_K embedding
 // table and, on a last stage asked for logits, logits = Wlm RMSNorm(x) * w_final
-// and the arg-max token.  The position lives in device memory, so the whole
-// stage step is one CUDA graph replayed for every token (the attention's launch
-// shape does not depend on the position); the GEMVs are programmatically
-// serialised, so each starts streaming its weights as the kernel before it
-// leaves each SM.
+// and the arg-max token.  Two launches per layer: the attention, then ONE GEMV
+// chain (gemv_chain.cu) holding the O projection, gate/up, down and the next
+// layer's QKV projection (or the LM head), whose weights stream back to back
+// while only its consumer warps wait grid-wide between the dependent jobs.
+// The position lives in device memory, so the whole stage step is one CUDA
+// graph replayed for every token (the attention's launch shape does not depend
+// on the position); the chains and the attention are programmatically
+// serialised, so each starts (streaming weights, or loading cache rows) as the
+// kernel before it leaves each SM.
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
@@ -40,43 +46,8 @@ namespace {
 
 using glc::grid_dep_launch_dependents;
 using glc::grid_dep_wait;
-using glc::warp_tree;
 
 constexpr int kHeadDim = 128;
-constexpr int kNormThreads = 512;
-
-// y = x * (1 / sqrt(mean(x^2) + eps)) * w (w may be null: no weight).  One
-// CTA; the sum of squares in a fixed order (strided partials, warp butterfly,
-// warp sums in order), so the result is deterministic.
-__global__ void __launch_bounds__(kNormThreads) rmsnorm_w_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                                                                 int D, float eps, float* __restrict__ y) {
-    __shared__ float red[kNormThreads / 32];
-    __shared__ float s_scale;
-    // the next (weight-streaming) GEMV may start on the SMs this CTA leaves free
-    grid_dep_launch_dependents();
-    grid_dep_wait();
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    float a = 0.f;
-    for (int d = tid; d < D; d += kNormThreads) a = fmaf(x[d], x[d], a);
-    a = warp_tree(a);
-    if (lane == 0) red[warp] = a;
-    __syncthreads();
-    if (tid == 0) {
-        float ss = 0.f;
-        for (int i = 0; i < kNormThreads / 32; ++i) ss += red[i];
-        s_scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), eps)));
-    }
-    __syncthreads();
-    const float r = s_scale;
-    for (int d = tid; d < D; d += kNormThreads) y[d] = w ? __fmul_rn(__fmul_rn(x[d], r), w[d]) : __fmul_rn(x[d], r);
-}
-
-__global__ void __launch_bounds__(256) bias_add_kernel(float* __restrict__ y, const float* __restrict__ b, int n) {
-    grid_dep_launch_dependents();
-    grid_dep_wait();
-    const int i = blockIdx.x * 256 + threadIdx.x;
-    if (i < n) y[i] = __fadd_rn(y[i], b[i]);
-}
 
 // x[0..D) = dequantised row *token of a Q4_K table [rows][D/256*144]
 // ((d*sc)*q - dmin*m, the GGUF Q4_K values), one thread per weight.
@@ -184,17 +155,15 @@ struct glc_stage {
     uint8_t* lm_head = nullptr;   // Q4_K [vocab][rowbytes(D)] (last stage)
     // device workspace
     float* x = nullptr;      // [D] the stage's residual stream
-    float* h = nullptr;      // [max(D, Hq*128)] normalised input
     float* qkv = nullptr;    // [(Hq + 2 Hkv) * 128]
     float* attn = nullptr;   // [Hq * 128]
     float* act = nullptr;    // [FF]
     float* logits = nullptr; // [vocab]
     float* attn_work = nullptr;
-    float* ones = nullptr;   // [1]
-    int* zeros = nullptr;    // [1]
     int* pos = nullptr;      // the position the next step uses
     int* token = nullptr;    // input token (first stage) / arg-max token (last stage)
     int* err = nullptr;
+    unsigned long long* bar = nullptr;  // the GEMV chains' grid-barrier counter
     // the captured stage step per (embed, logits) variant
     cudaGraphExec_t graphs[4] = {};
 };
@@ -206,7 +175,27 @@ int check(glc_stage* h) {
     return GLC_OK;
 }
 
-// One token through the stage's layers on `st` (position from h->pos).
+glc::GemvJob job(const uint8_t* A, const float* x, float* y, int K, int N, int op, bool after_previous,
+               const float* norm_w = nullptr, float eps = 0.f, const uint8_t* B = nullptr) {
+    glc::GemvJob j{};
+    j.A = A;
+    j.B = B;
+    j.x = x;
+    j.y = y;
+    j.norm_w = norm_w;
+    j.norm_eps = eps;
+    j.K = K;
+    j.N = N;
+    j.op = op;
+    j.after_previous = after_previous ? 1 : 0;
+    return j;
+}
+
+// One token through the stage's layers on `st` (position from h->pos): the
+// QKV projection of the first layer, then per layer the attention and ONE
+// GEMV chain [x += Wo o; a = SwiGLU(Wg, Wu; RMSNorm(x) w_ffn); x += Wd a;
+// the next layer's QKV (or the LM head)], each job after the first waiting
+// grid-wide for the one before while the weights keep streaming.
 int stage_step(glc_stage* h, bool embed, bool logits, cudaStream_t st) {
     const glc_stage_desc& d = h->d;
     const int D = d.hidden_dim, FF = d.ffn_dim, Hq = d.n_heads, Hkv = d.n_kv_heads;
@@ -215,25 +204,17 @@ int stage_step(glc_stage* h, bool embed, bool logits, cudaStream_t st) {
         q4k_row_kernel<<<(D + 255) / 256, 256, 0, st>>>(h->embed, h->token, d.vocab, D, h->x);
         CUDA_TRY(cudaGetLastError());
     }
+    glc::GemvChainParams c{};
+    c.bar = h->bar;
+    c.err = h->err;
+    // qkv = [Wq; Wk; Wv] (RMSNorm(x) * w_attn) of the first layer
+    c.jobs[0] = job(h->layers[0].wqkv, h->x, h->qkv, D, qrows, glc::kChainSet, false, h->layers[0].attn_norm,
+                    d.rms_eps);
+    c.njobs = 1;
+    CUDA_TRY(glc::gemv_chain_launch(c, h->num_sms, st));
     for (int l = 0; l < d.layer_count; ++l) {
         StageLayer& L = h->layers[l];
-        rmsnorm_w_kernel<<<1, kNormThreads, 0, st>>>(h->x, L.attn_norm, D, d.rms_eps, h->h);
-        CUDA_TRY(cudaGetLastError());
-        glc::GemvParams g{};
-        g.mode = glc::kGemvPlain;
-        g.K = D;
-        g.rows = qrows;
-        g.nseg = 1;
-        g.kslots = 1;
-        g.num_experts = 1;
-        g.A = L.wqkv;
-        g.x = h->h;
-        g.y = h->qkv;
-        g.err = h->err;
-        CUDA_TRY(glc::gemv_launch(g, h->num_sms, st));
-        bias_add_kernel<<<(qrows + 255) / 256, 256, 0, st>>>(h->qkv, L.bqkv, qrows);
-        CUDA_TRY(cudaGetLastError());
-        glc::AttnParams ap{};
+        glc::AttnParams ap{};  // the biases are added as the attention reads q, k and v
         ap.q = h->qkv;
         ap.k_new = h->qkv + (size_t)Hq * kHeadDim;
         ap.v_new = h->qkv + (size_t)(Hq + Hkv) * kHeadDim;
@@ -246,61 +227,26 @@ int stage_step(glc_stage* h, bool embed, bool logits, cudaStream_t st) {
         ap.head_dim = kHeadDim;
         ap.max_len = d.max_len;
         ap.pos = 0;
-        ap.pos_dev = h->pos;
+        ap.pos_dev = h->pos;  // written by the step's first kernel, which has no early trigger
         ap.theta = d.rope_theta;
+        ap.bq = L.bqkv;
+        ap.bk = L.bqkv + (size_t)Hq * kHeadDim;
+        ap.bv = L.bqkv + (size_t)(Hq + Hkv) * kHeadDim;
         CUDA_TRY(glc::attn_decode_launch(ap, st));
-        glc::GemvParams o{};
-        o.mode = glc::kGemvDownCombine;  // x = x + Wo attn (one slot, unit weight)
-        o.K = Hq * kHeadDim;
-        o.rows = D;
-        o.nseg = 1;
-        o.kslots = 1;
-        o.num_experts = 1;
-        o.A = L.wo;
-        o.ids = h->zeros;
-        o.cw = h->ones;
-        o.x = h->attn;
-        o.y = h->x;
-        o.accumulate = 1;
-        o.err = h->err;
-        CUDA_TRY(glc::gemv_launch(o, h->num_sms, st));
-        rmsnorm_w_kernel<<<1, kNormThreads, 0, st>>>(h->x, L.ffn_norm, D, d.rms_eps, h->h);
-        CUDA_TRY(cudaGetLastError());
-        glc::GemvParams gu{};
-        gu.mode = glc::kGemvGateUp;  // act = SiLU(Wgate h) * (Wup h)
-        gu.K = D;
-        gu.rows = FF;
-        gu.nseg = 1;
-        gu.kslots = 1;
-        gu.num_experts = 1;
-        gu.A = L.wgate;
-        gu.B = L.wup;
-        gu.ids = h->zeros;
-        gu.x = h->h;
-        gu.y = h->act;
-        gu.err = h->err;
-        CUDA_TRY(glc::gemv_launch(gu, h->num_sms, st));
-        glc::GemvParams dn = o;  // x = x + Wdown act
-        dn.K = FF;
-        dn.A = L.wdown;
-        dn.x = h->act;
-        CUDA_TRY(glc::gemv_launch(dn, h->num_sms, st));
+        c.njobs = 0;
+        c.jobs[c.njobs++] = job(L.wo, h->attn, h->x, Hq * kHeadDim, D, glc::kChainAdd, false);
+        c.jobs[c.njobs++] = job(L.wgate, h->x, h->act, D, FF, glc::kChainGateUp, true, L.ffn_norm, d.rms_eps, L.wup);
+        c.jobs[c.njobs++] = job(L.wdown, h->act, h->x, FF, D, glc::kChainAdd, true);
+        if (l + 1 < d.layer_count) {
+            const StageLayer& N = h->layers[l + 1];
+            c.jobs[c.njobs++] = job(N.wqkv, h->x, h->qkv, D, qrows, glc::kChainSet, true, N.attn_norm, d.rms_eps);
+        } else if (logits) {  // logits = W_lm (RMSNorm(x) * w_final)
+            c.jobs[c.njobs++] = job(h->lm_head, h->x, h->logits, D, d.vocab, glc::kChainSet, true, h->final_norm,
+                                    d.rms_eps);
+        }
+        CUDA_TRY(glc::gemv_chain_launch(c, h->num_sms, st));
     }
     if (logits) {
-        rmsnorm_w_kernel<<<1, kNormThreads, 0, st>>>(h->x, h->final_norm, D, d.rms_eps, h->h);
-        CUDA_TRY(cudaGetLastError());
-        glc::GemvParams lm{};
-        lm.mode = glc::kGemvPlain;
-        lm.K = D;
-        lm.rows = d.vocab;
-        lm.nseg = 1;
-        lm.kslots = 1;
-        lm.num_experts = 1;
-        lm.A = h->lm_head;
-        lm.x = h->h;
-        lm.y = h->logits;
-        lm.err = h->err;
-        CUDA_TRY(glc::gemv_launch(lm, h->num_sms, st));
         argmax_kernel<<<1, 1024, 0, st>>>(h->logits, d.vocab, h->token);
         CUDA_TRY(cudaGetLastError());
     }
@@ -313,9 +259,10 @@ void free_stage(glc_stage* h) {
         cudaFree(L.wgate); cudaFree(L.wup); cudaFree(L.wdown); cudaFree(L.kc); cudaFree(L.vc);
     }
     cudaFree(h->embed); cudaFree(h->final_norm); cudaFree(h->lm_head);
-    cudaFree(h->x); cudaFree(h->h); cudaFree(h->qkv); cudaFree(h->attn); cudaFree(h->act); cudaFree(h->logits);
-    cudaFree(h->attn_work); cudaFree(h->ones); cudaFree(h->zeros); cudaFree(h->pos); cudaFree(h->token);
+    cudaFree(h->x); cudaFree(h->qkv); cudaFree(h->attn); cudaFree(h->act); cudaFree(h->logits);
+    cudaFree(h->attn_work); cudaFree(h->pos); cudaFree(h->token);
     cudaFree(h->err);
+    cudaFree(h->bar);
     for (auto& g : h->graphs)
         if (g) cudaGraphExecDestroy(g);
     if (h->stream) cudaStreamDestroy(h->stream);
@@ -382,20 +329,16 @@ int glc_stage_create(const glc_stage_desc* desc, glc_stage** out) {
         SALLOC(h->logits, sizeof(float) * d.vocab);
     }
     SALLOC(h->x, sizeof(float) * D);
-    SALLOC(h->h, sizeof(float) * std::max(D, Hq * kHeadDim));
     SALLOC(h->qkv, sizeof(float) * h->sz.qkv_rows);
     SALLOC(h->attn, sizeof(float) * Hq * kHeadDim);
     SALLOC(h->act, sizeof(float) * FF);
     SALLOC(h->attn_work, glc::attn_workspace_bytes(Hq, Hkv, d.max_len));
-    SALLOC(h->ones, sizeof(float));
-    SALLOC(h->zeros, sizeof(int));
     SALLOC(h->pos, sizeof(int));
     SALLOC(h->token, sizeof(int));
     SALLOC(h->err, sizeof(int) * 8);
+    SALLOC(h->bar, sizeof(unsigned long long));
 #undef SALLOC
-    const float one = 1.0f;
-    cudaMemcpy(h->ones, &one, sizeof(float), cudaMemcpyHostToDevice);
-    cudaMemset(h->zeros, 0, sizeof(int));
+    cudaMemset(h->bar, 0, sizeof(unsigned long long));
     cudaMemset(h->pos, 0, sizeof(int));
     cudaMemset(h->token, 0, sizeof(int));
     cudaMemset(h->err, 0, sizeof(int) * 8);
@@ -592,7 +535,10 @@ int glc_stage_poll_error(glc_stage* h) {
     int code = 0;
     CUDA_TRY(cudaMemcpy(&code, h->err, sizeof(int), cudaMemcpyDeviceToHost));
     if (code) {
+        // a wait that gave up leaves the chains' barrier counter short of a whole instance
+        cudaDeviceSynchronize();
         cudaMemset(h->err, 0, sizeof(int) * 8);
+        cudaMemset(h->bar, 0, sizeof(unsigned long long));
         return fail(code == glc::kDevBadArg ? GLC_ERR_INVALID_ARG : GLC_ERR_TIMEOUT, "device code %d", code);
     }
     return GLC_OK;

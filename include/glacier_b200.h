@@ -174,6 +174,35 @@ int glc_moe_graph_launch(glc_moe* h, void* stream);
  *      (call shape CpuWarmExpertPoolWorker.cs:379). K % 256 != 0 -> GLC_ERR_UNSUPPORTED. ---- */
 int glc_gemv_q4k_dev(const void* W, const float* x, float* y, int32_t K, int32_t N, void* stream);
 
+/* ---- a chain of MatVecMul calls in one launch: the GemvQ4K / SwiGLU /
+ *      VecAddWeighted dispatch sequence of a decode step
+ *      (GpuFirstExpertStageWorker.cs:482-519) with the weights of every job
+ *      streamed back to back.  Jobs run in order; a job with after_previous
+ *      set may read what earlier jobs of the chain wrote (a grid-wide wait
+ *      precedes it).  Device pointers; at most 64 jobs; K % 256 == 0;
+ *      x, norm_w 16-byte aligned.  Each job's output is bit-identical to
+ *      glc_gemv_q4k_dev's (op SET, no norm).  Asynchronous on `stream`. ---- */
+#define GLC_GEMV_SET 0      /* y = W x */
+#define GLC_GEMV_ADD 1      /* y = y + W x */
+#define GLC_GEMV_GATE_UP 2  /* y = SiLU(W x) * (W_up x) */
+typedef struct glc_gemv_job {
+    const void* W;        /* Q4_K [N][K/256*144] (the gate rows for GATE_UP) */
+    const void* W_up;     /* Q4_K [N][K/256*144] up rows (GATE_UP), else NULL */
+    const float* x;       /* [K] */
+    float* y;             /* [N] */
+    const float* norm_w;  /* NULL, or [K]: the input is RMSNorm(x) * norm_w */
+    float norm_eps;       /* RMSNorm epsilon (norm_w set) */
+    int32_t K;
+    int32_t N;
+    int32_t op;           /* GLC_GEMV_* */
+    int32_t after_previous;
+} glc_gemv_job;
+int glc_gemv_q4k_chain_dev(const glc_gemv_job* jobs, int32_t n, void* stream);
+/* Reads and clears the device error word of glc_gemv_q4k_dev /
+ * glc_gemv_q4k_chain_dev on the current device (synchronises the device):
+ * GLC_ERR_TIMEOUT when a bounded device-side wait gave up, else GLC_OK. */
+int glc_gemv_poll_error(void);
+
 /* ---- decode attention of one token (the attention half of a decode stage;
  *      caller side IClusterStageModel.ForwardStage, IClusterStageModel.cs:19,
  *      body external in the reference, Program.cs:1390).  Device pointers:
@@ -184,9 +213,10 @@ int glc_gemv_q4k_dev(const void* W, const float* x, float* y, int32_t K, int32_t
  *      rotated k and v as fp16; out [n_heads][128] = softmax(q.K^T/sqrt(128)) V
  *      over positions 0..pos, query head h reading KV head h / (n_heads /
  *      n_kv_heads).  head_dim must be 128; n_heads a multiple of n_kv_heads,
- *      at most 8 query heads per KV head; 0 <= pos < max_len <= 4096.  workspace:
- *      glc_attn_workspace_bytes(n_heads, n_kv_heads, max_len) bytes of device
- *      memory, 16-byte aligned.  Two launches on `stream`. ---- */
+ *      at most 8 query heads per KV head; 0 <= pos < max_len <= 32768.
+ *      workspace: glc_attn_workspace_bytes(n_heads, n_kv_heads, max_len) bytes
+ *      of device memory (reserved: the kernel keeps its partial results on
+ *      chip).  One launch on `stream` (a thread-block cluster per KV head). ---- */
 int glc_attn_workspace_bytes(int32_t n_heads, int32_t n_kv_heads, int32_t max_len, uint64_t* bytes);
 int glc_attn_decode_dev(const float* q, const float* k_new, const float* v_new, void* k_cache, void* v_cache,
                         int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t max_len, int32_t pos,
@@ -352,7 +382,7 @@ typedef struct glc_stage_desc {
     int32_t head_dim;      /* 128 */
     int32_t layer_begin;   /* first global layer of the stage (names its synthetic weights) */
     int32_t layer_count;   /* layers held */
-    int32_t max_len;       /* KV cache rows, <= 4096 */
+    int32_t max_len;       /* KV cache rows, <= 32768 */
     float rope_theta;      /* rotate-half RoPE base (1e6 for Qwen2.5) */
     float rms_eps;         /* RMSNorm epsilon (1e-6 for Qwen2.5) */
     int32_t vocab;         /* rows of the embedding / LM head tables */

@@ -92,7 +92,7 @@ def test_attention_rejects_bad_arguments(cuda, glc):
         glc.attn_decode_dev(p, p, p, p, p, 16, 1, 16, 0, THETA, p, p, 1 << 20, stream=1)
     with pytest.raises(glc.GlcError):  # position outside the cache
         glc.attn_decode_dev(p, p, p, p, p, 8, 8, 16, 16, THETA, p, p, 1 << 20, stream=1)
-    with pytest.raises(glc.GlcError):  # cache longer than the kernel merges
-        glc.attn_decode_dev(p, p, p, p, p, 8, 8, 8192, 3, THETA, p, p, 1 << 20, stream=1)
+    with pytest.raises(glc.GlcError):  # cache longer than the kernel takes (rejected before any launch)
+        glc.attn_decode_dev(p, p, p, p, p, 8, 8, 65536, 3, THETA, p, p, 1 << 20, stream=1)
     with pytest.raises(glc.GlcError):  # workspace too small
         glc.attn_decode_dev(p, p, p, p, p, 8, 8, 16, 3, THETA, p, p, 16, stream=1)
