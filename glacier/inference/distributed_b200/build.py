@@ -31,7 +31,7 @@ def _compile(src: str, force: bool) -> str:
     deps = [path] + [os.path.join(CSRC, h) for h in HEADERS] + [os.path.join(INCLUDE, "glacier_b200.h")]
     if not force and os.path.exists(obj) and os.path.getmtime(obj) >= max(os.path.getmtime(d) for d in deps):
         return obj
-    cmd = [NVCC, *ARCH, *COMMON, "-c", path, "-o", obj]
+    cmd = [NVCC, *ARCH, *COMMON, *os.environ.get("GLC_NVCC_DEFINES", "").split(), "-c", path, "-o", obj]
     if os.environ.get("GLC_PTXAS_VERBOSE") and src.endswith(".cu"):
         cmd.insert(1, "-Xptxas=-v")
     subprocess.check_call(cmd)

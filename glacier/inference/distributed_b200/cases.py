@@ -26,16 +26,18 @@ QWEN14B = dict(D=5120, FF=13824, Hq=40, Hkv=8, max_len=2048, seed=20241203)
 CASES = {
     "gemv_k4096": ("q4k_gemv_kernel x1", "y = W x, K=4096, N=28672 (gate+up rows of one expert pair), 4 rotating 66 MB copies"),
     "gemv_k14336": ("q4k_gemv_kernel x1", "y = W x, K=14336, N=8192 (down rows of two experts), 4 rotating 66 MB copies"),
+    "gemv_chain": ("q4k_gemv_chain_kernel x1",
+                   "64 GEMVs K=4096, N=28672 in one launch, each behind a grid-wide wait, 4 rotating 66 MB copies"),
     "router": ("router_kernel x1", "Mixtral router: T=64, D=4096, E=8, top-2 renormalised, RMSNorm"),
     "router_wide": ("router_wide_kernel x1", "Qwen2-57B router: T=16, D=3584, E=64, top-8, RMSNorm"),
     "wire": ("wire_quantize_kernel x1 + wire_dequantize_kernel x1",
              "symmetric INT8 per token, T=4096, D=4096 (64 MB fp32 in)"),
     "dispatch": ("dispatch_plan_kernel x1", "histogram / scan / stable permute of P=8192 slot ids over E=64"),
-    "attention": ("attn_decode_split_kernel x1 + attn_combine_kernel x1",
+    "attention": ("attn_decode_kernel x1 (a 16- or 8-CTA cluster per KV head)",
                   "40 query / 8 KV heads x 128, position 2047 of a 2048-row fp16 cache, 16 rotating layer caches"),
     "decode_fused": ("moe_decode_fused_kernel x1", "Mixtral-8x7B layer decode, T=1 (one launch)"),
     "decode_wide": ("moe_decode_wide_kernel x1", "Qwen2-57B-A14B layer decode with its shared expert, T=1 (one launch)"),
-    "stage": ("per layer: rmsnorm_w, q4k_gemv x4, bias_add, attention x2",
+    "stage": ("per layer: attn_decode_kernel x1, q4k_gemv_chain_kernel x1",
               "Qwen2.5-14B dense stage of 2 layers, one token at position 2040"),
 }
 
@@ -60,6 +62,26 @@ def case_gemv(torch, glc, K, N, reps):
         for i in range(3 + reps):
             glc.gemv_q4k_dev(base + (i % 4) * step, x.data_ptr(), y.data_ptr(), K, N, s)
     torch.cuda.synchronize()
+    worker.dispose()
+
+
+def case_gemv_chain(torch, glc, reps):
+    w = MIXTRAL
+    K, N = w["D"], 2 * w["F"]
+    worker = glc.GpuExpertStageWorker(w["D"], w["F"], w["E"], w["k"], max_tokens=1)
+    worker.synth_layer(0, w["seed"])
+    g = worker.layer_device_ptrs(0)[0]
+    step = N * glc.q4k_row_bytes(K)
+    x = torch.from_numpy(np.random.default_rng(7).standard_normal(K).astype(np.float32)).cuda()
+    y = torch.empty(N, device="cuda")
+    jobs = [dict(W=g + (i % 4) * step, x=x.data_ptr(), y=y.data_ptr(), K=K, N=N, after_previous=i > 0)
+            for i in range(64)]
+    st, s = _stream(torch)
+    with torch.cuda.stream(st):
+        for _ in range(3 + reps):
+            glc.gemv_q4k_chain_dev(jobs, s)
+    torch.cuda.synchronize()
+    glc.gemv_poll_error()
     worker.dispose()
 
 
@@ -181,6 +203,8 @@ def main(argv=None) -> int:
         case_gemv(torch, glc, 4096, 28672, n)
     elif c == "gemv_k14336":
         case_gemv(torch, glc, 14336, 8192, n)
+    elif c == "gemv_chain":
+        case_gemv_chain(torch, glc, n)
     elif c in ("router", "router_wide"):
         case_router(torch, glc, c == "router_wide", n)
     elif c == "wire":

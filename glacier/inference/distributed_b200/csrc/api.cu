@@ -1326,6 +1326,7 @@ int glc_gemv_q4k_dev(const void* W, const float* x, float* y, int32_t K, int32_t
     if (!W || !x || !y) return fail(GLC_ERR_INVALID_ARG, "null pointer");
     if (N <= 0 || K <= 0) return fail(GLC_ERR_INVALID_ARG, "K and N must be positive");
     if (K % 256) return fail(GLC_ERR_UNSUPPORTED, "Dimension %d is not a multiple of 256 for quantization Q4_K.", K);
+    if (((uintptr_t)W | (uintptr_t)x) & 15u) return fail(GLC_ERR_INVALID_ARG, "W and x must be 16-byte aligned");
     GemvDeviceState* st = nullptr;
     if (int rc = gemv_state(&st)) return rc;
     glc::GemvParams p{};
@@ -1363,8 +1364,8 @@ int glc_gemv_q4k_chain_dev(const glc_gemv_job* jobs, int32_t n, void* stream) {
         if (a.op != GLC_GEMV_SET && a.op != GLC_GEMV_ADD && a.op != GLC_GEMV_GATE_UP)
             return fail(GLC_ERR_INVALID_ARG, "job %d: unknown op %d", j, a.op);
         if (a.op == GLC_GEMV_GATE_UP && !a.W_up) return fail(GLC_ERR_INVALID_ARG, "job %d: GATE_UP needs W_up", j);
-        if (((uintptr_t)a.x | (uintptr_t)a.norm_w) & 15u)
-            return fail(GLC_ERR_INVALID_ARG, "job %d: x and norm_w must be 16-byte aligned", j);
+        if (((uintptr_t)a.W | (uintptr_t)a.W_up | (uintptr_t)a.x | (uintptr_t)a.norm_w) & 15u)
+            return fail(GLC_ERR_INVALID_ARG, "job %d: W, W_up, x and norm_w must be 16-byte aligned", j);
         if (a.norm_w && !(a.norm_eps >= 0.f)) return fail(GLC_ERR_INVALID_ARG, "job %d: bad norm_eps", j);
         glc::GemvJob& b = p.jobs[j];
         b.A = (const uint8_t*)a.W;
@@ -1375,7 +1376,7 @@ int glc_gemv_q4k_chain_dev(const glc_gemv_job* jobs, int32_t n, void* stream) {
         b.norm_eps = a.norm_eps;
         b.K = a.K;
         b.N = a.N;
-        b.op = a.op;  // GLC_GEMV_* and glc::GemvChainOp share their values
+        b.op = (unsigned short)a.op;  // GLC_GEMV_* and glc::GemvChainOp share their values
         b.after_previous = a.after_previous ? 1 : 0;
     }
     p.njobs = n;

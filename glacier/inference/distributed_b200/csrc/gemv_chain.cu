@@ -10,19 +10,22 @@
 // Why one launch: a stand-alone GEMV streams its weights at the HBM rate only
 // between its ramp and its tail; back to back, each launch's consumers must
 // wait for the whole previous grid before they read their input, so every
-// launch pays the slowest CTA of the one before.  Here one producer warp per
-// SM streams the weight rows of ALL jobs through the shared-memory ring
-// without a break (weights never depend on activations), and only the
+// launch pays the slowest CTA of the one before plus a ramp.  Here one
+// producer warp per SM streams the weight rows of ALL jobs through the
+// shared-memory ring (weights never depend on activations), and only the
 // consumer warps stop at the grid-wide barrier in front of a job whose input
-// is an earlier job's output -- the ring keeps filling meanwhile, so HBM
-// stays busy across job boundaries.
+// is an earlier job's output -- by then the ring already holds that job's
+// first stages, so the consumers resume at compute speed while the copies
+// catch up.  Measured per dependent job boundary on B200: ~2 us barrier
+// (the slowest CTA's arrival and the polls) and ~1.5 us input staging.
 //
 // Per job the layout is the stand-alone GEMV's (gemv_q4k.cu, gemv_lane.cuh):
 // lane u of a row owns one 32-byte quant chunk, nsegw warps cover a row, G
 // groups of warps take four row-units per stage; rows of a job are split
-// evenly over the CTAs; each row's reduction order is the stand-alone
-// kernel's, so a job's output is bit-identical to glc_gemv_q4k_dev's (and, for
-// a normed job, to the normed GEMV's).  Launched cooperatively (all CTAs
+// evenly over the CTAs.  A job's input is staged once per CTA
+// (stage_x_shared: coalesced reads, int16 codes in shared memory) and each
+// row's reduction order is the stand-alone kernel's, so a job's output is
+// bit-identical to glc_gemv_q4k_dev's.  Launched cooperatively (all CTAs
 // resident, one per SM) and programmatically serialised behind the kernel
 // before it.
 #include <algorithm>
@@ -38,7 +41,10 @@ namespace {
 constexpr int kChainWarps = kGemvMaxConsumerWarps;      // consumer warps
 constexpr int kChainThreads = (kChainWarps + 1) * 32;   // + the producer warp
 constexpr int kNormSlots = 32;                          // per-warp sums of x^2 of a normed job
-
+// (Measured on B200 with the input staged: holding the producer back at a
+// dependent job until the consumers hold its input, or prefetching the
+// stages beyond the ring into L2 so that HBM keeps streaming through the
+// wait, made both GEMV shapes slower; the ring runs free.)
 __device__ __forceinline__ void job_layout(const GemvJob& jb, int& nsegw, int& G, int& R, int& NM, int& rowBytes) {
     const int U = (jb.K >> 8) * 4;
     nsegw = (U + 31) / 32;
@@ -53,9 +59,13 @@ __global__ void __launch_bounds__(kChainThreads, 1) q4k_gemv_chain_kernel(const 
     const int S = p.stages;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * p.slot_bytes);
     uint64_t* empty = full + S;
-    float* nss0 = reinterpret_cast<float*>(empty + S);  // two buffers of kNormSlots (job parity)
-    float* part0 = nss0 + 2 * kNormSlots;                 // two buffers of p.part_floats (job parity)
-    __shared__ int s_ok;
+    float* nss = reinterpret_cast<float*>(empty + S);  // [kNormSlots] per-warp sums of x^2
+    // (dynamic shared memory only: the opt-in limit is set for the dynamic size)
+    int& s_ok = *reinterpret_cast<int*>(nss + kNormSlots);
+    // one region, used in turn: the staged input (xs_bytes(K)) while the
+    // lanes read it, then the job's per-row partial sums (p.part_floats)
+    float* part = nss + kNormSlots + 4;
+    uint32_t* xs = reinterpret_cast<uint32_t*>(part);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     grid_dep_launch_dependents();
@@ -109,12 +119,11 @@ __global__ void __launch_bounds__(kChainThreads, 1) q4k_gemv_chain_kernel(const 
         job_layout(jb, nsegw, G, R, NM, rowBytes);
         const int r0 = (int)((long long)jb.N * blockIdx.x / gridDim.x);
         const int r1 = (int)((long long)jb.N * (blockIdx.x + 1) / gridDim.x);
-        float* part = part0 + (j & 1) * p.part_floats;
-        float* nss = nss0 + (j & 1) * kNormSlots;
+        // the previous job's epilogue has read the region (partial sums)
+        named_bar_sync(1, kChainWarps * 32);
         if (jb.after_previous && j > 0) {
             // every CTA's outputs of the earlier jobs before this job's input
-            named_bar_sync(1, kChainWarps * 32);
-            if (threadIdx.x == 0) s_ok = grid_barrier(p.bar, gridDim.x, p.err) ? 1 : 0;
+            if (threadIdx.x == 0) s_ok = (ok && grid_barrier(p.bar, gridDim.x, p.err)) ? 1 : 0;
             named_bar_sync(1, kChainWarps * 32);
             if (!s_ok) ok = false;  // the barrier gave up (recorded): no further waits, no stores
         }
@@ -125,17 +134,16 @@ __global__ void __launch_bounds__(kChainThreads, 1) q4k_gemv_chain_kernel(const 
         const bool active = in_layout && u < U;
         const int sb = active ? (u >> 2) : 0, c = u & 3;
         XRegs xr;
-        if (r1 > r0) {
-            if (jb.norm_w) {
-                float ss;
-                load_x_norm<kXGlobalCG>(xr, reinterpret_cast<const float4*>(jb.x) + 16 * u,
-                                        reinterpret_cast<const float4*>(jb.norm_w) + 16 * u, active, ss);
-                ss = warp_tree(ss);
-                if (grp == 0 && lane == 0) nss[segw] = ss;
-            } else {
-                load_x<kXGlobalCG>(xr, reinterpret_cast<const float4*>(jb.x) + 16 * u, 1, active);
-            }
+        stage_x_shared<kXGlobalCG>(jb.x, jb.norm_w, jb.K, xs, nss, threadIdx.x, kChainWarps * 32);
+        named_bar_sync(1, kChainWarps * 32);
+        read_x_shared(xr, xs, U, u, active);
+        float rinv = 1.0f;
+        if (jb.norm_w) {
+            float ss = 0.f;
+            for (int q = 0; q < kChainWarps; ++q) ss += nss[q];
+            rinv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)jb.K), jb.norm_eps)));
         }
+        named_bar_sync(1, kChainWarps * 32);  // every lane holds its input: the region takes partial sums now
         for (int c0 = r0; c0 < r1; c0 += R) {
             const int nr = min(R, r1 - c0);
             const int buf = sidx % S;
@@ -152,13 +160,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) q4k_gemv_chain_kernel(const 
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[buf]);
         }
-        named_bar_sync(1, kChainWarps * 32);  // the job's partial sums (and norm sums) are in place
-        float rinv = 1.0f;
-        if (jb.norm_w) {
-            float ss = 0.f;
-            for (int q = 0; q < nsegw; ++q) ss += nss[q];
-            rinv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)jb.K), jb.norm_eps)));
-        }
+        named_bar_sync(1, kChainWarps * 32);  // the job's partial sums are in place
         if (ok) {
             for (int lr = threadIdx.x; lr < r1 - r0; lr += kChainWarps * 32) {
                 const float* pp = part + (size_t)lr * NM * nsegw;
@@ -186,14 +188,14 @@ __global__ void __launch_bounds__(kChainThreads, 1) q4k_gemv_chain_kernel(const 
 }  // namespace
 
 size_t gemv_chain_smem_bytes(const GemvChainParams& p) {
-    return (size_t)p.stages * (p.slot_bytes + 2 * sizeof(uint64_t)) + 2 * kNormSlots * sizeof(float) +
-           2 * (size_t)p.part_floats * sizeof(float);
+    return (size_t)p.stages * (p.slot_bytes + 2 * sizeof(uint64_t)) + (kNormSlots + 4) * sizeof(float) +
+           (size_t)p.part_floats * sizeof(float);
 }
 
 // Fills the derived fields (ring shape, partial-sum space) and checks the jobs.
 int gemv_chain_configure(GemvChainParams& p, int grid, size_t smem_limit, size_t* smem_bytes) {
     if (p.njobs <= 0 || p.njobs > kMaxChainJobs || grid <= 0) return -1;
-    int slot = 0, part = 0;
+    int slot = 0, part = 0;  // part: floats of the shared region (partial sums or the staged input)
     for (int j = 0; j < p.njobs; ++j) {
         const GemvJob& jb = p.jobs[j];
         if (jb.K <= 0 || (jb.K & 255) || jb.N <= 0 || !jb.A || !jb.x || !jb.y) return -1;
@@ -208,10 +210,11 @@ int gemv_chain_configure(GemvChainParams& p, int grid, size_t smem_limit, size_t
         slot = std::max(slot, NM * stage_rows_for(NM, G) * rowBytes);
         const int rows_per_cta = (jb.N + grid - 1) / grid;
         part = std::max(part, rows_per_cta * NM * nsegw);
+        part = std::max(part, (int)(xs_bytes(jb.K) / sizeof(float)));
     }
     p.slot_bytes = (slot + 127) / 128 * 128;
     p.part_floats = part;
-    const size_t fixed = 2 * kNormSlots * sizeof(float) + 2 * (size_t)part * sizeof(float);
+    const size_t fixed = (kNormSlots + 4) * sizeof(float) + (size_t)part * sizeof(float);
     const size_t per_stage = (size_t)p.slot_bytes + 2 * sizeof(uint64_t);
     if (smem_limit < fixed + 2 * per_stage) return -1;
     int S = (int)((smem_limit - fixed) / per_stage);

@@ -121,6 +121,100 @@ __device__ __forceinline__ void load_x_norm(XRegs& r, const float4* xp, const fl
     }
 }
 
+// ---- the input staged once per CTA --------------------------------------
+// load_x has every lane read its own 64 consecutive floats (a warp's 16-byte
+// loads then touch 32 lines each) and every warp group of a CTA repeat it;
+// for a row-major input that nothing has laid out for the lanes, a CTA then
+// issues ~K/2 line requests to L2 for a K-float vector, and 148 CTAs doing so
+// at once took ~10 us per input.  Here the CTA's threads read the vector once,
+// coalesced (thread t of n reads float4 t, t + n, ...), form each 32-block's
+// maximum and sum with shuffles among its 8 threads, quantise to int16 as
+// quant_block32 does, and write every lane's registers transposed into shared
+// memory (word w of unit u at w * xs_stride(U) + u, conflict-free); each lane
+// then reads its 36 words.  The block sums are formed in a different order
+// from quant_block32's, so values can differ from load_x's in the last bit.
+constexpr int kXsWords = 36;  // xa[16], xb[16], sA, sB16, sumA, sumB
+
+__host__ __device__ inline int xs_stride(int U) { return (U + 31) / 32 * 32 + 1; }
+__host__ __device__ inline size_t xs_bytes(int K) { return (size_t)kXsWords * xs_stride(K / 64) * 4; }
+
+// nthr threads (a multiple of 32) starting at thread 0 of the CTA; x, w
+// 16-byte aligned.  w may be null.  With w, ss_warp[warp] receives the warp's
+// sum of the raw x^2 (threads add their values in load order, then a warp
+// butterfly), from which the caller forms the RMSNorm scale.
+template <int SRC>
+__device__ __forceinline__ void stage_x_shared(const float* x, const float* w, int K, uint32_t* xs, float* ss_warp,
+                                               int tid, int nthr) {
+    const int F4 = K >> 2, U = K >> 6, st = xs_stride(U);
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+    float ss = 0.f;
+    for (int f0 = 0; f0 < F4; f0 += 8 * nthr) {
+        float4 v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int f = f0 + k * nthr + tid;
+            v[k] = f < F4 ? ldx4<SRC>(x4 + f) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int f = f0 + k * nthr + tid;  // F4 is a multiple of 64: an 8-thread group is in or out together
+            if (f0 + k * nthr >= F4) break;
+            float4 a = v[k];
+            if (w) {
+                ss = fmaf(a.x, a.x, ss); ss = fmaf(a.y, a.y, ss); ss = fmaf(a.z, a.z, ss); ss = fmaf(a.w, a.w, ss);
+                const float4 g = f < F4 ? __ldg(w4 + f) : make_float4(0.f, 0.f, 0.f, 0.f);
+                a = make_float4(__fmul_rn(a.x, g.x), __fmul_rn(a.y, g.y), __fmul_rn(a.z, g.z), __fmul_rn(a.w, g.w));
+            }
+            float mx = fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w)));
+            float sm = ((a.x + a.y) + a.z) + a.w;
+#pragma unroll
+            for (int o = 1; o <= 4; o <<= 1) {
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                sm += __shfl_xor_sync(0xffffffffu, sm, o);
+            }
+            if (f < F4) {
+                const float inv = mx > 0.f ? 32767.0f / mx : 0.f;
+                const float t0 = __fadd_rn(__fmul_rn(a.x, inv), 12582912.0f);
+                const float t1 = __fadd_rn(__fmul_rn(a.y, inv), 12582912.0f);
+                const float t2 = __fadd_rn(__fmul_rn(a.z, inv), 12582912.0f);
+                const float t3 = __fadd_rn(__fmul_rn(a.w, inv), 12582912.0f);
+                const int u = f >> 4, q = f & 15, blk = q >> 3, wi = blk * 16 + (q & 7) * 2;
+                xs[wi * st + u] = __byte_perm(__float_as_uint(t0), __float_as_uint(t1), 0x5410);
+                xs[(wi + 1) * st + u] = __byte_perm(__float_as_uint(t2), __float_as_uint(t3), 0x5410);
+                if ((q & 7) == 0) {
+                    const float scale = mx * (1.0f / 32767.0f);
+                    xs[(32 + blk) * st + u] = __float_as_uint(blk ? scale * 0.0625f : scale);
+                    xs[(34 + blk) * st + u] = __float_as_uint(sm);
+                }
+            }
+        }
+    }
+    if (w) {
+        ss = warp_tree(ss);
+        if ((tid & 31) == 0) ss_warp[tid >> 5] = ss;
+    }
+}
+
+__device__ __forceinline__ void read_x_shared(XRegs& r, const uint32_t* xs, int U, int u, bool active) {
+    const int st = xs_stride(U);
+    if (!active) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) r.xa[i] = r.xb[i] = 0;
+        r.sA = r.sB16 = r.sumA = r.sumB = 0.f;
+        return;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        r.xa[i] = (int)xs[i * st + u];
+        r.xb[i] = (int)xs[(16 + i) * st + u];
+    }
+    r.sA = __uint_as_float(xs[32 * st + u]);
+    r.sB16 = __uint_as_float(xs[33 * st + u]);
+    r.sumA = __uint_as_float(xs[34 * st + u]);
+    r.sumB = __uint_as_float(xs[35 * st + u]);
+}
+
 // Float index of element w (0..63) of unit u in the chunk-major layout.
 __device__ __forceinline__ int chunk_major_index(int u, int w, int U) { return ((w >> 2) * U + u) * 4 + (w & 3); }
 

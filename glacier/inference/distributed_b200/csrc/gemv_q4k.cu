@@ -24,6 +24,8 @@
 //     group g computes slot g % k, keeping that slot's activations in
 //     registers for the whole launch (no reload mid-stream, no half-empty
 //     stage at each slot's end).  Each row's reduction order is unchanged.
+#include <algorithm>
+
 #include "common.cuh"
 #include "gemv_lane.cuh"
 #include "kernels.h"
@@ -157,6 +159,17 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
     int cur_x = -1;
     bool ok = true;
     grid_dep_wait();  // the input is the previous kernel's output
+    // one input for the whole CTA (plain mode): staged once, coalesced, in the
+    // partial-sum region before any partial sum is written
+    const bool staged = p.mode == kGemvPlain && p.nseg == 1;
+    if (staged) {
+        uint32_t* xs = reinterpret_cast<uint32_t*>(part);
+        stage_x_shared<kXGlobalRO>(p.x, NORM ? p.norm_w : nullptr, p.K, xs, nss, threadIdx.x, NW * 32);
+        named_bar_sync(1, NW * 32);
+        read_x_shared(xr, xs, U, u, active);
+        named_bar_sync(1, NW * 32);
+        cur_x = 0;
+    }
     for_each_stage<SPLIT>(p, r0, r1, [&](int sidx, int seg, int j, int, int nr, int lr0) {
         if (!ok) return;
         const int jj = SPLIT ? js : j;
@@ -192,8 +205,8 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
     // ------------------------------------------------------------ epilogue
     float rinv = 1.0f;
     if constexpr (NORM) {
-        float ss = 0.f;
-        for (int q = 0; q < nsegw; ++q) ss += nss[q];
+        float ss = 0.f;  // per-warp sums when staged, per-segment sums otherwise
+        for (int q = 0; q < (staged ? NW : nsegw); ++q) ss += nss[q];
         rinv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)p.K), p.norm_eps)));
     }
     const int nrows = r1 - r0;
@@ -249,7 +262,9 @@ int gemv_configure(GemvParams& p, int num_sms, size_t smem_limit, size_t* smem_b
     if (g > total) g = (int)total;
     if (p.norm_w && (p.nseg != 1 || p.mode == kGemvDownCombine)) return -1;
     // the per-CTA row sums, then the norm's per-segment sums of squares
-    const size_t part_bytes = (size_t)((total + g - 1) / g) * NMP * nsegw * sizeof(float) + 32 * sizeof(float);
+    size_t part_bytes = (size_t)((total + g - 1) / g) * NMP * nsegw * sizeof(float);
+    if (p.mode == kGemvPlain && p.nseg == 1) part_bytes = std::max(part_bytes, xs_bytes(p.K));  // staged input
+    part_bytes += 32 * sizeof(float);
     const size_t per_stage = stage_bytes + 2 * sizeof(uint64_t);
     if (smem_limit < part_bytes + 2 * per_stage) return -1;
     int S = (int)((smem_limit - part_bytes) / per_stage);

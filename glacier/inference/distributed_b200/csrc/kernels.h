@@ -67,15 +67,16 @@ int gemv_configure(GemvParams& p, int num_sms, size_t smem_limit, size_t* smem_b
 // A chain of Q4_K GEMVs in one persistent launch (gemv_chain.cu).
 enum GemvChainOp : int { kChainSet = 0, kChainAdd = 1, kChainGateUp = 2 };
 constexpr int kMaxChainJobs = 64;
-struct GemvJob {
+struct GemvJob {          // 56 bytes: 64 jobs and the rest stay under 4 KB of kernel parameters
     const uint8_t* A;      // Q4_K [N][K/256*144] (gate rows for kChainGateUp)
     const uint8_t* B;      // up rows (kChainGateUp)
     const float* x;        // [K]
     float* y;              // [N]
     const float* norm_w;   // nullptr, or the input is RMSNorm(x) * norm_w
     float norm_eps;
-    int K, N, op;
-    int after_previous;    // x may be an earlier job's output: grid-wide barrier first
+    int K, N;
+    unsigned short op;
+    unsigned short after_previous;  // x may be an earlier job's output: grid-wide barrier first
 };
 struct GemvChainParams {
     GemvJob jobs[kMaxChainJobs];
@@ -85,6 +86,7 @@ struct GemvChainParams {
     // filled by gemv_chain_configure
     int stages, slot_bytes, part_floats;
 };
+static_assert(sizeof(GemvChainParams) <= 4096, "chain parameters fit the classic kernel-parameter limit");
 int gemv_chain_configure(GemvChainParams& p, int grid, size_t smem_limit, size_t* smem_bytes);
 cudaError_t gemv_chain_launch(GemvChainParams p, int num_sms, cudaStream_t stream);
 

@@ -171,7 +171,8 @@ int glc_moe_graph_build(glc_moe* h, int32_t layer, const float* x, int32_t T, ui
 int glc_moe_graph_launch(glc_moe* h, void* stream);
 
 /* ---- raw primitive: QuantKernels.MatVecMul(Q4_K, W, x, y, nCols=K, nRows=N)
- *      (call shape CpuWarmExpertPoolWorker.cs:379). K % 256 != 0 -> GLC_ERR_UNSUPPORTED. ---- */
+ *      (call shape CpuWarmExpertPoolWorker.cs:379). K % 256 != 0 -> GLC_ERR_UNSUPPORTED;
+ *      W and x 16-byte aligned. ---- */
 int glc_gemv_q4k_dev(const void* W, const float* x, float* y, int32_t K, int32_t N, void* stream);
 
 /* ---- a chain of MatVecMul calls in one launch: the GemvQ4K / SwiGLU /
@@ -180,7 +181,7 @@ int glc_gemv_q4k_dev(const void* W, const float* x, float* y, int32_t K, int32_t
  *      streamed back to back.  Jobs run in order; a job with after_previous
  *      set may read what earlier jobs of the chain wrote (a grid-wide wait
  *      precedes it).  Device pointers; at most 64 jobs; K % 256 == 0;
- *      x, norm_w 16-byte aligned.  Each job's output is bit-identical to
+ *      W, W_up, x, norm_w 16-byte aligned.  Each job's output is bit-identical to
  *      glc_gemv_q4k_dev's (op SET, no norm).  Asynchronous on `stream`. ---- */
 #define GLC_GEMV_SET 0      /* y = W x */
 #define GLC_GEMV_ADD 1      /* y = y + W x */
