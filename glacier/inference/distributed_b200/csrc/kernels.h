@@ -111,6 +111,8 @@ struct AttnParams {
     const float* bq = nullptr;
     const float* bk = nullptr;
     const float* bv = nullptr;
+    // theta^(-2i/128) for pair i, in double (filled by attn_decode_launch)
+    double inv_freq[64];
 };
 size_t attn_workspace_bytes(int n_heads, int n_kv_heads, int max_len);
 cudaError_t attn_decode_launch(AttnParams p, cudaStream_t stream);
