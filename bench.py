@@ -396,7 +396,7 @@ def run_ours(args, w):
     if not args.skip_qwen:
         worker.dispose()  # the Qwen layer (1.1 GB) gets the device to itself
         worker = None
-        qwen = measure_qwen(torch, glc, args, stream, rank == 0 and world == 1 and not args.skip_cpu_baseline)
+        qwen = measure_qwen(torch, glc, args, stream, rank == 0 and world == 1 and not args.skip_cpu_baseline, local)
     ep_leg = measure_ep(torch, dist, glc, w, stream, args, world, rank, local) if not args.skip_ep else None
     dense = measure_dense(torch, dist, glc, args, stream, world, rank, local) if not args.skip_dense else None
 
@@ -428,7 +428,7 @@ def run_ours(args, w):
                          # timed region's CUDA events give its average duration
                          "avg_launch_ms": ms_total / args.steps,
                          "isolated_launch_ms": fused_avg,
-                         "traffic": profile_traffic("moe_decode_fused_mixtral_decode")},
+                         "traffic": profile_traffic("moe_decode_fused_kernel_mixtral_t1")},
             "kernels": {"fused_layer_ms": fused_avg, "fused_layer_ms_median": float(np.median(kf[:, 0])),
                         "fused_layer_note": "event marks around each launch (adds the marks' own gaps)",
                         "isolated_launch_gbs": fused_gbs,
@@ -642,7 +642,7 @@ def qwen_host_layer(glc, w, worker):
     return o, L
 
 
-def measure_qwen(torch, glc, args, stream, want_cpu):
+def measure_qwen(torch, glc, args, stream, want_cpu, local=0):
     """Qwen2-57B-A14B-shaped MoE layer (hidden 3584, 64 experts top-8 softmax
     without renormalisation, SwiGLU experts 3584->2560->3584, a sigmoid-gated
     shared expert 3584->20480->3584, all Q4_K) at token batches of 1, 16 and
@@ -653,7 +653,8 @@ def measure_qwen(torch, glc, args, stream, want_cpu):
     123,863,040 B + the router + activations."""
     w = QWEN
     D, F, E, k, Fs = w["D"], w["F"], w["E"], w["k"], w["Fs"]
-    worker = glc.GpuExpertStageWorker(D, F, E, k, shared_ffn_dim=Fs, renormalize=False, max_tokens=max(QWEN_T))
+    worker = glc.GpuExpertStageWorker(D, F, E, k, shared_ffn_dim=Fs, renormalize=False, device=local,
+                                      max_tokens=max(QWEN_T))
     worker.synth_layer(0, w["seed"])
     s = stream.cuda_stream
     peak, _ = peaks()

@@ -35,6 +35,13 @@
 #ifndef GLC_FUSED_MAX_STAGES
 #define GLC_FUSED_MAX_STAGES 8
 #endif
+// Launch the decode layer programmatically serialised behind the kernel
+// before it (its CTAs take SMs as that kernel's leave them and stage the
+// router weights before waiting) instead of cooperatively.
+#ifndef GLC_FUSED_PDL
+#define GLC_FUSED_PDL 0
+#endif
+
 namespace glc {
 
 namespace {
@@ -196,6 +203,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
     const int T = p.T, D = p.D, F = p.F, k = p.k, P = T * k;
     const uint64_t lim = p.wait_limit_ns > 0 ? (uint64_t)p.wait_limit_ns : kWaitLimitNs;
     const int slot = p.slot_bytes;
+#if GLC_FUSED_PDL
+    grid_dep_launch_dependents();
+#endif
 
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
@@ -217,11 +227,23 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
     const float* xraw = reinterpret_cast<const float*>(smem + wb);
     if (tid == 0) {
         const uint32_t xb = (uint32_t)T * D * 4u;
+#if GLC_FUSED_PDL
+        // the router weights never depend on the kernel before; the input may
+        mbar_arrive_expect_tx(wbar, wb);
+        bulk_g2s_nohint(smem, p.Wr, wb, wbar);
+        grid_dep_wait();
+        mbar_arrive_expect_tx(xbar, xb);
+        bulk_g2s_nohint(smem + wb, p.x, xb, xbar);
+#else
         mbar_arrive_expect_tx(xbar, xb);
         bulk_g2s_nohint(smem + wb, p.x, xb, xbar);
         mbar_arrive_expect_tx(wbar, wb);
         bulk_g2s_nohint(smem, p.Wr, wb, wbar);
+#endif
     }
+#if GLC_FUSED_PDL
+    grid_dep_wait();  // every thread: what the kernel before wrote is visible
+#endif
     // Every CTA reports its end when the caller waits on host memory (see
     // FusedDecodeParams::done_ctr): its writes become visible system-wide
     // first, and the CTA that completes a multiple of the grid size publishes
@@ -552,8 +574,13 @@ cudaError_t fused_decode_launch(const FusedDecodeParams& p0, int num_sms, cudaSt
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
+#if GLC_FUSED_PDL
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+#else
     attr[0].id = cudaLaunchAttributeCooperative;  // all CTAs co-resident: the grid barrier needs it
     attr[0].val.cooperative = 1;
+#endif
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, moe_decode_fused_kernel, p);
