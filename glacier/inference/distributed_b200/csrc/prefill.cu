@@ -154,26 +154,46 @@ struct SharedCombine {
     const float* sg;   // [T] sigmoid gate values
 };
 
+// CTA (t, chunk): dimensions chunk * 256 + thread of token t.  Every load of
+// a thread (its k expert rows and the shared expert's slices) is issued
+// before the sums, which keep the k-ordered order (y * w) + acc, then the
+// shared term (y_shared * gate) + acc.
+constexpr int kCombineMaxK = 16, kCombineMaxSlices = 8;
 __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ y, int D, int k,
                                                       const int* __restrict__ inv, const float* __restrict__ w,
                                                       const float* __restrict__ resid, float* __restrict__ out,
                                                       SharedCombine sh, const int* __restrict__ count) {
     const int t = blockIdx.x;
     if (count && t >= *count) return;  // a token past the batch sized on the device
-    for (int d = threadIdx.x; d < D; d += 256) {
-        float acc = resid ? resid[(size_t)t * D + d] : 0.f;
-        for (int j = 0; j < k; ++j) {
-            const int pos = inv[t * k + j];
-            acc = __fadd_rn(__fmul_rn(y[(size_t)pos * D + d], w[t * k + j]), acc);
-        }
-        if (sh.ysh) {
-            const float* ys = sh.ysh + (size_t)t * D + d;
-            float v = ys[0];
-            for (int s = 1; s < sh.nslices; ++s) v = __fadd_rn(v, ys[(size_t)s * sh.stride]);
-            acc = __fadd_rn(__fmul_rn(v, sh.sg[t]), acc);
-        }
-        out[(size_t)t * D + d] = acc;
+    __shared__ int s_pos[kCombineMaxK];
+    __shared__ float s_w[kCombineMaxK];
+    if (threadIdx.x < k) {
+        s_pos[threadIdx.x] = inv[t * k + threadIdx.x];
+        s_w[threadIdx.x] = w[t * k + threadIdx.x];
     }
+    __syncthreads();
+    const int d = blockIdx.y * 256 + threadIdx.x;
+    if (d >= D) return;
+    float yv[kCombineMaxK], sv[kCombineMaxSlices];
+#pragma unroll
+    for (int j = 0; j < kCombineMaxK; ++j)
+        if (j < k) yv[j] = __ldg(y + (size_t)s_pos[j] * D + d);
+    const int ns = sh.ysh ? sh.nslices : 0;
+#pragma unroll
+    for (int s = 0; s < kCombineMaxSlices; ++s)
+        if (s < ns) sv[s] = __ldg(sh.ysh + (size_t)s * sh.stride + (size_t)t * D + d);
+    float acc = resid ? __ldg(resid + (size_t)t * D + d) : 0.f;
+#pragma unroll
+    for (int j = 0; j < kCombineMaxK; ++j)
+        if (j < k) acc = __fadd_rn(__fmul_rn(yv[j], s_w[j]), acc);
+    if (ns > 0) {
+        float v = sv[0];
+#pragma unroll
+        for (int s = 1; s < kCombineMaxSlices; ++s)
+            if (s < ns) v = __fadd_rn(v, sv[s]);
+        acc = __fadd_rn(__fmul_rn(v, sh.sg[t]), acc);
+    }
+    out[(size_t)t * D + d] = acc;
 }
 
 cudaError_t dispatch_plan_launch(const int* ids, int P, int E, const DispatchPlan& plan, cudaStream_t st,
@@ -194,9 +214,10 @@ cudaError_t combine_launch(const float* y, int T, int D, int k, const int* inv, 
                            float* out, cudaStream_t st, const float* ysh, int ysh_slices, long long ysh_stride,
                            const float* sg, const int* count) {
     if (T <= 0) return cudaSuccess;
-    if (ysh && (ysh_slices < 1 || !sg)) return cudaErrorInvalidValue;
-    combine_kernel<<<T, 256, 0, st>>>(y, D, k, inv, w, resid, out, SharedCombine{ysh, ysh_slices, ysh_stride, sg},
-                                      count);
+    if (ysh && (ysh_slices < 1 || ysh_slices > kCombineMaxSlices || !sg)) return cudaErrorInvalidValue;
+    if (k < 1 || k > kCombineMaxK) return cudaErrorInvalidValue;
+    combine_kernel<<<dim3(T, (D + 255) / 256), 256, 0, st>>>(y, D, k, inv, w, resid, out,
+                                                             SharedCombine{ysh, ysh_slices, ysh_stride, sg}, count);
     return cudaGetLastError();
 }
 

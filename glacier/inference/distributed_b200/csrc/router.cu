@@ -404,8 +404,10 @@ cudaError_t router_launch(const RouterParams& p, cudaStream_t stream) {
     // Few tokens: one token per CTA for parallelism; many: amortise Wr loads.
     const bool many = p.T > 64;
     if (p.E <= 8) return many ? launch_router<8, 4, 4>(p, stream) : launch_router<8, 1, 4>(p, stream);
-    // wider routers: a cluster of E/8 CTAs per token block
-    return p.T > 4 ? launch_router_wide<4, 4>(p, stream) : launch_router_wide<1, 8>(p, stream);
+    // wider routers: a cluster of E/8 CTAs per token block; one token per
+    // block up to 64 tokens (more CTAs in flight), four beyond (fewer
+    // re-reads of the router columns)
+    return p.T > 64 ? launch_router_wide<4, 4>(p, stream) : launch_router_wide<1, 8>(p, stream);
 }
 
 }  // namespace glc
