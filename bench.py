@@ -367,7 +367,7 @@ def run_ours(args, w):
 
     # End to end through the public host API: pinned host input -> H2D ->
     # layer -> D2H output + expert ids/weights, every step.
-    e2e_steps = min(args.steps, 2000)
+    e2e_steps = max(200, min(args.steps, 2000))  # at least 200 calls (~15 ms) for a stable host-clock figure
     hx = torch.from_numpy(make_tokens(w, N_TOKENS)).pin_memory().numpy()
     hout = torch.empty(T, D, pin_memory=True).numpy()
     hids = torch.empty(T, w["k"], dtype=torch.int32, pin_memory=True).numpy()
@@ -405,6 +405,9 @@ def run_ours(args, w):
         qwen = measure_qwen(torch, glc, args, stream, rank == 0 and world == 1 and not args.skip_cpu_baseline, local)
     ep_leg = measure_ep(torch, dist, glc, w, stream, args, world, rank, local) if not args.skip_ep else None
     dense = measure_dense(torch, dist, glc, args, stream, world, rank, local) if not args.skip_dense else None
+    # configs[4] fits one GPU (~80 GB); measured at N = 1 only (the ranks of a
+    # multi-GPU run would each synthesise their own copy on the same host)
+    mix22 = measure_mixtral22b(torch, glc, args, stream, local) if (world == 1 and not args.skip_dense) else None
 
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.skip_cpu_baseline:
@@ -463,6 +466,8 @@ def run_ours(args, w):
             line["qwen2_57b"] = qwen
         if dense is not None:
             line["dense_pp"] = dense
+        if mix22 is not None:
+            line["mixtral8x22b"] = mix22
         if ep_leg is not None:
             line["ep"] = ep_leg
         print(json.dumps(line), flush=True)
@@ -876,6 +881,66 @@ def measure_dense(torch, dist, glc, args, stream, world, rank, local):
                         else "single GPU", "submission": "one captured graph per stage step, replayed per token"}
 
 
+MIXTRAL22B = dict(name="mixtral8x22b_decode", D=6144, F=16384, E=8, k=2, Hq=48, Hkv=8, layers=56, vocab=32768,
+                  max_len=4096, seed=20241204)
+
+
+def moe_token_bytes(q, pos):
+    """Bytes one token moves through the whole mixture-of-experts model: every
+    layer's attention matrices, its KV cache rows 0..pos, the router and the
+    k routed experts' gate / up / down Q4_K rows, the embedding row and the LM
+    head."""
+    rb = q4k_row_bytes
+    D, F, Hq, Hkv, E, k = q["D"], q["F"], q["Hq"], q["Hkv"], q["E"], q["k"]
+    attn = (Hq + 2 * Hkv) * 128 * rb(D) + D * rb(Hq * 128)
+    experts = k * (2 * F * rb(D) + D * rb(F))
+    kv = 2 * Hkv * (pos + 1) * 128 * 2
+    return q["layers"] * (attn + experts + D * E * 4 + kv) + q["vocab"] * rb(D) + rb(D)
+
+
+def measure_mixtral22b(torch, glc, args, stream, local):
+    """the whole Mixtral-8x22B-shaped model (56 layers of attention
+    (48 query / 8 KV heads, a 4096-position fp16 cache) and a mixture-of-experts
+    feed-forward of 8 SwiGLU experts, FFN 16384, top-2 renormalised, hidden 6144,
+    vocab 32768; random-init Q4_K, ~80 GB resident) decoding greedily at batch
+    1 at the last positions of the cache, one GPU: every layer through
+    glc_stage_forward_dev (attention launch, O projection, router, routed
+    gate/up and down GEMVs, next QKV), one captured graph per token."""
+    q = MIXTRAL22B
+    D = q["D"]
+    st = glc.DenseStage(D, 0, q["Hq"], q["Hkv"], 0, q["layers"], q["max_len"], 1e6, 1e-5, q["vocab"], True, True,
+                        local, num_experts=q["E"], top_k=q["k"], expert_ffn_dim=q["F"], moe_renormalize=True)
+    t0 = time.perf_counter()
+    for l in range(q["layers"]):
+        st.synth_layer(l, q["seed"])
+    st.synth_io(q["seed"])
+    synth_s = time.perf_counter() - t0
+    s = stream.cuda_stream
+    tok = torch.zeros(1, dtype=torch.int32, device="cuda")
+    steps = 16
+    p0 = q["max_len"] - steps - 3
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            st.forward_dev(p0 + i, token_ptr=tok.data_ptr(), token_out_ptr=tok.data_ptr(), stream=s)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(steps):
+            st.forward_dev(p0 + 3 + i, token_ptr=tok.data_ptr(), token_out_ptr=tok.data_ptr(), stream=s)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    st.poll_error()
+    st.dispose()
+    peak, _ = peaks()
+    tb = moe_token_bytes(q, q["max_len"] - 1)
+    gbs = tb / (ms * 1e-3) / 1e9
+    return {"workload": f"{q['name']}_batch1", "layers": q["layers"], "ms_per_token": ms, "tokens_per_s": 1000.0 / ms,
+            "steps": steps, "positions": [p0 + 3, p0 + 2 + steps], "bytes_per_token": tb,
+            "achieved_gbs": gbs, "frac": gbs / peak, "weights_synthesised_s": round(synth_s, 1),
+            "submission": "one captured graph per token (7 launches per layer), greedy token fed back on the device"}
+
+
 def measure_ep(torch, dist, glc, w, stream, args, world, rank, local):
     """Expert parallelism through the C ABI (glc_moe_ep_forward, the call a C#
     host binds: NCCL inside the library, no torch.distributed on the data
@@ -958,7 +1023,7 @@ def main():
     ap.add_argument("--skip-batched", action="store_true")
     ap.add_argument("--skip-qwen", action="store_true")
     ap.add_argument("--skip-ep", action="store_true")
-    ap.add_argument("--skip-dense", action="store_true")
+    ap.add_argument("--skip-dense", action="store_true", help="skip the configs[3] and configs[4] model legs")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -49,7 +49,8 @@ class StageDesc(C.Structure):
         ("hidden_dim", C.c_int32), ("ffn_dim", C.c_int32), ("n_heads", C.c_int32), ("n_kv_heads", C.c_int32),
         ("head_dim", C.c_int32), ("layer_begin", C.c_int32), ("layer_count", C.c_int32), ("max_len", C.c_int32),
         ("rope_theta", C.c_float), ("rms_eps", C.c_float), ("vocab", C.c_int32), ("has_embedding", C.c_int32),
-        ("has_lm_head", C.c_int32), ("device", C.c_int32),
+        ("has_lm_head", C.c_int32), ("device", C.c_int32), ("num_experts", C.c_int32), ("top_k", C.c_int32),
+        ("expert_ffn_dim", C.c_int32), ("moe_renormalize", C.c_int32),
     ]
 
 
@@ -137,6 +138,7 @@ _SIGNATURES = {
     "glc_stage_destroy": (C.c_int, [vp]),
     "glc_stage_load_layer": (C.c_int, [vp, i32, vp]),
     "glc_stage_load_io": (C.c_int, [vp, vp, vp, vp]),
+    "glc_stage_load_moe_layer": (C.c_int, [vp, i32, vp, vp, vp, vp, vp]),
     "glc_stage_synth_layer": (C.c_int, [vp, i32, C.c_uint64]),
     "glc_stage_synth_io": (C.c_int, [vp, C.c_uint64]),
     "glc_stage_reset": (C.c_int, [vp]),

@@ -502,19 +502,21 @@ class Communicator:
 
 
 class DenseStage:
-    """A dense decoder pipeline stage on one GPU, the counterpart of the
-    reference's IClusterStageModel (Pipeline/IClusterStageModel.cs:9-36):
-    layers [layer_begin, layer_begin + layer_count) of a Qwen2-style model with
+    """A decoder pipeline stage on one GPU, the counterpart of the reference's
+    IClusterStageModel (Pipeline/IClusterStageModel.cs:9-36): layers
+    [layer_begin, layer_begin + layer_count) of a Qwen2-style (dense) or
+    Mixtral-style (``num_experts`` > 0: routed SwiGLU experts) model with
     their fp16 KV caches, plus the embedding table on a first stage and the
     final norm and LM head on a last stage (glc_stage_*)."""
 
     def __init__(self, hidden_dim: int, ffn_dim: int, n_heads: int, n_kv_heads: int, layer_begin: int,
                  layer_count: int, max_len: int, rope_theta: float = 1e6, rms_eps: float = 1e-6,
-                 vocab: int = 0, has_embedding: bool = False, has_lm_head: bool = False, device: int = 0):
+                 vocab: int = 0, has_embedding: bool = False, has_lm_head: bool = False, device: int = 0,
+                 num_experts: int = 0, top_k: int = 0, expert_ffn_dim: int = 0, moe_renormalize: bool = True):
         self._h = None
         self.desc = _lib.StageDesc(hidden_dim, ffn_dim, n_heads, n_kv_heads, 128, layer_begin, layer_count,
                                    max_len, rope_theta, rms_eps, vocab, int(has_embedding), int(has_lm_head),
-                                   device)
+                                   device, num_experts, top_k, expert_ffn_dim, int(moe_renormalize))
         h = C.c_void_p()
         check(lib().glc_stage_create(C.byref(self.desc), C.byref(h)))
         self._h = h
@@ -530,6 +532,17 @@ class DenseStage:
         arrays = [None if a is None else np.ascontiguousarray(a) for a in arrays]
         w = _lib.DenseLayerWeights(*[None if a is None else a.ctypes.data for a in arrays])
         check(lib().glc_stage_load_layer(self._handle(), layer, C.byref(w)))
+
+    def load_moe_layer(self, layer: int, attn_norm, wq, wk, wv, wo, ffn_norm, router, gate_exps, up_exps,
+                       down_exps) -> None:
+        """A mixture-of-experts layer: attention weights and norms, fp32 router
+        [D][E], experts' Q4_K gate / up [E][F][D] and down [E][D][F]."""
+        arrays = [np.ascontiguousarray(a) for a in (attn_norm, wq, wk, wv, wo, ffn_norm)]
+        w = _lib.DenseLayerWeights(arrays[0].ctypes.data, arrays[1].ctypes.data, arrays[2].ctypes.data,
+                                   arrays[3].ctypes.data, None, None, None, arrays[4].ctypes.data,
+                                   arrays[5].ctypes.data, None, None, None)
+        moe = [np.ascontiguousarray(a) for a in (np.asarray(router, np.float32), gate_exps, up_exps, down_exps)]
+        check(lib().glc_stage_load_moe_layer(self._handle(), layer, C.byref(w), *[a.ctypes.data for a in moe]))
 
     def load_io(self, embedding=None, final_norm=None, lm_head=None) -> None:
         arrays = [None if a is None else np.ascontiguousarray(a) for a in (embedding, final_norm, lm_head)]

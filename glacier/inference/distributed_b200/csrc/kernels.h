@@ -132,6 +132,11 @@ struct RouterParams {
     float* w;            // [T][k]
     const float* gate_vec;  // shared-expert gate [D] or nullptr
     float* gate_out;        // [T] sigmoid(xin . gate_vec)
+    // E <= 8 with rmsnorm: when set, xin = RMSNorm(x) * norm_w with epsilon
+    // norm_eps (a decoder layer's weighted feed-forward norm); else the
+    // unweighted norm with epsilon 1e-5
+    const float* norm_w = nullptr;
+    float norm_eps = 0.f;
 };
 cudaError_t router_launch(const RouterParams& p, cudaStream_t stream);
 

@@ -64,7 +64,8 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(const __grid_con
             float s[8];
             for (int w = 0; w < 8; ++w) s[w] = red[w][tid];
             const float ss = tree8(s);
-            rms_s[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), 1e-5f)));
+            const float eps = p.norm_w ? p.norm_eps : 1e-5f;
+            rms_s[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), eps)));
         }
         __syncthreads();
     }
@@ -89,10 +90,12 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(const __grid_con
         for (int u = 0; u < UNROLL; ++u) {
             const int d = d0 + u * kRouterThreads;
             const bool in = d < D;
+            const float nw = (in && p.norm_w) ? __ldg(p.norm_w + d) : 1.0f;
 #pragma unroll
             for (int tb = 0; tb < TB; ++tb) {
                 const float raw = (in && tb < ntb) ? __ldg(X + (size_t)tb * D + d) : 0.f;
                 xv[u][tb] = p.rmsnorm ? __fmul_rn(raw, rms[tb]) : raw;
+                if (p.norm_w) xv[u][tb] = __fmul_rn(xv[u][tb], nw);
             }
 #pragma unroll
             for (int e = 0; e < EP; ++e) wv[u][e] = (in && e < E) ? __ldg(p.Wr + (size_t)d * E + e) : 0.f;
@@ -401,6 +404,7 @@ cudaError_t router_launch(const RouterParams& p, cudaStream_t stream) {
     if (p.T <= 0) return cudaSuccess;
     if (p.E <= 0 || p.E > 64 || p.k <= 0 || p.k > 16 || p.k > p.E || p.D <= 0)
         return cudaErrorInvalidValue;
+    if (p.norm_w && (p.E > 8 || !p.rmsnorm)) return cudaErrorInvalidValue;
     // Few tokens: one token per CTA for parallelism; many: amortise Wr loads.
     const bool many = p.T > 64;
     if (p.E <= 8) return many ? launch_router<8, 4, 4>(p, stream) : launch_router<8, 1, 4>(p, stream);

@@ -18,7 +18,13 @@
 //   x   = x + Wdown a                             (GEMV, residual in the epilogue)
 // with, on a first stage, x = dequantised row `token` of the Q4_K embedding
 // table and, on a last stage asked for logits, logits = Wlm RMSNorm(x) * w_final
-// and the arg-max token.  Two launches per layer: the attention, then ONE GEMV
+// and the arg-max token.  A mixture-of-experts stage (Mixtral-style layers)
+// replaces the feed-forward by the router (the weighted RMSNorm folded in,
+// softmax top-k), the routed experts' gate/up GEMV with SwiGLU and their down
+// GEMV with the k-ordered weighted combine and the residual in its epilogue
+// (GpuFirstExpertStageWorker.ProcessRoutedTopK, GpuFirstExpertStageWorker.cs:
+// 416-583), between the attention's O projection and the next layer's QKV.
+// Dense stages use two launches per layer: the attention, then ONE GEMV
 // chain (gemv_chain.cu) holding the O projection, gate/up, down and the next
 // layer's QKV projection (or the LM head), whose weights stream back to back
 // while only its consumer warps wait grid-wide between the dependent jobs.
@@ -134,12 +140,18 @@ struct StageLayer {
     uint8_t* wdown = nullptr;  // [D][rowbytes(FF)]
     uint16_t* kc = nullptr;    // fp16 [Hkv][max_len][128]
     uint16_t* vc = nullptr;
+    // mixture-of-experts layers
+    float* router = nullptr;   // fp32 [D][E]
+    uint8_t* egate = nullptr;  // [E][F][rowbytes(D)]
+    uint8_t* eup = nullptr;
+    uint8_t* edown = nullptr;  // [E][D][rowbytes(F)]
     bool loaded = false;
 };
 
 // host-side bytes of each tensor of a layer
 struct Sizes {
     size_t qkv_rows, wqkv, wo, wgu, wdown, cache;
+    size_t egu, edown;  // one expert's gate (= up) and down bytes
 };
 
 }  // namespace
@@ -160,6 +172,9 @@ struct glc_stage {
     float* act = nullptr;    // [FF]
     float* logits = nullptr; // [vocab]
     float* attn_work = nullptr;
+    float* xin = nullptr;    // [D] RMSNorm(x) * w_ffn (mixture of experts)
+    int* ids = nullptr;      // [k] routed experts
+    float* rw = nullptr;     // [k] their weights
     int* pos = nullptr;      // the position the next step uses
     int* token = nullptr;    // input token (first stage) / arg-max token (last stage)
     int* err = nullptr;
@@ -176,7 +191,82 @@ int check(glc_stage* h) {
 }
 
 glc::GemvJob job(const uint8_t* A, const float* x, float* y, int K, int N, int op, bool after_previous,
-               const float* norm_w = nullptr, float eps = 0.f, const uint8_t* B = nullptr) {
+               const float* norm_w = nullptr, float eps = 0.f, const uint8_t* B = nullptr);
+
+// A mixture-of-experts layer after its attention: x += Wo o (a chain of one
+// job), the router on RMSNorm(x) * w_ffn, the routed gate/up GEMV with
+// SwiGLU, the routed down GEMV combining into x in k order, then the next
+// layer's QKV projection (or the LM head after the last layer).
+int moe_layer_ffn(glc_stage* h, const StageLayer& L, int l, bool logits, cudaStream_t st) {
+    const glc_stage_desc& d = h->d;
+    const int D = d.hidden_dim, F = d.expert_ffn_dim, E = d.num_experts, k = d.top_k;
+    const int Hq = d.n_heads, qrows = (Hq + 2 * d.n_kv_heads) * kHeadDim;
+    glc::GemvChainParams c{};
+    c.bar = h->bar;
+    c.err = h->err;
+    c.jobs[0] = job(L.wo, h->attn, h->x, Hq * kHeadDim, D, glc::kChainAdd, false);
+    c.njobs = 1;
+    CUDA_TRY(glc::gemv_chain_launch(c, h->num_sms, st));
+    glc::RouterParams rp{};
+    rp.x = h->x;
+    rp.Wr = L.router;
+    rp.T = 1;
+    rp.D = D;
+    rp.E = E;
+    rp.k = k;
+    rp.renorm = d.moe_renormalize;
+    rp.rmsnorm = 1;
+    rp.norm_w = L.ffn_norm;
+    rp.norm_eps = d.rms_eps;
+    rp.xin = h->xin;
+    rp.ids = h->ids;
+    rp.w = h->rw;
+    CUDA_TRY(glc::router_launch(rp, st));
+    glc::GemvParams gu{};  // act[j] = SiLU(Gate_ids[j] h) * (Up_ids[j] h)
+    gu.mode = glc::kGemvGateUp;
+    gu.K = D;
+    gu.rows = F;
+    gu.nseg = k;
+    gu.kslots = k;
+    gu.num_experts = E;
+    gu.A = L.egate;
+    gu.B = L.eup;
+    gu.expert_bytes = (long long)h->sz.egu;
+    gu.ids = h->ids;
+    gu.x = h->xin;
+    gu.y = h->act;
+    gu.err = h->err;
+    CUDA_TRY(glc::gemv_launch(gu, h->num_sms, st));
+    glc::GemvParams dn{};  // x = x + sum_j w_j Down_ids[j] act[j], in k order
+    dn.mode = glc::kGemvDownCombine;
+    dn.K = F;
+    dn.rows = D;
+    dn.nseg = 1;
+    dn.kslots = k;
+    dn.num_experts = E;
+    dn.A = L.edown;
+    dn.expert_bytes = (long long)h->sz.edown;
+    dn.ids = h->ids;
+    dn.cw = h->rw;
+    dn.x = h->act;
+    dn.y = h->x;
+    dn.accumulate = 1;
+    dn.err = h->err;
+    CUDA_TRY(glc::gemv_launch(dn, h->num_sms, st));
+    c.njobs = 0;
+    if (l + 1 < d.layer_count) {
+        const StageLayer& N = h->layers[l + 1];
+        c.jobs[c.njobs++] = job(N.wqkv, h->x, h->qkv, D, qrows, glc::kChainSet, false, N.attn_norm, d.rms_eps);
+    } else if (logits) {
+        c.jobs[c.njobs++] = job(h->lm_head, h->x, h->logits, D, d.vocab, glc::kChainSet, false, h->final_norm,
+                                d.rms_eps);
+    }
+    if (c.njobs) CUDA_TRY(glc::gemv_chain_launch(c, h->num_sms, st));
+    return GLC_OK;
+}
+
+glc::GemvJob job(const uint8_t* A, const float* x, float* y, int K, int N, int op, bool after_previous,
+               const float* norm_w, float eps, const uint8_t* B) {
     glc::GemvJob j{};
     j.A = A;
     j.B = B;
@@ -233,6 +323,11 @@ int stage_step(glc_stage* h, bool embed, bool logits, cudaStream_t st) {
         ap.bk = L.bqkv + (size_t)Hq * kHeadDim;
         ap.bv = L.bqkv + (size_t)(Hq + Hkv) * kHeadDim;
         CUDA_TRY(glc::attn_decode_launch(ap, st));
+        if (d.num_experts > 0) {
+            const int rc = moe_layer_ffn(h, L, l, logits, st);
+            if (rc) return rc;
+            continue;
+        }
         c.njobs = 0;
         c.jobs[c.njobs++] = job(L.wo, h->attn, h->x, Hq * kHeadDim, D, glc::kChainAdd, false);
         c.jobs[c.njobs++] = job(L.wgate, h->x, h->act, D, FF, glc::kChainGateUp, true, L.ffn_norm, d.rms_eps, L.wup);
@@ -257,10 +352,11 @@ void free_stage(glc_stage* h) {
     for (auto& L : h->layers) {
         cudaFree(L.attn_norm); cudaFree(L.wqkv); cudaFree(L.bqkv); cudaFree(L.wo); cudaFree(L.ffn_norm);
         cudaFree(L.wgate); cudaFree(L.wup); cudaFree(L.wdown); cudaFree(L.kc); cudaFree(L.vc);
+        cudaFree(L.router); cudaFree(L.egate); cudaFree(L.eup); cudaFree(L.edown);
     }
     cudaFree(h->embed); cudaFree(h->final_norm); cudaFree(h->lm_head);
     cudaFree(h->x); cudaFree(h->qkv); cudaFree(h->attn); cudaFree(h->act); cudaFree(h->logits);
-    cudaFree(h->attn_work); cudaFree(h->pos); cudaFree(h->token);
+    cudaFree(h->attn_work); cudaFree(h->xin); cudaFree(h->ids); cudaFree(h->rw); cudaFree(h->pos); cudaFree(h->token);
     cudaFree(h->err);
     cudaFree(h->bar);
     for (auto& g : h->graphs)
@@ -276,10 +372,17 @@ int glc_stage_create(const glc_stage_desc* desc, glc_stage** out) {
     if (!desc || !out) return fail(GLC_ERR_INVALID_ARG, "null argument");
     *out = nullptr;
     const glc_stage_desc& d = *desc;
-    if (d.hidden_dim <= 0 || d.ffn_dim <= 0 || d.n_heads <= 0 || d.n_kv_heads <= 0 || d.layer_count <= 0)
+    const bool moe = d.num_experts > 0;
+    if (d.hidden_dim <= 0 || (!moe && d.ffn_dim <= 0) || d.n_heads <= 0 || d.n_kv_heads <= 0 || d.layer_count <= 0)
         return fail(GLC_ERR_INVALID_ARG, "dimensions and layer count must be positive");
+    if (d.num_experts < 0 || (moe && (d.num_experts < 2 || d.num_experts > 8)))
+        return fail(GLC_ERR_UNSUPPORTED, "num_experts %d: 0 (dense) or 2..8", d.num_experts);
+    if (moe && (d.top_k < 1 || d.top_k > d.num_experts))
+        return fail(GLC_ERR_INVALID_ARG, "top_k %d outside 1..%d", d.top_k, d.num_experts);
+    if (moe && (d.expert_ffn_dim <= 0 || d.expert_ffn_dim % 256))
+        return fail(GLC_ERR_UNSUPPORTED, "expert_ffn_dim %d: a positive multiple of 256", d.expert_ffn_dim);
     if (d.head_dim != kHeadDim) return fail(GLC_ERR_UNSUPPORTED, "head_dim %d: 128 supported", d.head_dim);
-    if (d.hidden_dim % 256 || d.ffn_dim % 256 || (d.n_heads * kHeadDim) % 256)
+    if (d.hidden_dim % 256 || (!moe && d.ffn_dim % 256) || (d.n_heads * kHeadDim) % 256)
         return fail(GLC_ERR_UNSUPPORTED, "Q4_K needs hidden, ffn and head widths that are multiples of 256");
     if (d.n_heads % d.n_kv_heads || d.n_heads / d.n_kv_heads > glc::kAttnMaxGroup)
         return fail(GLC_ERR_UNSUPPORTED, "at most %d query heads per KV head", glc::kAttnMaxGroup);
@@ -292,13 +395,16 @@ int glc_stage_create(const glc_stage_desc* desc, glc_stage** out) {
     glc_stage* h = new glc_stage();
     h->d = d;
     h->num_sms = prop.multiProcessorCount;
-    const int D = d.hidden_dim, FF = d.ffn_dim, Hq = d.n_heads, Hkv = d.n_kv_heads;
+    const int D = d.hidden_dim, FF = moe ? 0 : d.ffn_dim, Hq = d.n_heads, Hkv = d.n_kv_heads;
+    const int F = moe ? d.expert_ffn_dim : 0, E = moe ? d.num_experts : 0;
     h->sz.qkv_rows = (size_t)(Hq + 2 * Hkv) * kHeadDim;
     h->sz.wqkv = h->sz.qkv_rows * rowbytes(D);
     h->sz.wo = (size_t)D * rowbytes(Hq * kHeadDim);
     h->sz.wgu = (size_t)FF * rowbytes(D);
     h->sz.wdown = (size_t)D * rowbytes(FF);
     h->sz.cache = (size_t)Hkv * d.max_len * kHeadDim * sizeof(uint16_t);
+    h->sz.egu = (size_t)F * rowbytes(D);
+    h->sz.edown = (size_t)D * rowbytes(F);
     h->layers.resize(d.layer_count);
     auto bad = [&](const char* what) {
         free_stage(h);
@@ -314,9 +420,16 @@ int glc_stage_create(const glc_stage_desc* desc, glc_stage** out) {
         SALLOC(L.bqkv, sizeof(float) * h->sz.qkv_rows);
         SALLOC(L.wo, h->sz.wo);
         SALLOC(L.ffn_norm, sizeof(float) * D);
-        SALLOC(L.wgate, h->sz.wgu);
-        SALLOC(L.wup, h->sz.wgu);
-        SALLOC(L.wdown, h->sz.wdown);
+        if (moe) {
+            SALLOC(L.router, sizeof(float) * D * E);
+            SALLOC(L.egate, h->sz.egu * E);
+            SALLOC(L.eup, h->sz.egu * E);
+            SALLOC(L.edown, h->sz.edown * E);
+        } else {
+            SALLOC(L.wgate, h->sz.wgu);
+            SALLOC(L.wup, h->sz.wgu);
+            SALLOC(L.wdown, h->sz.wdown);
+        }
         SALLOC(L.kc, h->sz.cache);
         SALLOC(L.vc, h->sz.cache);
         cudaMemset(L.kc, 0, h->sz.cache);
@@ -331,7 +444,12 @@ int glc_stage_create(const glc_stage_desc* desc, glc_stage** out) {
     SALLOC(h->x, sizeof(float) * D);
     SALLOC(h->qkv, sizeof(float) * h->sz.qkv_rows);
     SALLOC(h->attn, sizeof(float) * Hq * kHeadDim);
-    SALLOC(h->act, sizeof(float) * FF);
+    SALLOC(h->act, sizeof(float) * std::max(FF, d.top_k * F));
+    if (moe) {
+        SALLOC(h->xin, sizeof(float) * D);
+        SALLOC(h->ids, sizeof(int) * d.top_k);
+        SALLOC(h->rw, sizeof(float) * d.top_k);
+    }
     SALLOC(h->attn_work, glc::attn_workspace_bytes(Hq, Hkv, d.max_len));
     SALLOC(h->pos, sizeof(int));
     SALLOC(h->token, sizeof(int));
@@ -356,15 +474,12 @@ int glc_stage_destroy(glc_stage* h) {
     return GLC_OK;
 }
 
-int glc_stage_load_layer(glc_stage* h, int32_t layer, const glc_dense_layer_weights* w) {
-    int rc = check(h);
-    if (rc) return rc;
-    if (!w || !w->attn_norm || !w->wq || !w->wk || !w->wv || !w->wo || !w->ffn_norm || !w->w_gate || !w->w_up ||
-        !w->w_down)
-        return fail(GLC_ERR_INVALID_ARG, "null weight pointer");
-    if (layer < 0 || layer >= h->d.layer_count) return fail(GLC_ERR_INVALID_ARG, "layer %d out of range", layer);
-    CUDA_TRY(cudaSetDevice(h->d.device));
-    StageLayer& L = h->layers[layer];
+}  // extern "C"
+
+namespace {
+
+// The attention weights and norms of w into layer L (biases NULL = zero).
+int load_attention(glc_stage* h, StageLayer& L, const glc_dense_layer_weights* w) {
     const int D = h->d.hidden_dim, Hq = h->d.n_heads, Hkv = h->d.n_kv_heads;
     const size_t rq = (size_t)Hq * kHeadDim * rowbytes(D), rk = (size_t)Hkv * kHeadDim * rowbytes(D);
     CUDA_TRY(cudaMemcpy(L.attn_norm, w->attn_norm, sizeof(float) * D, cudaMemcpyHostToDevice));
@@ -380,9 +495,48 @@ int glc_stage_load_layer(glc_stage* h, int32_t layer, const glc_dense_layer_weig
     else CUDA_TRY(cudaMemset(L.bqkv + nq + nk, 0, sizeof(float) * nk));
     CUDA_TRY(cudaMemcpy(L.wo, w->wo, h->sz.wo, cudaMemcpyHostToDevice));
     CUDA_TRY(cudaMemcpy(L.ffn_norm, w->ffn_norm, sizeof(float) * D, cudaMemcpyHostToDevice));
+    return GLC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int glc_stage_load_layer(glc_stage* h, int32_t layer, const glc_dense_layer_weights* w) {
+    int rc = check(h);
+    if (rc) return rc;
+    if (h->d.num_experts > 0) return fail(GLC_ERR_STATE, "a mixture-of-experts stage loads layers with glc_stage_load_moe_layer");
+    if (!w || !w->attn_norm || !w->wq || !w->wk || !w->wv || !w->wo || !w->ffn_norm || !w->w_gate || !w->w_up ||
+        !w->w_down)
+        return fail(GLC_ERR_INVALID_ARG, "null weight pointer");
+    if (layer < 0 || layer >= h->d.layer_count) return fail(GLC_ERR_INVALID_ARG, "layer %d out of range", layer);
+    CUDA_TRY(cudaSetDevice(h->d.device));
+    StageLayer& L = h->layers[layer];
+    if ((rc = load_attention(h, L, w))) return rc;
     CUDA_TRY(cudaMemcpy(L.wgate, w->w_gate, h->sz.wgu, cudaMemcpyHostToDevice));
     CUDA_TRY(cudaMemcpy(L.wup, w->w_up, h->sz.wgu, cudaMemcpyHostToDevice));
     CUDA_TRY(cudaMemcpy(L.wdown, w->w_down, h->sz.wdown, cudaMemcpyHostToDevice));
+    L.loaded = true;
+    return GLC_OK;
+}
+
+int glc_stage_load_moe_layer(glc_stage* h, int32_t layer, const glc_dense_layer_weights* w, const float* router,
+                             const void* gate_exps, const void* up_exps, const void* down_exps) {
+    int rc = check(h);
+    if (rc) return rc;
+    if (h->d.num_experts <= 0) return fail(GLC_ERR_STATE, "a dense stage loads layers with glc_stage_load_layer");
+    if (!w || !w->attn_norm || !w->wq || !w->wk || !w->wv || !w->wo || !w->ffn_norm || !router || !gate_exps ||
+        !up_exps || !down_exps)
+        return fail(GLC_ERR_INVALID_ARG, "null weight pointer");
+    if (layer < 0 || layer >= h->d.layer_count) return fail(GLC_ERR_INVALID_ARG, "layer %d out of range", layer);
+    CUDA_TRY(cudaSetDevice(h->d.device));
+    StageLayer& L = h->layers[layer];
+    if ((rc = load_attention(h, L, w))) return rc;
+    const int E = h->d.num_experts;
+    CUDA_TRY(cudaMemcpy(L.router, router, sizeof(float) * h->d.hidden_dim * E, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(L.egate, gate_exps, h->sz.egu * E, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(L.eup, up_exps, h->sz.egu * E, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(L.edown, down_exps, h->sz.edown * E, cudaMemcpyHostToDevice));
     L.loaded = true;
     return GLC_OK;
 }
@@ -418,7 +572,7 @@ int glc_stage_synth_layer(glc_stage* h, int32_t layer, uint64_t seed) {
     const int D = h->d.hidden_dim, FF = h->d.ffn_dim;
     const uint64_t base = 200000ull + 16ull * (uint64_t)(h->d.layer_begin + layer);
     const int nt = 16;
-    std::vector<uint8_t> buf(std::max({h->sz.wqkv, h->sz.wo, h->sz.wgu, h->sz.wdown}));
+    std::vector<uint8_t> buf(std::max({h->sz.wqkv, h->sz.wo, h->sz.wgu, h->sz.wdown}));  // dense matrices
     const size_t rq = (size_t)h->d.n_heads * kHeadDim, rk = (size_t)h->d.n_kv_heads * kHeadDim;
     glc::synth_q4k(seed, base + 0, 0.001f, buf.data(), rq * rowbytes(D) / 144, nt);
     glc::synth_q4k(seed, base + 1, 0.001f, buf.data() + rq * rowbytes(D), rk * rowbytes(D) / 144, nt);
@@ -426,19 +580,40 @@ int glc_stage_synth_layer(glc_stage* h, int32_t layer, uint64_t seed) {
     CUDA_TRY(cudaMemcpy(L.wqkv, buf.data(), h->sz.wqkv, cudaMemcpyHostToDevice));
     glc::synth_q4k(seed, base + 3, 0.001f, buf.data(), h->sz.wo / 144, nt);
     CUDA_TRY(cudaMemcpy(L.wo, buf.data(), h->sz.wo, cudaMemcpyHostToDevice));
-    glc::synth_q4k(seed, base + 4, 0.001f, buf.data(), h->sz.wgu / 144, nt);
-    CUDA_TRY(cudaMemcpy(L.wgate, buf.data(), h->sz.wgu, cudaMemcpyHostToDevice));
-    glc::synth_q4k(seed, base + 5, 0.001f, buf.data(), h->sz.wgu / 144, nt);
-    CUDA_TRY(cudaMemcpy(L.wup, buf.data(), h->sz.wgu, cudaMemcpyHostToDevice));
-    glc::synth_q4k(seed, base + 6, 0.001f, buf.data(), h->sz.wdown / 144, nt);
-    CUDA_TRY(cudaMemcpy(L.wdown, buf.data(), h->sz.wdown, cudaMemcpyHostToDevice));
-    std::vector<float> v(std::max((size_t)D, h->sz.qkv_rows));
+    std::vector<float> v(std::max({(size_t)D, h->sz.qkv_rows, (size_t)D * std::max(h->d.num_experts, 1)}));
     glc::synth_normal(seed, base + 7, 0.02f, v.data(), D, 1);
     for (int i = 0; i < D; ++i) v[i] = 1.0f + v[i];
     CUDA_TRY(cudaMemcpy(L.attn_norm, v.data(), sizeof(float) * D, cudaMemcpyHostToDevice));
     glc::synth_normal(seed, base + 8, 0.02f, v.data(), D, 1);
     for (int i = 0; i < D; ++i) v[i] = 1.0f + v[i];
     CUDA_TRY(cudaMemcpy(L.ffn_norm, v.data(), sizeof(float) * D, cudaMemcpyHostToDevice));
+    if (h->d.num_experts > 0) {
+        // no q/k/v biases; the router N(0, 0.02) (tag base + 10); expert e's
+        // gate / up / down Q4_K (tags 1000000 + 64 global_layer + 3 e + m)
+        const int E = h->d.num_experts;
+        const uint64_t gl = (uint64_t)(h->d.layer_begin + layer);
+        CUDA_TRY(cudaMemset(L.bqkv, 0, sizeof(float) * h->sz.qkv_rows));
+        glc::synth_normal(seed, base + 10, 0.02f, v.data(), (size_t)D * E, 1);
+        CUDA_TRY(cudaMemcpy(L.router, v.data(), sizeof(float) * D * E, cudaMemcpyHostToDevice));
+        std::vector<uint8_t> eb(std::max(h->sz.egu, h->sz.edown));
+        for (int e = 0; e < E; ++e) {
+            const uint64_t t = 1000000ull + 64ull * gl + 3ull * (uint64_t)e;
+            glc::synth_q4k(seed, t + 0, 0.001f, eb.data(), h->sz.egu / 144, nt);
+            CUDA_TRY(cudaMemcpy(L.egate + (size_t)e * h->sz.egu, eb.data(), h->sz.egu, cudaMemcpyHostToDevice));
+            glc::synth_q4k(seed, t + 1, 0.001f, eb.data(), h->sz.egu / 144, nt);
+            CUDA_TRY(cudaMemcpy(L.eup + (size_t)e * h->sz.egu, eb.data(), h->sz.egu, cudaMemcpyHostToDevice));
+            glc::synth_q4k(seed, t + 2, 0.001f, eb.data(), h->sz.edown / 144, nt);
+            CUDA_TRY(cudaMemcpy(L.edown + (size_t)e * h->sz.edown, eb.data(), h->sz.edown, cudaMemcpyHostToDevice));
+        }
+        L.loaded = true;
+        return GLC_OK;
+    }
+    glc::synth_q4k(seed, base + 4, 0.001f, buf.data(), h->sz.wgu / 144, nt);
+    CUDA_TRY(cudaMemcpy(L.wgate, buf.data(), h->sz.wgu, cudaMemcpyHostToDevice));
+    glc::synth_q4k(seed, base + 5, 0.001f, buf.data(), h->sz.wgu / 144, nt);
+    CUDA_TRY(cudaMemcpy(L.wup, buf.data(), h->sz.wgu, cudaMemcpyHostToDevice));
+    glc::synth_q4k(seed, base + 6, 0.001f, buf.data(), h->sz.wdown / 144, nt);
+    CUDA_TRY(cudaMemcpy(L.wdown, buf.data(), h->sz.wdown, cudaMemcpyHostToDevice));
     glc::synth_normal(seed, base + 9, 0.02f, v.data(), h->sz.qkv_rows, 1);
     CUDA_TRY(cudaMemcpy(L.bqkv, v.data(), sizeof(float) * h->sz.qkv_rows, cudaMemcpyHostToDevice));
     (void)FF;

@@ -390,6 +390,14 @@ typedef struct glc_stage_desc {
     int32_t has_embedding; /* first stage: x = dequantised embedding row of the token */
     int32_t has_lm_head;   /* last stage: logits = LM_head * (RMSNorm(x) * final_norm) */
     int32_t device;
+    /* Mixture-of-experts feed-forward (Mixtral-style layers, no q/k/v biases)
+     * when num_experts > 0: h = RMSNorm(x) * w_ffn, fp32 router [D][E],
+     * softmax top-k (renormalised when moe_renormalize), x += sum_j p_j
+     * Down_j(SiLU(Gate_j h) * (Up_j h)); ffn_dim is then unused. */
+    int32_t num_experts;   /* 0 (dense) or 2..8 */
+    int32_t top_k;         /* 1..num_experts */
+    int32_t expert_ffn_dim;  /* F of each expert (multiple of 256) */
+    int32_t moe_renormalize;
 } glc_stage_desc;
 /* Host weights of one layer: norms fp32 [D]; wq Q4_K [n_heads*128][D], wk / wv
  * [n_kv_heads*128][D], wo [D][n_heads*128], w_gate / w_up [FF][D], w_down
@@ -412,11 +420,17 @@ int glc_stage_create(const glc_stage_desc* desc, glc_stage** out);
 int glc_stage_destroy(glc_stage* h);
 /* layer: index within the stage (0 .. layer_count - 1) */
 int glc_stage_load_layer(glc_stage* h, int32_t layer, const glc_dense_layer_weights* w);
+/* A mixture-of-experts layer: the attention weights and norms of w (its
+ * biases and feed-forward matrices are ignored), the fp32 router [D][E] and
+ * the experts' Q4_K gate / up [E][F][D] and down [E][D][F] (GGUF ffn_*_exps). */
+int glc_stage_load_moe_layer(glc_stage* h, int32_t layer, const glc_dense_layer_weights* w, const float* router,
+                             const void* gate_exps, const void* up_exps, const void* down_exps);
 /* embedding Q4_K [vocab][D] (first stage), final_norm fp32 [D] and lm_head Q4_K
  * [vocab][D] (last stage); the others may be NULL. */
 int glc_stage_load_io(glc_stage* h, const void* embedding, const float* final_norm, const void* lm_head);
 /* The documented seeded synthetic weights (Q4_K fields as glc_moe_synth_layer
- * with sigma_d 0.001; norms 1 + N(0, 0.02); biases N(0, 0.02)). */
+ * with sigma_d 0.001; norms 1 + N(0, 0.02); biases N(0, 0.02); in a
+ * mixture-of-experts stage no biases, the router N(0, 0.02) and the experts). */
 int glc_stage_synth_layer(glc_stage* h, int32_t layer, uint64_t seed);
 int glc_stage_synth_io(glc_stage* h, uint64_t seed);
 /* ResetKvCache (IClusterStageModel.cs:35): clears the caches (synchronous). */
