@@ -144,6 +144,7 @@ _SIGNATURES = {
     "glc_stage_reset": (C.c_int, [vp]),
     "glc_stage_forward_dev": (C.c_int, [vp, i32, vp, vp, vp, vp, vp, vp]),
     "glc_stage_poll_error": (C.c_int, [vp]),
+    "glc_stage_read_kv_cache": (C.c_int, [vp, i32, i32, vp, vp]),
 }
 GLC_COMM_ID_BYTES = 128
 

@@ -567,6 +567,14 @@ class DenseStage:
     def poll_error(self) -> None:
         check(lib().glc_stage_poll_error(self._handle()))
 
+    def read_kv_cache(self, layer: int, rows: int):
+        """Rows [0, rows) of a layer's fp16 K and V caches, each [n_kv_heads][rows][128]."""
+        hkv = self.desc.n_kv_heads
+        k = np.empty((hkv, rows, 128), np.float16)
+        v = np.empty((hkv, rows, 128), np.float16)
+        check(lib().glc_stage_read_kv_cache(self._handle(), layer, rows, k.ctypes.data, v.ctypes.data))
+        return k, v
+
     def dispose(self) -> None:
         if self._h is not None:
             lib().glc_stage_destroy(self._h)

@@ -704,6 +704,24 @@ int glc_stage_forward_dev(glc_stage* h, int32_t pos, const int32_t* token, const
     return GLC_OK;
 }
 
+int glc_stage_read_kv_cache(glc_stage* h, int32_t layer, int32_t rows, void* k_out, void* v_out) {
+    int rc = check(h);
+    if (rc) return rc;
+    if (!k_out || !v_out) return fail(GLC_ERR_INVALID_ARG, "null pointer");
+    if (layer < 0 || layer >= h->d.layer_count) return fail(GLC_ERR_INVALID_ARG, "layer %d out of range", layer);
+    if (rows < 0 || rows > h->d.max_len) return fail(GLC_ERR_INVALID_ARG, "rows %d outside 0..%d", rows, h->d.max_len);
+    if (rows == 0) return GLC_OK;
+    CUDA_TRY(cudaSetDevice(h->d.device));
+    CUDA_TRY(cudaStreamSynchronize(h->stream));
+    const size_t rowb = (size_t)kHeadDim * sizeof(uint16_t);
+    const StageLayer& L = h->layers[layer];
+    CUDA_TRY(cudaMemcpy2D(k_out, rows * rowb, L.kc, (size_t)h->d.max_len * rowb, rows * rowb, h->d.n_kv_heads,
+                          cudaMemcpyDeviceToHost));
+    CUDA_TRY(cudaMemcpy2D(v_out, rows * rowb, L.vc, (size_t)h->d.max_len * rowb, rows * rowb, h->d.n_kv_heads,
+                          cudaMemcpyDeviceToHost));
+    return GLC_OK;
+}
+
 int glc_stage_poll_error(glc_stage* h) {
     int rc = check(h);
     if (rc) return rc;

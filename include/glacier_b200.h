@@ -447,6 +447,10 @@ int glc_stage_forward_dev(glc_stage* h, int32_t pos, const int32_t* token, const
                           float* logits, int32_t* token_out, void* stream);
 /* Reads and clears the stage's device error word. */
 int glc_stage_poll_error(glc_stage* h);
+/* Copies rows [0, rows) of layer `layer`'s fp16 K and V caches to host
+ * buffers k_out / v_out [n_kv_heads][rows][128] (synchronous; the rotated
+ * keys and the values as stored). */
+int glc_stage_read_kv_cache(glc_stage* h, int32_t layer, int32_t rows, void* k_out, void* v_out);
 
 #ifdef __cplusplus
 }

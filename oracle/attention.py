@@ -29,8 +29,10 @@ def rope(x: np.ndarray, pos: int, theta: float) -> np.ndarray:
     return np.concatenate([x1 * c - x2 * s, x2 * c + x1 * s], axis=-1)
 
 
-def attn_decode(q, k_new, v_new, k_cache, v_cache, pos: int, theta: float):
-    """Returns (out [n_heads][d] float64, k_cache', v_cache' (fp16 copies with row pos written))."""
+def attn_decode(q, k_new, v_new, k_cache, v_cache, pos: int, theta: float, stored_rows=None):
+    """Returns (out [n_heads][d] float64, k_cache', v_cache' (fp16 copies with row pos written)).
+    stored_rows: optional (k_row, v_row) [n_kv][d] fp16 to use as row pos instead of this
+    function's own rounding (to compare a kernel's later arithmetic on the rows it stored)."""
     q = np.asarray(q, np.float32)
     n_heads, d = q.shape
     n_kv = k_new.shape[0]
@@ -39,6 +41,8 @@ def attn_decode(q, k_new, v_new, k_cache, v_cache, pos: int, theta: float):
     vc = np.array(v_cache, np.float16, copy=True)
     kc[:, pos] = rope(np.asarray(k_new, np.float32), pos, theta).astype(np.float16)
     vc[:, pos] = np.asarray(v_new, np.float32).astype(np.float16)
+    if stored_rows is not None:
+        kc[:, pos], vc[:, pos] = stored_rows[0], stored_rows[1]
     qr = rope(q, pos, theta)
     out = np.empty((n_heads, d), np.float64)
     for h in range(n_heads):

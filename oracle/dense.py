@@ -111,8 +111,9 @@ def moe_ffn(L: dict, x, D: int, F: int, k: int, eps: float):
 
 
 def moe_layer_forward(L: dict, x, pos: int, kc, vc, D: int, F: int, k: int, Hq: int, Hkv: int, theta: float,
-                      eps: float):
-    """One mixture-of-experts layer at position pos; returns (x', kc', vc', ids)."""
+                      eps: float, stored_rows=None):
+    """One mixture-of-experts layer at position pos; returns (x', kc', vc', ids).
+    stored_rows: optional fp16 (k, v) rows for position pos (see attn_decode)."""
     hd = 128
     x = np.asarray(x, np.float64)
     h = rmsnorm_w(x, L["attn_norm"], eps)
@@ -120,7 +121,7 @@ def moe_layer_forward(L: dict, x, pos: int, kc, vc, D: int, F: int, k: int, Hq: 
     kk = gemv(L["wk"], h, D, Hkv * hd)
     v = gemv(L["wv"], h, D, Hkv * hd)
     att, kc, vc = attn_decode(q.astype(np.float32).reshape(Hq, hd), kk.astype(np.float32).reshape(Hkv, hd),
-                              v.astype(np.float32).reshape(Hkv, hd), kc, vc, pos, theta)
+                              v.astype(np.float32).reshape(Hkv, hd), kc, vc, pos, theta, stored_rows)
     x = x + gemv(L["wo"], att.reshape(-1), Hq * hd, D)
     x, ids = moe_ffn(L, x, D, F, k, eps)
     return x, kc, vc, ids
