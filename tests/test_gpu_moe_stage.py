@@ -69,12 +69,15 @@ def test_mixtral_8x22b_layer_shape(cuda, glc, oracle):
     at positions 0, 1, 64 and 4095.
 
     The stored fp16 K / V rows of each position are checked against the
-    oracle's within one fp16 ulp, and the layer output is then compared with
-    the oracle run on the rows the stage stored: with these synthetic weights
-    (Q4_K fields with a positive mean) the residual becomes a nearly constant
+    oracle's within one fp16 ulp plus 3e-4 of the row's rms: the GEMV stages
+    its input as int16 codes per 32-block (error about max/32767/sqrt(12)
+    per element, ~2e-5 of the rms for normal inputs), so the projection
+    feeding a row carries ~2.5e-5 of its norm, ~1e-4 at the largest element
+    of a 1024-value row.  The layer output is then compared with the oracle
+    run on the rows the stage stored: with these synthetic weights (Q4_K
+    fields with a positive mean) the residual becomes a nearly constant
     vector that SwiGLU amplifies quadratically, so a one-ulp fp16 rounding
-    difference of a value row (an fp32 vs float64 projection on either side of
-    a rounding boundary) alone moves the output by ~1e-3."""
+    difference of a value row alone moves the output by ~1e-3."""
     from oracle import dense as dn
     torch = cuda
     D, F, E, k, Hq, Hkv, max_len, seed = 6144, 16384, 8, 2, 48, 8, 4096, 67
@@ -93,8 +96,12 @@ def test_mixtral_8x22b_layer_shape(cuda, glc, oracle):
         gk, gv = st.read_kv_cache(0, pos + 1)
         _, ok_, ov_, _ = dn.moe_layer_forward(L, x, pos, kc, vc, D, F, k, Hq, Hkv, 1e6, 1e-5)
         for got_row, want_row in ((gk[:, pos], ok_[:, pos]), (gv[:, pos], ov_[:, pos])):
-            ulp = np.abs(got_row.view(np.int16).astype(np.int32) - want_row.view(np.int16).astype(np.int32))
-            assert ulp.max() <= 1, pos
+            # one fp16 ulp of each value plus 3e-4 of the row's rms (the int16-staged projection's error)
+            g64, w64 = got_row.astype(np.float64), want_row.astype(np.float64)
+            ulp = np.spacing(np.abs(want_row)).astype(np.float64)
+            rms = np.sqrt(np.mean(w64 * w64))
+            assert np.all(np.abs(g64 - w64) <= ulp + 3e-4 * rms), (pos, float(np.abs(g64 - w64).max()), rms)
+            assert rel_l2(g64, w64) <= 3e-4, pos
         want, kc, vc, _ = dn.moe_layer_forward(L, x, pos, kc, vc, D, F, k, Hq, Hkv, 1e6, 1e-5,
                                                stored_rows=(gk[:, pos], gv[:, pos]))
         r = rel_l2(x_out.cpu().numpy(), want)
