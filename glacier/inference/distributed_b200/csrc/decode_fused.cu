@@ -41,6 +41,12 @@
 #ifndef GLC_FUSED_PDL
 #define GLC_FUSED_PDL 0
 #endif
+// Largest router split (CTAs per cluster sharing the router rows): 2 or 1
+// (1 turns the split off).  Clusters of four cannot all be resident at one
+// CTA per SM on B200's 148 SMs, so a four-way split would never launch.
+#ifndef GLC_FUSED_RSPLIT
+#define GLC_FUSED_RSPLIT 2
+#endif
 
 namespace glc {
 
@@ -59,7 +65,8 @@ __device__ __forceinline__ int xs_index(int d, int U) {
 
 // RMSNorm scale of every token, threads 0..255, from the raw input xr [T][D]:
 // canonical sum of squares (256 strided fused partials, warp butterfly,
-// pairwise tree over the 8 warp sums), then 1 / sqrt(ss / D + 1e-5).
+// pairwise tree over the 8 warp sums), then 1 / sqrt(ss / D + eps).
+template <bool NW>
 __device__ void router_rms(const FusedDecodeParams& p, const float* xr, float* red, float* rms_s, int tid) {
     const int warp = tid >> 5, lane = tid & 31;
     const int D = p.D, T = p.T;
@@ -82,14 +89,126 @@ __device__ void router_rms(const FusedDecodeParams& p, const float* xr, float* r
             if (lane == 0) red[t * 8 + warp] = v;
         }
     named_bar_sync(2, kRouterWidth);
-    if (tid < T) rms_s[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tree8(red + tid * 8), (float)D), 1e-5f)));
+    const float eps = NW ? p.norm_eps : 1e-5f;
+    if (tid < T) rms_s[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tree8(red + tid * 8), (float)D), eps)));
     named_bar_sync(2, kRouterWidth);
 }
+
+// Normalised input element d of token t: (raw * rms) * w[d] (NW: p.norm_w
+// is set), as router.cu.
+template <bool NW>
+__device__ __forceinline__ float norm_in(const FusedDecodeParams& p, float raw, float rms, int d) {
+    float v = p.rmsnorm ? __fmul_rn(raw, rms) : raw;
+    if (NW) v = __fmul_rn(v, __ldg(p.norm_w + d));
+    return v;
+}
+
+// Thread-block cluster primitives (the router split).  At kernel start every
+// thread arrives (relaxed) and later waits once, so no CTA writes a peer's
+// shared memory before that peer has started; the second phase publishes the
+// partial logits.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void st_cluster_f32(const float* local, uint32_t rank, float v) {
+    uint32_t a;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(local)), "r"(rank));
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
+}
+
+// Router logits split over the R = 2 CTAs of a cluster, threads 0..255.
+// The canonical order of router.cu is 256 strided partials (partial j sums
+// d = j, j + 256, ... in order), a butterfly per warp and the pairwise tree
+// ((w0+w1)+(w2+w3))+((w4+w5)+(w6+w7)) over the 8 warp sums.  CTA r computes
+// the partials of canonical warps [4r, 4r+4) on threads 0..127, from the
+// router rows those partials read (NL = 128 rows out of every 256, staged
+// compactly: row 256i + r*NL + l at local row i*NL + l), reduces its four
+// warps' subtree and stores it, for every (token, expert), into slot r of lh
+// in both CTAs of the cluster; once the cluster barrier has passed, each CTA
+// completes the tree from the two subtree values (logits_from_halves).
+// Threads 128..255 write the normalised input of the d this CTA's partials
+// do not visit.
+template <bool NW>
+__device__ void router_logits_split(const FusedDecodeParams& p, const float* Wl, const float* xr, float* xs,
+                                    float* red, float* lh, const float* rms_s, int tid, int rank) {
+    constexpr int R = 2, NL = kRouterWidth / R;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int D = p.D, E = p.E, T = p.T, U = D >> 6;
+    if (tid >= NL) {
+        const int t2 = tid - NL, o = t2 < rank * NL ? t2 : t2 + NL;  // the d this CTA's partials skip
+        for (int t = 0; t < T; ++t) {
+            const float* xt = xr + (size_t)t * D;
+            float* xo = xs + (size_t)t * (D + 64);
+            const float rms = p.rmsnorm ? rms_s[t] : 1.0f;
+            for (int d = o; d < D; d += kRouterWidth) xo[xs_index(d, U)] = norm_in<NW>(p, xt[d], rms, d);
+        }
+        return;
+    }
+    const int h = (E == 8) ? ((lane >> 2) & 1) : 0;
+    const int j = rank * NL + tid;  // canonical partial of this thread
+    for (int t = 0; t < T; ++t) {
+        const float* xt = xr + (size_t)t * D;
+        float* xo = xs + (size_t)t * (D + 64);
+        const float rms = p.rmsnorm ? rms_s[t] : 1.0f;
+        for (int e0 = 0; e0 < E; e0 += 8) {
+            float acc[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+            if ((E & 3) == 0 && e0 + 8 <= E) {
+#pragma unroll 4
+                for (int i = 0, d = j; d < D; ++i, d += kRouterWidth) {
+                    const float xv = norm_in<NW>(p, xt[d], rms, d);
+                    if (e0 == 0) xo[xs_index(d, U)] = xv;
+                    const float4* wr = reinterpret_cast<const float4*>(Wl + (size_t)(i * NL + tid) * E + e0);
+                    const float4 f = wr[h], g = wr[h ^ 1];
+                    const float4 lo = h ? g : f, hi = h ? f : g;
+                    acc[0] = fmaf(xv, lo.x, acc[0]); acc[1] = fmaf(xv, lo.y, acc[1]);
+                    acc[2] = fmaf(xv, lo.z, acc[2]); acc[3] = fmaf(xv, lo.w, acc[3]);
+                    acc[4] = fmaf(xv, hi.x, acc[4]); acc[5] = fmaf(xv, hi.y, acc[5]);
+                    acc[6] = fmaf(xv, hi.z, acc[6]); acc[7] = fmaf(xv, hi.w, acc[7]);
+                }
+            } else {
+                for (int i = 0, d = j; d < D; ++i, d += kRouterWidth) {
+                    const float xv = norm_in<NW>(p, xt[d], rms, d);
+                    if (e0 == 0) xo[xs_index(d, U)] = xv;
+                    const float* wr = Wl + (size_t)(i * NL + tid) * E + e0;
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        if (e0 + e < E) acc[e] = fmaf(xv, wr[e], acc[e]);
+                }
+            }
+            const float v = warp_tree8(acc, lane);
+            if ((lane & 3) == 0) red[((lane >> 2) & 7) * 8 + warp] = v;
+            named_bar_sync(2, NL);
+            if (tid < 8 && e0 + tid < E) {
+                const float* s = red + tid * 8;
+                const float c = (s[0] + s[1]) + (s[2] + s[3]);  // this CTA's four canonical warps
+                float* dst = lh + (size_t)(t * E + e0 + tid) * R + rank;
+                for (int r = 0; r < R; ++r) st_cluster_f32(dst, (uint32_t)r, c);
+            }
+            named_bar_sync(2, NL);
+        }
+    }
+}
+
+// Logit (t, e) from the two subtree values of the split: the top of the
+// canonical pairwise tree.
+__device__ __forceinline__ float logits_from_halves(const float* c) { return c[0] + c[1]; }
 
 // Router logits of every token, threads 0..255, in the canonical order of
 // router.cu (256 strided fused partials over the normalised input, warp
 // butterfly, pairwise tree over the 8 warp sums), eight experts per pass; the
 // first pass also writes the normalised input to xs (xs_index layout).
+template <bool NW>
 __device__ void router_logits(const FusedDecodeParams& p, const float* Wr, const float* xr, float* xs,
                               float* red, float* logit, const float* rms_s, int tid) {
     const int warp = tid >> 5, lane = tid & 31;
@@ -109,7 +228,7 @@ __device__ void router_logits(const FusedDecodeParams& p, const float* Wr, const
 #pragma unroll 4
                 for (int d = tid; d < D; d += kRouterWidth) {
                     const float raw = xt[d];
-                    const float xv = p.rmsnorm ? __fmul_rn(raw, rms) : raw;
+                    const float xv = norm_in<NW>(p, raw, rms, d);
                     if (e0 == 0) xo[xs_index(d, U)] = xv;
                     const float4* wr = reinterpret_cast<const float4*>(Wr + (size_t)d * E + e0);
                     const float4 f = wr[h], g = wr[h ^ 1];
@@ -122,7 +241,7 @@ __device__ void router_logits(const FusedDecodeParams& p, const float* Wr, const
             } else {
                 for (int d = tid; d < D; d += kRouterWidth) {
                     const float raw = xt[d];
-                    const float xv = p.rmsnorm ? __fmul_rn(raw, rms) : raw;
+                    const float xv = norm_in<NW>(p, raw, rms, d);
                     if (e0 == 0) xo[xs_index(d, U)] = xv;
                     const float* wr = Wr + (size_t)d * E + e0;
 #pragma unroll
@@ -181,6 +300,12 @@ __device__ void topk_token_warp(const FusedDecodeParams& p, const float* l, int 
     if (lane < k) s_w[t * k + lane] = ex[s_ids[t * k + lane]] / den;
 }
 
+// SPLIT: the router split over a 2-CTA cluster (launched with clusters of
+// two); NW: weighted RMSNorm (p.norm_w set).  Separate instantiations keep
+// the unsplit, unweighted kernel's code exactly what it is without them
+// (measured: folding both in as runtime branches cost 1.6 us per launch at
+// the Mixtral-8x7B shape).
+template <bool SPLIT, bool NW>
 __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(const __grid_constant__ FusedDecodeParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int s_ok, s_okx, s_okw;
@@ -203,6 +328,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
     const int T = p.T, D = p.D, F = p.F, k = p.k, P = T * k;
     const uint64_t lim = p.wait_limit_ns > 0 ? (uint64_t)p.wait_limit_ns : kWaitLimitNs;
     const int slot = p.slot_bytes;
+    constexpr int R = SPLIT ? 2 : 1;  // router split over a cluster of R CTAs
+    float* lh = reinterpret_cast<float*>(smem + p.off_lh);
+    if (R > 1) cluster_arrive_relaxed();
 #if GLC_FUSED_PDL
     grid_dep_launch_dependents();
 #endif
@@ -223,22 +351,35 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
     // ---- 1. stage x and the router in the (still idle) stage ring, each with
     // its own barrier so the sum of squares runs while the router lands; then
     // RMSNorm, logits and top-k (every CTA)
-    const uint32_t wb = (uint32_t)D * p.E * 4u;  // a multiple of 1024
+    // this CTA's router rows: all of them, or under the split the NL = 256/R
+    // rows r*NL .. of every 256 (see router_logits_split), a multiple of 256 B
+    const int rank = R > 1 ? (int)cluster_rank() : 0;
+    const uint32_t wb = (uint32_t)D * p.E * 4u / (uint32_t)R;
     const float* xraw = reinterpret_cast<const float*>(smem + wb);
     if (tid == 0) {
         const uint32_t xb = (uint32_t)T * D * 4u;
+        auto stage_router = [&]() {
+            mbar_arrive_expect_tx(wbar, wb);
+            if (R == 1) {
+                bulk_g2s_nohint(smem, p.Wr, wb, wbar);
+            } else {
+                const int NL = kRouterWidth / R;
+                const uint32_t blk = (uint32_t)NL * p.E * 4u;
+                for (int i = 0; i < (D >> 8); ++i)
+                    bulk_g2s_nohint(smem + (size_t)i * blk, p.Wr + ((size_t)i * kRouterWidth + (size_t)rank * NL) * p.E,
+                                    blk, wbar);
+            }
+        };
 #if GLC_FUSED_PDL
         // the router weights never depend on the kernel before; the input may
-        mbar_arrive_expect_tx(wbar, wb);
-        bulk_g2s_nohint(smem, p.Wr, wb, wbar);
+        stage_router();
         grid_dep_wait();
         mbar_arrive_expect_tx(xbar, xb);
         bulk_g2s_nohint(smem + wb, p.x, xb, xbar);
 #else
         mbar_arrive_expect_tx(xbar, xb);
         bulk_g2s_nohint(smem + wb, p.x, xb, xbar);
-        mbar_arrive_expect_tx(wbar, wb);
-        bulk_g2s_nohint(smem, p.Wr, wb, wbar);
+        stage_router();
 #endif
     }
 #if GLC_FUSED_PDL
@@ -275,22 +416,43 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
     float resid0 = 0.f;
     if (p.resid && tid < NT && tid < q1 - q0) resid0 = __ldg(p.resid + (size_t)q0 + tid);
     if (tid < kRouterWidth) {
+        if (R > 1) cluster_wait();  // every CTA of the cluster has started (its shared memory may be written)
         // Each wait's outcome goes through its own flag and a barrier of the
         // 256 router threads, so all of them take the same branch.
         if (!mbar_wait_spin(xbar, 0, p.err, kDevTimeoutFull, lim)) s_okx = 0;
         named_bar_sync(2, kRouterWidth);
         const bool okx = s_okx != 0;
-        if (okx && p.rmsnorm) router_rms(p, xraw, red, rms_s, tid);
+        if (okx && p.rmsnorm) router_rms<NW>(p, xraw, red, rms_s, tid);
         if (okx && !mbar_wait_spin(wbar, 0, p.err, kDevTimeoutFull, lim)) s_okw = 0;
         named_bar_sync(2, kRouterWidth);
-        if (okx && s_okw != 0)
-            router_logits(p, reinterpret_cast<const float*>(smem), xraw, xs, red, logit, rms_s, tid);
-        else if (tid == 0)
+        if (okx && s_okw != 0) {
+            if (R > 1)
+                router_logits_split<NW>(p, reinterpret_cast<const float*>(smem), xraw, xs, red, lh, rms_s, tid, rank);
+            else
+                router_logits<NW>(p, reinterpret_cast<const float*>(smem), xraw, xs, red, logit, rms_s, tid);
+        } else if (tid == 0) {
             s_ok = 0;
+        }
+    } else if (R > 1) {
+        cluster_wait();
     }
-    __syncthreads();
+    // Under the split, the cluster barrier publishes every CTA's partial
+    // logits (and, as it includes all of this CTA's threads, orders the
+    // CTA's own shared-memory writes); after it no CTA touches a peer's
+    // shared memory, so any CTA may exit.
+    if (R > 1)
+        cluster_sync_all();
+    else
+        __syncthreads();
     const bool staged = s_ok != 0;
-    if (staged && warp < T) topk_token_warp(p, logit + warp * p.E, warp, s_ids, s_w, red + warp * 64, lane);
+    if (staged && warp < T) {
+        if (R > 1) {
+            for (int e = lane; e < p.E; e += 32)
+                logit[warp * p.E + e] = logits_from_halves(lh + (size_t)(warp * p.E + e) * R);
+            __syncwarp();
+        }
+        topk_token_warp(p, logit + warp * p.E, warp, s_ids, s_w, red + warp * 64, lane);
+    }
     __syncthreads();
     if (!staged) {  // uniform: every thread read the same s_ok
         if (tid == 0) {  // the staging copies land (bounded) before the CTA exits
@@ -486,6 +648,38 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
 
 size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
 
+// Whether grid / R clusters of R CTAs (kernel fn, smem bytes each) can all
+// be resident at once; cached per device and shared-memory size.
+bool clusters_fit(const void* fn, int dev, int R, size_t smem, int grid) {
+    struct Entry {
+        size_t smem;
+        int clusters;
+    };
+    static Entry cache[kMaxDevices] = {};  // R = 2
+    Entry& c = cache[dev];
+    if (c.smem != smem) {
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(grid);
+        cfg.blockDim = dim3(kFusedThreads);
+        cfg.dynamicSmemBytes = smem;
+        cudaLaunchAttribute a[1];
+        a[0].id = cudaLaunchAttributeClusterDimension;
+        a[0].val.clusterDim.x = (unsigned)R;
+        a[0].val.clusterDim.y = 1;
+        a[0].val.clusterDim.z = 1;
+        cfg.attrs = a;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess) {
+            (void)cudaGetLastError();
+            n = 0;
+        }
+        c.smem = smem;
+        c.clusters = n;
+    }
+    return (long long)c.clusters * R >= grid;
+}
+
 }  // namespace
 
 int fused_decode_configure(FusedDecodeParams& p, int num_sms, size_t smem_limit, size_t* smem_bytes, int* grid) {
@@ -518,6 +712,9 @@ int fused_decode_configure(FusedDecodeParams& p, int num_sms, size_t smem_limit,
     const size_t o_rms = o;   o = align16(o + (size_t)T * 4);
     const size_t o_ids = o;   o = align16(o + (size_t)P * 4);
     const size_t o_w = o;     o = align16(o + (size_t)P * 4);
+    const int R = p.rsplit > 1 ? p.rsplit : 1;
+    if (R != 1 && R != 2) return -1;
+    const size_t o_lh = o;    o = align16(o + (R > 1 ? (size_t)T * E * R * 4 : 0));
     const size_t o_bars = o;
     const size_t fixed = o + (2 * GLC_FUSED_MAX_STAGES + 3) * 8;
     if (fixed >= smem_limit) return -1;
@@ -525,8 +722,9 @@ int fused_decode_configure(FusedDecodeParams& p, int num_sms, size_t smem_limit,
     if (S > GLC_FUSED_MAX_STAGES) S = GLC_FUSED_MAX_STAGES;
     if (S < 2) return -1;
     const size_t ring = (size_t)S * slot;
-    if ((size_t)D * E * 4 + (size_t)T * D * 4 > ring) return -1;  // router and raw input are staged in the ring
-    if ((size_t)T * D * 4 + (size_t)D * E * 4 >= (1u << 20)) return -1;  // one mbarrier transaction
+    const size_t wr_bytes = (size_t)D * E * 4 / R;  // this CTA's router rows
+    if (wr_bytes + (size_t)T * D * 4 > ring) return -1;  // router rows and raw input are staged in the ring
+    if ((size_t)T * D * 4 >= (1u << 20) || wr_bytes >= (1u << 20)) return -1;  // one mbarrier transaction each
     p.gu_nsegw = gu_nsegw; p.gu_G = gu_G; p.gu_R = gu_R;
     p.dn_nsegw = dn_nsegw; p.dn_G = dn_G; p.dn_R = dn_R; p.dn_split = dn_split;
     p.stages = S;
@@ -539,6 +737,8 @@ int fused_decode_configure(FusedDecodeParams& p, int num_sms, size_t smem_limit,
     p.off_rms = (int)(ring + o_rms);
     p.off_ids = (int)(ring + o_ids);
     p.off_w = (int)(ring + o_w);
+    p.off_lh = (int)(ring + o_lh);
+    p.rsplit = R;
     p.off_bars = (int)(ring + o_bars);
     *smem_bytes = ring + o_bars + (2 * (size_t)S + 3) * 8;
     *grid = g;
@@ -549,6 +749,10 @@ cudaError_t fused_decode_launch(const FusedDecodeParams& p0, int num_sms, cudaSt
     // a shared expert, or a router too large to stage: the wide kernel
     if (p0.Fs > 0) return wide_decode_launch(p0, num_sms, stream);
     FusedDecodeParams p = p0;
+    // the kernel instantiations: [split][weighted norm]
+    using Kernel = void (*)(FusedDecodeParams);
+    static const Kernel kernels[2][2] = {{moe_decode_fused_kernel<false, false>, moe_decode_fused_kernel<false, true>},
+                                         {moe_decode_fused_kernel<true, false>, moe_decode_fused_kernel<true, true>}};
     static int smem_optin[kMaxDevices] = {0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -560,20 +764,35 @@ cudaError_t fused_decode_launch(const FusedDecodeParams& p0, int num_sms, cudaSt
         if (e != cudaSuccess) return e;
         // static __shared__ of the kernel (s_ok) comes out of the same budget
         v -= 1024;
-        e = cudaFuncSetAttribute(moe_decode_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, v);
-        if (e != cudaSuccess) return e;
+        for (int s = 0; s < 2; ++s)
+            for (int w = 0; w < 2; ++w) {
+                e = cudaFuncSetAttribute(kernels[s][w], cudaFuncAttributeMaxDynamicSharedMemorySize, v);
+                if (e != cudaSuccess) return e;
+            }
         smem_optin[dev] = v;
     }
+    const int nw = p.norm_w ? 1 : 0;
+    // The smallest router split R (1, then 2 when GLC_FUSED_RSPLIT allows)
+    // for which the layer fits and all grid / R clusters of R CTAs can be
+    // resident at once (the grid barrier needs every CTA resident).  No split
+    // when the router fits: measured on B200 at the Mixtral-8x7B shape, the
+    // split launch took 46.5-46.6 us per step against 45.3 us unsplit (same
+    // box); it is what lets a router of twice the rows (Mixtral-8x22B,
+    // D = 6144) run in one launch at all.
     size_t smem = 0;
-    int grid = 0;
-    if (fused_decode_configure(p, num_sms, (size_t)smem_optin[dev], &smem, &grid) != 0)
-        return wide_decode_launch(p0, num_sms, stream);  // cudaErrorNotSupported when that does not fit either
+    int grid = 0, R = 1;
+    for (; R <= GLC_FUSED_RSPLIT; R <<= 1) {
+        p.rsplit = R;
+        if (fused_decode_configure(p, num_sms, (size_t)smem_optin[dev], &smem, &grid) != 0) continue;
+        if (R == 1 || (grid % R == 0 && clusters_fit((const void*)kernels[1][nw], dev, R, smem, grid))) break;
+    }
+    if (R > GLC_FUSED_RSPLIT) return wide_decode_launch(p0, num_sms, stream);  // cudaErrorNotSupported when that does not fit either
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kFusedThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
 #if GLC_FUSED_PDL
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -581,9 +800,13 @@ cudaError_t fused_decode_launch(const FusedDecodeParams& p0, int num_sms, cudaSt
     attr[0].id = cudaLaunchAttributeCooperative;  // all CTAs co-resident: the grid barrier needs it
     attr[0].val.cooperative = 1;
 #endif
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned)R;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, moe_decode_fused_kernel, p);
+    cfg.numAttrs = R > 1 ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, kernels[R > 1 ? 1 : 0][nw], p);
 }
 
 }  // namespace glc

@@ -611,6 +611,7 @@ int wide_decode_configure(FusedDecodeParams& p, int num_sms, size_t smem_limit, 
     if (!p.gate || !p.up || !p.down || !p.act || !p.out || !p.ids || !p.w || !p.bar || !p.route_bar || !p.route_slots)
         return -1;
     if (Fs > 0 && (!p.sh_gate || !p.sh_up || !p.sh_down || !p.sh_gate_vec || !p.act_sh)) return -1;
+    if (p.norm_w) return -1;  // the weighted RMSNorm is the fused kernel's only
     // gate/up lanes: D/64 units per row, whole warps per row
     const int gu_nsegw = ((D >> 6) + 31) / 32;
     if (gu_nsegw > kWConsumerWarps) return -1;

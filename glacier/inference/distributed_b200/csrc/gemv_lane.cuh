@@ -150,11 +150,13 @@ __device__ __forceinline__ void stage_x_shared(const float* x, const float* w, i
     const float4* w4 = reinterpret_cast<const float4*>(w);
     float ss = 0.f;
     for (int f0 = 0; f0 < F4; f0 += 8 * nthr) {
-        float4 v[8];
+        // every load of the pass (input and norm weights) issued before any is used: one L2 round trip
+        float4 v[8], g[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
             const int f = f0 + k * nthr + tid;
             v[k] = f < F4 ? ldx4<SRC>(x4 + f) : make_float4(0.f, 0.f, 0.f, 0.f);
+            g[k] = (w && f < F4) ? __ldg(w4 + f) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
@@ -163,8 +165,8 @@ __device__ __forceinline__ void stage_x_shared(const float* x, const float* w, i
             float4 a = v[k];
             if (w) {
                 ss = fmaf(a.x, a.x, ss); ss = fmaf(a.y, a.y, ss); ss = fmaf(a.z, a.z, ss); ss = fmaf(a.w, a.w, ss);
-                const float4 g = f < F4 ? __ldg(w4 + f) : make_float4(0.f, 0.f, 0.f, 0.f);
-                a = make_float4(__fmul_rn(a.x, g.x), __fmul_rn(a.y, g.y), __fmul_rn(a.z, g.z), __fmul_rn(a.w, g.w));
+                a = make_float4(__fmul_rn(a.x, g[k].x), __fmul_rn(a.y, g[k].y), __fmul_rn(a.z, g[k].z),
+                                __fmul_rn(a.w, g[k].w));
             }
             float mx = fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w)));
             float sm = ((a.x + a.y) + a.z) + a.w;

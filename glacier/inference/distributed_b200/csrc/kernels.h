@@ -179,6 +179,10 @@ struct FusedDecodeParams {
     long long wait_limit_ns;
     int stall_cta;
     int T, D, F, E, k, renorm, rmsnorm;
+    // Weighted RMSNorm (rmsnorm set): the input is x * rms * norm_w[d] with
+    // eps = norm_eps, as router.cu's norm_w; nullptr = unweighted, eps 1e-5.
+    const float* norm_w;
+    float norm_eps;
     // Qwen2-MoE shared expert (Fs > 0): rows [Fs][D/256*144] gate/up,
     // [D][Fs/256*144] down, gate vector [D]; act_sh [T][Fs] scratch.  A layer
     // with a shared expert, or whose router does not fit the shared-memory
@@ -196,6 +200,10 @@ struct FusedDecodeParams {
     // filled by fused_decode_configure
     int gu_nsegw, gu_G, gu_R, dn_nsegw, dn_G, dn_R, dn_split, stages, slot_bytes;
     int off_xs, off_pgu, off_pdn, off_red, off_logit, off_rms, off_ids, off_w, off_bars;
+    // router split over a cluster of rsplit CTAs (1 or 2; set at launch):
+    // each stages 1/rsplit of the router rows; off_lh holds the rsplit partial
+    // logits of every (token, expert) gathered over distributed shared memory
+    int rsplit, off_lh;
     // wide kernel: down-phase lane layout (units of 64 weights per routed slot
     // / shared row, warps covering them, partial-sum slots per output row)
     int wide, dn_Ur, dn_Pr, dn_nwr, dn_Us, dn_nws, dn_row_parts;

@@ -23,7 +23,9 @@
 // softmax top-k), the routed experts' gate/up GEMV with SwiGLU and their down
 // GEMV with the k-ordered weighted combine and the residual in its epilogue
 // (GpuFirstExpertStageWorker.ProcessRoutedTopK, GpuFirstExpertStageWorker.cs:
-// 416-583), between the attention's O projection and the next layer's QKV.
+// 416-583), between the attention's O projection and the next layer's QKV:
+// one launch of the fused decode kernel (decode_fused.cu, its router split
+// over a thread-block cluster when the router rows do not fit one CTA).
 // Dense stages use two launches per layer: the attention, then ONE GEMV
 // chain (gemv_chain.cu) holding the O projection, gate/up, down and the next
 // layer's QKV projection (or the LM head), whose weights stream back to back
@@ -193,20 +195,57 @@ int check(glc_stage* h) {
 glc::GemvJob job(const uint8_t* A, const float* x, float* y, int K, int N, int op, bool after_previous,
                const float* norm_w = nullptr, float eps = 0.f, const uint8_t* B = nullptr);
 
+int next_layer_qkv(glc_stage* h, int l, bool logits, cudaStream_t st);
+
 // A mixture-of-experts layer after its attention: x += Wo o (a chain of one
-// job), the router on RMSNorm(x) * w_ffn, the routed gate/up GEMV with
-// SwiGLU, the routed down GEMV combining into x in k order, then the next
-// layer's QKV projection (or the LM head after the last layer).
+// job), then the feed-forward: the router on RMSNorm(x) * w_ffn, the routed
+// gate/up GEMVs with SwiGLU and the routed down GEMVs combining into x in k
+// order, as one fused launch (decode_fused.cu) or, when the layer does not
+// fit it, as three launches; then the next layer's QKV projection (or the LM
+// head after the last layer).
 int moe_layer_ffn(glc_stage* h, const StageLayer& L, int l, bool logits, cudaStream_t st) {
     const glc_stage_desc& d = h->d;
     const int D = d.hidden_dim, F = d.expert_ffn_dim, E = d.num_experts, k = d.top_k;
-    const int Hq = d.n_heads, qrows = (Hq + 2 * d.n_kv_heads) * kHeadDim;
+    const int Hq = d.n_heads;
     glc::GemvChainParams c{};
     c.bar = h->bar;
     c.err = h->err;
     c.jobs[0] = job(L.wo, h->attn, h->x, Hq * kHeadDim, D, glc::kChainAdd, false);
     c.njobs = 1;
     CUDA_TRY(glc::gemv_chain_launch(c, h->num_sms, st));
+    // The feed-forward in one launch (router on RMSNorm(x) * w_ffn, routed
+    // gate/up + SwiGLU, down + k-ordered combine into x); the residual is
+    // updated in place (every CTA stages x before the kernel's grid barrier
+    // and writes its own rows of x after it).
+    glc::FusedDecodeParams fp{};
+    fp.x = h->x;
+    fp.resid = h->x;
+    fp.out = h->x;
+    fp.Wr = L.router;
+    fp.gate = L.egate;
+    fp.up = L.eup;
+    fp.down = L.edown;
+    fp.gu_expert_bytes = (long long)h->sz.egu;
+    fp.dn_expert_bytes = (long long)h->sz.edown;
+    fp.act = h->act;
+    fp.ids = h->ids;
+    fp.w = h->rw;
+    fp.bar = h->bar;
+    fp.err = h->err;
+    fp.T = 1;
+    fp.D = D;
+    fp.F = F;
+    fp.E = E;
+    fp.k = k;
+    fp.renorm = d.moe_renormalize;
+    fp.rmsnorm = 1;
+    fp.norm_w = L.ffn_norm;
+    fp.norm_eps = d.rms_eps;
+    const cudaError_t fe = glc::fused_decode_launch(fp, h->num_sms, st);
+    if (fe == cudaSuccess) return next_layer_qkv(h, l, logits, st);
+    if (fe != cudaErrorNotSupported) return fail(GLC_ERR_CUDA, "fused feed-forward: %s", cudaGetErrorString(fe));
+    (void)cudaGetLastError();
+    // does not fit the fused kernel: router, gate/up and down as three launches
     glc::RouterParams rp{};
     rp.x = h->x;
     rp.Wr = L.router;
@@ -253,7 +292,16 @@ int moe_layer_ffn(glc_stage* h, const StageLayer& L, int l, bool logits, cudaStr
     dn.accumulate = 1;
     dn.err = h->err;
     CUDA_TRY(glc::gemv_launch(dn, h->num_sms, st));
-    c.njobs = 0;
+    return next_layer_qkv(h, l, logits, st);
+}
+
+// After a mixture-of-experts layer: the next layer's QKV (or the LM head) as a chain launch.
+int next_layer_qkv(glc_stage* h, int l, bool logits, cudaStream_t st) {
+    const glc_stage_desc& d = h->d;
+    const int D = d.hidden_dim, qrows = (d.n_heads + 2 * d.n_kv_heads) * kHeadDim;
+    glc::GemvChainParams c{};
+    c.bar = h->bar;
+    c.err = h->err;
     if (l + 1 < d.layer_count) {
         const StageLayer& N = h->layers[l + 1];
         c.jobs[c.njobs++] = job(N.wqkv, h->x, h->qkv, D, qrows, glc::kChainSet, false, N.attn_norm, d.rms_eps);

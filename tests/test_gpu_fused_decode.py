@@ -30,6 +30,8 @@ def _run(w, x, flags):
     (768, 512, 16, 4, 2, 2, True),     # K = 768: one lane segment per row
     (1024, 512, 32, 4, 3, 3, False),   # softmax over all experts, 32-expert router
     (256, 2560, 8, 1, 1, 0, True),     # top-1, K of the down rows = 2560
+    (6144, 512, 8, 2, 1, 3, True),     # 196 KB router: staged split over a 2-CTA cluster
+    (4096, 512, 16, 4, 2, 3, True),    # 256 KB router, two tokens: split over a 2-CTA cluster
 ])
 def test_fused_matches_separate_launches_bit_exact(cuda, glc, oracle, D, F, E, k, T, flags, renorm):
     L = make_layer(oracle, 7000 + D + T, D, F, E, k, renorm=renorm)
