@@ -3,8 +3,8 @@
     python -m glacier.inference.distributed_b200.cases <case> [--reps N]
 
 Each case builds its inputs on cuda:0 (weights by the library's seeded
-synthetic generator, the shapes of the Mixtral-8x7B, Qwen2-57B-A14B and
-Qwen2.5-14B layers), runs three warm-up calls and then ``reps`` calls of the
+synthetic generator, the shapes of the Mixtral-8x7B, Qwen2-57B-A14B,
+Qwen2.5-14B and Mixtral-8x22B layers), runs three warm-up calls and then ``reps`` calls of the
 one kernel family it names, and exits 0.  Inputs that a kernel streams are
 larger than the 126 MB L2 (rotating copies where one copy is smaller), so the
 DRAM counters of a capture describe HBM traffic.  A capture names the kernel
@@ -21,6 +21,7 @@ import numpy as np
 MIXTRAL = dict(D=4096, F=14336, E=8, k=2, seed=20241201)
 QWEN = dict(D=3584, F=2560, E=64, k=8, Fs=20480, seed=20241202)
 QWEN14B = dict(D=5120, FF=13824, Hq=40, Hkv=8, max_len=2048, seed=20241203)
+MIXTRAL22B = dict(D=6144, F=16384, E=8, k=2, Hq=48, Hkv=8, max_len=4096, seed=20241204)
 
 # case -> (kernels launched per call, one line of what it runs)
 CASES = {
@@ -39,6 +40,8 @@ CASES = {
     "decode_wide": ("moe_decode_wide_kernel x1", "Qwen2-57B-A14B layer decode with its shared expert, T=1 (one launch)"),
     "stage": ("per layer: attn_decode_kernel x1, q4k_gemv_chain_kernel x1",
               "Qwen2.5-14B dense stage of 2 layers, one token at position 2040"),
+    "moe_stage": ("per layer: attn_decode_kernel x1, q4k_gemv_chain_kernel x2, moe_decode_fused_kernel x1",
+                  "Mixtral-8x22B mixture-of-experts stage of 2 layers, one token at position 4090"),
 }
 
 
@@ -186,6 +189,23 @@ def case_stage(torch, glc, reps):
     st_.dispose()
 
 
+def case_moe_stage(torch, glc, reps):
+    q = MIXTRAL22B
+    st_ = glc.DenseStage(q["D"], 0, q["Hq"], q["Hkv"], 0, 2, q["max_len"], 1e6, 1e-5, num_experts=q["E"],
+                         top_k=q["k"], expert_ffn_dim=q["F"], moe_renormalize=True)
+    for l in range(2):
+        st_.synth_layer(l, q["seed"])
+    x = torch.randn(q["D"], device="cuda")
+    y = torch.empty(q["D"], device="cuda")
+    st, s = _stream(torch)
+    with torch.cuda.stream(st):
+        for i in range(3 + reps):
+            st_.forward_dev(4090 + i % 4, x_in_ptr=x.data_ptr(), x_out_ptr=y.data_ptr(), stream=s)
+    torch.cuda.synchronize()
+    st_.poll_error()
+    st_.dispose()
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("case", choices=sorted(CASES))
@@ -217,6 +237,8 @@ def main(argv=None) -> int:
         case_decode(torch, glc, c == "decode_wide", n)
     elif c == "stage":
         case_stage(torch, glc, n)
+    elif c == "moe_stage":
+        case_moe_stage(torch, glc, n)
     print(f"{c}: {CASES[c][0]} per call, {3 + n} calls: ok")
     return 0
 
