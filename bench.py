@@ -994,11 +994,12 @@ def measure_ep(torch, dist, glc, w, stream, args, world, rank, local):
         q = QWEN
         Dq, Fq, Eq, kq, Fsq = q["D"], q["F"], q["E"], q["k"], q["Fs"]
         eq = Eq // world
-        shard = glc.GpuExpertStageWorker(Dq, Fq, Eq, kq, shared_ffn_dim=Fsq, renormalize=False, device=local,
-                                         max_tokens=world * max(EP_QWEN_T), expert_begin=rank * eq,
-                                         expert_count=eq)
-        shard.synth_layer(0, q["seed"])
         for Tq in EP_QWEN_T:
+            # a handle sized for this batch: the exchange blocks hold the worst
+            # case of max_tokens / world tokens per rank
+            shard = glc.GpuExpertStageWorker(Dq, Fq, Eq, kq, shared_ffn_dim=Fsq, renormalize=False, device=local,
+                                             max_tokens=world * Tq, expert_begin=rank * eq, expert_count=eq)
+            shard.synth_layer(0, q["seed"])
             xs = [torch.from_numpy(rng.standard_normal((Tq, Dq)).astype(np.float32)).cuda() for _ in range(2)]
             stq = max(5, min(steps, 2000 // Tq))
             ms, phases = ep_time(torch, dist, shard, comm, xs, Tq, q["flags"] | GLC_FWD_BATCHED, stream, stq)
@@ -1007,7 +1008,7 @@ def measure_ep(torch, dist, glc, w, stream, args, world, rank, local):
                                         "tokens_per_s": world * Tq / (ms * 1e-3),
                                         "tokens_per_s_per_gpu": Tq / (ms * 1e-3), "steps": stq,
                                         "phases_ms": phases}
-        shard.dispose()
+            shard.dispose()
     comm.dispose()
     return res
 
