@@ -25,8 +25,10 @@ Workload (one "step" = one decode token through one MoE layer):
 
 Multi-GPU (torchrun): each rank runs its own decode stream on its own GPU
 (weak scaling, replicas of the layer: the headline value); the line also
-carries an expert-parallel leg (experts split over the ranks, NCCL
-all-to-all dispatch and combine around the grouped tensor-core experts).
+carries an expert-parallel leg (experts split over the ranks, dispatch and
+return written into the peers' memory over NVLink -- or, for comparison and
+where peer mapping is unavailable, exchanged with NCCL -- around the grouped
+tensor-core experts).
 """
 from __future__ import annotations
 
@@ -981,12 +983,22 @@ def measure_ep(torch, dist, glc, w, stream, args, world, rank, local):
     ok = torch.tensor([1 if exact else 0], device="cuda")
     if dist:
         dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    peer = comm.peer_exchange_active()
+    res["exchange"] = ("NVLink peer memory: the pack and repack kernels write each rank's blocks into the "
+                       "destination's CUDA IPC window, an epoch flag per source, only routed rows cross"
+                       if peer else res["exchange"])
     steps = max(20, min(args.steps // 10, 200))
     ms, phases = ep_time(torch, dist, shard, comm, xs, T, flags, stream, steps)
+    nccl_ms = None
+    if peer:  # the same step with the blocks through NCCL, for comparison
+        comm.set_peer_exchange(False)
+        nccl_ms, _ = ep_time(torch, dist, shard, comm, xs, T, flags, stream, steps)
+        comm.set_peer_exchange(True)
     shard.dispose()
     res["mixtral"] = {"workload": f"mixtral8x7b_moe_layer_decode_ep{world}", "experts_per_rank": epr,
                       "tokens_per_rank": T, "ms_per_step": ms, "tokens_per_s": world * T / (ms * 1e-3),
                       "tokens_per_s_per_gpu": T / (ms * 1e-3), "steps": steps, "phases_ms": phases,
+                      "nccl_exchange_ms_per_step": nccl_ms,
                       "parity": {"bit_exact_vs_single_gpu_all_ranks": bool(ok.item() == 1),
                                  "reference": "each rank's own single-GPU layer, batched path, same tokens"}}
     # ---- Qwen2-57B layer, 64 / world experts per rank + the shared expert

@@ -475,6 +475,18 @@ class Communicator:
             raise GlcError(-5, "communicator was destroyed")
         return self._h
 
+    def set_peer_exchange(self, enable: bool) -> None:
+        """Expert-parallel exchanges over NVLink peer memory (default) or
+        through NCCL (glc_comm_peer_exchange); every rank alike."""
+        check(lib().glc_comm_peer_exchange(self._handle(), 1 if enable else 0))
+
+    def peer_exchange_active(self) -> bool:
+        """Whether the expert-parallel exchanges go over peer memory (the
+        window mapped on every rank, the option on)."""
+        r = lib().glc_comm_peer_exchange(self._handle(), -1)
+        check(r if r < 0 else 0)
+        return r == 1
+
     def pp_send(self, peer: int, header: "FusedActivationHeader", x_ptr: int, stream=None) -> None:
         """Stage boundary: quantise x [T][D] (from the header) on the GPU and send
         the header and the payload to ``peer``."""

@@ -1040,15 +1040,10 @@ int glc_moe_ep_forward(glc_moe* h, glc_comm* c, int32_t layer, const float* x, i
     int32_t* ids = static_cast<int32_t*>(scratch(3, sizeof(int32_t) * cap));
     float* w = static_cast<float*>(scratch(4, sizeof(float) * cap));
     int32_t* ints = static_cast<int32_t*>(scratch(5, sizeof(int32_t) * (3 * (size_t)cap + 3 * (size_t)world + 2)));
-    uint8_t* send = static_cast<uint8_t*>(scratch(6, (size_t)world * bb));
-    uint8_t* recv = static_cast<uint8_t*>(scratch(7, (size_t)world * bb));
     float* rows = static_cast<float*>(scratch(8, (size_t)world * cap * row));
     float* y = static_cast<float*>(scratch(9, (size_t)world * cap * row));
-    float* y_send = static_cast<float*>(scratch(10, (size_t)world * cap * row));
-    float* y_recv = static_cast<float*>(scratch(11, (size_t)world * cap * row));
     float* y_back = static_cast<float*>(scratch(12, (size_t)cap * row));
-    if (!xin || !ids || !w || !ints || !send || !recv || !rows || !y || !y_send || !y_recv || !y_back)
-        return fail(GLC_ERR_OOM, "expert-parallel scratch");
+    if (!xin || !ids || !w || !ints || !rows || !y || !y_back) return fail(GLC_ERR_OOM, "expert-parallel scratch");
     int32_t* counts = ints;                 // [world] pairs to each rank
     int32_t* offsets = counts + world;      // [world + 1]
     int32_t* perm = offsets + world + 1;    // [cap]
@@ -1059,6 +1054,26 @@ int glc_moe_ep_forward(glc_moe* h, glc_comm* c, int32_t layer, const float* x, i
     pl.offsets = offsets;
     pl.perm = perm;
     pl.inv = inv;
+    // The exchange: over the peer window when every rank has mapped every
+    // other rank's (the blocks written straight into the destination's
+    // memory, an epoch flag per source, only routed rows crossing NVLink),
+    // else the same blocks through one grouped NCCL send / receive each way.
+    uint8_t* win = nullptr;
+    void* const* peers = nullptr;
+    const int wr = glc::comm_window(c, glc::ep_window_bytes(world, cap, D), st, &win, &peers);
+    if (wr != GLC_OK && wr != GLC_ERR_UNSUPPORTED) return wr;
+    const bool peer = wr == GLC_OK;
+    uint8_t *send = nullptr, *recv = nullptr;
+    float *y_send = nullptr, *y_recv = nullptr;
+    if (!peer) {
+        send = static_cast<uint8_t*>(scratch(6, (size_t)world * bb));
+        recv = static_cast<uint8_t*>(scratch(7, (size_t)world * bb));
+        y_send = static_cast<float*>(scratch(10, (size_t)world * cap * row));
+        y_recv = static_cast<float*>(scratch(11, (size_t)world * cap * row));
+        if (!send || !recv || !y_send || !y_recv) return fail(GLC_ERR_OOM, "expert-parallel exchange buffers");
+    }
+    const unsigned long long epoch = peer ? glc::comm_window_next_epoch(c) : 0;
+    const int par = (int)(epoch & 1);
     h->n_marks = 0;
     mark_phase(h, st);
     struct Lock {
@@ -1071,24 +1086,41 @@ int glc_moe_ep_forward(glc_moe* h, glc_comm* c, int32_t layer, const float* x, i
         if (rc) return rc;
     }
     mark_phase(h, st);  // route
-    CUDA_TRY(glc::ep_pack_launch(xin, ids, Tl, D, k, E, world, cap, h->ep_keys, pl, send, st));
+    if (peer)  // pack into every destination's window, then its dispatch flag
+        CUDA_TRY(glc::ep_pack_peer_launch(xin, ids, Tl, D, k, E, world, rank, cap, h->ep_keys, pl, peers, par, epoch,
+                                          win, st));
+    else
+        CUDA_TRY(glc::ep_pack_launch(xin, ids, Tl, D, k, E, world, cap, h->ep_keys, pl, send, st));
     mark_phase(h, st);  // dispatch into per-rank blocks
     std::vector<size_t> off(world), cnt(world, bb), off_y(world), cnt_y(world, (size_t)cap * row);
     for (int p = 0; p < world; ++p) {
         off[p] = (size_t)p * bb;
         off_y[p] = (size_t)p * cap * row;
     }
-    rc = glc::comm_alltoallv(c, send, off.data(), cnt.data(), recv, off.data(), cnt.data(), st);
-    if (rc) return rc;
+    if (peer) {
+        CUDA_TRY(glc::ep_wait_launch(win, world, 0, epoch, h->err, st));
+        recv = win + glc::ep_win_disp_off(par, world, cap, D);
+    } else {
+        rc = glc::comm_alltoallv(c, send, off.data(), cnt.data(), recv, off.data(), cnt.data(), st);
+        if (rc) return rc;
+    }
     mark_phase(h, st);  // exchange out
     CUDA_TRY(glc::ep_unpack_launch(recv, world, cap, D, h->d.expert_begin, El, rows, h->ids, src_off, st));
     // this rank's experts on every row received, the row count on the device
     rc = run_experts_grouped(h, L, rows, world * cap, 1, h->ids, h->ones, nullptr, y, st, false, src_off + world);
     if (rc) return rc;
-    CUDA_TRY(glc::ep_repack_launch(y, src_off, world, cap, D, y_send, st));
+    if (peer)  // each output row into its home rank's window, then the return flags
+        CUDA_TRY(glc::ep_repack_peer_launch(y, src_off, world, rank, cap, D, peers, par, epoch, win, st));
+    else
+        CUDA_TRY(glc::ep_repack_launch(y, src_off, world, cap, D, y_send, st));
     mark_phase(h, st);  // experts
-    rc = glc::comm_alltoallv(c, y_send, off_y.data(), cnt_y.data(), y_recv, off_y.data(), cnt_y.data(), st);
-    if (rc) return rc;
+    if (peer) {
+        CUDA_TRY(glc::ep_wait_launch(win, world, 1, epoch, h->err, st));
+        y_recv = reinterpret_cast<float*>(win + glc::ep_win_ret_off(par, world, cap, D));
+    } else {
+        rc = glc::comm_alltoallv(c, y_send, off_y.data(), cnt_y.data(), y_recv, off_y.data(), cnt_y.data(), st);
+        if (rc) return rc;
+    }
     mark_phase(h, st);  // exchange back
     if (P > 0) {
         CUDA_TRY(glc::ep_unblock_launch(y_recv, P, cap, D, h->ep_keys, pl, y_back, st));

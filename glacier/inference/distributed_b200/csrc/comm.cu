@@ -99,6 +99,19 @@ struct glc_comm {
     std::vector<size_t> scratch_bytes;
     std::vector<void*> retired;  // outgrown scratch, possibly still in use by queued work: freed at destroy
     int32_t* h_counts = nullptr;  // pinned [2 * nranks]: counts sent, counts received
+    // Peer window (comm_window): this rank's buffer, every rank's buffer
+    // mapped into this process (CUDA IPC over NVLink), epochs of the
+    // exchanges made through it.  state 0 = not set up, 1 = mapped,
+    // -1 = unavailable or turned off (exchanges go through NCCL).
+    uint8_t* win = nullptr;
+    size_t win_bytes = 0;
+    std::vector<void*> win_peer;        // [nranks] host table (own buffer at [rank])
+    void** d_win_peer = nullptr;        // device copy of the table
+    std::vector<void*> win_mapped;      // peers' mappings to close at destroy
+    std::vector<void*> win_retired;     // outgrown own buffers (peers may still hold mappings)
+    unsigned long long win_epoch = 0;
+    int win_state = 0;
+    bool win_enabled = true;
 };
 
 namespace glc {
@@ -158,9 +171,108 @@ int comm_alltoallv(glc_comm* c, const void* send, const size_t* soff, const size
     return GLC_OK;
 }
 
+// Peer window of at least `bytes` on every rank (collective: every rank calls
+// it with the same size, in the same order as its other exchanges).  The
+// buffer is cudaMalloc'd and zeroed, its CUDA IPC handle and size go to every
+// peer (a grouped send/receive of 128 bytes each way), each peer's buffer is
+// opened in this process (peer access over NVLink), and the ranks agree --
+// one int32 each way -- that every rank mapped every peer at the same size;
+// if any did not, no rank uses the window (GLC_ERR_UNSUPPORTED: the callers
+// exchange through NCCL instead).  A window that must grow is retired, not
+// freed: peers may still hold mappings of it and queued work may still use it.
+int comm_window(glc_comm* c, size_t bytes, cudaStream_t st, uint8_t** own, void* const** d_peers) {
+    if (!c->win_enabled || c->win_state < 0) return GLC_ERR_UNSUPPORTED;
+    if (c->win_state == 1 && c->win_bytes >= bytes) {
+        *own = c->win;
+        *d_peers = c->d_win_peer;
+        return GLC_OK;
+    }
+    const int W = c->nranks, me = c->rank;
+    if (c->win) c->win_retired.push_back(c->win);
+    c->win = nullptr;
+    c->win_state = 0;
+    bytes = (bytes + 4095) & ~size_t(4095);
+    if (cudaMalloc(&c->win, bytes) != cudaSuccess) return fail(GLC_ERR_OOM, "peer window");
+    CUDA_OK(cudaMemset(c->win, 0, bytes));  // flags start at epoch 0 (synchronous: before any peer can write)
+    struct Msg {
+        cudaIpcMemHandle_t h;
+        unsigned long long bytes;
+        uint8_t pad[128 - sizeof(cudaIpcMemHandle_t) - 8];
+    };
+    static_assert(sizeof(Msg) == 128, "window message");
+    Msg m{};
+    CUDA_OK(cudaIpcGetMemHandle(&m.h, c->win));
+    m.bytes = bytes;
+    uint8_t* dmsg = static_cast<uint8_t*>(comm_scratch(c, 30, (size_t)(W + 1) * sizeof(Msg) + 64 * (size_t)W * 2));
+    if (!dmsg) return fail(GLC_ERR_OOM, "window handles");
+    CUDA_OK(cudaMemcpyAsync(dmsg + (size_t)W * sizeof(Msg), &m, sizeof(Msg), cudaMemcpyHostToDevice, st));
+    const NcclApi& n = nccl();
+    NCCL_TRY(n.GroupStart(), "ncclGroupStart");
+    for (int p = 0; p < W; ++p) {
+        NCCL_TRY(n.Send(dmsg + (size_t)W * sizeof(Msg), sizeof(Msg), ncclUint8, p, c->comm, st), "ncclSend");
+        NCCL_TRY(n.Recv(dmsg + (size_t)p * sizeof(Msg), sizeof(Msg), ncclUint8, p, c->comm, st), "ncclRecv");
+    }
+    NCCL_TRY(n.GroupEnd(), "ncclGroupEnd");
+    std::vector<Msg> all(W);
+    CUDA_OK(cudaMemcpyAsync(all.data(), dmsg, (size_t)W * sizeof(Msg), cudaMemcpyDeviceToHost, st));
+    CUDA_OK(cudaStreamSynchronize(st));
+    std::vector<void*> peer(W, nullptr);
+    int ok = 1;
+    for (int p = 0; p < W; ++p) {
+        if (all[p].bytes != bytes) ok = 0;
+        if (p == me) {
+            peer[p] = c->win;
+            continue;
+        }
+        if (!ok) continue;
+        void* ptr = nullptr;
+        if (cudaIpcOpenMemHandle(&ptr, all[p].h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            (void)cudaGetLastError();
+            ok = 0;
+            continue;
+        }
+        peer[p] = ptr;
+        c->win_mapped.push_back(ptr);
+    }
+    // every rank's verdict to every rank
+    int32_t* dok = reinterpret_cast<int32_t*>(dmsg + (size_t)(W + 1) * sizeof(Msg));
+    std::vector<int32_t> mine(W, ok), theirs(W, 0);
+    CUDA_OK(cudaMemcpyAsync(dok, mine.data(), sizeof(int32_t) * W, cudaMemcpyHostToDevice, st));
+    int rc = comm_alltoall_i32(c, dok, dok + W, st);
+    if (rc) return rc;
+    CUDA_OK(cudaMemcpyAsync(theirs.data(), dok + W, sizeof(int32_t) * W, cudaMemcpyDeviceToHost, st));
+    CUDA_OK(cudaStreamSynchronize(st));
+    for (int p = 0; p < W; ++p) ok &= theirs[p] ? 1 : 0;
+    if (!ok) {
+        c->win_state = -1;
+        return GLC_ERR_UNSUPPORTED;
+    }
+    if (!c->d_win_peer && cudaMalloc(&c->d_win_peer, sizeof(void*) * 64) != cudaSuccess)
+        return fail(GLC_ERR_OOM, "peer table");
+    CUDA_OK(cudaMemcpy(c->d_win_peer, peer.data(), sizeof(void*) * W, cudaMemcpyHostToDevice));
+    c->win_peer = peer;
+    c->win_bytes = bytes;
+    c->win_state = 1;
+    *own = c->win;
+    *d_peers = c->d_win_peer;
+    return GLC_OK;
+}
+
+// Epoch of the next exchange through the peer window (1, 2, ...; every rank
+// makes the same exchanges in the same order, so the ranks agree on it).
+unsigned long long comm_window_next_epoch(glc_comm* c) { return ++c->win_epoch; }
+
 }  // namespace glc
 
 extern "C" {
+
+int glc_comm_peer_exchange(glc_comm* c, int32_t enable) {
+    if (!c) return fail(GLC_ERR_INVALID_ARG, "null communicator");
+    if (enable < 0) return (c->win_enabled && c->win_state == 1) ? 1 : 0;
+    c->win_enabled = enable != 0;
+    return GLC_OK;
+}
+
 
 int glc_comm_unique_id(uint8_t* id_out) {
     if (!id_out) return fail(GLC_ERR_INVALID_ARG, "null pointer");
@@ -206,6 +318,10 @@ int glc_comm_destroy(glc_comm* c) {
     if (c->stream) cudaStreamSynchronize(c->stream);
     if (c->comm) nccl().CommDestroy(c->comm);
     cudaDeviceSynchronize();  // work of other streams may still use the scratch
+    for (void* p : c->win_mapped) cudaIpcCloseMemHandle(p);
+    for (void* p : c->win_retired) cudaFree(p);
+    cudaFree(c->win);
+    cudaFree(c->d_win_peer);
     for (void* p : c->scratch) cudaFree(p);
     for (void* p : c->retired) cudaFree(p);
     cudaFree(c->d_hdr);

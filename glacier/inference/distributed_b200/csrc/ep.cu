@@ -145,6 +145,154 @@ __global__ void __launch_bounds__(256) ep_unblock_kernel(const float* __restrict
     for (int i = threadIdx.x; i < (D >> 2); i += 256) d4[i] = s4[i];
 }
 
+// ---------------------------------------------------------------------------
+// Exchange over a peer window (comm_window: every rank's buffer mapped in
+// every rank over NVLink).  Instead of packing blocks locally for a grouped
+// NCCL send, the pack kernel writes each block straight into its
+// destination's window, and the repack kernel writes each expert output row
+// straight into its home rank's window: only the pairs actually routed cross
+// NVLink.  Window layout (the same on every rank):
+//   [0, 1024)     flags: uint64 [2 phases][64 sources], the epoch of the
+//                 source's last completed write of that phase
+//   [1024, 1032)  two uint32 launch counters (this rank's own)
+//   disp(parity)  world blocks of ep_block_bytes(cap, D), by source rank
+//   ret(parity)   world x cap rows of D floats, by source rank and slot
+// The areas are double-buffered by the parity of the exchange's epoch: a rank
+// cannot start exchange n + 2 before every peer has finished exchange n + 1
+// (it needs their returns of n + 1), so a peer never writes an area its
+// owner is still reading.
+
+constexpr size_t kWinFlags = 0, kWinCtr = 1024, kWinData = 2048;
+
+size_t ep_win_disp_off(int parity, int world, int cap, int D) {
+    return kWinData + (size_t)parity * world * ep_block_bytes(cap, D);
+}
+size_t ep_win_ret_off(int parity, int world, int cap, int D) {
+    return kWinData + 2 * (size_t)world * ep_block_bytes(cap, D) + (size_t)parity * world * cap * D * 4;
+}
+size_t ep_window_bytes(int world, int cap, int D) { return ep_win_ret_off(2, world, cap, D); }
+
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Called by every CTA of a launch after its writes: each CTA's writes are
+// fenced at system scope before it counts itself done; the last one (which
+// also returns the counter to 0 for the next launch, ordered after this one
+// on the stream) fences again and publishes the epoch in flag[phase][me] of
+// every rank's window.
+__device__ void signal_when_done(uint8_t* own, void* const* peers, int world, int me, int phase,
+                                 unsigned long long epoch) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        unsigned* ctr = reinterpret_cast<unsigned*>(own + kWinCtr) + phase;
+        const unsigned prev = atomicAdd(ctr, 1u);
+        if (prev == gridDim.x * gridDim.y - 1) {
+            *ctr = 0u;
+            __threadfence_system();
+            for (int p = 0; p < world; ++p)
+                st_release_sys_u64(reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(peers[p]) + kWinFlags) +
+                                       phase * 64 + me,
+                                   epoch);
+        }
+    }
+}
+
+// ep_pack_kernel with the block for rank p written into rank p's window
+// (source slot me of its dispatch area), then the dispatch flags.
+__global__ void __launch_bounds__(256) ep_pack_peer_kernel(const float* __restrict__ xin, const int* __restrict__ ids,
+                                                           int P, int D, int k, int world, int me, int cap,
+                                                           const int* __restrict__ keys, DispatchPlan plan,
+                                                           void* const* __restrict__ peers, size_t disp_off,
+                                                           size_t bb, uint8_t* own, unsigned long long epoch) {
+    const int pos = blockIdx.x;
+    if (pos == 0 && threadIdx.x < world)
+        *reinterpret_cast<int*>(static_cast<uint8_t*>(peers[threadIdx.x]) + disp_off + (size_t)me * bb) =
+            P > 0 ? plan.counts[threadIdx.x] : 0;
+    if (pos < P) {
+        const int pair = plan.perm[pos];
+        const int p = keys[pair];
+        const int slot = pos - plan.offsets[p];
+        uint8_t* blk = static_cast<uint8_t*>(peers[p]) + disp_off + (size_t)me * bb;
+        const float4* s4 = reinterpret_cast<const float4*>(xin + (size_t)(pair / k) * D);
+        float4* d4 = reinterpret_cast<float4*>(blk + ep_rows_off(cap) + (size_t)slot * D * 4);
+        for (int i = threadIdx.x; i < (D >> 2); i += 256) d4[i] = s4[i];
+        if (threadIdx.x == 0) reinterpret_cast<int*>(blk + ep_ids_off())[slot] = ids[pair];
+    }
+    signal_when_done(own, peers, world, me, 0, epoch);
+}
+
+// ep_repack_kernel with row s of source q written into rank q's window
+// (source slot me of its return area), then the return flags.
+__global__ void __launch_bounds__(256) ep_repack_peer_kernel(const float* __restrict__ y,
+                                                             const int* __restrict__ src_off, int world, int me,
+                                                             int cap, int D, void* const* __restrict__ peers,
+                                                             size_t ret_off, uint8_t* own, unsigned long long epoch) {
+    const int s = blockIdx.x, q = blockIdx.y;
+    if (s < src_off[q + 1] - src_off[q]) {
+        const float4* s4 = reinterpret_cast<const float4*>(y + (size_t)(src_off[q] + s) * D);
+        float4* d4 = reinterpret_cast<float4*>(static_cast<uint8_t*>(peers[q]) + ret_off +
+                                               ((size_t)me * cap + s) * D * 4);
+        for (int i = threadIdx.x; i < (D >> 2); i += 256) d4[i] = s4[i];
+    }
+    signal_when_done(own, peers, world, me, 1, epoch);
+}
+
+// Waits (bounded) until every rank has published `epoch` for `phase` in this
+// rank's window; on time-out records kDevTimeoutGrid and returns, so the
+// launch sequence ends and the host reports the error.
+__global__ void ep_wait_kernel(const uint8_t* own, int world, int phase, unsigned long long epoch, int* err) {
+    const int p = threadIdx.x;
+    if (p >= world) return;
+    const unsigned long long* f = reinterpret_cast<const unsigned long long*>(own + kWinFlags) + phase * 64 + p;
+    if (ld_acquire_sys_u64(f) >= epoch) return;
+    const uint64_t t0 = global_timer_ns();
+    while (ld_acquire_sys_u64(f) < epoch) {
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+            if (err) atomicExch(err, kDevTimeoutGrid);
+            return;
+        }
+        __nanosleep(64);
+    }
+}
+
+cudaError_t ep_pack_peer_launch(const float* xin, const int* ids, int T, int D, int k, int num_experts, int world,
+                                int me, int cap, int* keys, const DispatchPlan& plan, void* const* peers, int parity,
+                                unsigned long long epoch, uint8_t* own, cudaStream_t st) {
+    const int P = T * k;
+    if (world < 1 || world > 64 || me < 0 || me >= world || num_experts % world || (D & 3) || P > cap)
+        return cudaErrorInvalidValue;
+    if (P > 0) {
+        ep_rank_keys_kernel<<<(P + 255) / 256, 256, 0, st>>>(ids, P, num_experts / world, world, keys);
+        const cudaError_t e = dispatch_plan_launch(keys, P, world, plan, st);
+        if (e != cudaSuccess) return e;
+    }
+    ep_pack_peer_kernel<<<P > 0 ? P : 1, 256, 0, st>>>(xin, ids, P, D, k, world, me, cap, keys, plan, peers,
+                                                         ep_win_disp_off(parity, world, cap, D),
+                                                         ep_block_bytes(cap, D), own, epoch);
+    return cudaGetLastError();
+}
+
+cudaError_t ep_repack_peer_launch(const float* y, const int* src_off, int world, int me, int cap, int D,
+                                  void* const* peers, int parity, unsigned long long epoch, uint8_t* own,
+                                  cudaStream_t st) {
+    ep_repack_peer_kernel<<<dim3(cap, world), 256, 0, st>>>(y, src_off, world, me, cap, D, peers,
+                                                            ep_win_ret_off(parity, world, cap, D), own, epoch);
+    return cudaGetLastError();
+}
+
+cudaError_t ep_wait_launch(const uint8_t* own, int world, int phase, unsigned long long epoch, int* err,
+                           cudaStream_t st) {
+    ep_wait_kernel<<<1, 64, 0, st>>>(own, world, phase, epoch, err);
+    return cudaGetLastError();
+}
+
 cudaError_t ep_pack_launch(const float* xin, const int* ids, int T, int D, int k, int num_experts, int world, int cap,
                            int* keys, const DispatchPlan& plan, uint8_t* blocks, cudaStream_t st) {
     const int P = T * k;

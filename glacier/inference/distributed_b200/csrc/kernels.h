@@ -290,6 +290,20 @@ cudaError_t ep_unpack_launch(const uint8_t* blocks, int world, int cap, int D, i
                              int* local_ids, int* src_off, cudaStream_t st);
 cudaError_t ep_repack_launch(const float* y, const int* src_off, int world, int cap, int D, float* out,
                              cudaStream_t st);
+// Exchange over a peer window (see ep.cu): layout, and the pack / repack
+// kernels that write into the peers' windows and publish an epoch flag, and
+// the bounded wait for every peer's flag.
+size_t ep_window_bytes(int world, int cap, int D);
+size_t ep_win_disp_off(int parity, int world, int cap, int D);
+size_t ep_win_ret_off(int parity, int world, int cap, int D);
+cudaError_t ep_pack_peer_launch(const float* xin, const int* ids, int T, int D, int k, int num_experts, int world,
+                                int me, int cap, int* keys, const DispatchPlan& plan, void* const* peers, int parity,
+                                unsigned long long epoch, uint8_t* own, cudaStream_t st);
+cudaError_t ep_repack_peer_launch(const float* y, const int* src_off, int world, int me, int cap, int D,
+                                  void* const* peers, int parity, unsigned long long epoch, uint8_t* own,
+                                  cudaStream_t st);
+cudaError_t ep_wait_launch(const uint8_t* own, int world, int phase, unsigned long long epoch, int* err,
+                           cudaStream_t st);
 cudaError_t ep_unblock_launch(const float* blocks, int P, int cap, int D, const int* keys, const DispatchPlan& plan,
                               float* y_back, cudaStream_t st);
 cudaError_t fill_launch(float* p, int n, float v, cudaStream_t st);
@@ -308,6 +322,10 @@ int comm_rank(const glc_comm* c);
 int32_t* comm_host_counts(glc_comm* c);  // pinned [2 * world]
 void* comm_scratch(glc_comm* c, int slot, size_t bytes);
 int comm_alltoall_i32(glc_comm* c, const int32_t* send, int32_t* recv, cudaStream_t st);
+// Peer window of at least `bytes` on every rank (collective); GLC_ERR_UNSUPPORTED
+// when it cannot be mapped on every rank or is turned off (glc_comm_peer_exchange).
+int comm_window(glc_comm* c, size_t bytes, cudaStream_t st, uint8_t** own, void* const** d_peers);
+unsigned long long comm_window_next_epoch(glc_comm* c);
 int comm_alltoallv(glc_comm* c, const void* send, const size_t* soff, const size_t* scnt, void* recv,
                    const size_t* roff, const size_t* rcnt, cudaStream_t st);
 

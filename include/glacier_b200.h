@@ -330,6 +330,16 @@ typedef struct glc_comm glc_comm;
 int glc_comm_unique_id(uint8_t* id_out);
 int glc_comm_create(const uint8_t* id, int32_t nranks, int32_t rank, int32_t device, glc_comm** out);
 int glc_comm_destroy(glc_comm* c);
+/* Expert-parallel exchanges over NVLink peer memory (default on): the first
+ * glc_moe_ep_forward maps every rank's exchange window into every rank with
+ * CUDA IPC (collective); the dispatch and return blocks are then written
+ * straight into the destination's window by the pack kernels, with an epoch
+ * flag per source, and only routed rows cross the links.  If any rank cannot
+ * map every peer, or enable = 0 (call it on every rank alike, between
+ * exchanges), the same blocks go through grouped NCCL send / receive.
+ * enable < 0 changes nothing and returns 1 when the exchanges go over peer
+ * memory (the window is mapped and the option on), else 0. */
+int glc_comm_peer_exchange(glc_comm* c, int32_t enable);
 
 /* Stage boundary, replacing the socket transport of a FusedActivationHeader and
  * its wire payload (FusedSocketTransport.cs:51-135, DistributedClusterSession.cs:1123):
@@ -356,10 +366,12 @@ int glc_pp_recv(glc_comm* c, int32_t peer, glc_fused_header* hdr_out, float* x_o
  * size the handle's max_tokens as world x the largest per-rank batch), and
  * out [T][D], ids_out [T][k], w_out [T][k] equal the single-GPU layer's
  * batched path bit for bit (the rows a rank receives are a batch: they run on
- * the grouped tensor-core experts whatever the decode flag).  Device pointers (ids_out, w_out may be NULL); NULL stream = the
- * handle's stream.  Asynchronous: the exchanges move fixed-size blocks (the
- * most pairs one rank can send one peer) whose counts are read on the device
- * only, so nothing waits on the host.  A rank whose T is out of range still
+ * the grouped tensor-core experts whatever the decode flag).  Device pointers
+ * (ids_out, w_out may be NULL); NULL stream = the handle's stream.
+ * Asynchronous: the exchange blocks are sized for the most pairs one rank can
+ * send one peer and their counts are read on the device only, so nothing
+ * waits on the host; over peer memory (glc_comm_peer_exchange) only the
+ * routed rows are written, through NCCL the whole blocks move.  A rank whose T is out of range still
  * takes part in both exchanges with no pairs (its peers do not wait on it)
  * and returns GLC_ERR_INVALID_ARG.  With profiling on, glc_moe_kernel_times
  * returns the phases: route, dispatch, exchange out, experts, exchange back,

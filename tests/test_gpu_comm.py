@@ -8,7 +8,8 @@ process) uses for multi-GPU work.  Skipped with fewer than two GPUs.
 * Expert parallelism: glc_moe_ep_forward over 2 ranks (experts 0..3 and 4..7)
   equals a full single-GPU layer on the same tokens bit for bit (the rows a
   rank receives are a batch: the grouped tensor-core experts, whatever the
-  decode/batched flag).
+  decode/batched flag), with the exchanges over NVLink peer memory and
+  through NCCL.
 """
 import os
 import sys
@@ -116,7 +117,9 @@ def _ep_case(rank, world, comm):
     full.synth_layer(0, seed)
     x = o.fill_normal(900 + rank, 1, 1.0, T * D).reshape(T, D)
     xd = torch.from_numpy(x).cuda()
-    for mode in (DECODE, BATCHED):
+    # over peer memory (three calls: both parities of the window's areas), then through NCCL
+    for peer, mode in ((True, DECODE), (True, BATCHED), (True, BATCHED), (False, DECODE), (False, BATCHED)):
+        comm.set_peer_exchange(peer)
         flags = 3 | mode
         out = torch.empty(T, D, device="cuda")
         ids = torch.empty(T, k, dtype=torch.int32, device="cuda")
@@ -127,7 +130,7 @@ def _ep_case(rank, world, comm):
         fo, fids, fw = full.forward(0, x, 3 | BATCHED)
         assert np.array_equal(ids.cpu().numpy(), fids)
         assert np.array_equal(w.cpu().numpy(), fw)
-        assert np.array_equal(out.cpu().numpy(), fo), (mode, float(np.abs(out.cpu().numpy() - fo).max()))
+        assert np.array_equal(out.cpu().numpy(), fo), (peer, mode, float(np.abs(out.cpu().numpy() - fo).max()))
         ro, rids, _ = o.moe_forward(L, x, flags)
         assert np.array_equal(fids, rids)
         assert rel_l2(fo, ro) <= LAYER_TOL
@@ -182,11 +185,11 @@ def test_expert_parallel_rank_over_capacity_does_not_stall_peers(cuda):
 
 def test_expert_parallel_one_rank_equals_single_gpu_layer(cuda, glc, oracle):
     """The whole expert-parallel call on a one-rank communicator (one GPU):
-    route, fixed-size dispatch blocks, the NCCL exchange (to itself), the
-    experts on the rows sized on the device, the exchange back and the
-    combine give the single-GPU layer bit for bit, on repeated calls with
-    changing batch sizes and either flag; the phase marks are the six of the
-    call."""
+    route, fixed-size dispatch blocks, the exchange to itself (through its own
+    peer window, then through NCCL), the experts on the rows sized on the
+    device, the exchange back and the combine give the single-GPU layer bit
+    for bit, on repeated calls with changing batch sizes and either flag; the
+    phase marks are the six of the call."""
     import torch
     from test_gpu_parity import LAYER_TOL, make_layer, rel_l2
     D, F, E, k, seed = 512, 1024, 8, 2, 779
@@ -196,7 +199,10 @@ def test_expert_parallel_one_rank_equals_single_gpu_layer(cuda, glc, oracle):
     shard.synth_layer(0, seed)
     full = glc.GpuExpertStageWorker(D, F, E, k, max_tokens=6)
     full.synth_layer(0, seed)
-    for T, mode in ((6, BATCHED), (1, BATCHED), (4, DECODE), (0, BATCHED), (5, BATCHED)):
+    # over the (self-mapped) peer window, then through NCCL
+    for peer, T, mode in [(p, T, m) for p in (True, False)
+                          for T, m in ((6, BATCHED), (1, BATCHED), (4, DECODE), (0, BATCHED), (5, BATCHED))]:
+        comm.set_peer_exchange(peer)
         x = oracle.fill_normal(990 + T, 1, 1.0, max(T, 1) * D).reshape(max(T, 1), D)[:T]
         xd = torch.from_numpy(np.ascontiguousarray(x)).cuda() if T else torch.empty(1, D, device="cuda")
         out = torch.empty(max(T, 1), D, device="cuda")
