@@ -130,6 +130,9 @@ _SIGNATURES = {
     "glc_comm_create": (C.c_int, [vp, i32, i32, i32, C.POINTER(vp)]),
     "glc_comm_destroy": (C.c_int, [vp]),
     "glc_comm_peer_exchange": (C.c_int, [vp, C.c_int32]),
+    "glc_moe_set_expert_slots": (C.c_int, [vp, C.c_int32]),
+    "glc_moe_prefetch_experts": (C.c_int, [vp, C.c_int32, C.POINTER(C.c_int32), C.c_int32]),
+    "glc_moe_expert_residency": (C.c_int, [vp, C.POINTER(C.c_int64)]),
     "glc_pp_send": (C.c_int, [vp, i32, C.POINTER(FusedHeader), vp, vp]),
     "glc_pp_recv": (C.c_int, [vp, i32, C.POINTER(FusedHeader), vp, i32, i32, vp]),
     "glc_moe_ep_forward": (C.c_int, [vp, vp, i32, vp, i32, C.c_uint32, vp, vp, vp, vp]),

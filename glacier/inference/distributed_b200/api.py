@@ -63,13 +63,22 @@ class GpuExpertStageWorker:
     def __init__(self, hidden_dim: int, expert_ffn_dim: int, num_experts: int, top_k: int, *,
                  shared_ffn_dim: int = 0, renormalize: bool = True, device: int = 0,
                  num_layers: int = 1, max_tokens: int = 1, expert_begin: int = 0,
-                 expert_count: int = 0):
+                 expert_count: int = 0, expert_slots: int = 0):
+        """expert_slots > 0: expert residency (glc_moe_set_expert_slots) -- the
+        routed experts stay in pinned host memory and that many of them at a
+        time in HBM, paged in as the routing selects them."""
         self.desc = _lib.MoeDesc(hidden_dim, expert_ffn_dim, num_experts, top_k, shared_ffn_dim,
                                  int(renormalize), _lib.GLC_GGUF_Q4_K, device, num_layers,
                                  max_tokens, expert_begin, expert_count)
         h = C.c_void_p()
         check(lib().glc_moe_create(C.byref(self.desc), C.byref(h)))
         self._h = h
+        if expert_slots:
+            try:
+                check(lib().glc_moe_set_expert_slots(h, expert_slots))
+            except GlcError:
+                self.dispose()
+                raise
         self.hidden_dim, self.expert_ffn_dim = hidden_dim, expert_ffn_dim
         self.num_experts, self.top_k = num_experts, top_k
         self.max_tokens = max_tokens
@@ -92,6 +101,19 @@ class GpuExpertStageWorker:
         if not self._h:
             raise GlcError(-5, "handle was disposed")
         return self._h
+
+    # -- expert residency --------------------------------------------------
+    def prefetch_experts(self, layer: int, expert_ids) -> None:
+        """Stage these experts of ``layer`` into HBM slots (router lookahead)."""
+        ids = np.ascontiguousarray(np.asarray(expert_ids, dtype=np.int32))
+        check(lib().glc_moe_prefetch_experts(self._handle(), layer,
+                                             ids.ctypes.data_as(C.POINTER(C.c_int32)), len(ids)))
+
+    def expert_residency(self) -> dict:
+        """Slot capacity and the VRAM-hit / transfer / prefetch counters."""
+        out = (C.c_int64 * 4)()
+        check(lib().glc_moe_expert_residency(self._handle(), out))
+        return {"slots": out[0], "hits": out[1], "transfers": out[2], "prefetches": out[3]}
 
     # -- weights ----------------------------------------------------------
     def load_layer(self, layer: int, gate_exps: np.ndarray, up_exps: np.ndarray,

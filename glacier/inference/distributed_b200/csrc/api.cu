@@ -73,6 +73,7 @@ struct LayerDev {
     alignas(64) uint8_t tmap_sh_up[128];
     alignas(64) uint8_t tmap_sh_down[128];
     bool tmaps = false;
+    bool host_experts = false;  // gate/up/down in pinned host memory (expert residency mode)
 };
 
 }  // namespace
@@ -144,6 +145,21 @@ struct glc_moe {
     long long debug_wait_limit_ns = 0;
     int* h_ids = nullptr;
     float* h_w = nullptr;
+    // Expert residency (glc_moe_set_expert_slots), GpuFirstExpertStageWorker's
+    // GPU slot cache (GpuFirstExpertStageWorker.cs:144-151, 354-407): the routed
+    // experts of every layer in pinned host memory, `slots` of them at a time
+    // in an HBM pool, the least recently used out first.
+    int slots = 0;
+    uint8_t* pool_gate = nullptr;
+    uint8_t* pool_up = nullptr;
+    uint8_t* pool_down = nullptr;
+    LayerDev pool_maps{};                       // tensor maps over the pool
+    std::vector<long long> slot_key;            // layer * El + local expert held, or -1
+    std::vector<unsigned long long> slot_used;  // call stamp of the last use
+    unsigned long long slot_clock = 0;
+    long long res_hits = 0, res_transfers = 0, res_prefetches = 0;
+    int* d_slot_ids = nullptr;  // [max_tokens * k] slot of each (token, slot) pair
+    int* h_slot_ids = nullptr;  // pinned
     // optional per-kernel CUDA-event timing of the last forward (launch order)
     int profiling = 0;
     int n_marks = 0;
@@ -294,9 +310,11 @@ int run_shared_expert(glc_moe* h, LayerDev* L, const float* xin, int T, float* o
 
 int make_layer_tmaps(glc_moe* h, LayerDev& L) {
     const int D = h->d.hidden_dim, F = h->d.expert_ffn_dim, El = local_experts(h);
-    if (glc::make_q4k_tensor_map(L.tmap_gate, L.gate, (long long)El * F, (int)rowbytes(D)) ||
-        glc::make_q4k_tensor_map(L.tmap_up, L.up, (long long)El * F, (int)rowbytes(D)) ||
-        glc::make_q4k_tensor_map(L.tmap_down, L.down, (long long)El * D, (int)rowbytes(F)))
+    // (host-resident routed experts are read through the slot pool's maps)
+    if (!L.host_experts &&
+        (glc::make_q4k_tensor_map(L.tmap_gate, L.gate, (long long)El * F, (int)rowbytes(D)) ||
+         glc::make_q4k_tensor_map(L.tmap_up, L.up, (long long)El * F, (int)rowbytes(D)) ||
+         glc::make_q4k_tensor_map(L.tmap_down, L.down, (long long)El * D, (int)rowbytes(F))))
         return fail(GLC_ERR_CUDA, "cuTensorMapEncodeTiled failed for the expert tensors");
     const int Fs = h->d.shared_ffn_dim;
     if (Fs > 0 && (glc::make_q4k_tensor_map(L.tmap_sh_gate, L.sh_gate, Fs, (int)rowbytes(D)) ||
@@ -400,7 +418,12 @@ int run_experts_grouped(glc_moe* h, LayerDev* L, const float* xin, int T, int k,
 }
 
 void free_layer(LayerDev& L) {
-    cudaFree(L.gate); cudaFree(L.up); cudaFree(L.down); cudaFree(L.router);
+    if (L.host_experts) {
+        cudaFreeHost(L.gate); cudaFreeHost(L.up); cudaFreeHost(L.down);
+    } else {
+        cudaFree(L.gate); cudaFree(L.up); cudaFree(L.down);
+    }
+    cudaFree(L.router);
     cudaFree(L.sh_gate); cudaFree(L.sh_up); cudaFree(L.sh_down); cudaFree(L.sh_gate_vec);
     L = LayerDev{};
 }
@@ -409,9 +432,16 @@ int alloc_layer(glc_moe* h, LayerDev& L) {
     if (L.gate) return GLC_OK;
     const int D = h->d.hidden_dim, F = h->d.expert_ffn_dim, E = h->d.num_experts, El = local_experts(h);
     const size_t gsz = (size_t)El * F * rowbytes(D), dsz = (size_t)El * D * rowbytes(F);
-    CUDA_TRY(cudaMalloc(&L.gate, gsz));
-    CUDA_TRY(cudaMalloc(&L.up, gsz));
-    CUDA_TRY(cudaMalloc(&L.down, dsz));
+    if (h->slots > 0) {  // routed experts stay in pinned host memory, paged into the slot pool
+        L.host_experts = true;
+        CUDA_TRY(cudaMallocHost(&L.gate, gsz));
+        CUDA_TRY(cudaMallocHost(&L.up, gsz));
+        CUDA_TRY(cudaMallocHost(&L.down, dsz));
+    } else {
+        CUDA_TRY(cudaMalloc(&L.gate, gsz));
+        CUDA_TRY(cudaMalloc(&L.up, gsz));
+        CUDA_TRY(cudaMalloc(&L.down, dsz));
+    }
     CUDA_TRY(cudaMalloc(&L.router, sizeof(float) * (size_t)D * E));
     if (h->d.shared_ffn_dim > 0) {
         const int Fs = h->d.shared_ffn_dim;
@@ -423,11 +453,184 @@ int alloc_layer(glc_moe* h, LayerDev& L) {
     return GLC_OK;
 }
 
+// ---- expert residency (glc_moe_set_expert_slots)
+
+// Slot holding local expert e of `layer`, loading it into the least recently
+// used slot not yet used by this call (stamp) on a miss -- the three matrices
+// copied from pinned host memory on `st`, behind the work already queued
+// there that may still read the slot.  Returns the slot, -1 when every slot
+// is in use by this call, -2 on a CUDA error (recorded).
+int ensure_slot(glc_moe* h, int layer, int e, unsigned long long stamp, cudaStream_t st, bool* loaded) {
+    const int D = h->d.hidden_dim, F = h->d.expert_ffn_dim, El = local_experts(h);
+    const long long key = (long long)layer * El + e;
+    *loaded = false;
+    for (int s = 0; s < h->slots; ++s)
+        if (h->slot_key[s] == key) {
+            h->slot_used[s] = stamp;
+            return s;
+        }
+    int victim = -1;
+    for (int s = 0; s < h->slots; ++s)
+        if (h->slot_used[s] < stamp && (victim < 0 || h->slot_used[s] < h->slot_used[victim])) victim = s;
+    if (victim < 0) return -1;
+    const size_t gsl = (size_t)F * rowbytes(D), dsl = (size_t)D * rowbytes(F);
+    const LayerDev& L = h->layers[layer];
+    h->slot_key[victim] = -1;  // until the copies are queued
+    if (cudaMemcpyAsync(h->pool_gate + victim * gsl, L.gate + e * gsl, gsl, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(h->pool_up + victim * gsl, L.up + e * gsl, gsl, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(h->pool_down + victim * dsl, L.down + e * dsl, dsl, cudaMemcpyHostToDevice, st) != cudaSuccess) {
+        fail(GLC_ERR_CUDA, "expert page-in copy: %s", cudaGetErrorString(cudaGetLastError()));
+        return -2;
+    }
+    h->slot_key[victim] = key;
+    h->slot_used[victim] = stamp;
+    *loaded = true;
+    return victim;
+}
+
+// A layer's routed experts were (re)written: its slots no longer hold them.
+// Layer 0's first min(slots, experts) experts are then staged, as
+// GpuFirstExpertStageWorker.WarmInitialGpuSlots (GpuFirstExpertStageWorker.cs:344-352)
+// (not counted as transfers).
+int warm_slots(glc_moe* h, int layer) {
+    if (h->slots == 0) return GLC_OK;
+    const int El = local_experts(h);
+    for (int s = 0; s < h->slots; ++s)
+        if (h->slot_key[s] >= 0 && h->slot_key[s] / El == layer) {
+            h->slot_key[s] = -1;
+            h->slot_used[s] = 0;
+        }
+    if (layer != 0) return GLC_OK;
+    const unsigned long long stamp = ++h->slot_clock;
+    for (int e = 0; e < std::min(h->slots, El); ++e) {
+        bool loaded;
+        if (ensure_slot(h, 0, e, stamp, h->stream, &loaded) < 0) return GLC_ERR_CUDA;
+    }
+    CUDA_TRY(cudaStreamSynchronize(h->stream));
+    return GLC_OK;
+}
+
+// After the router of a call on a residency-mode handle: the routed ids
+// [P] to the host, every selected expert into a slot (hits and transfers
+// counted per pair, as EnsureExpertInGpuSlot, GpuFirstExpertStageWorker.cs:354-385),
+// and the slot of each pair back to the device for the expert kernels, which
+// read the pool as their expert array.
+int page_in(glc_moe* h, int layer, const int* ids_dev, int P, cudaStream_t st, const int** slot_ids) {
+    const int El = local_experts(h);
+    CUDA_TRY(cudaMemcpyAsync(h->h_slot_ids, ids_dev, sizeof(int) * P, cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaStreamSynchronize(st));
+    const unsigned long long stamp = ++h->slot_clock;
+    for (int i = 0; i < P; ++i) {
+        int e = h->h_slot_ids[i];
+        e = e < 0 ? 0 : (e >= El ? El - 1 : e);  // clamped like ProcessRoutedTopK
+        bool loaded;
+        const int sl = ensure_slot(h, layer, e, stamp, st, &loaded);
+        if (sl == -1)
+            return fail(GLC_ERR_UNSUPPORTED, "the call routes to more distinct experts than the %d expert slots",
+                        h->slots);
+        if (sl < 0) return GLC_ERR_CUDA;
+        if (loaded) ++h->res_transfers;
+        else ++h->res_hits;
+        h->h_slot_ids[i] = sl;
+    }
+    CUDA_TRY(cudaMemcpyAsync(h->d_slot_ids, h->h_slot_ids, sizeof(int) * P, cudaMemcpyHostToDevice, st));
+    *slot_ids = h->d_slot_ids;
+    return GLC_OK;
+}
+
+// The layer as the expert kernels see it in residency mode: the slot pool
+// as its expert array (router and shared expert its own).
+LayerDev pool_view(const glc_moe* h, const LayerDev* L) {
+    LayerDev V = *L;
+    V.gate = h->pool_gate;
+    V.up = h->pool_up;
+    V.down = h->pool_down;
+    std::memcpy(V.tmap_gate, h->pool_maps.tmap_gate, sizeof(V.tmap_gate));
+    std::memcpy(V.tmap_up, h->pool_maps.tmap_up, sizeof(V.tmap_up));
+    std::memcpy(V.tmap_down, h->pool_maps.tmap_down, sizeof(V.tmap_down));
+    V.host_experts = false;
+    return V;
+}
+
+// The layer and pair ids the expert kernels run on: as given, or in
+// residency mode the selected experts paged into slots (ids [P] on the
+// device) and the pool as the expert array (*V holds that view).
+int expert_operands(glc_moe* h, LayerDev* L, const int* ids, int P, cudaStream_t st, LayerDev* V, LayerDev** LR,
+                    const int** run_ids) {
+    *LR = L;
+    *run_ids = ids;
+    if (!h->slots || P <= 0) return GLC_OK;
+    const int rc = page_in(h, (int)(L - h->layers.data()), ids, P, st, run_ids);
+    if (rc) return rc;
+    *V = pool_view(h, L);
+    *LR = V;
+    return GLC_OK;
+}
+
 }  // namespace
 
 extern "C" {
 
 int glc_abi_version(void) { return GLC_ABI_VERSION; }
+
+int glc_moe_set_expert_slots(glc_moe* h, int32_t slots) {
+    int rc = check_handle(h);
+    if (rc) return rc;
+    for (const auto& L : h->layers)
+        if (L.gate) return fail(GLC_ERR_STATE, "expert slots are set before the first layer is loaded");
+    if (h->slots) return fail(GLC_ERR_STATE, "expert slots are already set");
+    if (local_experts(h) != h->d.num_experts)
+        return fail(GLC_ERR_UNSUPPORTED, "expert residency on an expert-parallel shard");
+    const int E = h->d.num_experts, D = h->d.hidden_dim, F = h->d.expert_ffn_dim;
+    slots = slots < 1 ? 1 : (slots > E ? E : slots);  // clamped like GpuFirstExpertStageWorker.cs:144
+    const size_t gsl = (size_t)F * rowbytes(D), dsl = (size_t)D * rowbytes(F);
+    CUDA_TRY(cudaSetDevice(h->d.device));
+    CUDA_TRY(cudaMalloc(&h->pool_gate, slots * gsl));
+    CUDA_TRY(cudaMalloc(&h->pool_up, slots * gsl));
+    CUDA_TRY(cudaMalloc(&h->pool_down, slots * dsl));
+    if (glc::make_q4k_tensor_map(h->pool_maps.tmap_gate, h->pool_gate, (long long)slots * F, (int)rowbytes(D)) ||
+        glc::make_q4k_tensor_map(h->pool_maps.tmap_up, h->pool_up, (long long)slots * F, (int)rowbytes(D)) ||
+        glc::make_q4k_tensor_map(h->pool_maps.tmap_down, h->pool_down, (long long)slots * D, (int)rowbytes(F)))
+        return fail(GLC_ERR_CUDA, "cuTensorMapEncodeTiled failed for the expert slot pool");
+    const size_t P = (size_t)h->d.max_tokens * h->d.top_k;
+    CUDA_TRY(cudaMalloc(&h->d_slot_ids, sizeof(int) * P));
+    CUDA_TRY(cudaMallocHost(&h->h_slot_ids, sizeof(int) * P));
+    h->slot_key.assign(slots, -1);
+    h->slot_used.assign(slots, 0);
+    h->slots = slots;
+    return GLC_OK;
+}
+
+int glc_moe_prefetch_experts(glc_moe* h, int32_t layer, const int32_t* expert_ids, int32_t n) {
+    int rc = check_handle(h);
+    if (rc) return rc;
+    if (h->slots == 0) return GLC_OK;  // every expert is resident
+    if (n < 0 || (n > 0 && !expert_ids)) return fail(GLC_ERR_INVALID_ARG, "bad expert list");
+    const int El = local_experts(h);
+    const int l = (int)(layer_of(h, layer) - h->layers.data());
+    if (!h->layers[l].loaded) return fail(GLC_ERR_STATE, "layer %d has no weights", l);
+    const unsigned long long stamp = ++h->slot_clock;
+    for (int i = 0; i < n; ++i) {
+        const int e = expert_ids[i] < 0 ? 0 : (expert_ids[i] >= El ? El - 1 : expert_ids[i]);
+        bool loaded;
+        const int sl = ensure_slot(h, l, e, stamp, h->stream, &loaded);
+        if (sl == -2) return GLC_ERR_CUDA;
+        if (sl == -1) break;  // every slot already taken by this prefetch
+        if (loaded) ++h->res_prefetches;
+    }
+    return GLC_OK;
+}
+
+int glc_moe_expert_residency(glc_moe* h, int64_t* out4) {
+    int rc = check_handle(h);
+    if (rc) return rc;
+    if (!out4) return fail(GLC_ERR_INVALID_ARG, "null pointer");
+    out4[0] = h->slots ? h->slots : local_experts(h);
+    out4[1] = h->res_hits;
+    out4[2] = h->res_transfers;
+    out4[3] = h->res_prefetches;
+    return GLC_OK;
+}
 
 const char* glc_last_error(void) { return g_last_error.c_str(); }
 
@@ -595,6 +798,8 @@ int glc_moe_destroy(glc_moe* h) {
     cudaFree(h->plan_sh.grp_N); cudaFree(h->plan_sh.grp_pos0); cudaFree(h->plan_sh.grp_units);
     cudaFree(h->plan_sh.meta); cudaFree(h->rscale_sh); cudaFree(h->ysh);
     cudaFreeHost(h->h_x); cudaFreeHost(h->h_res); cudaFreeHost(h->h_sig); cudaFreeHost(h->h_ids); cudaFreeHost(h->h_w);
+    cudaFree(h->pool_gate); cudaFree(h->pool_up); cudaFree(h->pool_down); cudaFree(h->d_slot_ids);
+    cudaFreeHost(h->h_slot_ids);
     if (h->stream) cudaStreamDestroy(h->stream);
     h->disposed = 1;
     delete h;
@@ -611,9 +816,9 @@ int glc_moe_load_layer(glc_moe* h, int32_t layer, const glc_layer_weights* w) {
     if (rc) return rc;
     const int D = h->d.hidden_dim, F = h->d.expert_ffn_dim, E = h->d.num_experts, El = local_experts(h);
     const size_t gsz = (size_t)El * F * rowbytes(D), dsz = (size_t)El * D * rowbytes(F);
-    CUDA_TRY(cudaMemcpy(L.gate, w->gate_exps, gsz, cudaMemcpyHostToDevice));
-    CUDA_TRY(cudaMemcpy(L.up, w->up_exps, gsz, cudaMemcpyHostToDevice));
-    CUDA_TRY(cudaMemcpy(L.down, w->down_exps, dsz, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(L.gate, w->gate_exps, gsz, cudaMemcpyDefault));  // HBM, or pinned host (residency mode)
+    CUDA_TRY(cudaMemcpy(L.up, w->up_exps, gsz, cudaMemcpyDefault));
+    CUDA_TRY(cudaMemcpy(L.down, w->down_exps, dsz, cudaMemcpyDefault));
     if (w->router) CUDA_TRY(cudaMemcpy(L.router, w->router, sizeof(float) * (size_t)D * E, cudaMemcpyHostToDevice));
     else CUDA_TRY(cudaMemset(L.router, 0, sizeof(float) * (size_t)D * E));
     if (h->d.shared_ffn_dim > 0) {
@@ -626,7 +831,8 @@ int glc_moe_load_layer(glc_moe* h, int32_t layer, const glc_layer_weights* w) {
         CUDA_TRY(cudaMemcpy(L.sh_gate_vec, w->shared_gate_vec, sizeof(float) * D, cudaMemcpyHostToDevice));
     }
     L.loaded = true;
-    return make_layer_tmaps(h, L);
+    rc = make_layer_tmaps(h, L);
+    return rc ? rc : warm_slots(h, layer);
 }
 
 int glc_moe_synth_layer(glc_moe* h, int32_t layer, uint64_t seed) {
@@ -644,11 +850,11 @@ int glc_moe_synth_layer(glc_moe* h, int32_t layer, uint64_t seed) {
     for (int el = 0; el < El; ++el) {
         const int e = h->d.expert_begin + el;
         glc::synth_q4k(seed, glc::expert_tag(e, 0), 0.01f, buf.data(), gsl / 144, nt);
-        CUDA_TRY(cudaMemcpy(L.gate + el * gsl, buf.data(), gsl, cudaMemcpyHostToDevice));
+        CUDA_TRY(cudaMemcpy(L.gate + el * gsl, buf.data(), gsl, cudaMemcpyDefault));
         glc::synth_q4k(seed, glc::expert_tag(e, 1), 0.01f, buf.data(), gsl / 144, nt);
-        CUDA_TRY(cudaMemcpy(L.up + el * gsl, buf.data(), gsl, cudaMemcpyHostToDevice));
+        CUDA_TRY(cudaMemcpy(L.up + el * gsl, buf.data(), gsl, cudaMemcpyDefault));
         glc::synth_q4k(seed, glc::expert_tag(e, 2), 0.01f, buf.data(), dsl / 144, nt);
-        CUDA_TRY(cudaMemcpy(L.down + el * dsl, buf.data(), dsl, cudaMemcpyHostToDevice));
+        CUDA_TRY(cudaMemcpy(L.down + el * dsl, buf.data(), dsl, cudaMemcpyDefault));
     }
     std::vector<float> r((size_t)D * E);
     glc::synth_normal(seed, glc::kTagRouter, 0.02f, r.data(), r.size(), nt);
@@ -669,7 +875,8 @@ int glc_moe_synth_layer(glc_moe* h, int32_t layer, uint64_t seed) {
         CUDA_TRY(cudaMemcpy(L.sh_gate_vec, gv.data(), sizeof(float) * D, cudaMemcpyHostToDevice));
     }
     L.loaded = true;
-    return make_layer_tmaps(h, L);
+    rc = make_layer_tmaps(h, L);
+    return rc ? rc : warm_slots(h, layer);
 }
 
 int glc_moe_set_profiling(glc_moe* h, int32_t enable) {
@@ -718,6 +925,7 @@ int glc_moe_layer_device_ptrs(glc_moe* h, int32_t layer, const void** gate, cons
     if (rc) return rc;
     LayerDev* L = layer_of(h, layer);
     if (!L->loaded) return fail(GLC_ERR_STATE, "layer %d has no weights", layer);
+    if (L->host_experts) return fail(GLC_ERR_STATE, "the routed experts are host-resident (expert slots)");
     if (gate) *gate = L->gate;
     if (up) *up = L->up;
     if (down) *down = L->down;
@@ -740,7 +948,12 @@ int glc_expert_forward_dev(glc_moe* h, int32_t layer, int32_t expert, const floa
     h->h_w[0] = 1.0f;
     CUDA_TRY(cudaMemcpyAsync(h->ids, h->h_ids, sizeof(int), cudaMemcpyHostToDevice, st));
     CUDA_TRY(cudaMemcpyAsync(h->wts, h->h_w, sizeof(float), cudaMemcpyHostToDevice, st));
-    return run_experts(h, L, x, 1, 1, h->ids, h->wts, nullptr, y, st);
+    const int* run_ids = nullptr;
+    LayerDev V;
+    LayerDev* LR = nullptr;
+    rc = expert_operands(h, L, h->ids, 1, st, &V, &LR, &run_ids);
+    if (rc) return rc;
+    return run_experts(h, LR, x, 1, 1, run_ids, h->wts, nullptr, y, st);
 }
 
 int glc_expert_forward(glc_moe* h, int32_t layer, int32_t expert, const float* x, float* y) {
@@ -780,7 +993,12 @@ int glc_routed_topk(glc_moe* h, int32_t layer, const float* x, const int32_t* id
     CUDA_TRY(cudaMemcpyAsync(h->ids, h->h_ids, sizeof(int) * k, cudaMemcpyHostToDevice, st));
     CUDA_TRY(cudaMemcpyAsync(h->wts, h->h_w, sizeof(float) * k, cudaMemcpyHostToDevice, st));
     if (k > h->d.top_k * h->d.max_tokens) return fail(GLC_ERR_INVALID_ARG, "k too large");
-    rc = run_experts(h, L, h->x, 1, k, h->ids, h->wts, nullptr, h->out, st);
+    const int* run_ids = nullptr;
+    LayerDev V;
+    LayerDev* LR = nullptr;
+    rc = expert_operands(h, L, h->ids, k, st, &V, &LR, &run_ids);
+    if (rc) return rc;
+    rc = run_experts(h, LR, h->x, 1, k, run_ids, h->wts, nullptr, h->out, st);
     if (rc) return rc;
     CUDA_TRY(cudaMemcpyAsync(out, h->out, sizeof(float) * D, cudaMemcpyDeviceToHost, st));
     CUDA_TRY(cudaStreamSynchronize(st));
@@ -792,7 +1010,8 @@ namespace {
 // The whole-layer fused decode launch serves this call (T tokens, flags).
 bool fused_applies(const glc_moe* h, int T, uint32_t flags) {
     const bool grouped = (flags & GLC_FWD_BATCHED) ? true : (flags & GLC_FWD_DECODE) ? false : (T > 1);
-    return !grouped && !(flags & GLC_FWD_UNFUSED);
+    // residency mode routes first and pages the selected experts in before they run
+    return !grouped && !(flags & GLC_FWD_UNFUSED) && h->slots == 0;
 }
 
 // Fused-kernel parameters of a layer; the caller sets x, resid and out.
@@ -888,11 +1107,17 @@ int glc_moe_forward_dev(glc_moe* h, int32_t layer, const float* x, int32_t T, ui
     mark(h, st);
     CUDA_TRY(glc::router_launch(rp, st));
     mark(h, st);
-    rc = grouped ? run_experts_grouped(h, L, h->xin, T, k, h->ids, h->wts, resid, out, st, true)
-                 : run_experts(h, L, h->xin, T, k, h->ids, h->wts, resid, out, st);
+    // residency mode: the selected experts into HBM slots, the kernels on the pool
+    const int* run_ids = nullptr;
+    LayerDev V;
+    LayerDev* LR = nullptr;
+    rc = expert_operands(h, L, h->ids, T * k, st, &V, &LR, &run_ids);
+    if (rc) return rc;
+    rc = grouped ? run_experts_grouped(h, LR, h->xin, T, k, run_ids, h->wts, resid, out, st, true)
+                 : run_experts(h, LR, h->xin, T, k, run_ids, h->wts, resid, out, st);
     if (rc) return rc;
     if (h->d.shared_ffn_dim > 0 && !grouped) {  // the grouped path ran it already
-        rc = run_shared_expert(h, L, h->xin, T, out, st);
+        rc = run_shared_expert(h, LR, h->xin, T, out, st);
         if (rc) return rc;
     }
     if (ids_out) CUDA_TRY(cudaMemcpyAsync(ids_out, h->ids, sizeof(int) * T * k, cudaMemcpyDeviceToDevice, st));
@@ -964,8 +1189,13 @@ int glc_moe_experts_dev(glc_moe* h, int32_t layer, const float* rows, const int3
     const bool grouped = (flags & GLC_FWD_BATCHED) ? true : (flags & GLC_FWD_DECODE) ? false : (R > 1);
     if (!h->mark_lock) h->n_marks = 0;
     mark(h, st);
-    return grouped ? run_experts_grouped(h, L, rows, R, 1, h->ids, h->ones, nullptr, y_out, st, false)
-                   : run_experts(h, L, rows, R, 1, h->ids, h->ones, nullptr, y_out, st);
+    const int* run_ids = nullptr;
+    LayerDev V;
+    LayerDev* LR = nullptr;
+    rc = expert_operands(h, L, h->ids, R, st, &V, &LR, &run_ids);
+    if (rc) return rc;
+    return grouped ? run_experts_grouped(h, LR, rows, R, 1, run_ids, h->ones, nullptr, y_out, st, false)
+                   : run_experts(h, LR, rows, R, 1, run_ids, h->ones, nullptr, y_out, st);
 }
 
 int glc_moe_combine_dev(glc_moe* h, int32_t layer, const float* y_back, const int32_t* inv, const float* w,
@@ -1003,6 +1233,7 @@ int glc_moe_ep_forward(glc_moe* h, glc_comm* c, int32_t layer, const float* x, i
     int rc = check_handle(h);
     if (rc) return rc;
     if (!c) return fail(GLC_ERR_INVALID_ARG, "null communicator");
+    if (h->slots) return fail(GLC_ERR_UNSUPPORTED, "expert parallelism on a handle with expert slots");
     const int world = glc::comm_world(c), rank = glc::comm_rank(c);
     const int E = h->d.num_experts, El = local_experts(h);
     if (E % world || El * world != E || h->d.expert_begin != rank * El)
@@ -1248,6 +1479,7 @@ int glc_moe_graph_build(glc_moe* h, int32_t layer, const float* x, int32_t T, ui
     int rc = check_handle(h);
     if (rc) return rc;
     if (!x || !out || T <= 0) return fail(GLC_ERR_INVALID_ARG, "bad graph arguments");
+    if (h->slots) return fail(GLC_ERR_UNSUPPORTED, "expert slots page in on the host: not capturable");
     // One eager run first: first-use set-up (shared-memory opt-in) is not capturable.
     rc = glc_moe_forward_dev(h, layer, x, T, flags, out, nullptr, nullptr, h->stream);
     if (rc) return rc;

@@ -111,6 +111,38 @@ int glc_moe_load_layer(glc_moe* h, int32_t layer, const glc_layer_weights* w);
  * Q4_K d/dmin = fp16(|N(0,sigma_d)|), uniform 6-bit scales/mins and 4-bit quants,
  * router N(0, 0.02), shared gate N(0, 0.02)).  Only this device's experts are made. */
 int glc_moe_synth_layer(glc_moe* h, int32_t layer, uint64_t seed);
+
+/* Expert residency, GpuFirstExpertStageWorker's GPU slot cache
+ * (GpuFirstExpertStageWorker.cs:144-151, 344-407).  Called after
+ * glc_moe_create and before the first layer is loaded, it keeps every layer's
+ * routed experts in pinned host memory and `slots` of them at a time in HBM
+ * (clamped to [1, num_experts], as GpuFirstExpertStageWorker.cs:144; router and
+ * shared expert stay resident).  A forward routes first, then brings each
+ * selected expert into a slot -- a hit when it is there, else the least
+ * recently used slot not used by this call is refilled from host memory --
+ * and runs the expert kernels on the slots: results equal the fully resident
+ * layer's bit for bit.  Loading layer 0 stages its first experts
+ * (WarmInitialGpuSlots, GpuFirstExpertStageWorker.cs:344-352).  A call that
+ * routes to more distinct experts than there are slots returns
+ * GLC_ERR_UNSUPPORTED (the reference sends those to its CPU pool; this
+ * library has no CPU path).  With slots the decode step is not one fused
+ * launch and a forward waits on the host for its routing; expert-parallel
+ * calls, glc_moe_graph_build and glc_moe_layer_device_ptrs are then not
+ * available, and expert-parallel shards cannot use slots.  One stream per
+ * handle: a refilled slot is written behind the work queued on it. */
+int glc_moe_set_expert_slots(glc_moe* h, int32_t slots);
+/* Router lookahead prefetch (PrefetchLookaheadExperts,
+ * GpuFirstExpertStageWorker.cs:388-407): stages the listed experts of `layer`
+ * into slots, asynchronously on the handle's stream (ids clamped; a no-op
+ * without expert slots). */
+int glc_moe_prefetch_experts(glc_moe* h, int32_t layer, const int32_t* expert_ids, int32_t n);
+/* out4 = {slot capacity (num_experts when every expert is resident), VRAM
+ * hits, host-to-HBM expert transfers, lookahead prefetches}: the
+ * GpuResidentSlotCapacity, GpuVramHitCount, GpuPcieTransferCount and
+ * LookaheadPrefetchCount of GpuFirstExpertStageWorker.GetTelemetry
+ * (GpuFirstExpertStageWorker.cs:763-783); a hit or transfer is counted per
+ * (token, slot) pair. */
+int glc_moe_expert_residency(glc_moe* h, int64_t* out4);
 /* Device pointers of a resident layer (for the _dev raw primitives). */
 int glc_moe_layer_device_ptrs(glc_moe* h, int32_t layer, const void** gate, const void** up,
                               const void** down, const float** router);
