@@ -410,6 +410,7 @@ def run_ours(args, w):
     # configs[4] fits one GPU (~80 GB); measured at N = 1 only (the ranks of a
     # multi-GPU run would each synthesise their own copy on the same host)
     mix22 = measure_mixtral22b(torch, glc, args, stream, local) if (world == 1 and not args.skip_dense) else None
+    paging = measure_residency(glc, w, local) if (world == 1 and not args.skip_batched) else None
 
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.skip_cpu_baseline:
@@ -470,6 +471,8 @@ def run_ours(args, w):
             line["dense_pp"] = dense
         if mix22 is not None:
             line["mixtral8x22b"] = mix22
+        if paging is not None:
+            line["expert_residency"] = paging
         if ep_leg is not None:
             line["ep"] = ep_leg
         print(json.dumps(line), flush=True)
@@ -627,6 +630,36 @@ def measure_batched(torch, worker, w, stream, args):
             "grouped_down_gbs": (w["E"] * D * q4k_row_bytes(w["F"])) / (dn * 1e-3) / 1e9,
             "peak_gbs": peak,
             "kernel_ms": {n: float(v) for n, v in zip(names, kt)}}
+
+
+def measure_residency(glc, w, local):
+    """Expert residency (glc_moe_set_expert_slots): the same Mixtral layer with
+    HBM slots for 4 of its 8 experts, the others paged in from pinned host
+    memory as the routing selects them (least recently used out); decode
+    tokens through the host-buffer forward.  Host wall clock per synchronous
+    call: the forward waits on the host for each call's routing."""
+    D, F, E, k = w["D"], w["F"], w["E"], w["k"]
+    slots = 4
+    paged = glc.GpuExpertStageWorker(D, F, E, k, renormalize=True, device=local, max_tokens=1, expert_slots=slots)
+    paged.synth_layer(0, w["seed"])
+    toks = make_tokens(w, N_TOKENS)
+    for i in range(3):
+        paged.forward(0, toks[i], w["flags"])
+    c0 = paged.expert_residency()
+    n = 48
+    t0 = time.perf_counter()
+    for i in range(n):
+        paged.forward(0, toks[i % N_TOKENS], w["flags"])
+    el = time.perf_counter() - t0
+    c1 = paged.expert_residency()
+    paged.poll_error()
+    paged.dispose()
+    hits, tr = c1["hits"] - c0["hits"], c1["transfers"] - c0["transfers"]
+    eb = 3 * F * q4k_row_bytes(D)
+    return {"workload": "mixtral8x7b_moe_layer_decode_paged", "slots": slots, "experts": E, "tokens": n,
+            "ms_per_token": el * 1e3 / n, "hit_rate": hits / max(hits + tr, 1), "transfers_per_token": tr / n,
+            "expert_bytes": eb, "host_to_hbm_gbs": tr * eb / el / 1e9,
+            "note": f"{N_TOKENS} rotating tokens; every miss copies one expert (gate, up, down) from pinned host memory"}
 
 
 QWEN = dict(name="qwen2_57b_a14b_moe_layer", D=3584, F=2560, E=64, k=8, Fs=20480, seed=20241202, flags=3)
