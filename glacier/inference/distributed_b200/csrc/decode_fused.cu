@@ -66,10 +66,10 @@ __device__ __forceinline__ int xs_index(int d, int U) {
 // RMSNorm scale of every token, threads 0..255, from the raw input xr [T][D]:
 // canonical sum of squares (256 strided fused partials, warp butterfly,
 // pairwise tree over the 8 warp sums), then 1 / sqrt(ss / D + eps).
-template <bool NW>
+template <bool NW, int TT>
 __device__ void router_rms(const FusedDecodeParams& p, const float* xr, float* red, float* rms_s, int tid) {
     const int warp = tid >> 5, lane = tid & 31;
-    const int D = p.D, T = p.T;
+    const int D = p.D, T = TT ? TT : p.T;
     float a[kFusedMaxTokens];
 #pragma unroll
     for (int t = 0; t < kFusedMaxTokens; ++t) a[t] = 0.f;
@@ -137,12 +137,12 @@ __device__ __forceinline__ void st_cluster_f32(const float* local, uint32_t rank
 // completes the tree from the two subtree values (logits_from_halves).
 // Threads 128..255 write the normalised input of the d this CTA's partials
 // do not visit.
-template <bool NW>
+template <bool NW, int TT>
 __device__ void router_logits_split(const FusedDecodeParams& p, const float* Wl, const float* xr, float* xs,
                                     float* red, float* lh, const float* rms_s, int tid, int rank) {
     constexpr int R = 2, NL = kRouterWidth / R;
     const int warp = tid >> 5, lane = tid & 31;
-    const int D = p.D, E = p.E, T = p.T, U = D >> 6;
+    const int D = p.D, E = p.E, T = TT ? TT : p.T, U = D >> 6;
     if (tid >= NL) {
         const int t2 = tid - NL, o = t2 < rank * NL ? t2 : t2 + NL;  // the d this CTA's partials skip
         for (int t = 0; t < T; ++t) {
@@ -208,11 +208,11 @@ __device__ __forceinline__ float logits_from_halves(const float* c) { return c[0
 // router.cu (256 strided fused partials over the normalised input, warp
 // butterfly, pairwise tree over the 8 warp sums), eight experts per pass; the
 // first pass also writes the normalised input to xs (xs_index layout).
-template <bool NW>
+template <bool NW, int TT>
 __device__ void router_logits(const FusedDecodeParams& p, const float* Wr, const float* xr, float* xs,
                               float* red, float* logit, const float* rms_s, int tid) {
     const int warp = tid >> 5, lane = tid & 31;
-    const int D = p.D, E = p.E, T = p.T, U = D >> 6;
+    const int D = p.D, E = p.E, T = TT ? TT : p.T, U = D >> 6;
     // At E = 8 rows are 32 B apart across lanes; lanes 4..7 of each 8 read
     // their second half first so one 16-byte read covers all banks.
     const int h = (E == 8) ? ((lane >> 2) & 1) : 0;
@@ -301,11 +301,12 @@ __device__ void topk_token_warp(const FusedDecodeParams& p, const float* l, int 
 }
 
 // SPLIT: the router split over a 2-CTA cluster (launched with clusters of
-// two); NW: weighted RMSNorm (p.norm_w set).  Separate instantiations keep
-// the unsplit, unweighted kernel's code exactly what it is without them
-// (measured: folding both in as runtime branches cost 1.6 us per launch at
-// the Mixtral-8x7B shape).
-template <bool SPLIT, bool NW>
+// two); NW: weighted RMSNorm (p.norm_w set); TT: the token count when it is
+// known at compile time (1: one decode token), 0 = p.T.  Separate
+// instantiations keep the unsplit, unweighted kernel's code exactly what it
+// is without them (measured: folding the split and the weighted norm in as
+// runtime branches cost 1.6 us per launch at the Mixtral-8x7B shape).
+template <bool SPLIT, bool NW, int TT>
 __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(const __grid_constant__ FusedDecodeParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int s_ok, s_okx, s_okw;
@@ -325,7 +326,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
     uint64_t* go_bar = wbar + 1;  // the producer has issued its first ring's worth of stages
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int T = p.T, D = p.D, F = p.F, k = p.k, P = T * k;
+    const int T = TT ? TT : p.T, D = p.D, F = p.F, k = p.k, P = T * k;
     const uint64_t lim = p.wait_limit_ns > 0 ? (uint64_t)p.wait_limit_ns : kWaitLimitNs;
     const int slot = p.slot_bytes;
     constexpr int R = SPLIT ? 2 : 1;  // router split over a cluster of R CTAs
@@ -422,14 +423,14 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
         if (!mbar_wait_spin(xbar, 0, p.err, kDevTimeoutFull, lim)) s_okx = 0;
         named_bar_sync(2, kRouterWidth);
         const bool okx = s_okx != 0;
-        if (okx && p.rmsnorm) router_rms<NW>(p, xraw, red, rms_s, tid);
+        if (okx && p.rmsnorm) router_rms<NW, TT>(p, xraw, red, rms_s, tid);
         if (okx && !mbar_wait_spin(wbar, 0, p.err, kDevTimeoutFull, lim)) s_okw = 0;
         named_bar_sync(2, kRouterWidth);
         if (okx && s_okw != 0) {
             if (R > 1)
-                router_logits_split<NW>(p, reinterpret_cast<const float*>(smem), xraw, xs, red, lh, rms_s, tid, rank);
+                router_logits_split<NW, TT>(p, reinterpret_cast<const float*>(smem), xraw, xs, red, lh, rms_s, tid, rank);
             else
-                router_logits<NW>(p, reinterpret_cast<const float*>(smem), xraw, xs, red, logit, rms_s, tid);
+                router_logits<NW, TT>(p, reinterpret_cast<const float*>(smem), xraw, xs, red, logit, rms_s, tid);
         } else if (tid == 0) {
             s_ok = 0;
         }
@@ -749,10 +750,13 @@ cudaError_t fused_decode_launch(const FusedDecodeParams& p0, int num_sms, cudaSt
     // a shared expert, or a router too large to stage: the wide kernel
     if (p0.Fs > 0) return wide_decode_launch(p0, num_sms, stream);
     FusedDecodeParams p = p0;
-    // the kernel instantiations: [split][weighted norm]
+    // the kernel instantiations: [split][weighted norm][one token]
     using Kernel = void (*)(FusedDecodeParams);
-    static const Kernel kernels[2][2] = {{moe_decode_fused_kernel<false, false>, moe_decode_fused_kernel<false, true>},
-                                         {moe_decode_fused_kernel<true, false>, moe_decode_fused_kernel<true, true>}};
+    static const Kernel kernels[2][2][2] = {
+        {{moe_decode_fused_kernel<false, false, 0>, moe_decode_fused_kernel<false, false, 1>},
+         {moe_decode_fused_kernel<false, true, 0>, moe_decode_fused_kernel<false, true, 1>}},
+        {{moe_decode_fused_kernel<true, false, 0>, moe_decode_fused_kernel<true, false, 1>},
+         {moe_decode_fused_kernel<true, true, 0>, moe_decode_fused_kernel<true, true, 1>}}};
     static int smem_optin[kMaxDevices] = {0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -765,13 +769,14 @@ cudaError_t fused_decode_launch(const FusedDecodeParams& p0, int num_sms, cudaSt
         // static __shared__ of the kernel (s_ok) comes out of the same budget
         v -= 1024;
         for (int s = 0; s < 2; ++s)
-            for (int w = 0; w < 2; ++w) {
-                e = cudaFuncSetAttribute(kernels[s][w], cudaFuncAttributeMaxDynamicSharedMemorySize, v);
-                if (e != cudaSuccess) return e;
-            }
+            for (int w = 0; w < 2; ++w)
+                for (int t = 0; t < 2; ++t) {
+                    e = cudaFuncSetAttribute(kernels[s][w][t], cudaFuncAttributeMaxDynamicSharedMemorySize, v);
+                    if (e != cudaSuccess) return e;
+                }
         smem_optin[dev] = v;
     }
-    const int nw = p.norm_w ? 1 : 0;
+    const int nw = p.norm_w ? 1 : 0, one = p.T == 1 ? 1 : 0;
     // The smallest router split R (1, then 2 when GLC_FUSED_RSPLIT allows)
     // for which the layer fits and all grid / R clusters of R CTAs can be
     // resident at once (the grid barrier needs every CTA resident).  No split
@@ -784,7 +789,7 @@ cudaError_t fused_decode_launch(const FusedDecodeParams& p0, int num_sms, cudaSt
     for (; R <= GLC_FUSED_RSPLIT; R <<= 1) {
         p.rsplit = R;
         if (fused_decode_configure(p, num_sms, (size_t)smem_optin[dev], &smem, &grid) != 0) continue;
-        if (R == 1 || (grid % R == 0 && clusters_fit((const void*)kernels[1][nw], dev, R, smem, grid))) break;
+        if (R == 1 || (grid % R == 0 && clusters_fit((const void*)kernels[1][nw][one], dev, R, smem, grid))) break;
     }
     if (R > GLC_FUSED_RSPLIT) return wide_decode_launch(p0, num_sms, stream);  // cudaErrorNotSupported when that does not fit either
     cudaLaunchConfig_t cfg{};
@@ -806,7 +811,7 @@ cudaError_t fused_decode_launch(const FusedDecodeParams& p0, int num_sms, cudaSt
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = R > 1 ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, kernels[R > 1 ? 1 : 0][nw], p);
+    return cudaLaunchKernelEx(&cfg, kernels[R > 1 ? 1 : 0][nw][one], p);
 }
 
 }  // namespace glc
