@@ -137,12 +137,12 @@ __device__ __forceinline__ void st_cluster_f32(const float* local, uint32_t rank
 // completes the tree from the two subtree values (logits_from_halves).
 // Threads 128..255 write the normalised input of the d this CTA's partials
 // do not visit.
-template <bool NW, int TT>
+template <bool NW, int TT, int EE>
 __device__ void router_logits_split(const FusedDecodeParams& p, const float* Wl, const float* xr, float* xs,
                                     float* red, float* lh, const float* rms_s, int tid, int rank) {
     constexpr int R = 2, NL = kRouterWidth / R;
     const int warp = tid >> 5, lane = tid & 31;
-    const int D = p.D, E = p.E, T = TT ? TT : p.T, U = D >> 6;
+    const int D = p.D, E = EE ? EE : p.E, T = TT ? TT : p.T, U = D >> 6;
     if (tid >= NL) {
         const int t2 = tid - NL, o = t2 < rank * NL ? t2 : t2 + NL;  // the d this CTA's partials skip
         for (int t = 0; t < T; ++t) {
@@ -208,11 +208,11 @@ __device__ __forceinline__ float logits_from_halves(const float* c) { return c[0
 // router.cu (256 strided fused partials over the normalised input, warp
 // butterfly, pairwise tree over the 8 warp sums), eight experts per pass; the
 // first pass also writes the normalised input to xs (xs_index layout).
-template <bool NW, int TT>
+template <bool NW, int TT, int EE>
 __device__ void router_logits(const FusedDecodeParams& p, const float* Wr, const float* xr, float* xs,
                               float* red, float* logit, const float* rms_s, int tid) {
     const int warp = tid >> 5, lane = tid & 31;
-    const int D = p.D, E = p.E, T = TT ? TT : p.T, U = D >> 6;
+    const int D = p.D, E = EE ? EE : p.E, T = TT ? TT : p.T, U = D >> 6;
     // At E = 8 rows are 32 B apart across lanes; lanes 4..7 of each 8 read
     // their second half first so one 16-byte read covers all banks.
     const int h = (E == 8) ? ((lane >> 2) & 1) : 0;
@@ -265,9 +265,10 @@ __device__ void router_logits(const FusedDecodeParams& p, const float* Wr, const
 // kernel's repeated arg-max in router.cu; the weights use the same expf
 // arguments and the same sequential fp32 sums, so ids and weights are
 // bit-identical to it.  ex holds E floats of scratch.
+template <int KK, int EE>
 __device__ void topk_token_warp(const FusedDecodeParams& p, const float* l, int t, int* s_ids, float* s_w,
                                 float* ex, int lane) {
-    const int E = p.E, k = p.k;
+    const int E = EE ? EE : p.E, k = KK ? KK : p.k;
     const int e0 = lane, e1 = lane + 32;
     const float v0 = (e0 < E && !isnan(l[e0])) ? l[e0] : -INFINITY;
     const float v1 = (e1 < E && !isnan(l[e1])) ? l[e1] : -INFINITY;
@@ -301,12 +302,13 @@ __device__ void topk_token_warp(const FusedDecodeParams& p, const float* l, int 
 }
 
 // SPLIT: the router split over a 2-CTA cluster (launched with clusters of
-// two); NW: weighted RMSNorm (p.norm_w set); TT: the token count when it is
-// known at compile time (1: one decode token), 0 = p.T.  Separate
-// instantiations keep the unsplit, unweighted kernel's code exactly what it
-// is without them (measured: folding the split and the weighted norm in as
-// runtime branches cost 1.6 us per launch at the Mixtral-8x7B shape).
-template <bool SPLIT, bool NW, int TT>
+// two); NW: weighted RMSNorm (p.norm_w set); TT, KK, EE: the token count,
+// top-k and expert count when they are known at compile time, 0 = from p.
+// Separate instantiations keep the unsplit, unweighted kernel's code exactly
+// what it is without them (measured: folding the split and the weighted norm
+// in as runtime branches cost 1.6 us per launch at the Mixtral-8x7B shape;
+// the one-token instantiation saved 0.5 us).
+template <bool SPLIT, bool NW, int TT, int KK, int EE>
 __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(const __grid_constant__ FusedDecodeParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int s_ok, s_okx, s_okw;
@@ -326,7 +328,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
     uint64_t* go_bar = wbar + 1;  // the producer has issued its first ring's worth of stages
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int T = TT ? TT : p.T, D = p.D, F = p.F, k = p.k, P = T * k;
+    const int T = TT ? TT : p.T, D = p.D, F = p.F, k = KK ? KK : p.k, P = T * k, E = EE ? EE : p.E;
     const uint64_t lim = p.wait_limit_ns > 0 ? (uint64_t)p.wait_limit_ns : kWaitLimitNs;
     const int slot = p.slot_bytes;
     constexpr int R = SPLIT ? 2 : 1;  // router split over a cluster of R CTAs
@@ -355,7 +357,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
     // this CTA's router rows: all of them, or under the split the NL = 256/R
     // rows r*NL .. of every 256 (see router_logits_split), a multiple of 256 B
     const int rank = R > 1 ? (int)cluster_rank() : 0;
-    const uint32_t wb = (uint32_t)D * p.E * 4u / (uint32_t)R;
+    const uint32_t wb = (uint32_t)D * E * 4u / (uint32_t)R;
     const float* xraw = reinterpret_cast<const float*>(smem + wb);
     if (tid == 0) {
         const uint32_t xb = (uint32_t)T * D * 4u;
@@ -365,9 +367,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
                 bulk_g2s_nohint(smem, p.Wr, wb, wbar);
             } else {
                 const int NL = kRouterWidth / R;
-                const uint32_t blk = (uint32_t)NL * p.E * 4u;
+                const uint32_t blk = (uint32_t)NL * E * 4u;
                 for (int i = 0; i < (D >> 8); ++i)
-                    bulk_g2s_nohint(smem + (size_t)i * blk, p.Wr + ((size_t)i * kRouterWidth + (size_t)rank * NL) * p.E,
+                    bulk_g2s_nohint(smem + (size_t)i * blk, p.Wr + ((size_t)i * kRouterWidth + (size_t)rank * NL) * E,
                                     blk, wbar);
             }
         };
@@ -428,9 +430,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
         named_bar_sync(2, kRouterWidth);
         if (okx && s_okw != 0) {
             if (R > 1)
-                router_logits_split<NW, TT>(p, reinterpret_cast<const float*>(smem), xraw, xs, red, lh, rms_s, tid, rank);
+                router_logits_split<NW, TT, EE>(p, reinterpret_cast<const float*>(smem), xraw, xs, red, lh, rms_s, tid, rank);
             else
-                router_logits<NW, TT>(p, reinterpret_cast<const float*>(smem), xraw, xs, red, logit, rms_s, tid);
+                router_logits<NW, TT, EE>(p, reinterpret_cast<const float*>(smem), xraw, xs, red, logit, rms_s, tid);
         } else if (tid == 0) {
             s_ok = 0;
         }
@@ -448,11 +450,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
     const bool staged = s_ok != 0;
     if (staged && warp < T) {
         if (R > 1) {
-            for (int e = lane; e < p.E; e += 32)
-                logit[warp * p.E + e] = logits_from_halves(lh + (size_t)(warp * p.E + e) * R);
+            for (int e = lane; e < E; e += 32)
+                logit[warp * E + e] = logits_from_halves(lh + (size_t)(warp * E + e) * R);
             __syncwarp();
         }
-        topk_token_warp(p, logit + warp * p.E, warp, s_ids, s_w, red + warp * 64, lane);
+        topk_token_warp<KK, EE>(p, logit + warp * E, warp, s_ids, s_w, red + warp * 64, lane);
     }
     __syncthreads();
     if (!staged) {  // uniform: every thread read the same s_ok
@@ -487,7 +489,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
                 const int buf = sidx % S;
                 const uint32_t ph = (uint32_t)(sidx / S) & 1u;
                 if (!mbar_wait_spin(&empty[buf], ph ^ 1u, p.err, kDevTimeoutEmpty, lim)) { ok = false; return; }
-                const int e = clamp_expert(s_ids[seg], p.E);
+                const int e = clamp_expert(s_ids[seg], E);
                 const size_t off = (size_t)e * p.gu_expert_bytes + (size_t)rin * rbG;
                 const uint32_t bytes = (uint32_t)(nr * rbG);
                 uint8_t* dst = smem + (size_t)buf * slot;
@@ -510,7 +512,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
                 const uint32_t bytes = (uint32_t)(nr * rbD);
                 mbar_arrive_expect_tx(&full[buf], bytes * ncp);
                 for (int c = 0; c < ncp; ++c) {
-                    const int e = clamp_expert(s_ids[seg * k + j + c], p.E);
+                    const int e = clamp_expert(s_ids[seg * k + j + c], E);
                     bulk_g2s(smem + (size_t)buf * slot + (size_t)c * p.dn_R * rbD,
                              p.down + (size_t)e * p.dn_expert_bytes + (size_t)rin * rbD, bytes, &full[buf], pol);
                 }
@@ -753,10 +755,12 @@ cudaError_t fused_decode_launch(const FusedDecodeParams& p0, int num_sms, cudaSt
     // the kernel instantiations: [split][weighted norm][one token]
     using Kernel = void (*)(FusedDecodeParams);
     static const Kernel kernels[2][2][2] = {
-        {{moe_decode_fused_kernel<false, false, 0>, moe_decode_fused_kernel<false, false, 1>},
-         {moe_decode_fused_kernel<false, true, 0>, moe_decode_fused_kernel<false, true, 1>}},
-        {{moe_decode_fused_kernel<true, false, 0>, moe_decode_fused_kernel<true, false, 1>},
-         {moe_decode_fused_kernel<true, true, 0>, moe_decode_fused_kernel<true, true, 1>}}};
+        {{moe_decode_fused_kernel<false, false, 0, 0, 0>, moe_decode_fused_kernel<false, false, 1, 0, 0>},
+         {moe_decode_fused_kernel<false, true, 0, 0, 0>, moe_decode_fused_kernel<false, true, 1, 0, 0>}},
+        {{moe_decode_fused_kernel<true, false, 0, 0, 0>, moe_decode_fused_kernel<true, false, 1, 0, 0>},
+         {moe_decode_fused_kernel<true, true, 0, 0, 0>, moe_decode_fused_kernel<true, true, 1, 0, 0>}}};
+    // Mixtral-style decode (one token, top-2 of 8 experts, unsplit, unweighted norm)
+    static const Kernel mixtral_decode = moe_decode_fused_kernel<false, false, 1, 2, 8>;
     static int smem_optin[kMaxDevices] = {0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -774,6 +778,8 @@ cudaError_t fused_decode_launch(const FusedDecodeParams& p0, int num_sms, cudaSt
                     e = cudaFuncSetAttribute(kernels[s][w][t], cudaFuncAttributeMaxDynamicSharedMemorySize, v);
                     if (e != cudaSuccess) return e;
                 }
+        e = cudaFuncSetAttribute(mixtral_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, v);
+        if (e != cudaSuccess) return e;
         smem_optin[dev] = v;
     }
     const int nw = p.norm_w ? 1 : 0, one = p.T == 1 ? 1 : 0;
@@ -811,7 +817,8 @@ cudaError_t fused_decode_launch(const FusedDecodeParams& p0, int num_sms, cudaSt
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = R > 1 ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, kernels[R > 1 ? 1 : 0][nw][one], p);
+    const bool mix = R == 1 && !nw && p.T == 1 && p.k == 2 && p.E == 8;
+    return cudaLaunchKernelEx(&cfg, mix ? mixtral_decode : kernels[R > 1 ? 1 : 0][nw][one], p);
 }
 
 }  // namespace glc
