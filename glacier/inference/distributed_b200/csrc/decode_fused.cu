@@ -66,10 +66,10 @@ __device__ __forceinline__ int xs_index(int d, int U) {
 // RMSNorm scale of every token, threads 0..255, from the raw input xr [T][D]:
 // canonical sum of squares (256 strided fused partials, warp butterfly,
 // pairwise tree over the 8 warp sums), then 1 / sqrt(ss / D + eps).
-template <bool NW, int TT>
+template <bool NW, int TT, int DD>
 __device__ void router_rms(const FusedDecodeParams& p, const float* xr, float* red, float* rms_s, int tid) {
     const int warp = tid >> 5, lane = tid & 31;
-    const int D = p.D, T = TT ? TT : p.T;
+    const int D = DD ? DD : p.D, T = TT ? TT : p.T;
     float a[kFusedMaxTokens];
 #pragma unroll
     for (int t = 0; t < kFusedMaxTokens; ++t) a[t] = 0.f;
@@ -137,12 +137,12 @@ __device__ __forceinline__ void st_cluster_f32(const float* local, uint32_t rank
 // completes the tree from the two subtree values (logits_from_halves).
 // Threads 128..255 write the normalised input of the d this CTA's partials
 // do not visit.
-template <bool NW, int TT, int EE>
+template <bool NW, int TT, int EE, int DD>
 __device__ void router_logits_split(const FusedDecodeParams& p, const float* Wl, const float* xr, float* xs,
                                     float* red, float* lh, const float* rms_s, int tid, int rank) {
     constexpr int R = 2, NL = kRouterWidth / R;
     const int warp = tid >> 5, lane = tid & 31;
-    const int D = p.D, E = EE ? EE : p.E, T = TT ? TT : p.T, U = D >> 6;
+    const int D = DD ? DD : p.D, E = EE ? EE : p.E, T = TT ? TT : p.T, U = D >> 6;
     if (tid >= NL) {
         const int t2 = tid - NL, o = t2 < rank * NL ? t2 : t2 + NL;  // the d this CTA's partials skip
         for (int t = 0; t < T; ++t) {
@@ -208,11 +208,11 @@ __device__ __forceinline__ float logits_from_halves(const float* c) { return c[0
 // router.cu (256 strided fused partials over the normalised input, warp
 // butterfly, pairwise tree over the 8 warp sums), eight experts per pass; the
 // first pass also writes the normalised input to xs (xs_index layout).
-template <bool NW, int TT, int EE>
+template <bool NW, int TT, int EE, int DD>
 __device__ void router_logits(const FusedDecodeParams& p, const float* Wr, const float* xr, float* xs,
                               float* red, float* logit, const float* rms_s, int tid) {
     const int warp = tid >> 5, lane = tid & 31;
-    const int D = p.D, E = EE ? EE : p.E, T = TT ? TT : p.T, U = D >> 6;
+    const int D = DD ? DD : p.D, E = EE ? EE : p.E, T = TT ? TT : p.T, U = D >> 6;
     // At E = 8 rows are 32 B apart across lanes; lanes 4..7 of each 8 read
     // their second half first so one 16-byte read covers all banks.
     const int h = (E == 8) ? ((lane >> 2) & 1) : 0;
@@ -302,13 +302,14 @@ __device__ void topk_token_warp(const FusedDecodeParams& p, const float* l, int 
 }
 
 // SPLIT: the router split over a 2-CTA cluster (launched with clusters of
-// two); NW: weighted RMSNorm (p.norm_w set); TT, KK, EE: the token count,
-// top-k and expert count when they are known at compile time, 0 = from p.
+// two); NW: weighted RMSNorm (p.norm_w set); TT, KK, EE, DD, FF: the token
+// count, top-k, expert count, hidden and expert widths when they are known at
+// compile time, 0 = from p (with D, F and k known, so is the lane layout).
 // Separate instantiations keep the unsplit, unweighted kernel's code exactly
 // what it is without them (measured: folding the split and the weighted norm
 // in as runtime branches cost 1.6 us per launch at the Mixtral-8x7B shape;
 // the one-token instantiation saved 0.5 us).
-template <bool SPLIT, bool NW, int TT, int KK, int EE>
+template <bool SPLIT, bool NW, int TT, int KK, int EE, int DD, int FF>
 __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(const __grid_constant__ FusedDecodeParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int s_ok, s_okx, s_okw;
@@ -328,7 +329,18 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
     uint64_t* go_bar = wbar + 1;  // the producer has issued its first ring's worth of stages
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int T = TT ? TT : p.T, D = p.D, F = p.F, k = KK ? KK : p.k, P = T * k, E = EE ? EE : p.E;
+    const int T = TT ? TT : p.T, D = DD ? DD : p.D, F = FF ? FF : p.F, k = KK ? KK : p.k, P = T * k,
+              E = EE ? EE : p.E;
+    // lane layout: fused_decode_configure's values (its formulas, with
+    // stage_rows_for(2, G) = 2G and stage_rows_for(1, G) = 4G) when D, F and k
+    // are constants; read from p at each use otherwise
+    constexpr int kGuNsegw = DD ? ((DD >> 8) * 4 + 31) / 32 : 0;
+    constexpr int kGuG = DD ? kFusedConsumerWarps / kGuNsegw : 0;
+    constexpr int kGuR = DD ? 2 * kGuG : 0;
+    constexpr int kDnNsegw = FF ? ((FF >> 8) * 4 + 31) / 32 : 0;
+    constexpr int kDnG = FF ? kFusedConsumerWarps / kDnNsegw : 0;
+    constexpr int kDnSplit = (FF && KK) ? ((kDnG % KK) == 0 ? 1 : 0) : 0;
+    constexpr int kDnR = (FF && KK) ? (kDnSplit ? 4 * (kDnG / KK) : 4 * kDnG) : 0;
     const uint64_t lim = p.wait_limit_ns > 0 ? (uint64_t)p.wait_limit_ns : kWaitLimitNs;
     const int slot = p.slot_bytes;
     constexpr int R = SPLIT ? 2 : 1;  // router split over a cluster of R CTAs
@@ -425,14 +437,14 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
         if (!mbar_wait_spin(xbar, 0, p.err, kDevTimeoutFull, lim)) s_okx = 0;
         named_bar_sync(2, kRouterWidth);
         const bool okx = s_okx != 0;
-        if (okx && p.rmsnorm) router_rms<NW, TT>(p, xraw, red, rms_s, tid);
+        if (okx && p.rmsnorm) router_rms<NW, TT, DD>(p, xraw, red, rms_s, tid);
         if (okx && !mbar_wait_spin(wbar, 0, p.err, kDevTimeoutFull, lim)) s_okw = 0;
         named_bar_sync(2, kRouterWidth);
         if (okx && s_okw != 0) {
             if (R > 1)
-                router_logits_split<NW, TT, EE>(p, reinterpret_cast<const float*>(smem), xraw, xs, red, lh, rms_s, tid, rank);
+                router_logits_split<NW, TT, EE, DD>(p, reinterpret_cast<const float*>(smem), xraw, xs, red, lh, rms_s, tid, rank);
             else
-                router_logits<NW, TT, EE>(p, reinterpret_cast<const float*>(smem), xraw, xs, red, logit, rms_s, tid);
+                router_logits<NW, TT, EE, DD>(p, reinterpret_cast<const float*>(smem), xraw, xs, red, logit, rms_s, tid);
         } else if (tid == 0) {
             s_ok = 0;
         }
@@ -484,7 +496,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
             const uint64_t pol = l2_evict_first_policy();
             bool ok = true;
             int issued = 0;  // stages issued so far
-            const int nxt = for_each_stage_rows(F, 1, p.gu_R, g0, g1, 0, [&](int sidx, int seg, int, int rin, int nr, int) {
+            const int nxt = for_each_stage_rows(F, 1, (DD ? kGuR : p.gu_R), g0, g1, 0, [&](int sidx, int seg, int, int rin, int nr, int) {
                 if (!ok) return;
                 const int buf = sidx % S;
                 const uint32_t ph = (uint32_t)(sidx / S) & 1u;
@@ -495,7 +507,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
                 uint8_t* dst = smem + (size_t)buf * slot;
                 mbar_arrive_expect_tx(&full[buf], 2u * bytes);
                 bulk_g2s(dst, p.gate + off, bytes, &full[buf], pol);
-                bulk_g2s(dst + (size_t)p.gu_R * rbG, p.up + off, bytes, &full[buf], pol);
+                bulk_g2s(dst + (size_t)(DD ? kGuR : p.gu_R) * rbG, p.up + off, bytes, &full[buf], pol);
                 issued = sidx + 1;
                 if (sidx == S - 1) mbar_arrive(go_bar);
             });
@@ -503,8 +515,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
             // Down-projection stages: with the slot-split layout a stage holds the
             // same dn_R rows of all k selected experts (one copy each), else dn_R
             // rows of one expert.
-            const int nsl = p.dn_split ? 1 : k, ncp = p.dn_split ? k : 1;
-            for_each_stage_rows(D, nsl, p.dn_R, q0, q1, nxt, [&](int sidx, int seg, int j, int rin, int nr, int) {
+            const int nsl = ((FF && KK) ? kDnSplit : p.dn_split) ? 1 : k, ncp = ((FF && KK) ? kDnSplit : p.dn_split) ? k : 1;
+            for_each_stage_rows(D, nsl, ((FF && KK) ? kDnR : p.dn_R), q0, q1, nxt, [&](int sidx, int seg, int j, int rin, int nr, int) {
                 if (!ok) return;
                 const int buf = sidx % S;
                 const uint32_t ph = (uint32_t)(sidx / S) & 1u;
@@ -513,7 +525,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
                 mbar_arrive_expect_tx(&full[buf], bytes * ncp);
                 for (int c = 0; c < ncp; ++c) {
                     const int e = clamp_expert(s_ids[seg * k + j + c], E);
-                    bulk_g2s(smem + (size_t)buf * slot + (size_t)c * p.dn_R * rbD,
+                    bulk_g2s(smem + (size_t)buf * slot + (size_t)c * ((FF && KK) ? kDnR : p.dn_R) * rbD,
                              p.down + (size_t)e * p.dn_expert_bytes + (size_t)rin * rbD, bytes, &full[buf], pol);
                 }
                 issued = sidx + 1;
@@ -531,7 +543,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
     bool ok = true;
     int nxt;
     {  // ---- 2. gate/up + SwiGLU
-        const int nsegw = p.gu_nsegw, G = p.gu_G;
+        const int nsegw = (DD ? kGuNsegw : p.gu_nsegw), G = (DD ? kGuG : p.gu_G);
         const bool wact = warp < nsegw * G;  // warps outside the layout only pace the ring
         const int segw = warp % nsegw, grp = warp / nsegw;
         const int u = segw * 32 + lane;
@@ -543,7 +555,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
         // are out: their shared-memory traffic would otherwise hold up the
         // producer's barrier and copy operations at the start of the stream.
         if (!mbar_wait_spin(go_bar, 0, p.err, kDevTimeoutFull, lim)) ok = false;
-        nxt = for_each_stage_rows(F, 1, p.gu_R, g0, g1, 0, [&](int sidx, int seg, int, int, int nr, int lr0) {
+        nxt = for_each_stage_rows(F, 1, (DD ? kGuR : p.gu_R), g0, g1, 0, [&](int sidx, int seg, int, int, int nr, int lr0) {
             if (!ok) return;
             const int t = seg / k;
             if (t != cur) {
@@ -554,7 +566,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
             const uint32_t ph = (uint32_t)(sidx / S) & 1u;
             if (!mbar_wait_spin(&full[buf], ph, p.err, kDevTimeoutFull, lim)) { ok = false; return; }
             if (wact)
-                consume_stage(smem + (size_t)buf * slot, nr, p.gu_R, 2, G, grp, rbG, sb, c, active, xr, lane,
+                consume_stage(smem + (size_t)buf * slot, nr, (DD ? kGuR : p.gu_R), 2, G, grp, rbG, sb, c, active, xr, lane,
                               [&](int i, int m, float v) { pgu[((size_t)(lr0 + i) * 2 + m) * nsegw + segw] = v; });
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[buf]);
@@ -563,7 +575,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
     if (!ok) s_ok = 0;
     named_bar_sync(1, NT);
     {
-        const int nsegw = p.gu_nsegw;
+        const int nsegw = (DD ? kGuNsegw : p.gu_nsegw);
         for (int lr = tid; lr < g1 - g0; lr += NT) {
             const int g = g0 + lr, seg = g / F, rin = g - seg * F;
             const float* pp = pgu + (size_t)lr * 2 * nsegw;
@@ -591,21 +603,21 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
     }
 
     {  // ---- 4. down projection, all k slots of each row, then the combine
-        const int nsegw = p.dn_nsegw, G = p.dn_G;
+        const int nsegw = (FF ? kDnNsegw : p.dn_nsegw), G = (FF ? kDnG : p.dn_G);
         const bool wact = warp < nsegw * G;
         const int segw = warp % nsegw, grp = warp / nsegw;
         // slot-split layout: group grp works on slot grp % k of every stage
         // (its activations loaded once per token), as group grp / k of G / k
-        const int js = p.dn_split ? grp % k : 0;
-        const int Gs = p.dn_split ? G / k : G, gs = p.dn_split ? grp / k : grp;
+        const int js = ((FF && KK) ? kDnSplit : p.dn_split) ? grp % k : 0;
+        const int Gs = ((FF && KK) ? kDnSplit : p.dn_split) ? G / k : G, gs = ((FF && KK) ? kDnSplit : p.dn_split) ? grp / k : grp;
         const int u = segw * 32 + lane;
         const bool active = wact && u < (F >> 8) * 4;
         const int sb = active ? (u >> 2) : 0, c = u & 3;
         XRegs xr;
         int cur = -1;
-        for_each_stage_rows(D, p.dn_split ? 1 : k, p.dn_R, q0, q1, nxt, [&](int sidx, int seg, int j0, int, int nr, int lr0) {
+        for_each_stage_rows(D, ((FF && KK) ? kDnSplit : p.dn_split) ? 1 : k, ((FF && KK) ? kDnR : p.dn_R), q0, q1, nxt, [&](int sidx, int seg, int j0, int, int nr, int lr0) {
             if (!ok) return;
-            const int j = p.dn_split ? js : j0;
+            const int j = ((FF && KK) ? kDnSplit : p.dn_split) ? js : j0;
             const int pair = seg * k + j;
             if (pair != cur) {
                 load_x<kXGlobalCG>(xr, reinterpret_cast<const float4*>(p.act + (size_t)pair * F) + u, F >> 6, active);
@@ -614,9 +626,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
             const int buf = sidx % S;
             const uint32_t ph = (uint32_t)(sidx / S) & 1u;
             if (!mbar_wait_spin(&full[buf], ph, p.err, kDevTimeoutFull, lim)) { ok = false; return; }
-            const uint8_t* st = smem + (size_t)buf * slot + (p.dn_split ? (size_t)j * p.dn_R * rbD : 0);
+            const uint8_t* st = smem + (size_t)buf * slot + (((FF && KK) ? kDnSplit : p.dn_split) ? (size_t)j * ((FF && KK) ? kDnR : p.dn_R) * rbD : 0);
             if (wact)
-                consume_stage(st, nr, p.dn_R, 1, Gs, gs, rbD, sb, c, active, xr, lane,
+                consume_stage(st, nr, ((FF && KK) ? kDnR : p.dn_R), 1, Gs, gs, rbD, sb, c, active, xr, lane,
                               [&](int i, int, float v) { pdn[((size_t)(lr0 + i) * k + j) * nsegw + segw] = v; });
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[buf]);
@@ -629,7 +641,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
         return;
     }
     {
-        const int nsegw = p.dn_nsegw;
+        const int nsegw = (FF ? kDnNsegw : p.dn_nsegw);
         for (int lr = tid; lr < q1 - q0; lr += NT) {
             const int g = q0 + lr, t = g / D, rin = g - t * D;
             const size_t o = (size_t)t * D + rin;
@@ -755,12 +767,14 @@ cudaError_t fused_decode_launch(const FusedDecodeParams& p0, int num_sms, cudaSt
     // the kernel instantiations: [split][weighted norm][one token]
     using Kernel = void (*)(FusedDecodeParams);
     static const Kernel kernels[2][2][2] = {
-        {{moe_decode_fused_kernel<false, false, 0, 0, 0>, moe_decode_fused_kernel<false, false, 1, 0, 0>},
-         {moe_decode_fused_kernel<false, true, 0, 0, 0>, moe_decode_fused_kernel<false, true, 1, 0, 0>}},
-        {{moe_decode_fused_kernel<true, false, 0, 0, 0>, moe_decode_fused_kernel<true, false, 1, 0, 0>},
-         {moe_decode_fused_kernel<true, true, 0, 0, 0>, moe_decode_fused_kernel<true, true, 1, 0, 0>}}};
-    // Mixtral-style decode (one token, top-2 of 8 experts, unsplit, unweighted norm)
-    static const Kernel mixtral_decode = moe_decode_fused_kernel<false, false, 1, 2, 8>;
+        {{moe_decode_fused_kernel<false, false, 0, 0, 0, 0, 0>, moe_decode_fused_kernel<false, false, 1, 0, 0, 0, 0>},
+         {moe_decode_fused_kernel<false, true, 0, 0, 0, 0, 0>, moe_decode_fused_kernel<false, true, 1, 0, 0, 0, 0>}},
+        {{moe_decode_fused_kernel<true, false, 0, 0, 0, 0, 0>, moe_decode_fused_kernel<true, false, 1, 0, 0, 0, 0>},
+         {moe_decode_fused_kernel<true, true, 0, 0, 0, 0, 0>, moe_decode_fused_kernel<true, true, 1, 0, 0, 0, 0>}}};
+    // Mixtral-8x7B decode (one token, top-2 of 8 experts, D = 4096, F = 14336,
+    // unsplit, unweighted norm) and the same routing at other widths
+    static const Kernel mixtral_decode = moe_decode_fused_kernel<false, false, 1, 2, 8, 4096, 14336>;
+    static const Kernel top2of8_decode = moe_decode_fused_kernel<false, false, 1, 2, 8, 0, 0>;
     static int smem_optin[kMaxDevices] = {0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -778,8 +792,10 @@ cudaError_t fused_decode_launch(const FusedDecodeParams& p0, int num_sms, cudaSt
                     e = cudaFuncSetAttribute(kernels[s][w][t], cudaFuncAttributeMaxDynamicSharedMemorySize, v);
                     if (e != cudaSuccess) return e;
                 }
-        e = cudaFuncSetAttribute(mixtral_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, v);
-        if (e != cudaSuccess) return e;
+        for (Kernel kf : {mixtral_decode, top2of8_decode}) {
+            e = cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, v);
+            if (e != cudaSuccess) return e;
+        }
         smem_optin[dev] = v;
     }
     const int nw = p.norm_w ? 1 : 0, one = p.T == 1 ? 1 : 0;
@@ -817,8 +833,11 @@ cudaError_t fused_decode_launch(const FusedDecodeParams& p0, int num_sms, cudaSt
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = R > 1 ? 2 : 1;
-    const bool mix = R == 1 && !nw && p.T == 1 && p.k == 2 && p.E == 8;
-    return cudaLaunchKernelEx(&cfg, mix ? mixtral_decode : kernels[R > 1 ? 1 : 0][nw][one], p);
+    const bool top2of8 = R == 1 && !nw && p.T == 1 && p.k == 2 && p.E == 8;
+    // (and only when the configured lane layout is the one it has built in)
+    const bool mix = top2of8 && p.D == 4096 && p.F == 14336 && p.gu_nsegw == 2 && p.gu_G == 7 && p.gu_R == 14 &&
+                     p.dn_nsegw == 7 && p.dn_G == 2 && p.dn_split == 1 && p.dn_R == 4;
+    return cudaLaunchKernelEx(&cfg, mix ? mixtral_decode : top2of8 ? top2of8_decode : kernels[R > 1 ? 1 : 0][nw][one], p);
 }
 
 }  // namespace glc
