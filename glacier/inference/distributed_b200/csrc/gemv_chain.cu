@@ -45,15 +45,21 @@ constexpr int kNormSlots = 32;                          // per-warp sums of x^2 
 // dependent job until the consumers hold its input, or prefetching the
 // stages beyond the ring into L2 so that HBM keeps streaming through the
 // wait, made both GEMV shapes slower; the ring runs free.)
+// KK, OPK: every job's K and op when the launch's jobs share them (known at
+// compile time: the lane layout and loop bounds become constants), 0 / -1 =
+// each job's own.
+template <int KK, int OPK>
 __device__ __forceinline__ void job_layout(const GemvJob& jb, int& nsegw, int& G, int& R, int& NM, int& rowBytes) {
-    const int U = (jb.K >> 8) * 4;
+    const int K = KK ? KK : jb.K;
+    const int U = (K >> 8) * 4;
     nsegw = (U + 31) / 32;
     G = kChainWarps / nsegw;
-    NM = (jb.op == kChainGateUp) ? 2 : 1;
+    NM = ((OPK >= 0 ? OPK : (int)jb.op) == kChainGateUp) ? 2 : 1;
     R = stage_rows_for(NM, G);
-    rowBytes = (jb.K >> 8) * 144;
+    rowBytes = (K >> 8) * 144;
 }
 
+template <int KK, int OPK>
 __global__ void __launch_bounds__(kChainThreads, 1) q4k_gemv_chain_kernel(const __grid_constant__ GemvChainParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int S = p.stages;
@@ -87,7 +93,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) q4k_gemv_chain_kernel(const 
             for (int j = 0; j < p.njobs && ok; ++j) {
                 const GemvJob& jb = p.jobs[j];
                 int nsegw, G, R, NM, rowBytes;
-                job_layout(jb, nsegw, G, R, NM, rowBytes);
+                job_layout<KK, OPK>(jb, nsegw, G, R, NM, rowBytes);
                 const int r0 = (int)((long long)jb.N * blockIdx.x / gridDim.x);
                 const int r1 = (int)((long long)jb.N * (blockIdx.x + 1) / gridDim.x);
                 for (int c = r0; c < r1 && ok; c += R) {
@@ -116,7 +122,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) q4k_gemv_chain_kernel(const 
     for (int j = 0; j < p.njobs; ++j) {
         const GemvJob& jb = p.jobs[j];
         int nsegw, G, R, NM, rowBytes;
-        job_layout(jb, nsegw, G, R, NM, rowBytes);
+        job_layout<KK, OPK>(jb, nsegw, G, R, NM, rowBytes);
         const int r0 = (int)((long long)jb.N * blockIdx.x / gridDim.x);
         const int r1 = (int)((long long)jb.N * (blockIdx.x + 1) / gridDim.x);
         // the previous job's epilogue has read the region (partial sums)
@@ -129,19 +135,19 @@ __global__ void __launch_bounds__(kChainThreads, 1) q4k_gemv_chain_kernel(const 
         }
         const int segw = warp % nsegw, grp = warp / nsegw;
         const bool in_layout = grp < G;
-        const int U = (jb.K >> 8) * 4;
+        const int U = ((KK ? KK : jb.K) >> 8) * 4;
         const int u = segw * 32 + lane;
         const bool active = in_layout && u < U;
         const int sb = active ? (u >> 2) : 0, c = u & 3;
         XRegs xr;
-        stage_x_shared<kXGlobalCG>(jb.x, jb.norm_w, jb.K, xs, nss, threadIdx.x, kChainWarps * 32);
+        stage_x_shared<kXGlobalCG>(jb.x, jb.norm_w, (KK ? KK : jb.K), xs, nss, threadIdx.x, kChainWarps * 32);
         named_bar_sync(1, kChainWarps * 32);
         read_x_shared(xr, xs, U, u, active);
         float rinv = 1.0f;
         if (jb.norm_w) {
             float ss = 0.f;
             for (int q = 0; q < kChainWarps; ++q) ss += nss[q];
-            rinv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)jb.K), jb.norm_eps)));
+            rinv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)(KK ? KK : jb.K)), jb.norm_eps)));
         }
         named_bar_sync(1, kChainWarps * 32);  // every lane holds its input: the region takes partial sums now
         for (int c0 = r0; c0 < r1; c0 += R) {
@@ -178,7 +184,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) q4k_gemv_chain_kernel(const 
                     for (int q = 0; q < nsegw; ++q) s += pp[q];
                     if (jb.norm_w) s = __fmul_rn(s, rinv);
                     // y += W x as the down-combine epilogue with one unit-weight slot: (s * 1) + y
-                    jb.y[row] = (jb.op == kChainAdd) ? __fadd_rn(__fmul_rn(s, 1.0f), jb.y[row]) : s;
+                    jb.y[row] = ((OPK >= 0 ? OPK : (int)jb.op) == kChainAdd) ? __fadd_rn(__fmul_rn(s, 1.0f), jb.y[row]) : s;
                 }
             }
         }
@@ -224,6 +230,29 @@ int gemv_chain_configure(GemvChainParams& p, int grid, size_t smem_limit, size_t
     return 0;
 }
 
+namespace {
+using Kernel = void (*)(GemvChainParams);
+// the generic kernel, and instantiations for launches whose jobs all share
+// one (K, op): the Q4_K GEMV at K = 4096 (Mixtral gate/up rows), 14336
+// (Mixtral down rows) and 6144 (Mixtral-8x22B projections)
+const Kernel kChainGeneric = q4k_gemv_chain_kernel<0, -1>;
+const Kernel kChainK4096Set = q4k_gemv_chain_kernel<4096, kChainSet>;
+const Kernel kChainK14336Set = q4k_gemv_chain_kernel<14336, kChainSet>;
+const Kernel kChainK6144Set = q4k_gemv_chain_kernel<6144, kChainSet>;
+const Kernel kChainK6144Add = q4k_gemv_chain_kernel<6144, kChainAdd>;
+
+Kernel pick_chain_kernel(const GemvChainParams& p) {
+    const int K = p.jobs[0].K, op = p.jobs[0].op;
+    for (int j = 1; j < p.njobs; ++j)
+        if (p.jobs[j].K != K || p.jobs[j].op != op) return kChainGeneric;
+    if (op == kChainSet && K == 4096) return kChainK4096Set;
+    if (op == kChainSet && K == 14336) return kChainK14336Set;
+    if (op == kChainSet && K == 6144) return kChainK6144Set;
+    if (op == kChainAdd && K == 6144) return kChainK6144Add;
+    return kChainGeneric;
+}
+}  // namespace
+
 cudaError_t gemv_chain_launch(GemvChainParams p, int num_sms, cudaStream_t stream) {
     int dev = 0;
     cudaGetDevice(&dev);
@@ -232,8 +261,10 @@ cudaError_t gemv_chain_launch(GemvChainParams p, int num_sms, cudaStream_t strea
     if (smem_optin[dev] == 0) {
         int v = 0;
         cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-        cudaError_t e = cudaFuncSetAttribute(q4k_gemv_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, v);
-        if (e != cudaSuccess) return e;
+        for (Kernel kf : {kChainGeneric, kChainK4096Set, kChainK14336Set, kChainK6144Set, kChainK6144Add}) {
+            cudaError_t e = cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, v);
+            if (e != cudaSuccess) return e;
+        }
         smem_optin[dev] = v;
     }
     size_t smem = 0;
@@ -250,7 +281,7 @@ cudaError_t gemv_chain_launch(GemvChainParams p, int num_sms, cudaStream_t strea
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, q4k_gemv_chain_kernel, p);
+    return cudaLaunchKernelEx(&cfg, pick_chain_kernel(p), p);
 }
 
 }  // namespace glc
