@@ -663,6 +663,17 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
 
 size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
 
+// Whether the configured launch has widths D, F and the lane layout that an
+// instantiation with those widths (and p.k) derives at compile time.
+bool layout_is(const FusedDecodeParams& p, int D, int F) {
+    if (p.D != D || p.F != F || p.k < 1) return false;
+    const int gn = ((D >> 8) * 4 + 31) / 32, gG = kFusedConsumerWarps / gn;
+    const int dn = ((F >> 8) * 4 + 31) / 32, dG = kFusedConsumerWarps / dn;
+    const int split = (dG % p.k == 0) ? 1 : 0;
+    return p.gu_nsegw == gn && p.gu_G == gG && p.gu_R == 2 * gG && p.dn_nsegw == dn && p.dn_G == dG &&
+           p.dn_split == split && p.dn_R == (split ? 4 * (dG / p.k) : 4 * dG);
+}
+
 // Whether grid / R clusters of R CTAs (kernel fn, smem bytes each) can all
 // be resident at once; cached per device and shared-memory size.
 bool clusters_fit(const void* fn, int dev, int R, size_t smem, int grid) {
@@ -772,9 +783,12 @@ cudaError_t fused_decode_launch(const FusedDecodeParams& p0, int num_sms, cudaSt
         {{moe_decode_fused_kernel<true, false, 0, 0, 0, 0, 0>, moe_decode_fused_kernel<true, false, 1, 0, 0, 0, 0>},
          {moe_decode_fused_kernel<true, true, 0, 0, 0, 0, 0>, moe_decode_fused_kernel<true, true, 1, 0, 0, 0, 0>}}};
     // Mixtral-8x7B decode (one token, top-2 of 8 experts, D = 4096, F = 14336,
-    // unsplit, unweighted norm) and the same routing at other widths
+    // unsplit, unweighted norm), the same routing at other widths, and a
+    // Mixtral-8x22B decoder layer's feed-forward (D = 6144, F = 16384: the
+    // router split, the weighted norm)
     static const Kernel mixtral_decode = moe_decode_fused_kernel<false, false, 1, 2, 8, 4096, 14336>;
     static const Kernel top2of8_decode = moe_decode_fused_kernel<false, false, 1, 2, 8, 0, 0>;
+    static const Kernel mixtral22b_ffn = moe_decode_fused_kernel<true, true, 1, 2, 8, 6144, 16384>;
     static int smem_optin[kMaxDevices] = {0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -792,7 +806,7 @@ cudaError_t fused_decode_launch(const FusedDecodeParams& p0, int num_sms, cudaSt
                     e = cudaFuncSetAttribute(kernels[s][w][t], cudaFuncAttributeMaxDynamicSharedMemorySize, v);
                     if (e != cudaSuccess) return e;
                 }
-        for (Kernel kf : {mixtral_decode, top2of8_decode}) {
+        for (Kernel kf : {mixtral_decode, top2of8_decode, mixtral22b_ffn}) {
             e = cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, v);
             if (e != cudaSuccess) return e;
         }
@@ -833,11 +847,14 @@ cudaError_t fused_decode_launch(const FusedDecodeParams& p0, int num_sms, cudaSt
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = R > 1 ? 2 : 1;
-    const bool top2of8 = R == 1 && !nw && p.T == 1 && p.k == 2 && p.E == 8;
-    // (and only when the configured lane layout is the one it has built in)
-    const bool mix = top2of8 && p.D == 4096 && p.F == 14336 && p.gu_nsegw == 2 && p.gu_G == 7 && p.gu_R == 14 &&
-                     p.dn_nsegw == 7 && p.dn_G == 2 && p.dn_split == 1 && p.dn_R == 4;
-    return cudaLaunchKernelEx(&cfg, mix ? mixtral_decode : top2of8 ? top2of8_decode : kernels[R > 1 ? 1 : 0][nw][one], p);
+    const bool top2of8 = p.T == 1 && p.k == 2 && p.E == 8;
+    // (a fixed-width instantiation only when the configured lane layout is the one it has built in)
+    Kernel kf = kernels[R > 1 ? 1 : 0][nw][one];
+    if (top2of8 && R == 1 && !nw)
+        kf = layout_is(p, 4096, 14336) ? mixtral_decode : top2of8_decode;
+    else if (top2of8 && R == 2 && nw && layout_is(p, 6144, 16384))
+        kf = mixtral22b_ffn;
+    return cudaLaunchKernelEx(&cfg, kf, p);
 }
 
 }  // namespace glc
