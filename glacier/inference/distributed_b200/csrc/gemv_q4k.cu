@@ -45,21 +45,28 @@
 
 namespace glc {
 
-template <bool SPLIT, class F>
-__device__ __forceinline__ void for_each_stage(const GemvParams& p, int r0, int r1, F&& f) {
-    for_each_stage_rows(p.rows, (p.mode == kGemvDownCombine && !SPLIT) ? p.kslots : 1, p.stage_rows, r0, r1, 0, f);
+template <bool SPLIT, bool FIX, class F>
+__device__ __forceinline__ void for_each_stage(const GemvParams& p, int R, int r0, int r1, F&& f) {
+    for_each_stage_rows(p.rows, (!FIX && p.mode == kGemvDownCombine && !SPLIT) ? p.kslots : 1, R, r0, r1, 0, f);
 }
 
 // SPLIT: the slot-split down layout (p.split); NORM: the folded RMSNorm
-// (p.norm_w); separate instantiations so the other modes keep their code.
-template <bool SPLIT, bool NORM>
+// (p.norm_w); KK > 0: a plain one-input launch with K = KK, whose mode, lane
+// layout and stage rows (gemv_configure's values) are then compile-time
+// constants; separate instantiations so the other modes keep their code.
+template <bool SPLIT, bool NORM, int KK>
 __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __grid_constant__ GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
-    const int NM = (p.mode == kGemvGateUp) ? 2 : 1;
-    const int NMP = (p.mode == kGemvGateUp) ? 2 : (p.mode == kGemvDownCombine ? p.kslots : 1);
+    constexpr bool FIX = KK > 0;
+    constexpr int kNsegw = FIX ? (((KK >> 8) * 4) + 31) / 32 : 0;
+    constexpr int kG = FIX ? kGemvMaxConsumerWarps / kNsegw : 0;
+    constexpr int kNw = FIX ? kNsegw * kG : 0;
+    constexpr int kR = FIX ? 4 * kG : 0;  // stage_rows_for(1, G)
+    const int NM = ((FIX ? (int)kGemvPlain : p.mode) == kGemvGateUp) ? 2 : 1;
+    const int NMP = ((FIX ? (int)kGemvPlain : p.mode) == kGemvGateUp) ? 2 : ((FIX ? (int)kGemvPlain : p.mode) == kGemvDownCombine ? p.kslots : 1);
     const int NCP = SPLIT ? p.kslots : 1;  // expert copies per stage
-    const int rowBytes = (p.K >> 8) * 144;
-    const int R = p.stage_rows;
+    const int rowBytes = ((FIX ? KK : p.K) >> 8) * 144;
+    const int R = (FIX ? kR : p.stage_rows);
     const int stage_bytes = NM * NCP * R * rowBytes;
     const int S = p.stages;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);
@@ -68,8 +75,8 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
     float* nss = reinterpret_cast<float*>(smem + p.nss_off);  // [nsegw] sums of x^2 (norm_w set)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int NW = p.nw;
-    const long long total = (long long)p.nseg * p.rows;
+    const int NW = (FIX ? kNw : p.nw);
+    const long long total = (long long)(FIX ? 1 : p.nseg) * p.rows;
     const int r0 = (int)(total * blockIdx.x / gridDim.x);
     const int r1 = (int)(total * (blockIdx.x + 1) / gridDim.x);
 
@@ -92,12 +99,12 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
         // Launched behind another kernel with programmatic serialisation, the
         // weight stream of a plain GEMV starts at once (no kernel writes
         // weights); the other modes first wait for the expert ids.
-        if (p.mode != kGemvPlain) grid_dep_wait();
+        if ((FIX ? (int)kGemvPlain : p.mode) != kGemvPlain) grid_dep_wait();
         if (lane == 0) {
             const uint64_t pol = GLC_GEMV_L2_HINT ? l2_evict_first_policy() : 0ull;
             bool ok = true;
             int issued = 0;  // stages issued so far
-            for_each_stage<SPLIT>(p, r0, r1, [&](int sidx, int seg, int j, int rin, int nr, int) {
+            for_each_stage<SPLIT, FIX>(p, R, r0, r1, [&](int sidx, int seg, int j, int rin, int nr, int) {
                 if (!ok) return;
                 const int buf = sidx % S;
                 const uint32_t ph = (uint32_t)(sidx / S) & 1u;
@@ -105,9 +112,9 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
                 issued = sidx + 1;
                 const uint8_t* srcA;
                 const uint8_t* srcB = nullptr;
-                if (p.mode == kGemvPlain) {
+                if ((FIX ? (int)kGemvPlain : p.mode) == kGemvPlain) {
                     srcA = p.A + (size_t)rin * rowBytes;
-                } else if (p.mode == kGemvGateUp) {
+                } else if ((FIX ? (int)kGemvPlain : p.mode) == kGemvGateUp) {
                     const int e = clamp_expert(__ldg(p.ids + seg), p.num_experts);
                     srcA = p.A + (size_t)e * p.expert_bytes + (size_t)rin * rowBytes;
                     srcB = p.B + (size_t)e * p.expert_bytes + (size_t)rin * rowBytes;
@@ -145,13 +152,13 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
     }
 
     // ---------------------------------------------------------- consumer warps
-    const int nsegw = p.nsegw;
+    const int nsegw = (FIX ? kNsegw : p.nsegw);
     const int segw = warp % nsegw, grp0 = warp / nsegw, G0 = NW / nsegw;
     // slot-split layout: group grp0 works on slot js of every stage, as group
     // grp of G per slot
     const int js = SPLIT ? grp0 % p.kslots : 0;
     const int G = SPLIT ? G0 / p.kslots : G0, grp = SPLIT ? grp0 / p.kslots : grp0;
-    const int U = (p.K >> 8) * 4;
+    const int U = ((FIX ? KK : p.K) >> 8) * 4;
     const int u = segw * 32 + lane;
     const bool active = u < U;
     const int sb = active ? (u >> 2) : 0, c = u & 3;
@@ -161,20 +168,20 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
     grid_dep_wait();  // the input is the previous kernel's output
     // one input for the whole CTA (plain mode): staged once, coalesced, in the
     // partial-sum region before any partial sum is written
-    const bool staged = p.mode == kGemvPlain && p.nseg == 1;
+    const bool staged = (FIX ? (int)kGemvPlain : p.mode) == kGemvPlain && (FIX ? 1 : p.nseg) == 1;
     if (staged) {
         uint32_t* xs = reinterpret_cast<uint32_t*>(part);
-        stage_x_shared<kXGlobalRO>(p.x, NORM ? p.norm_w : nullptr, p.K, xs, nss, threadIdx.x, NW * 32);
+        stage_x_shared<kXGlobalRO>(p.x, NORM ? p.norm_w : nullptr, (FIX ? KK : p.K), xs, nss, threadIdx.x, NW * 32);
         named_bar_sync(1, NW * 32);
         read_x_shared(xr, xs, U, u, active);
         named_bar_sync(1, NW * 32);
         cur_x = 0;
     }
-    for_each_stage<SPLIT>(p, r0, r1, [&](int sidx, int seg, int j, int, int nr, int lr0) {
+    for_each_stage<SPLIT, FIX>(p, R, r0, r1, [&](int sidx, int seg, int j, int, int nr, int lr0) {
         if (!ok) return;
         const int jj = SPLIT ? js : j;
-        const int xid = (p.mode == kGemvPlain) ? 0
-                        : (p.mode == kGemvGateUp ? seg / p.kslots : seg * p.kslots + jj);
+        const int xid = ((FIX ? (int)kGemvPlain : p.mode) == kGemvPlain) ? 0
+                        : ((FIX ? (int)kGemvPlain : p.mode) == kGemvGateUp ? seg / p.kslots : seg * p.kslots + jj);
         if (xid != cur_x) {
             if constexpr (NORM) {  // one segment: xid is 0
                 float ss;
@@ -183,7 +190,7 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
                 ss = warp_tree(ss);
                 if (grp0 == 0 && lane == 0) nss[segw] = ss;
             } else {
-                load_x<kXGlobalRO>(xr, reinterpret_cast<const float4*>(p.x + (size_t)xid * p.K) + 16 * u, 1, active);
+                load_x<kXGlobalRO>(xr, reinterpret_cast<const float4*>(p.x + (size_t)xid * (FIX ? KK : p.K)) + 16 * u, 1, active);
             }
             cur_x = xid;
         }
@@ -192,7 +199,7 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
         if (!mbar_wait_spin(&full[buf], ph, p.err, kDevTimeoutFull)) { ok = false; return; }
         const uint8_t* st = smem + (size_t)buf * stage_bytes + (SPLIT ? (size_t)js * R * rowBytes : 0);
         consume_stage(st, nr, R, NM, G, grp, rowBytes, sb, c, active, xr, lane, [&](int i, int m, float v) {
-            const int slot = (p.mode == kGemvDownCombine) ? jj : m;
+            const int slot = ((FIX ? (int)kGemvPlain : p.mode) == kGemvDownCombine) ? jj : m;
             part[((size_t)(lr0 + i) * NMP + slot) * nsegw + segw] = v;
         });
         __syncwarp();
@@ -207,18 +214,18 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) q4k_gemv_kernel(const __gr
     if constexpr (NORM) {
         float ss = 0.f;  // per-warp sums when staged, per-segment sums otherwise
         for (int q = 0; q < (staged ? NW : nsegw); ++q) ss += nss[q];
-        rinv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)p.K), p.norm_eps)));
+        rinv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)(FIX ? KK : p.K)), p.norm_eps)));
     }
     const int nrows = r1 - r0;
     for (int lr = threadIdx.x; lr < nrows; lr += NW * 32) {
         const int g = r0 + lr;
         const int seg = g / p.rows, rin = g - seg * p.rows;
         const float* pp = part + (size_t)lr * NMP * nsegw;
-        if (p.mode == kGemvPlain) {
+        if ((FIX ? (int)kGemvPlain : p.mode) == kGemvPlain) {
             float s = 0.f;
             for (int q = 0; q < nsegw; ++q) s += pp[q];
             p.y[rin] = NORM ? __fmul_rn(s, rinv) : s;
-        } else if (p.mode == kGemvGateUp) {
+        } else if ((FIX ? (int)kGemvPlain : p.mode) == kGemvGateUp) {
             float gs = 0.f, us = 0.f;
             for (int q = 0; q < nsegw; ++q) { gs += pp[q]; us += pp[nsegw + q]; }
             if constexpr (NORM) {
@@ -288,12 +295,10 @@ cudaError_t gemv_launch(const GemvParams& p0, int num_sms, cudaStream_t stream) 
     if (smem_optin[dev] == 0) {
         int v = 0;
         cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-        cudaError_t e = cudaFuncSetAttribute(q4k_gemv_kernel<false, false>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, v);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(q4k_gemv_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, v);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(q4k_gemv_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, v);
+        cudaError_t e = cudaSuccess;
+        for (auto kf : {q4k_gemv_kernel<false, false, 0>, q4k_gemv_kernel<true, false, 0>, q4k_gemv_kernel<false, true, 0>,
+                        q4k_gemv_kernel<false, false, 4096>, q4k_gemv_kernel<false, false, 14336>})
+            if (e == cudaSuccess) e = cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, v);
         if (e != cudaSuccess) return e;
         smem_optin[dev] = v;
     }
@@ -313,9 +318,18 @@ cudaError_t gemv_launch(const GemvParams& p0, int num_sms, cudaStream_t stream) 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (p.split) return cudaLaunchKernelEx(&cfg, q4k_gemv_kernel<true, false>, p);
-    if (p.norm_w) return cudaLaunchKernelEx(&cfg, q4k_gemv_kernel<false, true>, p);
-    return cudaLaunchKernelEx(&cfg, q4k_gemv_kernel<false, false>, p);
+    if (p.split) return cudaLaunchKernelEx(&cfg, q4k_gemv_kernel<true, false, 0>, p);
+    if (p.norm_w) return cudaLaunchKernelEx(&cfg, q4k_gemv_kernel<false, true, 0>, p);
+    // a plain one-input GEMV at K = 4096 or 14336 (the Mixtral gate/up and
+    // down rows): the instantiation with K built in, when the configured
+    // layout is the one it derives
+    if (p.mode == kGemvPlain && p.nseg == 1 && (p.K == 4096 || p.K == 14336)) {
+        const int nsegw = ((p.K >> 8) * 4 + 31) / 32, G = kGemvMaxConsumerWarps / nsegw;
+        if (p.nsegw == nsegw && p.nw == nsegw * G && p.stage_rows == 4 * G)
+            return cudaLaunchKernelEx(&cfg, p.K == 4096 ? q4k_gemv_kernel<false, false, 4096>
+                                                        : q4k_gemv_kernel<false, false, 14336>, p);
+    }
+    return cudaLaunchKernelEx(&cfg, q4k_gemv_kernel<false, false, 0>, p);
 }
 
 }  // namespace glc
