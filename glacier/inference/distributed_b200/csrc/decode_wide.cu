@@ -65,6 +65,14 @@ __device__ __forceinline__ float rms_scale(float ss, int D) {
     return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), 1e-5f)));
 }
 
+// QW: the Qwen2-57B-A14B decode shape (one token, 64 experts, top-8, D = 3584,
+// F = 2560, shared expert Fs = 20480) with wide_decode_configure's lane layout
+// for it (gate/up: 2 lane segments, 6 warp groups, 12 stage rows; down: 4
+// stage rows, slot units 40, shared units 320 on 10 + 10 warps, 2 partial
+// sums per slot, 26 per row) built in as constants; the launch uses it only
+// when the configured layout is exactly that.  Otherwise every value comes
+// from the parameters.
+template <bool QW>
 __global__ void __launch_bounds__(kWThreads, 1) moe_decode_wide_kernel(const __grid_constant__ FusedDecodeParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int s_ok, s_route_ok;
@@ -87,7 +95,8 @@ __global__ void __launch_bounds__(kWThreads, 1) moe_decode_wide_kernel(const __g
     float* xraw = reinterpret_cast<float*>(smem + p.off_red);  // [T][D] raw input
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int T = p.T, D = p.D, F = p.F, Fs = p.Fs, k = p.k, E = p.E;
+    const int T = QW ? 1 : p.T, D = QW ? 3584 : p.D, F = QW ? 2560 : p.F, Fs = QW ? 20480 : p.Fs,
+              k = QW ? 8 : p.k, E = QW ? 64 : p.E;
     const uint64_t lim = p.wait_limit_ns > 0 ? (uint64_t)p.wait_limit_ns : kWaitLimitNs;
     const int slot = p.slot_bytes;
     const int G = gridDim.x, b = blockIdx.x;
@@ -323,7 +332,7 @@ __global__ void __launch_bounds__(kWThreads, 1) moe_decode_wide_kernel(const __g
                 if (sidx == S - 1) mbar_arrive(go_bar);
             };
             // shared-expert gate/up rows: no routing needed
-            int nxt = for_each_stage_rows(Fs > 0 ? Fs : 1, 1, p.gu_R, sh0, sh1, 0, [&](int sidx, int, int, int rin, int nr, int) {
+            int nxt = for_each_stage_rows(Fs > 0 ? Fs : 1, 1, (QW ? 12 : p.gu_R), sh0, sh1, 0, [&](int sidx, int, int, int rin, int nr, int) {
                 int buf;
                 if (!ok || !ring_wait(sidx, buf)) return;
                 const size_t off = (size_t)rin * rbG;
@@ -331,12 +340,12 @@ __global__ void __launch_bounds__(kWThreads, 1) moe_decode_wide_kernel(const __g
                 uint8_t* dst = smem + (size_t)buf * slot;
                 mbar_arrive_expect_tx(&full[buf], 2u * bytes);
                 bulk_g2s(dst, p.sh_gate + off, bytes, &full[buf], pol);
-                bulk_g2s(dst + (size_t)p.gu_R * rbG, p.sh_up + off, bytes, &full[buf], pol);
+                bulk_g2s(dst + (size_t)(QW ? 12 : p.gu_R) * rbG, p.sh_up + off, bytes, &full[buf], pol);
                 mark_issued(sidx);
             });
             // the routed rows need the ids
             if (ok && (!mbar_wait(route_mb, 0, p.err, kDevTimeoutFull, lim) || !s_route_ok)) ok = false;
-            nxt = for_each_stage_rows(F, 1, p.gu_R, r0, r1, nxt, [&](int sidx, int seg, int, int rin, int nr, int) {
+            nxt = for_each_stage_rows(F, 1, (QW ? 12 : p.gu_R), r0, r1, nxt, [&](int sidx, int seg, int, int rin, int nr, int) {
                 int buf;
                 if (!ok || !ring_wait(sidx, buf)) return;
                 const int e = clamp_expert(s_ids[seg], E);
@@ -345,25 +354,25 @@ __global__ void __launch_bounds__(kWThreads, 1) moe_decode_wide_kernel(const __g
                 uint8_t* dst = smem + (size_t)buf * slot;
                 mbar_arrive_expect_tx(&full[buf], 2u * bytes);
                 bulk_g2s(dst, p.gate + off, bytes, &full[buf], pol);
-                bulk_g2s(dst + (size_t)p.gu_R * rbG, p.up + off, bytes, &full[buf], pol);
+                bulk_g2s(dst + (size_t)(QW ? 12 : p.gu_R) * rbG, p.up + off, bytes, &full[buf], pol);
                 mark_issued(sidx);
             });
             if (issued < S) mbar_arrive(go_bar);  // fewer stages than the ring, or gave up
             // routed down rows: dn_R rows of each of the k slots
-            nxt = for_each_stage_rows(D, 1, p.dn_R, q0, q1, nxt, [&](int sidx, int t, int, int rin, int nr, int) {
+            nxt = for_each_stage_rows(D, 1, (QW ? 4 : p.dn_R), q0, q1, nxt, [&](int sidx, int t, int, int rin, int nr, int) {
                 int buf;
                 if (!ok || !ring_wait(sidx, buf)) return;
                 const uint32_t bytes = (uint32_t)(nr * rbD);
                 mbar_arrive_expect_tx(&full[buf], bytes * k);
                 for (int j = 0; j < k; ++j) {
                     const int e = clamp_expert(s_ids[t * k + j], E);
-                    bulk_g2s(smem + (size_t)buf * slot + (size_t)j * p.dn_R * rbD,
+                    bulk_g2s(smem + (size_t)buf * slot + (size_t)j * (QW ? 4 : p.dn_R) * rbD,
                              p.down + (size_t)e * p.dn_expert_bytes + (size_t)rin * rbD, bytes, &full[buf], pol);
                 }
                 issued = sidx + 1;
             });
             if (Fs > 0)
-                for_each_stage_rows(D, 1, p.dn_R, q0, q1, nxt, [&](int sidx, int, int, int rin, int nr, int) {
+                for_each_stage_rows(D, 1, (QW ? 4 : p.dn_R), q0, q1, nxt, [&](int sidx, int, int, int rin, int nr, int) {
                     int buf;
                     if (!ok || !ring_wait(sidx, buf)) return;
                     const uint32_t bytes = (uint32_t)(nr * rbS);
@@ -396,7 +405,7 @@ __global__ void __launch_bounds__(kWThreads, 1) moe_decode_wide_kernel(const __g
     bool ok = true;
     int nxt;
     {  // ---- gate/up + SwiGLU: the shared expert's rows, then the routed pairs'
-        const int nsegw = p.gu_nsegw, Gg = p.gu_G;
+        const int nsegw = (QW ? 2 : p.gu_nsegw), Gg = (QW ? 6 : p.gu_G);
         const bool wact = warp < nsegw * Gg;
         const int segw = warp % nsegw, grp = warp / nsegw;
         const int u = segw * 32 + lane;
@@ -415,14 +424,14 @@ __global__ void __launch_bounds__(kWThreads, 1) moe_decode_wide_kernel(const __g
             const uint32_t ph = (uint32_t)(sidx / S) & 1u;
             if (!mbar_wait_spin(&full[buf], ph, p.err, kDevTimeoutFull, lim)) { ok = false; return; }
             if (wact)
-                consume_stage(smem + (size_t)buf * slot, nr, p.gu_R, 2, Gg, grp, rbG, sb, c, active, xr, lane,
+                consume_stage(smem + (size_t)buf * slot, nr, (QW ? 12 : p.gu_R), 2, Gg, grp, rbG, sb, c, active, xr, lane,
                               [&](int i, int m, float v) { pgu[((size_t)(lrow0 + i) * 2 + m) * nsegw + segw] = v; });
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[buf]);
         };
-        nxt = for_each_stage_rows(Fs > 0 ? Fs : 1, 1, p.gu_R, sh0, sh1, 0,
+        nxt = for_each_stage_rows(Fs > 0 ? Fs : 1, 1, (QW ? 12 : p.gu_R), sh0, sh1, 0,
                                   [&](int sidx, int t, int, int, int nr, int lr0) { consume(sidx, t, nr, lr0); });
-        nxt = for_each_stage_rows(F, 1, p.gu_R, r0, r1, nxt,
+        nxt = for_each_stage_rows(F, 1, (QW ? 12 : p.gu_R), r0, r1, nxt,
                                   [&](int sidx, int seg, int, int, int nr, int lr0) { consume(sidx, seg / k, nr, nsh + lr0); });
     }
     if (!ok) s_ok = 0;
@@ -452,7 +461,7 @@ __global__ void __launch_bounds__(kWThreads, 1) moe_decode_wide_kernel(const __g
     if (b == 0 && p.xin)
         for (int i = tid; i < T * D; i += kWNT) p.xin[i] = p.rmsnorm ? __fmul_rn(xraw[i], s_rms[i / D]) : xraw[i];
     {
-        const int nsegw = p.gu_nsegw;
+        const int nsegw = (QW ? 2 : p.gu_nsegw);
         const int nrow = nsh + (r1 - r0);
         for (int lr = tid; lr < nrow; lr += kWNT) {
             const float* pp = pgu + (size_t)lr * 2 * nsegw;
@@ -490,13 +499,13 @@ __global__ void __launch_bounds__(kWThreads, 1) moe_decode_wide_kernel(const __g
         return;
     }
 
-    const int PR = p.dn_row_parts;
+    const int PR = (QW ? 26 : p.dn_row_parts);
     // The shared row's lanes: unit L of Fs / 64 (its activations are loaded
     // when its sub-phase starts: holding both sets of activations at once
     // would not fit the registers).
-    const int Us = p.dn_Us;
+    const int Us = (QW ? 320 : p.dn_Us);
     const int Ls = warp * 32 + lane;
-    const bool act_s = Fs > 0 && warp < p.dn_nws && Ls < Us;
+    const bool act_s = Fs > 0 && warp < (QW ? 10 : p.dn_nws) && Ls < Us;
     XRegs xr_s;
     int cur_s = -1;
     auto load_shared_x = [&](int t) {
@@ -504,9 +513,9 @@ __global__ void __launch_bounds__(kWThreads, 1) moe_decode_wide_kernel(const __g
         cur_s = t;
     };
     {  // ---- down projection, routed slots: lane unit L -> slot L / Ur, unit L % Ur
-        const int Ur = p.dn_Ur, Pr = p.dn_Pr;
+        const int Ur = (QW ? 40 : p.dn_Ur), Pr = (QW ? 2 : p.dn_Pr);
         const int L = warp * 32 + lane;
-        const bool wact = warp < p.dn_nwr;
+        const bool wact = warp < (QW ? 10 : p.dn_nwr);
         const int j = L / Ur, unit = L - (L / Ur) * Ur;
         const bool active = wact && j < k;
         const int jA = (warp * 32) / Ur;                // first slot in this warp
@@ -515,7 +524,7 @@ __global__ void __launch_bounds__(kWThreads, 1) moe_decode_wide_kernel(const __g
         const int sb = active ? (unit >> 2) : 0, c = unit & 3;
         XRegs xr;
         int cur = -1;
-        nxt = for_each_stage_rows(D, 1, p.dn_R, q0, q1, nxt, [&](int sidx, int t, int, int, int nr, int lr0) {
+        nxt = for_each_stage_rows(D, 1, (QW ? 4 : p.dn_R), q0, q1, nxt, [&](int sidx, int t, int, int, int nr, int lr0) {
             if (!ok) return;
             if (t != cur) {
                 load_x<kXGlobalCG>(xr, reinterpret_cast<const float4*>(p.act + (size_t)(t * k + (active ? j : 0)) * F) + unit,
@@ -526,7 +535,7 @@ __global__ void __launch_bounds__(kWThreads, 1) moe_decode_wide_kernel(const __g
             const uint32_t ph = (uint32_t)(sidx / S) & 1u;
             if (!mbar_wait_spin(&full[buf], ph, p.err, kDevTimeoutFull, lim)) { ok = false; return; }
             if (wact) {
-                const uint8_t* st = smem + (size_t)buf * slot + (size_t)(active ? j : 0) * p.dn_R * rbD;
+                const uint8_t* st = smem + (size_t)buf * slot + (size_t)(active ? j : 0) * (QW ? 4 : p.dn_R) * rbD;
                 float va[4], vb[4];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
@@ -552,17 +561,17 @@ __global__ void __launch_bounds__(kWThreads, 1) moe_decode_wide_kernel(const __g
         });
     }
     if (Fs > 0) {  // ---- down projection, the shared row: lane unit L of Fs / 64
-        const bool wact = warp < p.dn_nws;
+        const bool wact = warp < (QW ? 10 : p.dn_nws);
         const int sb = act_s ? (Ls >> 2) : 0, c = Ls & 3;
-        for_each_stage_rows(D, 1, p.dn_R, q0, q1, nxt, [&](int sidx, int t, int, int, int nr, int lr0) {
+        for_each_stage_rows(D, 1, (QW ? 4 : p.dn_R), q0, q1, nxt, [&](int sidx, int t, int, int, int nr, int lr0) {
             if (!ok) return;
             if (t != cur_s) load_shared_x(t);
             const int buf = sidx % S;
             const uint32_t ph = (uint32_t)(sidx / S) & 1u;
             if (!mbar_wait_spin(&full[buf], ph, p.err, kDevTimeoutFull, lim)) { ok = false; return; }
             if (wact)
-                consume_stage(smem + (size_t)buf * slot, nr, p.dn_R, 1, 1, 0, rbS, sb, c, act_s, xr_s, lane,
-                              [&](int i, int, float v) { pdn[(size_t)(lr0 + i) * PR + k * p.dn_Pr + warp] = v; });
+                consume_stage(smem + (size_t)buf * slot, nr, (QW ? 4 : p.dn_R), 1, 1, 0, rbS, sb, c, act_s, xr_s, lane,
+                              [&](int i, int, float v) { pdn[(size_t)(lr0 + i) * PR + k * (QW ? 2 : p.dn_Pr) + warp] = v; });
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[buf]);
         });
@@ -574,7 +583,7 @@ __global__ void __launch_bounds__(kWThreads, 1) moe_decode_wide_kernel(const __g
         return;
     }
     {  // ---- combine in k order (+ residual, + gated shared expert)
-        const int Ur = p.dn_Ur, Pr = p.dn_Pr;
+        const int Ur = (QW ? 40 : p.dn_Ur), Pr = (QW ? 2 : p.dn_Pr);
         for (int lr = tid; lr < q1 - q0; lr += kWNT) {
             const int g = q0 + lr, t = g / D, rin = g - t * D;
             const size_t o = (size_t)t * D + rin;
@@ -588,7 +597,7 @@ __global__ void __launch_bounds__(kWThreads, 1) moe_decode_wide_kernel(const __g
             }
             if (Fs > 0) {
                 float s = 0.f;
-                for (int q = 0; q < p.dn_nws; ++q) s += pr[k * Pr + q];
+                for (int q = 0; q < (QW ? 10 : p.dn_nws); ++q) s += pr[k * Pr + q];
                 acc = __fadd_rn(__fmul_rn(s, s_sg[t]), acc);
             }
             p.out[o] = acc;
@@ -691,8 +700,10 @@ cudaError_t wide_decode_launch(const FusedDecodeParams& p0, int num_sms, cudaStr
         e = cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
         if (e != cudaSuccess) return e;
         v -= 2048;  // the kernel's static shared memory comes out of the same budget
-        e = cudaFuncSetAttribute(moe_decode_wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, v);
-        if (e != cudaSuccess) return e;
+        for (auto kf : {moe_decode_wide_kernel<false>, moe_decode_wide_kernel<true>}) {
+            e = cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, v);
+            if (e != cudaSuccess) return e;
+        }
         smem_optin[dev] = v;
     }
     size_t smem = 0;
@@ -708,7 +719,10 @@ cudaError_t wide_decode_launch(const FusedDecodeParams& p0, int num_sms, cudaStr
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, moe_decode_wide_kernel, p);
+    const bool qw = p.T == 1 && p.D == 3584 && p.F == 2560 && p.Fs == 20480 && p.k == 8 && p.E == 64 &&
+                    p.gu_nsegw == 2 && p.gu_G == 6 && p.gu_R == 12 && p.dn_R == 4 && p.dn_Ur == 40 && p.dn_Pr == 2 &&
+                    p.dn_nwr == 10 && p.dn_Us == 320 && p.dn_nws == 10 && p.dn_row_parts == 26;
+    return cudaLaunchKernelEx(&cfg, qw ? moe_decode_wide_kernel<true> : moe_decode_wide_kernel<false>, p);
 }
 
 }  // namespace glc
