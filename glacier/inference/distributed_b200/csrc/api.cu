@@ -133,6 +133,7 @@ struct glc_moe {
     float* ysh = nullptr;        // [kShSlicesMax][T][D]
     // pinned host staging
     float* h_x = nullptr;
+    const float* d_x_map = nullptr;  // device address of h_x (mapped), or null
     uint8_t* h_res = nullptr;  // pinned (and mapped) copy of the result block
     uint8_t* d_res_map = nullptr;  // device address of h_res
     // mapped completion words of the fused decode launch the host-buffer
@@ -770,6 +771,10 @@ int glc_moe_create(const glc_moe_desc* desc, glc_moe** out) {
         h->d_sig_map = nullptr;
         cudaGetLastError();
     }
+    if (cudaHostGetDevicePointer(reinterpret_cast<void**>(const_cast<float**>(&h->d_x_map)), h->h_x, 0) != cudaSuccess) {
+        h->d_x_map = nullptr;  // the input then goes over with a host-to-device copy
+        cudaGetLastError();
+    }
     if (cudaDeviceSynchronize() != cudaSuccess) return cleanup(fail(GLC_ERR_CUDA, "device sync failed"));
     *out = h;
     return GLC_OK;
@@ -1008,6 +1013,29 @@ int glc_routed_topk(glc_moe* h, int32_t layer, const float* x, const int32_t* id
 namespace {
 
 // The whole-layer fused decode launch serves this call (T tokens, flags).
+// The host-buffer forward's input: the token in the pinned staging buffer,
+// read through its mapped device address, into the device input -- the
+// kernel in front of the fused decode launch, which is programmatically
+// serialised behind it (stages its router weights meanwhile and waits for
+// this kernel before reading the input).
+// (256 threads: small enough that the fused launch's CTA fits beside it on its SM.)
+__global__ void __launch_bounds__(256) copy_in_kernel(const float4* __restrict__ src, float4* __restrict__ dst,
+                                                      int n4) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the fused launch may start at once
+    for (int i = threadIdx.x; i < n4; i += 256) dst[i] = src[i];
+}
+
+// The input of a host-buffer call onto the device: the copy kernel from the
+// mapped staging buffer, or a host-to-device copy.
+cudaError_t stage_input(glc_moe* h, size_t xbytes, cudaStream_t st) {
+    if (h->d_x_map) {
+        copy_in_kernel<<<1, 256, 0, st>>>(reinterpret_cast<const float4*>(h->d_x_map), reinterpret_cast<float4*>(h->x),
+                                           (int)(xbytes / 16));
+        return cudaGetLastError();
+    }
+    return cudaMemcpyAsync(h->x, h->h_x, xbytes, cudaMemcpyHostToDevice, st);
+}
+
 bool fused_applies(const glc_moe* h, int T, uint32_t flags) {
     const bool grouped = (flags & GLC_FWD_BATCHED) ? true : (flags & GLC_FWD_DECODE) ? false : (T > 1);
     // residency mode routes first and pages the selected experts in before they run
@@ -1396,6 +1424,7 @@ int glc_moe_forward(glc_moe* h, int32_t layer, const float* x, int32_t T, uint32
             fp.done_ctr = reinterpret_cast<unsigned long long*>(h->err + 4);
             fp.host_done = h->d_sig_map;
             fp.host_err = reinterpret_cast<int*>(h->d_sig_map + 1);
+            fp.pdl = h->d_x_map ? 1 : 0;  // behind the copy kernel
             return fp;
         };
         cudaGraphExec_t cached = nullptr;
@@ -1406,7 +1435,7 @@ int glc_moe_forward(glc_moe* h, int32_t layer, const float* x, int32_t T, uint32
         if (replay) {
             CUDA_TRY(cudaGraphLaunch(cached, st));
         } else {
-            CUDA_TRY(cudaMemcpyAsync(h->x, h->h_x, xbytes, cudaMemcpyHostToDevice, st));
+            CUDA_TRY(stage_input(h, xbytes, st));
             const cudaError_t e = glc::fused_decode_launch(host_params(), h->num_sms, st);
             if (e == cudaErrorNotSupported) goto separate_launches;
             if (e != cudaSuccess) return fail(GLC_ERR_CUDA, "fused decode launch: %s", cudaGetErrorString(e));
@@ -1439,7 +1468,7 @@ int glc_moe_forward(glc_moe* h, int32_t layer, const float* x, int32_t T, uint32
             cudaGraphExec_t exec = nullptr;
             if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
                 const glc::FusedDecodeParams fp = host_params();
-                const bool ok = cudaMemcpyAsync(h->x, h->h_x, xbytes, cudaMemcpyHostToDevice, st) == cudaSuccess &&
+                const bool ok = stage_input(h, xbytes, st) == cudaSuccess &&
                                 glc::fused_decode_launch(fp, h->num_sms, st) == cudaSuccess;
                 if (cudaStreamEndCapture(st, &g) != cudaSuccess || !ok || cudaGraphInstantiate(&exec, g, 0) != cudaSuccess)
                     exec = nullptr;

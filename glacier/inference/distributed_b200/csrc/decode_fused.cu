@@ -35,12 +35,6 @@
 #ifndef GLC_FUSED_MAX_STAGES
 #define GLC_FUSED_MAX_STAGES 8
 #endif
-// Launch the decode layer programmatically serialised behind the kernel
-// before it (its CTAs take SMs as that kernel's leave them and stage the
-// router weights before waiting) instead of cooperatively.
-#ifndef GLC_FUSED_PDL
-#define GLC_FUSED_PDL 0
-#endif
 // Largest router split (CTAs per cluster sharing the router rows): 2 or 1
 // (1 turns the split off).  Clusters of four cannot all be resident at one
 // CTA per SM on B200's 148 SMs, so a four-way split would never launch.
@@ -308,8 +302,10 @@ __device__ void topk_token_warp(const FusedDecodeParams& p, const float* l, int 
 // Separate instantiations keep the unsplit, unweighted kernel's code exactly
 // what it is without them (measured: folding the split and the weighted norm
 // in as runtime branches cost 1.6 us per launch at the Mixtral-8x7B shape;
-// the one-token instantiation saved 0.5 us).
-template <bool SPLIT, bool NW, int TT, int KK, int EE, int DD, int FF>
+// the one-token instantiation saved 0.5 us).  PDL: launched programmatically
+// serialised behind the kernel that writes its input (FusedDecodeParams::pdl):
+// the router weights are staged before the kernel waits for that one.
+template <bool SPLIT, bool NW, int TT, int KK, int EE, int DD, int FF, bool PDL = false>
 __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(const __grid_constant__ FusedDecodeParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int s_ok, s_okx, s_okw;
@@ -346,9 +342,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
     constexpr int R = SPLIT ? 2 : 1;  // router split over a cluster of R CTAs
     float* lh = reinterpret_cast<float*>(smem + p.off_lh);
     if (R > 1) cluster_arrive_relaxed();
-#if GLC_FUSED_PDL
-    grid_dep_launch_dependents();
-#endif
+    if constexpr (PDL) grid_dep_launch_dependents();
 
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
@@ -385,21 +379,18 @@ __global__ void __launch_bounds__(kFusedThreads, 1) moe_decode_fused_kernel(cons
                                     blk, wbar);
             }
         };
-#if GLC_FUSED_PDL
-        // the router weights never depend on the kernel before; the input may
-        stage_router();
-        grid_dep_wait();
-        mbar_arrive_expect_tx(xbar, xb);
-        bulk_g2s_nohint(smem + wb, p.x, xb, xbar);
-#else
-        mbar_arrive_expect_tx(xbar, xb);
-        bulk_g2s_nohint(smem + wb, p.x, xb, xbar);
-        stage_router();
-#endif
+        if constexpr (PDL) {  // the router weights never depend on the kernel before; the input does
+            stage_router();
+            grid_dep_wait();
+            mbar_arrive_expect_tx(xbar, xb);
+            bulk_g2s_nohint(smem + wb, p.x, xb, xbar);
+        } else {
+            mbar_arrive_expect_tx(xbar, xb);
+            bulk_g2s_nohint(smem + wb, p.x, xb, xbar);
+            stage_router();
+        }
     }
-#if GLC_FUSED_PDL
-    grid_dep_wait();  // every thread: what the kernel before wrote is visible
-#endif
+    if constexpr (PDL) grid_dep_wait();  // every thread: what the kernel before wrote is visible
     // Every CTA reports its end when the caller waits on host memory (see
     // FusedDecodeParams::done_ctr): its writes become visible system-wide
     // first, and the CTA that completes a multiple of the grid size publishes
@@ -789,6 +780,7 @@ cudaError_t fused_decode_launch(const FusedDecodeParams& p0, int num_sms, cudaSt
     static const Kernel mixtral_decode = moe_decode_fused_kernel<false, false, 1, 2, 8, 4096, 14336>;
     static const Kernel top2of8_decode = moe_decode_fused_kernel<false, false, 1, 2, 8, 0, 0>;
     static const Kernel mixtral22b_ffn = moe_decode_fused_kernel<true, true, 1, 2, 8, 6144, 16384>;
+    static const Kernel mixtral_decode_pdl = moe_decode_fused_kernel<false, false, 1, 2, 8, 4096, 14336, true>;
     static int smem_optin[kMaxDevices] = {0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -806,7 +798,7 @@ cudaError_t fused_decode_launch(const FusedDecodeParams& p0, int num_sms, cudaSt
                     e = cudaFuncSetAttribute(kernels[s][w][t], cudaFuncAttributeMaxDynamicSharedMemorySize, v);
                     if (e != cudaSuccess) return e;
                 }
-        for (Kernel kf : {mixtral_decode, top2of8_decode, mixtral22b_ffn}) {
+        for (Kernel kf : {mixtral_decode, top2of8_decode, mixtral22b_ffn, mixtral_decode_pdl}) {
             e = cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, v);
             if (e != cudaSuccess) return e;
         }
@@ -833,20 +825,6 @@ cudaError_t fused_decode_launch(const FusedDecodeParams& p0, int num_sms, cudaSt
     cfg.blockDim = dim3(kFusedThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[2];
-#if GLC_FUSED_PDL
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-#else
-    attr[0].id = cudaLaunchAttributeCooperative;  // all CTAs co-resident: the grid barrier needs it
-    attr[0].val.cooperative = 1;
-#endif
-    attr[1].id = cudaLaunchAttributeClusterDimension;
-    attr[1].val.clusterDim.x = (unsigned)R;
-    attr[1].val.clusterDim.y = 1;
-    attr[1].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = R > 1 ? 2 : 1;
     const bool top2of8 = p.T == 1 && p.k == 2 && p.E == 8;
     // (a fixed-width instantiation only when the configured lane layout is the one it has built in)
     Kernel kf = kernels[R > 1 ? 1 : 0][nw][one];
@@ -854,6 +832,26 @@ cudaError_t fused_decode_launch(const FusedDecodeParams& p0, int num_sms, cudaSt
         kf = layout_is(p, 4096, 14336) ? mixtral_decode : top2of8_decode;
     else if (top2of8 && R == 2 && nw && layout_is(p, 6144, 16384))
         kf = mixtral22b_ffn;
+    // programmatic serialisation behind the input's writer only where the
+    // instantiation waits for it (the others run in plain stream order)
+    const bool pdl = p.pdl && kf == mixtral_decode;
+    if (pdl) kf = mixtral_decode_pdl;
+    cudaLaunchAttribute attr[3];
+    int na = 0;
+    attr[na].id = cudaLaunchAttributeCooperative;  // all CTAs co-resident: the grid barrier needs it
+    attr[na++].val.cooperative = 1;
+    if (pdl) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na++].val.programmaticStreamSerializationAllowed = 1;
+    }
+    if (R > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = (unsigned)R;
+        attr[na].val.clusterDim.y = 1;
+        attr[na++].val.clusterDim.z = 1;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
     return cudaLaunchKernelEx(&cfg, kf, p);
 }
 

@@ -183,6 +183,10 @@ struct FusedDecodeParams {
     // eps = norm_eps, as router.cu's norm_w; nullptr = unweighted, eps 1e-5.
     const float* norm_w;
     float norm_eps;
+    // x (and resid) are written by the kernel launched just before on the
+    // stream: where an instantiation can, the launch is programmatically
+    // serialised behind it and stages the router weights before waiting.
+    int pdl;
     // Qwen2-MoE shared expert (Fs > 0): rows [Fs][D/256*144] gate/up,
     // [D][Fs/256*144] down, gate vector [D]; act_sh [T][Fs] scratch.  A layer
     // with a shared expert, or whose router does not fit the shared-memory
