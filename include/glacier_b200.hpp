@@ -122,6 +122,15 @@ struct QuantizationKernels {
     }
 };
 
+// The slot counters of GpuFirstExpertStageWorker.GetTelemetry
+// (GpuFirstExpertStageWorker.cs:763-783).
+struct GpuFirstWorkerTelemetry {
+    int64_t GpuResidentSlotCapacity = 0;
+    int64_t GpuVramHitCount = 0;
+    int64_t GpuPcieTransferCount = 0;
+    int64_t LookaheadPrefetchCount = 0;
+};
+
 // One MoE layer family resident in one GPU's HBM (GGUF Q4_K experts).
 class GpuExpertStageWorker {
 public:
@@ -143,6 +152,24 @@ public:
     }
     void LoadLayer(int layer, const glc_layer_weights& w) { Check(glc_moe_load_layer(Handle(), layer, &w)); }
     void SynthLayer(int layer, uint64_t seed) { Check(glc_moe_synth_layer(Handle(), layer, seed)); }
+
+    // Expert residency (before the first LoadLayer / SynthLayer): the routed
+    // experts in pinned host memory and `gpuSlotCapacity` of them in HBM slots.
+    void SetExpertSlots(int gpuSlotCapacity) { Check(glc_moe_set_expert_slots(Handle(), gpuSlotCapacity)); }
+    // Router lookahead prefetch (GpuFirstExpertStageWorker.cs:388-407).
+    void PrefetchLookaheadExperts(int nextLayerIdx, const int32_t* predictedExpertIds, int count) {
+        Check(glc_moe_prefetch_experts(Handle(), nextLayerIdx, predictedExpertIds, count));
+    }
+    GpuFirstWorkerTelemetry GetTelemetry() {
+        int64_t v[4] = {};
+        Check(glc_moe_expert_residency(Handle(), v));
+        GpuFirstWorkerTelemetry t;
+        t.GpuResidentSlotCapacity = v[0];
+        t.GpuVramHitCount = v[1];
+        t.GpuPcieTransferCount = v[2];
+        t.LookaheadPrefetchCount = v[3];
+        return t;
+    }
 
     // Allocating form: the output buffer belongs to the caller (the reference
     // returns a RefCountedPartitionBuffer the caller disposes).

@@ -52,6 +52,22 @@ int main(int argc, char** argv) {
         double diff = 0, ref = 0;
         for (int i = 0; i < 512; ++i) { diff += std::fabs(o[i] - y[i]); ref += std::fabs(y[i]); }
         EXPECT(diff <= 1e-5 * ref);
+        // the same layer with two HBM slots: experts 0 and 1 are staged when
+        // it is made; expert 2 is paged in on first use, then hit
+        GpuExpertStageWorker pw(d);
+        pw.SetExpertSlots(2);
+        pw.SynthLayer(0, 99);
+        std::vector<float> py = pw.ProcessActivation(ah, x.data(), x.size());
+        EXPECT(std::memcmp(py.data(), y.data(), sizeof(float) * 512) == 0);
+        std::vector<float> po(512);
+        pw.ProcessRoutedTopK(0, x.data(), ids, wts, 2, po.data());
+        EXPECT(std::memcmp(po.data(), o.data(), sizeof(float) * 512) == 0);
+        const int32_t next[1] = {3};
+        pw.PrefetchLookaheadExperts(0, next, 1);
+        const GpuFirstWorkerTelemetry t = pw.GetTelemetry();
+        EXPECT(t.GpuResidentSlotCapacity == 2 && t.GpuPcieTransferCount == 1 && t.GpuVramHitCount == 2 &&
+               t.LookaheadPrefetchCount == 1);
+        EXPECT(w.GetTelemetry().GpuResidentSlotCapacity == 4);  // every expert resident
         w.Dispose();
         threw = false;
         try { w.ProcessActivation(ah, x.data(), x.size()); } catch (const GlcException& e) { threw = e.Status() == GLC_ERR_DISPOSED; }
