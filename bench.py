@@ -407,7 +407,7 @@ def run_ours(args, w):
         qwen = measure_qwen(torch, glc, args, stream, rank == 0 and world == 1 and not args.skip_cpu_baseline, local)
     ep_leg = measure_ep(torch, dist, glc, w, stream, args, world, rank, local) if not args.skip_ep else None
     dense = measure_dense(torch, dist, glc, args, stream, world, rank, local) if not args.skip_dense else None
-    # configs[4] fits one GPU (~80 GB); measured at N = 1 only (the ranks of a
+    # the Mixtral-8x22B model fits one GPU (~80 GB); measured at N = 1 only (the ranks of a
     # multi-GPU run would each synthesise their own copy on the same host)
     mix22 = measure_mixtral22b(torch, glc, args, stream, local) if (world == 1 and not args.skip_dense) else None
     paging = measure_residency(glc, w, local) if (world == 1 and not args.skip_batched) else None
@@ -934,7 +934,7 @@ def moe_token_bytes(q, pos):
 
 
 def measure_mixtral22b(torch, glc, args, stream, local):
-    """the whole Mixtral-8x22B-shaped model (56 layers of attention
+    """The whole Mixtral-8x22B-shaped model (56 layers of attention
     (48 query / 8 KV heads, a 4096-position fp16 cache) and a mixture-of-experts
     feed-forward of 8 SwiGLU experts, FFN 16384, top-2 renormalised, hidden 6144,
     vocab 32768; random-init Q4_K, ~80 GB resident) decoding greedily at batch
@@ -1069,7 +1069,7 @@ def main():
     ap.add_argument("--skip-batched", action="store_true")
     ap.add_argument("--skip-qwen", action="store_true")
     ap.add_argument("--skip-ep", action="store_true")
-    ap.add_argument("--skip-dense", action="store_true", help="skip the configs[3] and configs[4] model legs")
+    ap.add_argument("--skip-dense", action="store_true", help="skip the whole-model legs (Qwen2.5-14B dense, Mixtral-8x22B)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
