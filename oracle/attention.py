@@ -1,6 +1,6 @@
 """CPU restatement of decode attention over an fp16 KV cache (float64 numpy).
 
-TEST INFRASTRUCTURE ONLY: imported by tests/ as the checker of
+TEST INFRASTRUCTURE ONLY: imported by tests/ as the CPU reference for
 glc_attn_decode_dev; the product package never imports it.
 
 Parity unpinned: the reference's attention body lives in its external model

@@ -1,7 +1,7 @@
 """CPU restatement of one token through a dense decoder stage (Qwen2-style).
 
-TEST INFRASTRUCTURE ONLY: imported by tests/ as the checker of the stage
-entry points (glc_stage_*); the product package never imports it.
+TEST INFRASTRUCTURE ONLY: imported by tests/ as the CPU reference for the
+stage entry points (glc_stage_*); the product package never imports it.
 
 Parity unpinned: the reference's stage bodies live in its external model
 package (caller side IClusterStageModel.ForwardStage, Pipeline/IClusterStageModel.cs:19;

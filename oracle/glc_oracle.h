@@ -3,9 +3,9 @@
  *
  * TEST INFRASTRUCTURE ONLY.  Nothing in the product (the CUDA library and its
  * host bindings) links, loads or calls this code.  It is used by tests/ as the
- * parity checker, by __graft_entry__.smoke() as the checker of one small GPU
- * run, and by bench.py's CPU-baseline leg as the timed CPU port of the
- * reference's CPU path.
+ * CPU reference of the parity tests, by __graft_entry__.smoke() to verify one
+ * small GPU run, and by bench.py's CPU-baseline leg as the timed CPU port of
+ * the reference's CPU path.
  *
  * The reference (Glacier.Inference.Distributed, C# / .NET 10) cannot be built
  * or run here (no .NET SDK; its Q4_K mat-vec, SwiGLU and router live in the

@@ -1,7 +1,7 @@
 """ctypes view of the CPU oracle (oracle/glc_oracle.c).
 
 TEST INFRASTRUCTURE ONLY: imported by tests/, by ``__graft_entry__.smoke()``
-(as the checker of one small GPU run) and by bench.py's CPU-baseline leg.  The
+(to verify one small GPU run) and by bench.py's CPU-baseline leg.  The
 product package never imports this module.
 """
 from __future__ import annotations
