@@ -666,6 +666,10 @@ QWEN = dict(name="qwen2_57b_a14b_moe_layer", D=3584, F=2560, E=64, k=8, Fs=20480
 QWEN_T = (1, 16, 256)
 
 
+def qwen_tokens(args):
+    return tuple(int(t) for t in str(getattr(args, "qwen_tokens", "")).split(",") if t.strip()) or QWEN_T
+
+
 def qwen_host_layer(glc, w, worker):
     """Host copies of the config's weights for the CPU port: the routed experts
     and router read back from the device, the shared expert from the same
@@ -700,7 +704,7 @@ def measure_qwen(torch, glc, args, stream, want_cpu, local=0):
     w = QWEN
     D, F, E, k, Fs = w["D"], w["F"], w["E"], w["k"], w["Fs"]
     worker = glc.GpuExpertStageWorker(D, F, E, k, shared_ffn_dim=Fs, renormalize=False, device=local,
-                                      max_tokens=max(QWEN_T))
+                                      max_tokens=max(qwen_tokens(args)))
     worker.synth_layer(0, w["seed"])
     s = stream.cuda_stream
     peak, _ = peaks()
@@ -708,7 +712,7 @@ def measure_qwen(torch, glc, args, stream, want_cpu, local=0):
     shared_bytes = 2 * Fs * q4k_row_bytes(D) + D * q4k_row_bytes(Fs)
     legs = {}
     rng = np.random.default_rng(w["seed"])
-    for T in QWEN_T:
+    for T in qwen_tokens(args):
         xs = [torch.from_numpy(rng.standard_normal((T, D)).astype(np.float32)).cuda() for _ in range(4)]
         out = torch.empty(T, D, device="cuda")
         ids = [torch.empty(T, k, dtype=torch.int32, device="cuda") for _ in range(4)]
@@ -1068,6 +1072,8 @@ def main():
     ap.add_argument("--skip-cpu-baseline", action="store_true")
     ap.add_argument("--skip-batched", action="store_true")
     ap.add_argument("--skip-qwen", action="store_true")
+    ap.add_argument("--qwen-tokens", default=",".join(map(str, QWEN_T)),
+                    help="token batches of the Qwen2-57B layer leg (comma-separated)")
     ap.add_argument("--skip-ep", action="store_true")
     ap.add_argument("--skip-dense", action="store_true", help="skip the whole-model legs (Qwen2.5-14B dense, Mixtral-8x22B)")
     args = ap.parse_args()

@@ -14,6 +14,7 @@
 #include <chrono>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -326,6 +327,32 @@ int make_layer_tmaps(glc_moe* h, LayerDev& L) {
     return GLC_OK;
 }
 
+// Layouts of the grouped tensor-core GEMMs for a batch of `pairs` (token,
+// expert) pairs over `experts` experts.  Groups of up to 64 tokens (the wide
+// kernel layout) once the batch averages 32 or more pairs per expert, where
+// experts with more than 32 tokens are common and groups of 32 would
+// dequantise their weights once per 32 tokens.  The down projection runs the
+// wide kernel layout for either group size (it holds groups of 32 as well:
+// the same time on the Mixtral 64-token batch, 3 % less on the Qwen2-57B
+// 16-token one); gate/up, two matrices per raw stage, keeps the narrow
+// layout's four raw stages (two in the wide one) for groups of 32, where the
+// wide layout measured 4 % slower.  GLC_GROUPED_WIDE=0 / 1
+// forces the narrow / wide layout everywhere (read on every call).  Every
+// choice gives the same bits: an output is the same fp32 sum over the same K
+// order in both layouts.
+struct GroupedLayouts {
+    bool wide_groups, gateup_wide, down_wide;
+};
+static GroupedLayouts grouped_layouts(int pairs, int experts) {
+    const char* v = getenv("GLC_GROUPED_WIDE");
+    if (v && (v[0] == '0' || v[0] == '1') && v[1] == 0) {
+        const bool w = v[0] == '1';
+        return {w, w, w};
+    }
+    const bool w = pairs > glc::kGroupTokens && pairs >= glc::kGroupTokens * experts;
+    return {w, w, true};
+}
+
 // The shared expert of a batched call (T > 1) on the grouped tensor-core
 // path: all T tokens are one expert's groups, so its weights are read once
 // per launch whatever T is; the down projection (few 128-row tiles at small
@@ -334,12 +361,15 @@ int make_layer_tmaps(glc_moe* h, LayerDev& L) {
 int run_shared_grouped(glc_moe* h, LayerDev* L, const float* xin, int T, int* slices, cudaStream_t st) {
     const int D = h->d.hidden_dim, Fs = h->d.shared_ffn_dim;
     if (!L->sh_gate || !L->tmaps) return fail(GLC_ERR_STATE, "layer has no shared expert tensor maps");
-    CUDA_TRY(glc::dispatch_plan_launch(h->zeros_i, T, 1, h->plan_sh, st));
+    const GroupedLayouts lay = grouped_layouts(T, 1);
+    const int gtok = lay.wide_groups ? glc::kGroupTokensWide : glc::kGroupTokens;
+    CUDA_TRY(glc::dispatch_plan_launch(h->zeros_i, T, 1, h->plan_sh, st, nullptr, gtok));
     mark(h, st);
     CUDA_TRY(glc::split_rows_launch(xin, T, D, 1, 1, h->plan_sh, h->btiles, h->rscale_sh, st));
     mark(h, st);
-    const int gsh = (T + glc::kGroupTokens - 1) / glc::kGroupTokens;
+    const int gsh = (T + gtok - 1) / gtok;
     glc::GroupedParams sg{};
+    sg.wide = lay.gateup_wide;
     sg.K = D;
     sg.rows_per_e = Fs;
     sg.nm = 2;
@@ -354,13 +384,17 @@ int run_shared_grouped(glc_moe* h, LayerDev* L, const float* xin, int T, int* sl
     CUDA_TRY(glc::split_rows_launch(h->act_sh, T, Fs, 1, 0, h->plan_sh, h->btiles, h->rscale_sh, st));
     mark(h, st);
     const int tiles = gsh * (D / 128);
-    const int n = std::min(std::min(kShSlicesMax, Fs / 256), std::max(1, (h->num_sms + tiles - 1) / tiles));
+    // the K-slice count (and so the order of the partial sums) follows the
+    // narrow layout's tile count whichever layout runs: both give the same bits
+    const int tiles_n = (T + glc::kGroupTokens - 1) / glc::kGroupTokens * (D / 128);
+    const int n = std::min(std::min(kShSlicesMax, Fs / 256), std::max(1, (h->num_sms + tiles_n - 1) / tiles_n));
     glc::GroupedParams sd = sg;
     sd.K = Fs;
     sd.rows_per_e = D;
     sd.nm = 1;
     sd.out = h->ysh;
     sd.ksplit = n;
+    sd.wide = lay.down_wide;
     sd.part_stride = (long long)T * D;
     CUDA_TRY(glc::grouped_launch(L->tmap_sh_down, nullptr, sd, tiles * n, h->num_sms, st));
     mark(h, st);
@@ -379,12 +413,15 @@ int run_experts_grouped(glc_moe* h, LayerDev* L, const float* xin, int T, int k,
     const int D = h->d.hidden_dim, F = h->d.expert_ffn_dim, E = local_experts(h);
     const int P = T * k;
     if (!L->tmaps) return fail(GLC_ERR_STATE, "layer has no tensor maps");
-    CUDA_TRY(glc::dispatch_plan_launch(ids, P, E, h->plan, st, count));
+    const GroupedLayouts lay = grouped_layouts(P, E);
+    CUDA_TRY(glc::dispatch_plan_launch(ids, P, E, h->plan, st, count,
+                                       lay.wide_groups ? glc::kGroupTokensWide : glc::kGroupTokens));
     mark(h, st);
     CUDA_TRY(glc::split_rows_launch(xin, P, D, k, 1, h->plan, h->btiles, h->rscale, st, count));
     mark(h, st);
     const int gmax = glc::plan_max_groups(P, E);
     glc::GroupedParams g{};
+    g.wide = lay.gateup_wide;
     g.K = D;
     g.rows_per_e = F;
     g.nm = 2;
@@ -402,6 +439,7 @@ int run_experts_grouped(glc_moe* h, LayerDev* L, const float* xin, int T, int k,
     dn.K = F;
     dn.rows_per_e = D;
     dn.nm = 1;
+    dn.wide = lay.down_wide;
     dn.out = h->ysort;
     CUDA_TRY(glc::grouped_launch(L->tmap_down, nullptr, dn, gmax * (D / 128), h->num_sms, st));
     mark(h, st);

@@ -3,7 +3,8 @@
 // fly.  Replaces the per-token expert loop behind IClusterStageModel.ForwardBatchStage
 // (IClusterStageModel.cs:24) for MoE layers.
 //
-// One work item = (group g of <= 32 tokens routed to expert e, 128 output rows).
+// One work item = (group g of <= 32 tokens routed to expert e, 128 output rows;
+// <= 64 tokens in the wide layout below).
 //   D[128 x N] = A[128 x K] * B[N x K]^T,  A = expert weight rows (fp16 values
 //   d*sc*q - dmin*m, one rounding), B = the group's activations as fp16 hi/lo
 //   halves (N = 2 * roundup8(ntok)); the epilogue adds the hi and lo columns and
@@ -36,11 +37,15 @@
 //           tensor core near its ~44-cycle floor per M=128 MMA.
 //   w10..13 epilogue: tcgen05.ld of the accumulators, SwiGLU (gate/up) or the
 //           sum of the two K halves (down), coalesced fp32 stores per token.
-// TMEM columns: accumulator i at [64i, +64); a ring of kAUnits A units at
+// TMEM columns: accumulator i at [64i, +64); a ring of three A units at
 // [128 + 128u, +128).  The unit size is set by the tensor core: an M=128
 // kind::f16 MMA costs ~44 cycles for any N <= 64 (measured), and a wait +
 // fence + commit between every 8 MMAs nearly doubled that, so each hand-off
 // covers 16 MMAs; the ring lets dequantisation run up to two units ahead.
+// Wide layout (groups of <= 64 tokens, N <= 128): accumulator i at
+// [128i, +128), two A units at [256 + 128u, +128), B stages of 128 rows.  A
+// group's weights are dequantised once for up to 64 tokens instead of once
+// per 32; each output is the same fp32 sum over the same K order.
 #include <cuda.h>
 
 #include "common.cuh"
@@ -51,11 +56,19 @@ namespace glc {
 constexpr int kTcThreads = 16 * 32;
 constexpr int kBStages = 2;          // B-tile ring, separate from the raw-weight ring
 constexpr unsigned kPollNs = 64;     // sleep between polls of the roles that wait most (see mbar_wait_backoff)
-constexpr int kAUnits = 3;           // TMEM A ring: 3 x 128 columns after the 128 accumulator columns
-constexpr uint32_t kAccCols = 128;
 constexpr int kRawTile = 128 * 144;          // one super-block x 128 rows
-constexpr int kBStageBytes = 64 * 512;       // N_max rows x 256 K x fp16
 constexpr uint32_t kTmemCols = 512;
+
+// TMEM and B-ring layout of the narrow (WIDE = false) and wide instantiations.
+template <bool WIDE>
+struct TcLayout {
+    static constexpr int kNMax = WIDE ? 128 : 64;                 // MMA N: hi + lo columns of the group
+    static constexpr uint32_t kAccStride = WIDE ? 128u : 64u;     // TMEM columns of one accumulator
+    static constexpr uint32_t kAccCols = 2u * kAccStride;         // both accumulators
+    static constexpr int kAUnits = WIDE ? 2 : 3;                  // TMEM A ring of 128-column units
+    static constexpr int kBStageBytes = kNMax * 512;              // N_max rows x 256 K x fp16
+    static_assert(kAccCols + 128u * kAUnits <= kTmemCols, "TMEM layout exceeds the allocation");
+};
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, int y, uint64_t* bar) {
     asm volatile(
@@ -226,14 +239,14 @@ __device__ __forceinline__ void dequant_chunk(const Q4kRowHdr& hd, const uint4 q
                  : "memory")
 
 // Epilogue of one row for the group's tokens.  Accumulator i (TMEM columns
-// [64i, +64)) holds hi columns [0, HALF) and lo columns [HALF, 2 HALF).
+// [ACS i, +ACS)) holds hi columns [0, HALF) and lo columns [HALF, 2 HALF).
 // Gate/up (nm = 2): accumulator 0 = gate, 1 = up, SwiGLU.  Down (nm = 1): the
 // two accumulators are the two K halves of every super-block, added in fixed
 // order.  The tensor core waits for the accumulators to be released
 // (acc_empty) before the next work item, so up to 16 tokens (64 registers)
 // are loaded in one go and released before any arithmetic; wider groups go
 // in passes of 8 tokens (released after the last pass's loads).
-template <int HALF>
+template <int HALF, uint32_t ACS>
 __device__ __forceinline__ void epilogue_item(uint32_t trow, int nm, int ntok, const float* rs, float* o, int stride,
                                               uint64_t* acc_empty, int lane) {
     constexpr int PASS = (HALF <= 16) ? HALF : 8;
@@ -244,8 +257,8 @@ __device__ __forceinline__ void epilogue_item(uint32_t trow, int nm, int ntok, c
         for (int c = 0; c < PASS; c += 8) {
             TC_LD8(trow + (uint32_t)(p0 + c), (&ah[c]));
             TC_LD8(trow + (uint32_t)(HALF + p0 + c), (&al[c]));
-            TC_LD8(trow + 64u + (uint32_t)(p0 + c), (&bh[c]));
-            TC_LD8(trow + 64u + (uint32_t)(HALF + p0 + c), (&bl[c]));
+            TC_LD8(trow + ACS + (uint32_t)(p0 + c), (&bh[c]));
+            TC_LD8(trow + ACS + (uint32_t)(HALF + p0 + c), (&bl[c]));
         }
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
         if (p0 + PASS >= HALF) {
@@ -290,9 +303,14 @@ __device__ __forceinline__ ItemCoords item_coords(int item, int mtiles, int kspl
     return c;
 }
 
+template <bool WIDE>
 __global__ void __launch_bounds__(kTcThreads, 1)
     grouped_q4k_mma_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                            const __grid_constant__ GroupedParams p, int stages) {
+    using L = TcLayout<WIDE>;
+    constexpr int kAUnits = L::kAUnits;
+    constexpr uint32_t kAccCols = L::kAccCols;
+    constexpr int kBStageBytes = L::kBStageBytes;
     // shared memory: [kBStages][kBStageBytes] B ring (1024-aligned) | [S][nm][kRawTile] raw ring | mbarriers
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -356,6 +374,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             int it = 0;
             for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
                 const ItemCoords ic = item_coords(item, mtiles, ksplit, nsb);
+                // a group wider than this layout's B stage (a plan built for
+                // the wide layout given to the narrow one): every role stops
+                // at the same item, nothing of it issued
+                if (p.plan.grp_N[ic.g] > L::kNMax) { atomicExch(p.err, kDevBadArg); break; }
                 const int e = p.plan.grp_e[ic.g];
                 const int row0 = e * p.rows_per_e + ic.mt * 128;
                 for (int s = ic.s0; s < ic.s1; ++s, ++it) {
@@ -380,6 +402,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
                 const ItemCoords ic = item_coords(item, mtiles, ksplit, nsb);
                 const int N = p.plan.grp_N[ic.g];
+                if (N > L::kNMax) break;
                 const uint8_t* bsrc = p.btiles + (size_t)p.plan.grp_units[ic.g] * 512u * nsb;
                 for (int s = ic.s0; s < ic.s1; ++s, ++it) {
                     const int stg = it % kBStages;
@@ -403,6 +426,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         int it = 0, u = 0;                     // super-block and unit counters over all items
         for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
             const ItemCoords ic = item_coords(item, mtiles, ksplit, nsb);
+            if (p.plan.grp_N[ic.g] > L::kNMax) break;
             for (int s = ic.s0; s < ic.s1 && ok; ++s, ++it) {
                 const int stg = it % S;
                 const uint32_t ph = (uint32_t)(it / S) & 1u;
@@ -457,10 +481,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             bool ok = true;
             int it = 0, u = 0, icount = 0;
             const int upsb = (nm == 2) ? 2 : 1;
-            const uint32_t dcol = tmem + 64u * (uint32_t)v;
+            const uint32_t dcol = tmem + L::kAccStride * (uint32_t)v;
             for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x, ++icount) {
                 const ItemCoords ic = item_coords(item, mtiles, ksplit, nsb);
                 const int N = p.plan.grp_N[ic.g];
+                if (N > L::kNMax) break;
                 const uint32_t idesc = idesc_f16(N);
                 const uint32_t cstride = (uint32_t)N * 128u;  // bytes between the 4 K chunks of the B tile
                 if (!mbar_wait_backoff(acc_empty, ((uint32_t)icount & 1u) ^ 1u, p.err, kDevTimeoutEmpty, kPollNs)) { ok = false; break; }
@@ -514,17 +539,29 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const int N = p.plan.grp_N[g];
             const int ntok = p.plan.grp_ntok[g];
             const int pos0 = p.plan.grp_pos0[g];
+            if (N > L::kNMax) break;
             if (!mbar_wait_backoff(acc_full, (uint32_t)icount & 1u, p.err, kDevTimeoutFull, kPollNs)) { ok = false; break; }
             tc_fence_after();
             // a K slice writes its partial sums to its own plane of the output
             float* o = p.out + (size_t)ic.ks * (size_t)p.part_stride + (size_t)pos0 * p.rows_per_e +
                        (size_t)mt * 128 + row;
             const float* rs = p.rscale + pos0;
+            constexpr uint32_t A = L::kAccStride;
             switch (N) {  // hi columns [0, N/2), lo columns [N/2, N) of each accumulator
-                case 16: epilogue_item<8>(trow, nm, ntok, rs, o, p.rows_per_e, acc_empty, lane); break;
-                case 32: epilogue_item<16>(trow, nm, ntok, rs, o, p.rows_per_e, acc_empty, lane); break;
-                case 48: epilogue_item<24>(trow, nm, ntok, rs, o, p.rows_per_e, acc_empty, lane); break;
-                default: epilogue_item<32>(trow, nm, ntok, rs, o, p.rows_per_e, acc_empty, lane); break;
+                case 16: epilogue_item<8, A>(trow, nm, ntok, rs, o, p.rows_per_e, acc_empty, lane); break;
+                case 32: epilogue_item<16, A>(trow, nm, ntok, rs, o, p.rows_per_e, acc_empty, lane); break;
+                case 48: epilogue_item<24, A>(trow, nm, ntok, rs, o, p.rows_per_e, acc_empty, lane); break;
+                case 64: epilogue_item<32, A>(trow, nm, ntok, rs, o, p.rows_per_e, acc_empty, lane); break;
+                default:
+                    if constexpr (WIDE) {
+                        switch (N) {
+                            case 80: epilogue_item<40, A>(trow, nm, ntok, rs, o, p.rows_per_e, acc_empty, lane); break;
+                            case 96: epilogue_item<48, A>(trow, nm, ntok, rs, o, p.rows_per_e, acc_empty, lane); break;
+                            case 112: epilogue_item<56, A>(trow, nm, ntok, rs, o, p.rows_per_e, acc_empty, lane); break;
+                            default: epilogue_item<64, A>(trow, nm, ntok, rs, o, p.rows_per_e, acc_empty, lane); break;
+                        }
+                    }
+                    break;
             }
         }
     }
@@ -567,28 +604,34 @@ cudaError_t grouped_launch(const void* tmapA, const void* tmapB, const GroupedPa
     if ((p.K & 255) || (p.rows_per_e & 127) || (p.nm != 1 && p.nm != 2)) return cudaErrorInvalidValue;
     // K slices only for the plain projection (the SwiGLU epilogue needs whole sums)
     if (p.ksplit < 1 || (p.ksplit > 1 && p.nm != 1) || p.ksplit > (p.K >> 8)) return cudaErrorInvalidValue;
-    static int optin[kMaxDevices] = {0};
+    const bool wide = p.wide != 0;
+    static int optin[2][kMaxDevices] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-    if (!optin[dev]) {
+    const void* fn = wide ? (const void*)grouped_q4k_mma_kernel<true> : (const void*)grouped_q4k_mma_kernel<false>;
+    if (!optin[wide][dev]) {
         int v = 0;
         cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-        cudaError_t e = cudaFuncSetAttribute(grouped_q4k_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, v);
+        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, v);
         if (e != cudaSuccess) return e;
-        optin[dev] = v;
+        optin[wide][dev] = v;
     }
+    const size_t bring = (size_t)kBStages * (wide ? TcLayout<true>::kBStageBytes : TcLayout<false>::kBStageBytes);
     const size_t per_stage = (size_t)p.nm * kRawTile;
     const size_t fixed = 1024 + 512;  // alignment slack + mbarriers + TMEM address slot
-    int S = (int)(((size_t)optin[dev] - fixed - (size_t)kBStages * kBStageBytes) / per_stage);
+    int S = (int)(((size_t)optin[wide][dev] - fixed - bring) / per_stage);
     if (S > 8) S = 8;
     if (S < 2) return cudaErrorInvalidValue;
-    const size_t smem = fixed + (size_t)kBStages * kBStageBytes + (size_t)S * per_stage;
+    const size_t smem = fixed + bring + (size_t)S * per_stage;
     int grid = num_sms;
     if (max_items < grid) grid = max_items > 0 ? max_items : 1;
     const CUtensorMap* a = reinterpret_cast<const CUtensorMap*>(tmapA);
     const CUtensorMap* b = reinterpret_cast<const CUtensorMap*>(tmapB ? tmapB : tmapA);
-    grouped_q4k_mma_kernel<<<grid, kTcThreads, smem, st>>>(*a, *b, p, S);
+    if (wide)
+        grouped_q4k_mma_kernel<true><<<grid, kTcThreads, smem, st>>>(*a, *b, p, S);
+    else
+        grouped_q4k_mma_kernel<false><<<grid, kTcThreads, smem, st>>>(*a, *b, p, S);
     return cudaGetLastError();
 }
 

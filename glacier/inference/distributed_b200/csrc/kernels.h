@@ -223,7 +223,8 @@ int wide_decode_configure(FusedDecodeParams& p, int num_sms, size_t smem_limit, 
 cudaError_t wide_decode_launch(const FusedDecodeParams& p, int num_sms, cudaStream_t stream);
 
 // ---------------------------------------------------------------- batched path
-constexpr int kGroupTokens = 32;  // tokens per MMA group (N = 2*roundup8(ntok) <= 64)
+constexpr int kGroupTokens = 32;      // tokens per MMA group (N = 2*roundup8(ntok) <= 64)
+constexpr int kGroupTokensWide = 64;  // the wide layout's (N <= 128; see GroupedParams::wide)
 
 // Device-resident dispatch plan (all arrays device memory).
 struct DispatchPlan {
@@ -243,8 +244,10 @@ inline int plan_max_groups(int P, int E) { return E + P / kGroupTokens + 1; }
 
 // count (optional, device memory): the pairs actually present, <= P; the
 // split and combine below take the same pointer and skip the rest.
+// group_tokens: the most tokens of one expert in one MMA group (kGroupTokens,
+// or kGroupTokensWide for the grouped kernel's wide layout).
 cudaError_t dispatch_plan_launch(const int* ids, int P, int E, const DispatchPlan& plan, cudaStream_t st,
-                                 const int* count = nullptr);
+                                 const int* count = nullptr, int group_tokens = kGroupTokens);
 // B tiles: per group, per super-block s of K: [4 chunks][N rows][128 B] SWIZZLE_128B.
 cudaError_t split_rows_launch(const float* src, int P, int K, int kslots, int src_is_token,
                               const DispatchPlan& plan, uint8_t* btiles, float* rscale, cudaStream_t st,
@@ -269,6 +272,12 @@ struct GroupedParams {
     int* err;
     int ksplit = 1;       // nm=1 only: K split into ksplit slices of whole super-blocks,
     long long part_stride = 0;  // each writing partial sums to its own plane (elements apart)
+    // Groups of up to kGroupTokensWide tokens (the plan built with that group
+    // size): accumulators of 128 TMEM columns, a ring of two A units instead
+    // of three, B stages of 128 rows.  Each output column is the same sum as
+    // in the narrow layout, so the results are identical; fewer groups mean
+    // each expert's weights are dequantised fewer times.
+    int wide = 0;
 };
 // Tensor maps are built once per weight tensor (2-D [rows][rowBytes] uint8, box 144 x 128).
 int make_q4k_tensor_map(void* tmap64, const void* base, long long rows, int row_bytes);

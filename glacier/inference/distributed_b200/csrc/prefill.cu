@@ -1,7 +1,7 @@
 // prefill.cu -- batched (T > 1) MoE path around the grouped tensor-core GEMMs:
 //   * dispatch plan: token->expert histogram, exclusive offsets and a stable
 //     permutation of the (token, slot) pairs grouped by expert (ascending pair
-//     order inside an expert), plus the MMA group table (<= 32 tokens a group);
+//     order inside an expert), plus the MMA group table (<= 32 or <= 64 tokens a group);
 //   * operand split: one activation row per pair -> power-of-two row scale and
 //     fp16 hi/lo halves written straight into the SWIZZLE_128B K-major tiles the
 //     MMA reads (rows 0..N/2-1 hi, N/2..N-1 lo of each group);
@@ -20,7 +20,8 @@ constexpr int kPlanThreads = 1024;
 // count (optional, device): the pairs actually present, <= P (a batch sized
 // on the device, e.g. the rows an expert-parallel exchange delivered).
 __global__ void __launch_bounds__(kPlanThreads) dispatch_plan_kernel(const int* __restrict__ ids, int P, int E,
-                                                                     DispatchPlan plan, const int* __restrict__ count) {
+                                                                     DispatchPlan plan, const int* __restrict__ count,
+                                                                     int gtok) {
     if (count) P = min(P, *count);
     __shared__ int s_count[64];
     __shared__ int s_off[65];
@@ -42,8 +43,8 @@ __global__ void __launch_bounds__(kPlanThreads) dispatch_plan_kernel(const int* 
             s_off[e + 1] = s_off[e] + s_count[e];
             plan.counts[e] = s_count[e];
             plan.grp_first[e] = g;
-            for (int base = 0; base < s_count[e]; base += kGroupTokens) {
-                const int nt = min(kGroupTokens, s_count[e] - base);
+            for (int base = 0; base < s_count[e]; base += gtok) {
+                const int nt = min(gtok, s_count[e] - base);
                 const int N = 2 * ((nt + 7) / 8) * 8;
                 plan.grp_e[g] = e;
                 plan.grp_ntok[g] = nt;
@@ -197,9 +198,9 @@ __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ 
 }
 
 cudaError_t dispatch_plan_launch(const int* ids, int P, int E, const DispatchPlan& plan, cudaStream_t st,
-                                 const int* count) {
-    if (E > 64) return cudaErrorInvalidValue;
-    dispatch_plan_kernel<<<1, kPlanThreads, 0, st>>>(ids, P, E, plan, count);
+                                 const int* count, int group_tokens) {
+    if (E > 64 || (group_tokens != kGroupTokens && group_tokens != kGroupTokensWide)) return cudaErrorInvalidValue;
+    dispatch_plan_kernel<<<1, kPlanThreads, 0, st>>>(ids, P, E, plan, count, group_tokens);
     return cudaGetLastError();
 }
 

@@ -96,3 +96,32 @@ def test_batched_qwen_shapes_with_shared_expert(cuda, glc, oracle):
     assert np.array_equal(ids[sel], rids)
     assert rel_l2(out[sel], ro) <= LAYER_TOL
     w.dispose()
+
+
+@pytest.mark.parametrize("D,F,E,k,T,Fs", [(512, 1024, 2, 1, 150, 0), (512, 768, 8, 2, 200, 2048)])
+def test_wide_groups_equal_narrow_groups(cuda, glc, oracle, monkeypatch, D, F, E, k, T, Fs):
+    """The grouped GEMMs' wide layout (groups of up to 64 tokens, MMA N up to
+    128) against the narrow one (32 tokens, N up to 64) on batches where
+    experts hold 33..64 and more than 64 tokens (74 and 76 routed; the
+    shared expert's 200, whose down projection is K-sliced by the same count
+    in both layouts): identical outputs, and the oracle's within the layer
+    tolerance.  GLC_GROUPED_WIDE forces the layout; the default choice (wide
+    groups here, the wide down projection always) gives the same bits."""
+    L = make_layer(oracle, 6100 + T, D, F, E, k, Fs=Fs)
+    w = worker_for(glc, L, max_tokens=T)
+    x = oracle.fill_normal(6100 + T, 1, 1.0, T * D).reshape(T, D)
+    outs = {}
+    for wide in ("0", "1", ""):  # narrow, wide, the default choice
+        monkeypatch.setenv("GLC_GROUPED_WIDE", wide)
+        outs[wide] = w.forward(0, x, 1 | BATCHED)
+    monkeypatch.delenv("GLC_GROUPED_WIDE")
+    (on, idn, wn), (ow, idw, ww) = outs["0"], outs["1"]
+    assert np.bincount(idw.ravel(), minlength=E).max() > 32
+    assert np.array_equal(idn, idw) and np.array_equal(wn, ww)
+    assert np.array_equal(on, ow), float(np.abs(on - ow).max())
+    assert np.array_equal(outs[""][0], ow)
+    ro, rids, _ = oracle.moe_forward(L, x, 1)
+    assert np.array_equal(idw, rids)
+    assert rel_l2(ow, ro) <= LAYER_TOL
+    w.poll_error()
+    w.dispose()
