@@ -82,6 +82,7 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_older() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 __device__ __forceinline__ float ld_bias(const float* b, int i) { return b ? __ldg(b + i) : 0.f; }
 
@@ -150,18 +151,25 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_decode_kernel(const __gr
         const int np = max(0, min(kRound, hi - base));
         const int nold = max(0, min(np, pos - base));  // rows already in the cache
         // the round's cache rows straight into shared memory (no register
-        // staging); rows past the range are zeroed (their weights are zero)
+        // staging), K rows in one copy group and V rows in the next, so the
+        // scores start while V is in flight; rows past the range are zeroed
+        // (their weights are zero)
 #pragma unroll
         for (int j = 0; j < kLd; ++j) {
             const int idx = tid + j * kAttnThreads, rr = idx / (kHd / 8), c8 = idx - rr * (kHd / 8);
-            if (rr < nold) {
-                const size_t src = head_off + (size_t)(base + rr) * kHd + c8 * 8;
-                cp_async16(S.ks + rr * kRow + c8 * 8, p.k_cache + src);
-                cp_async16(S.vs + rr * kRow + c8 * 8, p.v_cache + src);
-            } else if (rr >= np) {
-                *reinterpret_cast<uint4*>(S.vs + rr * kRow + c8 * 8) = make_uint4(0u, 0u, 0u, 0u);
+            if (rr < nold)
+                cp_async16(S.ks + rr * kRow + c8 * 8, p.k_cache + head_off + (size_t)(base + rr) * kHd + c8 * 8);
+            else if (rr >= np)
                 *reinterpret_cast<uint4*>(S.ks + rr * kRow + c8 * 8) = make_uint4(0u, 0u, 0u, 0u);
-            }
+        }
+        cp_async_commit();
+#pragma unroll
+        for (int j = 0; j < kLd; ++j) {
+            const int idx = tid + j * kAttnThreads, rr = idx / (kHd / 8), c8 = idx - rr * (kHd / 8);
+            if (rr < nold)
+                cp_async16(S.vs + rr * kRow + c8 * 8, p.v_cache + head_off + (size_t)(base + rr) * kHd + c8 * 8);
+            else if (rr >= np)
+                *reinterpret_cast<uint4*>(S.vs + rr * kRow + c8 * 8) = make_uint4(0u, 0u, 0u, 0u);
         }
         cp_async_commit();
         if (first) {
@@ -184,7 +192,10 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_decode_kernel(const __gr
             }
             first = false;
         }
-        if (np == 0) break;  // an empty range: the partials stay (-inf, 0, 0)
+        if (np == 0) {  // an empty range: the partials stay (-inf, 0, 0)
+            cp_async_wait_all();
+            break;
+        }
         // the row of pos comes from the inputs
         if (pos >= base && pos < base + np && tid < kHd / 2) {
             const int rr = pos - base, i = tid, o_ = g * kHd;
@@ -204,16 +215,18 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_decode_kernel(const __gr
             p.v_cache[dst + i] = __half_as_ushort(v0);
             p.v_cache[dst + i + kHd / 2] = __half_as_ushort(v1);
         }
-        cp_async_wait_all();
+        cp_async_wait_older();  // this thread's K rows have landed
         __syncthreads();
 
-        // scores S = Q K^T: warp w -> positions 16 w .. 16 w + 15 (two n-tiles of 8)
+        // scores S = Q K^T: warp w -> positions 16 w .. 16 w + 15 (two n-tiles
+        // of 8); the q_hi and q_lo products in separate accumulators (four
+        // independent MMA chains instead of two), added at the end
         {
-            float sacc[2][4];
+            float sacc[2][4], sacl[2][4];
 #pragma unroll
             for (int t = 0; t < 2; ++t)
 #pragma unroll
-                for (int e = 0; e < 4; ++e) sacc[t][e] = 0.f;
+                for (int e = 0; e < 4; ++e) sacc[t][e] = sacl[t][e] = 0.f;
 #pragma unroll
             for (int k0 = 0; k0 < kHd; k0 += 16) {
                 uint32_t ah[4], al[4];
@@ -225,9 +238,13 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_decode_kernel(const __gr
                     uint32_t b0, b1;
                     ldsm_x2(S.ks + (n0 + (lane & 7)) * kRow + k0 + ((lane >> 3) & 1) * 8, b0, b1);
                     mma16816(sacc[t], ah, b0, b1);
-                    mma16816(sacc[t], al, b0, b1);
+                    mma16816(sacl[t], al, b0, b1);
                 }
             }
+#pragma unroll
+            for (int t = 0; t < 2; ++t)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) sacc[t][e] += sacl[t][e];
 #pragma unroll
             for (int t = 0; t < 2; ++t) {
                 const int col = 16 * warp + 8 * t + (lane & 3) * 2, row = lane >> 2;
@@ -271,18 +288,24 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_decode_kernel(const __gr
                 S.m[warp] = M;
             }
         }
+        cp_async_wait_all();  // this thread's V rows have landed
         __syncthreads();
 
-        // O = O * corr + P V: warp w -> dims 16 w .. 16 w + 15 (two n-tiles of 8)
+        // O = O * corr + P V: warp w -> dims 16 w .. 16 w + 15 (two n-tiles
+        // of 8); the round's p_lo products in their own accumulators, added
+        // after the loop
         {
             const int row = lane >> 2;
             const float c0 = S.corr[row], c1 = S.corr[row + 8];
+            float ol[2][4];
 #pragma unroll
             for (int t = 0; t < 2; ++t) {
                 o[t][0] *= c0;
                 o[t][1] *= c0;
                 o[t][2] *= c1;
                 o[t][3] *= c1;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) ol[t][e] = 0.f;
             }
 #pragma unroll
             for (int k0 = 0; k0 < kRound; k0 += 16) {
@@ -295,9 +318,13 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_decode_kernel(const __gr
                     uint32_t b0, b1;
                     ldsm_x2_trans(S.vs + (k0 + (lane & 7) + ((lane >> 3) & 1) * 8) * kRow + d0, b0, b1);
                     mma16816(o[t], ah, b0, b1);
-                    mma16816(o[t], al, b0, b1);
+                    mma16816(ol[t], al, b0, b1);
                 }
             }
+#pragma unroll
+            for (int t = 0; t < 2; ++t)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) o[t][e] += ol[t][e];
         }
         __syncthreads();  // the next round overwrites the staged rows, scores and exponentials
     }
